@@ -1,0 +1,317 @@
+"""Benchmark of the SMEL FT MoE expert layer on B200: tokens/s of forward + recompute + backward at the
+Qwen3.6-35B-A3B layer shape (config 2), as one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = the layer-major training unit of the reference (smel/layer_runner.py:319-364): a no-grad forward of the
+micro-batch, then a recompute under autograd and the backward (dX plus all LoRA gradients), on 4092 tokens of seeded
+synthetic input (Zipf-skewed routing, 244 int4 + 12 bf16 LoRA experts, shared expert with LoRA).
+With N > 1 (torchrun) every rank runs its own replica on its own tokens (weak scaling); the step time is the maximum
+over ranks. `--impl reference` times the CPU restatement of the reference's torch path on the host cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "smel-ft_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer tokens/s fwd+recompute+bwd (Qwen3.6 shape) and % of HBM/TC roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.index)], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def layer_config(args):
+    return dict(T=args.tokens, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=32.0)
+
+
+def config_json(cfg, meta, world):
+    return {"workload": "qwen3.6-35b-a3b moe layer (config 2): fwd + recompute + bwd", "tokens": cfg["T"],
+            "hidden": cfg["H"], "experts": cfg["E"], "top_k": cfg["K"], "expert_inter": cfg["I"],
+            "shared_inter": cfg["S"], "frozen": "int4 group-64", "lora_experts": cfg["n_sel"],
+            "lora_rank": cfg["r"], "routing": f"zipf s=1.1 over a seeded permutation, top-12 gate share "
+            f"{meta.get('share', 0):.3f}", "seed": meta.get("seed"),
+            "l2": "weights 0.53 GB > L2 126 MB: each step streams the banks from HBM",
+            "parallelism": "single" if world == 1 else f"replicas x{world} (weak scaling)"}
+
+
+# ------------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(layer, tokens, dtype=torch.float32):
+    """The reference's torch CPU path (oracle/cpu_step.py) on `tokens` tokens, one warm-up + one timed step."""
+    from oracle import cpu_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    p = cpu_step.prepare(layer, dtype=dtype, tokens=tokens)
+    gy = torch.randn(p["x"].shape, generator=torch.Generator().manual_seed(9)).to(dtype)
+    small = dict(p)
+    small["x"] = p["x"][:64]
+    cpu_step.step(small, gy[:64])  # warm-up (allocator, thread pool)
+    t0 = time.perf_counter()
+    cpu_step.step(p, gy)
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{tokens} tokens of the same layer, 1 step (fwd no-grad + recompute + bwd), {str(dtype)[6:]}, "
+                      f"{dt:.2f} s"}
+
+
+# ------------------------------------------------------------------------------------------ our arm
+def run_ours(args, world, rank, local):
+    import smelb
+    from smelb import _lib
+    from smelb.synth import flops_per_token, qwen_layer
+    dev = torch.device("cuda", local)
+    cfg = layer_config(args)
+    layer = qwen_layer(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"], n_sel=cfg["n_sel"],
+                       r=cfg["r"], alpha=cfg["alpha"], seed=rank, device=dev)
+    W, ex, lora, K = layer["W"], layer["ex"], layer["lora"], cfg["K"]
+    params = list(lora.parameters())
+    x = layer["x"]
+    gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(9), device=dev).bfloat16()
+
+    def step(xd, gd):
+        for p in params:
+            p.grad = None
+        with torch.no_grad():
+            smelb.moe_forward(xd, W, ex, K, lora)
+        xr = xd.detach().requires_grad_(True)
+        out = smelb.moe_forward(xr, W, ex, K, lora)
+        out.backward(gd)
+        return xr.grad
+
+    for _ in range(args.warmup):
+        step(x, gy)
+    torch.cuda.synchronize()
+    assert smelb.read_status() == 0, "device status word set during warm-up"
+
+    # ---------------- device-resident timing
+    clocks = Clocks(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step(x, gy)
+    e1.record()
+    torch.cuda.synchronize()
+    ck = clocks.stop()
+    launches = _lib.launch_count() - n0
+    barrier(world)
+    # the expert-GEMM launches of the same steps, timed with CUDA events on their stream (separate pass)
+    _lib.gemm_timing(True)
+    _lib.gemm_timing_read()
+    for _ in range(args.steps):
+        step(x, gy)
+    gemm_ms, gemm_n = _lib.gemm_timing_read()
+    _lib.gemm_timing(False)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    ms_step = ms / args.steps
+    value = world * cfg["T"] * args.steps / (ms / 1e3)
+
+    # ---------------- end to end through the public API with host buffers
+    xh = x.cpu().pin_memory()
+    gh = gy.cpu().pin_memory()
+    dxh = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
+    xd, gd = torch.empty_like(x), torch.empty_like(gy)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        xd.copy_(xh, non_blocking=True)
+        gd.copy_(gh, non_blocking=True)
+        dx = step(xd, gd)
+        dxh.copy_(dx, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e = {"value": world * cfg["T"] * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": xh.numel() * 2 + gh.numel() * 2, "d2h_bytes_per_step": dxh.numel() * 2}
+    assert smelb.read_status() == 0, "device status word set during the timed region"
+
+    # ---------------- roofline of the dominant kernel (the expert GEMM engine)
+    with torch.no_grad():
+        rec = {}
+        smelb.moe_forward(x, W, ex, K, lora, stats=lambda p, v, i: rec.update(i=i))
+    sel = torch.zeros(cfg["E"], dtype=torch.bool, device=dev)
+    sel[layer["meta"]["selected"]] = True
+    frac = float(sel[rec["i"]].float().mean())
+    f_tok = flops_per_token(cfg["H"], cfg["E"], cfg["K"], cfg["I"], cfg["S"], n_lora_rows_frac=frac, r=cfg["r"])
+    flops_step = 3 * f_tok * cfg["T"]  # forward + recompute + backward (dX), LoRA terms included per pass
+    pk, pk_kind = peaks()
+    gemm_ms_step = gemm_ms / args.steps
+    achieved = flops_step / (gemm_ms_step / 1e3) / 1e12
+    peak = pk["bf16_tflops"]
+    roof = {"bound": "tensor", "kernel": "moe_gemm_kernel (all expert / router / LoRA GEMMs of the step)",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "peak_kind": f"{pk_kind} bf16 burst", "traffic": None,
+            "gemm_ms_per_step": round(gemm_ms_step, 4), "gemm_launches_per_step": gemm_n // max(args.steps, 1),
+            "algorithmic_flops_per_step": flops_step,
+            "layer_frac_of_roofline": round((flops_step / (ms_step / 1e3) / 1e12) / peak, 4)}
+    res = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random-init weights of the layer shape)",
+           "config": config_json(cfg, layer["meta"], world), "roofline": roof, "e2e": e2e,
+           "gpu_launches": int(launches), "clocks": ck}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(layer, min(cfg["T"], args.cpu_tokens))
+    return res
+
+
+# ------------------------------------------------------------------------------------------ reference arm
+def run_reference(args, world, rank):
+    """The reference's CPU torch path (restated in oracle/cpu_step.py) on the host cores, same metric and config."""
+    if rank != 0:
+        return None
+    from oracle import cpu_step
+    from smelb.synth import qwen_layer
+    cfg = layer_config(args)
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    if dev.type == "cpu":
+        return {"impl": "reference", "unavailable": "building the synthetic layer needs the GPU quantizer"}
+    layer = qwen_layer(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"], n_sel=cfg["n_sel"],
+                       r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = min(cfg["T"], args.ref_tokens)
+    p = cpu_step.prepare(layer, dtype=torch.float32, tokens=tokens)
+    gy = torch.randn(p["x"].shape, generator=torch.Generator().manual_seed(9))
+    del layer
+    torch.cuda.empty_cache()
+    times = []
+    budget = args.ref_budget_s
+    t_start = time.perf_counter()
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        cpu_step.step(p, gy)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+        if time.perf_counter() - t_start > budget and len(times) >= 1:
+            break
+    tot = sum(times)
+    value = tokens * len(times) / tot
+    res = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": len(times),
+           "warmup": args.warmup, "ms_per_step": round(1e3 * tot / len(times), 2), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+           "config": config_json(cfg, {"seed": 0}, 1), "impl": "reference",
+           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                            "kind": "port", "sample": f"{tokens} tokens per step, fp32 (the reference's faster CPU "
+                                                      f"dtype), {len(times)} timed steps"},
+           "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=4092)
+    ap.add_argument("--cpu-tokens", type=int, default=4092, help="tokens of the CPU-baseline sample")
+    ap.add_argument("--ref-tokens", type=int, default=4092, help="tokens per reference-arm step")
+    ap.add_argument("--ref-budget-s", type=float, default=150.0, help="stop the reference arm after this long")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, world, rank)
+        else:
+            res = run_ours(args, world, rank, local)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,203 @@
+/*
+ * smelb — B200 (sm_100a) implementation of the SMEL FT MoE expert layer, C ABI.
+ *
+ * Conventions
+ *   - All tensors are device pointers to row-major, contiguous storage. bf16 values are passed as `void*`.
+ *   - `stream` is a cudaStream_t passed as `void*` (NULL = legacy default stream). Every call is stream-ordered and
+ *     keeps no state between calls except a per-device 4-byte status word (see smelb_read_status).
+ *   - Every function returns 0 on success or a negative SMELB_ERR_* code; smelb_last_error() gives the text.
+ *   - Nothing here allocates memory except the per-device status word (4 bytes, on first use) — the caller owns and
+ *     passes every buffer.
+ *
+ * Reference interfaces (paths relative to the smel-ft source tree) are cited per entry point.
+ */
+#ifndef SMELB_H
+#define SMELB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SMELB_OK 0
+#define SMELB_ERR_SHAPE (-1)
+#define SMELB_ERR_DTYPE (-2)
+#define SMELB_ERR_WORKSPACE (-3)
+#define SMELB_ERR_TIMEOUT (-4)
+#define SMELB_ERR_CUDA (-5)
+#define SMELB_ERR_ARG (-6)
+
+#define SMELB_ACT_SILU 0      /* moe.py:91-96 act("silu") */
+#define SMELB_ACT_GELU_TANH 1 /* moe.py:91-96 act("gelu_tanh") */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int smelb_version(void);
+
+/* Copies the text of the last error of the calling thread into buf (NUL-terminated). Returns its length. */
+int smelb_last_error(char* buf, size_t len);
+
+/* Synchronizes `device` and reads its status word: 0, or the code of the first device-side wait that gave up
+ * (a pipeline barrier that was never satisfied) or of an out-of-range expert index. reset != 0 clears it. */
+int smelb_read_status(int device, int* status, int reset);
+
+/* ---------------------------------------------------------------------------------------------------- int4 format
+ * smel/quant.py:74-94 dequant_int4 / dequant_int4_torch: q uint8 [rows, k/2] (low nibble = even column),
+ * scale/zero bf16 [rows, groups] -> out [rows, k], out = q * scale + zero computed in fp32 and rounded once to the
+ * output type (bf16, or fp32 when out_fp32 != 0). */
+int smelb_int4_dequant(const void* q, const void* scale, const void* zero, void* out, int64_t rows, int64_t k,
+                       int64_t groups, int out_fp32, void* stream);
+
+/* smel/moe.py:35-55 Int4Experts: builds the (scale | zero << 16) uint32 pairs transposed to [nw, groups, rows],
+ * the layout the fused expert GEMMs stage per k-block. scale/zero bf16 [nw, rows, groups]. */
+int smelb_int4_pack_sz(const void* scale, const void* zero, uint32_t* sz_t, int64_t nw, int64_t rows,
+                       int64_t groups, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- routing
+ * smel/moe.py:162-167 route (softmax / top-k / renorm part) and moe.py:178-180 (route_gemma4 tail):
+ * logits bf16 [T, E] (row pitch ld elements) -> probs fp32 [T, E], topv [T, K] (bf16, or fp32 if topv_fp32),
+ * topi int64 [T, K]. Ties in probs are broken towards the smaller expert id. per_expert_scale (bf16 [E]) may be NULL.
+ * E <= 512, K <= 32. */
+int smelb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t K, float* probs, void* topv,
+                      int topv_fp32, int64_t* topi, const void* per_expert_scale, void* stream);
+
+/* Backward of smelb_router_topk: d topv -> d logits (bf16 [T, E], row pitch ld). */
+int smelb_router_bwd(const void* dtopv, int dtopv_fp32, const float* probs, const int64_t* topi,
+                     const void* per_expert_scale, int64_t T, int64_t E, int64_t K, void* dlogits, int64_t ld,
+                     void* stream);
+
+/* smel/moe.py:216-223 (routed_experts dispatch): stable counting sort of topi.reshape(-1).
+ *   counts[E]    int32  tokens per expert                   (bincount)
+ *   gcounts[E]   int32  rows of each expert's segment (counts, rounded up to `pad` for experts with sel_mask[e])
+ *   offsets[E]   int32  first row of each expert's segment
+ *   row_of[T*K]  int32  dispatch row of choice t*K+k
+ *   src_of[max]  int32  choice of each dispatch row (-1 on padding rows); max = T*K + (#selected) * pad
+ *   order[T*K]   int64  torch.argsort(topi.reshape(-1), stable=True)
+ *   total[1]     int32  rows used
+ * sel_mask (uint8 [E]) may be NULL (no padding). E <= 512. */
+int smelb_dispatch_plan(const int64_t* topi, int64_t T, int64_t K, int64_t E, const uint8_t* sel_mask, int64_t pad,
+                        int32_t* counts, int32_t* gcounts, int32_t* offsets, int32_t* row_of, int32_t* src_of,
+                        int64_t* order, int32_t* total, void* stream);
+
+/* xs[row] = x[src_of[row] / K] (zeros on padding rows) for rows < total[0]. x bf16 [T, H], xs bf16 [max_rows, H]. */
+int smelb_gather_rows(const void* x, int64_t H, int64_t K, const int32_t* src_of, const int32_t* total,
+                      int64_t max_rows, void* xs, void* stream);
+
+/* smel/moe.py:248-252 combine: out[t] = bf16(sum_k fp32(y[row_of[t,k]]) * fp32(topv[t,k])), k in order. */
+int smelb_combine_fwd(const void* y, const int32_t* row_of, const void* topv, int topv_fp32, int64_t T, int64_t K,
+                      int64_t H, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- experts
+ * smel/moe.py:110-126 FrozenExpertsFn.forward / frozen_experts_forward: xs bf16 [rows, H] grouped by expert with
+ * counts (device int32 [E], sum = rows); int4 bank gate_up (q [E, 2I, H/2], sz_t [E, H/64, 2I]) and down
+ * (q [E, H, I/2], sz_t [E, I/64, H]); out bf16 [rows, H]. h_save (bf16 [rows, 2I]) may be NULL; a_buf
+ * (bf16 [rows, I]) is caller scratch. The int4 unpack and group-64 dequant happen inside the GEMM producer. */
+int smelb_frozen_experts_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E,
+                             const void* gu_q, const uint32_t* gu_sz, const void* dn_q, const uint32_t* dn_sz,
+                             int act, void* h_save, void* a_buf, void* out, void* stream);
+
+/* smel/moe.py:128-143 FrozenExpertsFn.backward: dx = dh @ W_gu with dh from dy @ W_dn and the activation gradient
+ * (fp32). h (bf16 [rows, 2I]) is the saved gate/up pre-activation; when NULL it is recomputed into dh_buf's
+ * companion h_buf. dh_buf bf16 [rows, 2I] and h_buf bf16 [rows, 2I] are caller scratch. */
+int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
+                             const int32_t* counts, int64_t E, const void* gu_q, const uint32_t* gu_sz,
+                             const void* dn_q, const uint32_t* dn_sz, int act, const void* h, void* h_buf,
+                             void* dh_buf, void* dx, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- the layer
+ * smel/moe.py:255-263 moe_forward (route -> routed_experts -> + shared_mlp) and its autograd backward, as two calls.
+ * The flags select sub-paths so the same calls also serve route (moe.py:162-167), routed_experts (moe.py:214-252)
+ * and mlp_lora / shared_mlp (moe.py:183-201). */
+#define SMELB_F_ROUTER 1       /* compute routing from x and w_router (else topv_in / topi_in are used) */
+#define SMELB_F_ROUTED 2       /* routed experts (frozen int4 bank + selected bf16 experts with LoRA) */
+#define SMELB_F_SHARED 4       /* shared expert / dense MLP with LoRA */
+#define SMELB_F_SHARED_GATE 8  /* multiply the shared expert by sigmoid(x @ w_sgate^T) */
+#define SMELB_F_SAVE 16        /* keep activations for smelb_moe_layer_bwd */
+#define SMELB_F_TOPV_FP32 32   /* topv / topv_in are fp32 (Gemma 4 routing) */
+
+typedef struct smelb_moe_layer {
+  /* shapes */
+  int64_t T, H, E, K;   /* tokens, hidden, experts, top-k */
+  int64_t I;            /* routed expert intermediate size */
+  int64_t S;            /* shared expert intermediate size */
+  int64_t n_sel;        /* selected (trainable bf16) experts */
+  int64_t r_sel, r_sh;  /* LoRA ranks (0 = no LoRA) */
+  float s_sel, s_sh;    /* LoRA scales alpha / r */
+  int32_t act;          /* SMELB_ACT_* */
+  int32_t flags;        /* SMELB_F_* */
+  int64_t max_rows;     /* rows of the dispatch buffers: T*K + n_sel*64 */
+  void* stream;
+  /* inputs */
+  const void* x;            /* bf16 [T, H] */
+  const void* w_router;     /* bf16 [E, H] */
+  const void* w_sgate;      /* bf16 [1, H] */
+  const void* topv_in;      /* [T, K] when routing is given */
+  const int64_t* topi_in;   /* [T, K] */
+  const int32_t* tok_count; /* device int32 [1] = T */
+  const void* gu_q; const uint32_t* gu_sz; /* [E, 2I, H/2] u8, [E, H/64, 2I] */
+  const void* dn_q; const uint32_t* dn_sz; /* [E, H, I/2] u8, [E, I/64, H] */
+  const int32_t* frozen_ids; /* device int32 [E - n_sel], ascending */
+  const int32_t* sel_ids;    /* device int32 [n_sel], slot order */
+  const int32_t* sel_slots;  /* device int32 [n_sel] = 0..n_sel-1 */
+  const uint8_t* sel_mask;   /* device uint8 [E] */
+  const void* sel_gu;        /* bf16 [n_sel, 2I, H] */
+  const void* sel_dn;        /* bf16 [n_sel, H, I] */
+  const float *A_gate, *B_gate, *A_up, *B_up, *A_down, *B_down; /* [n,r,H] [n,I,r] [n,r,H] [n,I,r] [n,r,I] [n,H,r] */
+  const void* sh_gu;         /* bf16 [2S, H]: gate rows then up rows */
+  const void* sh_dn;         /* bf16 [H, S] */
+  const float *shA_gate, *shB_gate, *shA_up, *shB_up, *shA_down, *shB_down;
+  /* outputs and activations (bf16 unless noted; R = max_rows; W64 = 64 columns, zero-initialised) */
+  void* out;                /* [T, H] */
+  float* probs;             /* fp32 [T, E] */
+  void* topv;               /* [T, K] */
+  int64_t* topi;            /* [T, K] */
+  void* logits;             /* [T, E] */
+  void* sgate_logit;        /* [T] */
+  int32_t *counts, *gcounts, *offsets, *row_of, *src_of, *total; /* [E] [E] [E] [T*K] [R] [1] */
+  int64_t* order;           /* [T*K] */
+  void *xs, *h, *a, *y;     /* [R, H] [R, 2I] [R, I] [R, H] */
+  void *xa, *z;             /* [R, W64] */
+  void *sh_xa, *sh_h, *sh_a, *sh_z, *sh_y; /* [T, W64] [T, 2S] [T, S] [T, W64] [T, H] */
+  void *p_xa_w, *p_gu_ext, *p_z_w, *p_dn_ext;     /* [n,2r,H] [n,2I,W64] [n,r,I] [n,H,W64] */
+  void *sp_xa_w, *sp_gu_ext, *sp_z_w, *sp_dn_ext; /* [2r,H] [2S,W64] [r,S] [H,W64] */
+  /* backward */
+  const void* g;            /* [T, H] upstream gradient */
+  void* dx;                 /* [T, H] */
+  void *dy, *dh, *dxs;      /* [R, H] [R, 2I] [R, H] */
+  void *dz, *dxa;           /* [R, W64] */
+  void *dtopv, *dlogits, *dx_router; /* [T, K] [T, Epad64] zero-initialised, [T, H] */
+  void *sh_dy, *sh_dh, *sh_dx;       /* [T, H] [T, 2S] [T, H] */
+  void *sh_dz, *sh_dxa;              /* [T, W64] */
+  float* dgl;                        /* fp32 [T] */
+  void *p_dz_w, *p_da_ext, *p_dxa_w, *p_dx_ext;     /* [n,r,H] [n,I,W64] [n,2r,2I] [n,H,W64] */
+  void *sp_dz_w, *sp_da_ext, *sp_dxa_w, *sp_dx_ext; /* [r,H] [S,W64] [2r,2S] [H,W64] */
+  float *gA_gate, *gB_gate, *gA_up, *gB_up, *gA_down, *gB_down;             /* LoRA grads, shapes of the params */
+  float *gshA_gate, *gshB_gate, *gshA_up, *gshB_up, *gshA_down, *gshB_down;
+  /* optional */
+  const float* dprobs;      /* fp32 [T, E] gradient w.r.t. probs (F_ROUTER backward), may be NULL */
+  const void* fz_gu;        /* frozen bank in bf16 instead of int4 (gu_q == NULL): [E, 2I, H] (moe.py:18-32) */
+  const void* fz_dn;        /* [E, H, I] */
+  int32_t act_sh;           /* activation of the shared expert / dense MLP (SMELB_ACT_*) */
+  int32_t reserved;
+} smelb_moe_layer;
+
+/* Instrumentation. smelb_launch_count: kernels launched by this library so far (all entry points).
+ * smelb_gemm_timing(1) records a CUDA event pair on the launching stream around every expert-GEMM launch;
+ * smelb_gemm_timing_read synchronizes on them and returns the summed duration (ms) and the number of launches
+ * recorded since the previous read. */
+long long smelb_launch_count(void);
+int smelb_gemm_timing(int enable);
+int smelb_gemm_timing_read(double* ms_total, long long* launches);
+
+/* sizeof(smelb_moe_layer), for bindings to check their mirror of the struct. */
+size_t smelb_moe_layer_size(void);
+
+int smelb_moe_layer_fwd(const smelb_moe_layer* L);
+int smelb_moe_layer_bwd(const smelb_moe_layer* L);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMELB_H */

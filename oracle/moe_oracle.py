@@ -1,0 +1,283 @@
+"""CPU oracle for the smelb MoE layer — TEST INFRASTRUCTURE ONLY.
+
+A restatement, on the CPU, of the reference algorithm of SMEL FT's MoE expert layer (smel/moe.py, smel/quant.py,
+smel/lora.py of the smel-ft source tree). Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline use it,
+as the checker / baseline; the product (smel-ft_b200/smelb) never imports it.
+
+Integer and byte work (int4 pack / unpack, the stable dispatch permutation) is numpy; floating-point work is torch on
+the CPU in the dtype the caller passes (fp32 for parity, fp64 for tight checks), with gradients by torch autograd of
+the same forward math. Each function names the reference lines it restates.
+
+Pinning: tests/golden/*.pt hold input/output vectors produced by the reference itself (tests/golden/make_golden.py,
+run where the reference is importable); tests/test_oracle.py checks this oracle against them.
+"""
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+GELU_C = 0.7978845608028654  # sqrt(2 / pi)
+
+
+# ============================================================================================== int4 format
+def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=(1.0, 0.95, 0.9, 0.85, 0.8)) -> dict:
+    """smel/quant.py:5-44. Per group of `group` values along the last dim: try each clip factor c (range shrunk
+    towards the group midpoint), scale = bf16(max((hi - lo) / 15, 1e-8)), zero = bf16(lo),
+    q = clamp(round((w - zero) / scale), 0, 15); keep the first c with the smallest squared error.
+    Packs two codes per byte, the even column in the low nibble."""
+    w = w.detach().cpu()
+    if w.dim() == 3 and w.shape[0] > 16:
+        parts = [quantize_int4(w[i:i + 16], group, clip_search) for i in range(0, w.shape[0], 16)]
+        return {k: torch.cat([p[k] for p in parts]) for k in parts[0]}
+    K = w.shape[-1]
+    assert K % group == 0 and group % 2 == 0
+    wg = w.float().reshape(*w.shape[:-1], K // group, group)
+    lo0 = wg.amin(-1, keepdim=True)
+    hi0 = wg.amax(-1, keepdim=True)
+    mid = (lo0 + hi0) / 2
+    best = None
+    for c in clip_search:
+        lo = mid + (lo0 - mid) * c
+        hi = mid + (hi0 - mid) * c
+        scale = ((hi - lo) / 15).clamp_min(1e-8).to(torch.bfloat16).float()
+        zero = lo.to(torch.bfloat16).float()
+        q = torch.round((wg - zero) / scale).clamp_(0, 15)
+        err = (q * scale + zero - wg).pow(2).sum(-1, keepdim=True)
+        if best is None:
+            best = [err, q, scale, zero]
+        else:
+            m = err < best[0]
+            best = [torch.where(m, err, best[0]), torch.where(m, q, best[1]), torch.where(m, scale, best[2]),
+                    torch.where(m, zero, best[3])]
+    codes = best[1].to(torch.uint8).reshape(*w.shape[:-1], K).numpy()
+    packed = pack_nibbles(codes)
+    return {"q": torch.from_numpy(packed), "scale": best[2].squeeze(-1).to(torch.bfloat16),
+            "zero": best[3].squeeze(-1).to(torch.bfloat16)}
+
+
+def pack_nibbles(codes: np.ndarray) -> np.ndarray:
+    """codes uint8 [..., K] (0..15) -> bytes [..., K/2]; byte j = codes[2j] | codes[2j+1] << 4 (quant.py:42)."""
+    return (codes[..., 0::2] | (codes[..., 1::2] << 4)).astype(np.uint8)
+
+
+def unpack_nibbles(q: np.ndarray) -> np.ndarray:
+    """bytes [..., K/2] -> codes [..., K]: column 2j = low nibble, 2j+1 = high nibble (quant.py:58-65, 90-92)."""
+    q = np.asarray(q, dtype=np.uint8)
+    out = np.empty(q.shape[:-1] + (q.shape[-1] * 2,), dtype=np.uint8)
+    out[..., 0::2] = q & 0xF
+    out[..., 1::2] = q >> 4
+    return out
+
+
+def dequant_int4(q, scale, zero, dtype=torch.float32) -> torch.Tensor:
+    """codes * scale + zero computed in fp32 (quant.py:63-64 / :87-94 with fp32 compute), then cast once."""
+    codes = torch.from_numpy(unpack_nibbles(q.cpu().numpy() if isinstance(q, torch.Tensor) else q)).float()
+    s, z = scale.cpu().float(), zero.cpu().float()
+    G = s.shape[-1]
+    K = codes.shape[-1]
+    w = codes.reshape(*codes.shape[:-1], G, K // G) * s.unsqueeze(-1) + z.unsqueeze(-1)
+    return w.reshape(*codes.shape[:-1], K).to(dtype)
+
+
+# ============================================================================================== routing
+def route(x, gate_w, top_k, logits_dtype=None):
+    """smel/moe.py:162-167: logits = x W^T (in the activation dtype), probs = softmax_fp32, top-k, renormalised in
+    fp32, cast back to the logits dtype. Ties in probs go to the smaller expert id (a stable descending sort)."""
+    logits = F.linear(x, gate_w)
+    if logits_dtype is not None:
+        logits = logits.to(logits_dtype)
+    return route_from_logits(logits, top_k)
+
+
+def route_from_logits(logits, top_k):
+    probs = torch.softmax(logits, dim=-1, dtype=torch.float32)
+    topi = topk_stable(probs, top_k)
+    topv = probs.gather(1, topi)
+    topv = topv / topv.sum(dim=-1, keepdim=True)
+    return probs, topv.to(logits.dtype), topi
+
+
+def topk_stable(probs, k):
+    """Top-k indices ordered by value descending, ties by ascending index (numpy stable sort on -probs)."""
+    p = probs.detach().cpu().double().numpy()
+    idx = np.argsort(-p, axis=-1, kind="stable")[..., :k]
+    return torch.from_numpy(idx.astype(np.int64))
+
+
+def forced_route(logits_or_probs, topi, from_probs=False):
+    """Routing weights at given expert choices (tests/helpers.py:89-106 patch_hf_routing): probs gathered at topi and
+    renormalised."""
+    probs = logits_or_probs if from_probs else torch.softmax(logits_or_probs, dim=-1, dtype=torch.float32)
+    top = probs.gather(1, topi)
+    return probs, top / top.sum(dim=-1, keepdim=True)
+
+
+# ============================================================================================== dispatch
+def dispatch(topi: np.ndarray, E: int):
+    """smel/moe.py:218-223: order = stable argsort of topi.reshape(-1); tok = order // K; counts = bincount."""
+    topi = np.asarray(topi)
+    K = topi.shape[1]
+    flat = topi.reshape(-1)
+    order = np.argsort(flat, kind="stable").astype(np.int64)
+    counts = np.bincount(flat, minlength=E).astype(np.int64)
+    return order, order // K, counts
+
+
+def dispatch_padded(topi: np.ndarray, E: int, sel_mask: np.ndarray, pad: int = 64):
+    """The dispatch layout of the fused path: experts in id order, selected experts' segments padded to `pad` rows.
+    Returns (counts, gcounts, offsets, row_of [T*K], src_of [total] with -1 on padding rows)."""
+    flat = np.asarray(topi).reshape(-1)
+    counts = np.bincount(flat, minlength=E).astype(np.int64)
+    gcounts = np.where(sel_mask.astype(bool), (counts + pad - 1) // pad * pad, counts)
+    offsets = np.concatenate([[0], np.cumsum(gcounts)[:-1]]).astype(np.int64)
+    row_of = np.empty(flat.shape[0], dtype=np.int64)
+    src_of = -np.ones(int(gcounts.sum()), dtype=np.int64)
+    seen = np.zeros(E, dtype=np.int64)
+    for i, e in enumerate(flat):  # stable: choices of one expert keep (t, k) order
+        r = offsets[e] + seen[e]
+        seen[e] += 1
+        row_of[i] = r
+        src_of[r] = i
+    return counts, gcounts, offsets, row_of, src_of
+
+
+# ============================================================================================== experts
+def act(x, name):
+    """smel/moe.py:91-96"""
+    if name == "silu":
+        return F.silu(x)
+    if name == "gelu_tanh":
+        return F.gelu(x, approximate="tanh")
+    raise ValueError(f"unknown activation {name}")
+
+
+def act_and_grad(g, name):
+    """smel/moe.py:99-107: (act(g), d act / d g) in the dtype of g."""
+    if name == "silu":
+        sg = torch.sigmoid(g)
+        return g * sg, sg * (1 + g * (1 - sg))
+    t = torch.tanh(GELU_C * (g + 0.044715 * g ** 3))
+    return 0.5 * g * (1 + t), 0.5 * (1 + t) + 0.5 * g * (1 - t * t) * GELU_C * (1 + 3 * 0.044715 * g * g)
+
+
+def frozen_experts(xs, counts, gu, dn, act_name="silu"):
+    """smel/moe.py:110-117 (per-expert loop of _gmm, moe.py:67-72): rows grouped by expert; gu [E, 2I, H],
+    dn [E, H, I] (already dequantized)."""
+    outs, s = [], 0
+    for e, c in enumerate(list(counts)):
+        c = int(c)
+        if c:
+            h = xs[s:s + c] @ gu[e].t()
+            g, u = h.chunk(2, dim=-1)
+            outs.append((act(g, act_name) * u) @ dn[e].t())
+            s += c
+    return torch.cat(outs) if outs else xs.new_zeros(0, dn.shape[1])
+
+
+def frozen_experts_backward(xs, dy, counts, gu, dn, act_name="silu"):
+    """smel/moe.py:128-143: dx of the frozen experts (no weight gradients)."""
+    dxs, s = [], 0
+    for e, c in enumerate(list(counts)):
+        c = int(c)
+        if c:
+            h = xs[s:s + c] @ gu[e].t()
+            g, u = h.chunk(2, dim=-1)
+            da = dy[s:s + c] @ dn[e]
+            a, dadg = act_and_grad(g, act_name)
+            dh = torch.cat([da * u * dadg, da * a], dim=-1)
+            dxs.append(dh @ gu[e])
+            s += c
+    return torch.cat(dxs) if dxs else xs.new_zeros(0, xs.shape[1])
+
+
+def lora_linear(x, w, A, B, scale):
+    """smel/lora.py:61-69: x W^T + scale (x A^T) B^T."""
+    y = x @ w.t()
+    if A is None:
+        return y
+    return y + scale * ((x @ A.to(x.dtype).t()) @ B.to(x.dtype).t())
+
+
+def mlp(x, w_gate, w_up, w_down, lora, act_name="silu"):
+    """smel/moe.py:183-194 (gate and up through lora_linear, smel/lora.py:72-83 is the same math stacked).
+    lora: None or dict with A_gate, B_gate, A_up, B_up, A_down, B_down, scale."""
+    L = lora or {}
+    s = L.get("scale", 0.0)
+    g = lora_linear(x, w_gate, L.get("A_gate"), L.get("B_gate"), s)
+    u = lora_linear(x, w_up, L.get("A_up"), L.get("B_up"), s)
+    return lora_linear(act(g, act_name) * u, w_down, L.get("A_down"), L.get("B_down"), s)
+
+
+def moe_layer(x, W, bank_gu, bank_dn, top_k, sel_ids=(), sel_gu=None, sel_dn=None, lora_ex=None, lora_sh=None,
+              act_name="silu", topi=None, logits=None):
+    """smel/moe.py:255-263 moe_forward (route -> routed_experts -> + shared_mlp), in the dtype of x.
+
+    bank_gu [E, 2I, H] / bank_dn [E, H, I]: the frozen bank, dequantized. Selected experts (sel_ids, slot order) use
+    sel_gu / sel_dn and per-slot LoRA (lora_ex: dict of [k, ...] tensors + scale). topi forces the expert choices
+    (tests/helpers.py:89-106); logits, when given, replace x W_gate^T (to route on another implementation's logits).
+    Returns (out, probs, topv, topi). Differentiable in x and the LoRA tensors (torch autograd)."""
+    if logits is None:
+        logits = F.linear(x, W["mlp.gate.weight"].to(x.dtype))
+    probs = torch.softmax(logits.to(x.dtype), dim=-1, dtype=torch.float32)
+    if topi is None:
+        topi = topk_stable(probs, top_k)
+    top = probs.gather(1, topi)
+    topv = (top / top.sum(dim=-1, keepdim=True)).to(x.dtype)
+    N, H = x.shape
+    K = topi.shape[1]
+    E = bank_gu.shape[0]
+    order, tok, counts = dispatch(topi.numpy(), E)
+    xs = x[torch.from_numpy(tok)]
+    e_sorted = topi.reshape(-1)[torch.from_numpy(order)]
+    slot = {int(e): j for j, e in enumerate(sel_ids)}
+    y = x.new_zeros(xs.shape[0], H)
+    rows_out, vals = [], []
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    for e in range(E):
+        c = int(counts[e])
+        if c == 0:
+            continue
+        r0 = int(starts[e])
+        xe = xs[r0:r0 + c]
+        if e in slot:  # moe.py:204-211 _selected_expert with lora.py:61-83
+            j = slot[e]
+            L = None if lora_ex is None else {k: (v[j] if k != "scale" else v) for k, v in lora_ex.items()}
+            I = sel_dn.shape[2]
+            ye = mlp(xe, sel_gu[j][:I], sel_gu[j][I:], sel_dn[j], L, act_name)
+        else:
+            I = bank_dn.shape[2]
+            g, u = (xe @ bank_gu[e].t()).chunk(2, dim=-1)
+            ye = (act(g, act_name) * u) @ bank_dn[e].t()
+        rows_out.append(torch.arange(r0, r0 + c))
+        vals.append(ye)
+    if rows_out:
+        y = y.index_put((torch.cat(rows_out),), torch.cat(vals))
+    inv = torch.empty(order.shape[0], dtype=torch.long)
+    inv[torch.from_numpy(order)] = torch.arange(order.shape[0])
+    yk = y[inv].view(N, K, H)
+    routed = (yk.float() * topv.float().unsqueeze(-1)).sum(1).to(x.dtype)  # moe.py:248-252
+    pre = "mlp.shared_expert."
+    sh = mlp(x, W[pre + "gate_proj.weight"].to(x.dtype), W[pre + "up_proj.weight"].to(x.dtype),
+             W[pre + "down_proj.weight"].to(x.dtype), lora_sh, "silu")
+    sh = sh * torch.sigmoid(F.linear(x, W["mlp.shared_expert_gate.weight"].to(x.dtype)))  # moe.py:197-201
+    return routed + sh, probs, topv, topi
+
+
+# ============================================================================================== metrics
+def rel_err(a, b) -> float:
+    """||a - b|| / ||b|| (smel/quant.py:108-110)."""
+    a, b = a.detach().double(), b.detach().double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def cosine(a, b) -> float:
+    a, b = a.detach().double().flatten(), b.detach().double().flatten()
+    return float((a @ b) / (a.norm() * b.norm()).clamp_min(1e-300))
+
+
+def kaiming_a(shape, gen):
+    """PEFT's LoRA-A init (kaiming_uniform_(a=sqrt(5)) on each [r, in] matrix, smel/lora.py:8-11): uniform in
+    +-1/sqrt(in)."""
+    bound = 1.0 / math.sqrt(shape[-1])
+    return (torch.rand(*shape, generator=gen) * 2 - 1) * bound

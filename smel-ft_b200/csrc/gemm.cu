@@ -1,0 +1,576 @@
+// Persistent grouped multi-problem GEMM for sm_100a: a TMA producer warp, a single-thread tcgen05.mma issuer with
+// TMEM accumulators (double-buffered across tiles), four int4 dequant warps and four epilogue warps. See gemm.cuh
+// for the operand conventions.
+#include "gemm.cuh"
+#include "host.h"
+
+namespace smelb {
+
+// ------------------------------------------------------------------------------------------ shared-memory plan
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kAStageBytes;
+constexpr int kOffQ = kOffB + kStages * kBStageBytes;
+constexpr int kOffSZ = kOffQ + kStages * kQStageBytes;
+constexpr int kOffTab = kOffSZ + kStages * kSZStageBytes;
+constexpr int kTabInts = 3 * kMaxGroups + (kMaxGroups + kMaxProblems) + (kMaxProblems + 1) + kMaxProblems;
+constexpr int kOffBar = (kOffTab + kTabInts * 4 + 7) & ~7;
+constexpr int kNumBars = 3 * kStages + 5;
+constexpr int kOffTmem = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffTmem + 16;
+constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment of the dynamic buffer
+static_assert(kSmemAlloc <= 232448, "shared memory budget exceeded");
+
+struct TileInfo {
+  int p, g, widx, mt, m0, n0, n_valid, nkb;
+};
+
+struct Tables {
+  int* gcnt;    // [kMaxGroups] tokens of each group
+  int* goff;    // [kMaxGroups] first token row of each group
+  int* gw;      // [kMaxGroups] weight index of each group
+  int* gpre;    // [kMaxGroups + kMaxProblems] exclusive prefix of token tiles per problem (kTokN)
+  int* tstart;  // [kMaxProblems + 1] first global tile of each problem
+  int* gbase;   // [kMaxProblems] first group slot of each problem
+};
+
+__device__ __forceinline__ int mtiles_of(const Problem& P) {
+  if (P.mode == kTokN && P.epi == kEpiGlu) return (P.inter + 63) / 64;
+  return (P.M + kBM - 1) / kBM;
+}
+
+__device__ __forceinline__ TileInfo decode_tile(const LaunchArgs& args, const Tables& T, int t) {
+  TileInfo ti;
+  int p = 0;
+  while (p + 1 < args.nprob && t >= T.tstart[p + 1]) ++p;
+  const Problem& P = args.p[p];
+  const int local = t - T.tstart[p];
+  const int mtiles = mtiles_of(P);
+  const int gb = T.gbase[p];
+  ti.p = p;
+  if (P.mode == kTokN) {
+    const int gp = gb + p;  // gpre holds ngroups + 1 entries per problem
+    const int ntg = local / mtiles;
+    ti.mt = local - ntg * mtiles;
+    int lo = 0, hi = P.ngroups;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (T.gpre[gp + mid] <= ntg) lo = mid; else hi = mid;
+    }
+    ti.g = lo;
+    const int nt = ntg - T.gpre[gp + lo];
+    const int cnt = T.gcnt[gb + lo];
+    ti.n0 = T.goff[gb + lo] + nt * P.BN;
+    ti.n_valid = min(P.BN, cnt - nt * P.BN);
+    ti.m0 = (P.epi == kEpiGlu) ? ti.mt * 64 : ti.mt * kBM;
+    ti.nkb = P.K / kBK + (P.has_ext ? 1 : 0);
+  } else {
+    ti.g = local / mtiles;
+    ti.mt = local - ti.g * mtiles;
+    ti.n0 = T.goff[gb + ti.g];
+    ti.n_valid = P.N;
+    ti.m0 = ti.mt * kBM;
+    ti.nkb = (T.gcnt[gb + ti.g] + kBK - 1) / kBK;
+  }
+  ti.widx = T.gw[gb + ti.g];
+  return ti;
+}
+
+// ------------------------------------------------------------------------------------------ int4 dequant helpers
+// A group takes the bf16x2 fast path when every value q*s + z (q in 0..15) is exactly representable in fp32: then
+// rounding the exact value once to bf16 (fma.rn.bf16x2) equals the reference's fp32 dequant followed by a bf16
+// cast. Other groups (extreme scale/zero exponent gaps, subnormals, non-finite) are expanded in fp32.
+__device__ __forceinline__ bool dq_fast_ok(uint32_t sz) {
+  const uint32_t s = sz & 0xFFFFu, z = sz >> 16;
+  if ((z & 0x7FFFu) == 0 || (s & 0x7FFFu) == 0) return true;
+  const int es = (s >> 7) & 0xFF, ez = (z >> 7) & 0xFF;
+  if (es < 32 || ez < 32 || es == 0xFF || ez == 0xFF) return false;
+  const int d = ez - es;
+  return d <= 15 && d >= -11;
+}
+
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bits_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
+
+// One 32-bit word = 8 nibbles, byte j holding element 2j (low nibble) and 2j+1 (high nibble) -> 8 bf16.
+// (0x4300 | n) is the bf16 encoding of 128 + n, so subtracting 128 recovers n exactly.
+__device__ __forceinline__ uint4 dq8_fast(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 z2) {
+  const uint32_t y = w >> 4;
+  const __nv_bfloat162 c128 = bits_bf162(0x43004300u);
+  const uint32_t p0 = (__byte_perm(w, y, 0x0400) & 0x000F000Fu) | 0x43004300u;
+  const uint32_t p1 = (__byte_perm(w, y, 0x0501) & 0x000F000Fu) | 0x43004300u;
+  const uint32_t p2 = (__byte_perm(w, y, 0x0602) & 0x000F000Fu) | 0x43004300u;
+  const uint32_t p3 = (__byte_perm(w, y, 0x0703) & 0x000F000Fu) | 0x43004300u;
+  uint4 r;
+  r.x = bf162_bits(__hfma2(__hsub2(bits_bf162(p0), c128), s2, z2));
+  r.y = bf162_bits(__hfma2(__hsub2(bits_bf162(p1), c128), s2, z2));
+  r.z = bf162_bits(__hfma2(__hsub2(bits_bf162(p2), c128), s2, z2));
+  r.w = bf162_bits(__hfma2(__hsub2(bits_bf162(p3), c128), s2, z2));
+  return r;
+}
+
+__device__ __forceinline__ uint4 dq8_exact(uint32_t w, float s, float z) {
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t b = (w >> (8 * j)) & 0xFFu;
+    o[j] = bf162_bits(__floats2bfloat162_rn(fmaf((float)(b & 0xFu), s, z), fmaf((float)(b >> 4), s, z)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// 32 packed bytes (64 values sharing one (scale, zero) pair) -> 8 chunks of 8 bf16 written to one 128-byte row of
+// a 128B-swizzled UMMA tile (chunk c lands at chunk position c ^ swz).
+__device__ __forceinline__ void dq64_to_row(const uint8_t* src, uint32_t sz, uint8_t* dst_row, int swz) {
+  const uint4 v0 = *reinterpret_cast<const uint4*>(src);
+  const uint4 v1 = *reinterpret_cast<const uint4*>(src + 16);
+  const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  if (dq_fast_ok(sz)) {
+    const __nv_bfloat162 s2 = bits_bf162((sz & 0xFFFFu) | (sz << 16));
+    const __nv_bfloat162 z2 = bits_bf162((sz >> 16) | (sz & 0xFFFF0000u));
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst_row + ((c ^ swz) << 4)) = dq8_fast(w[c], s2, z2);
+  } else {
+    const float s = __uint_as_float((sz & 0xFFFFu) << 16);
+    const float z = __uint_as_float(sz & 0xFFFF0000u);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst_row + ((c ^ swz) << 4)) = dq8_exact(w[c], s, z);
+  }
+}
+
+// ------------------------------------------------------------------------------------------ epilogue math
+__device__ __forceinline__ float act_fwd(float x, int act) {
+  if (act == kActSilu) return x / (1.0f + expf(-x));
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+// (act(g), d act / d g) in fp32
+__device__ __forceinline__ void act_and_grad(float g, int act, float& a, float& d) {
+  if (act == kActSilu) {
+    const float sg = 1.0f / (1.0f + expf(-g));
+    a = g * sg;
+    d = sg * (1.0f + g * (1.0f - sg));
+  } else {
+    const float c = 0.7978845608028654f;
+    const float t = tanhf(c * (g + 0.044715f * g * g * g));
+    a = 0.5f * g * (1.0f + t);
+    d = 0.5f * (1.0f + t) + 0.5f * g * (1.0f - t * t) * c * (1.0f + 3.0f * 0.044715f * g * g);
+  }
+}
+
+// GLU tiles interleave gate and up in 16-row blocks: A row 32*q + j holds gate feature f0 + 16*q + j for j < 16
+// and up feature f0 + 16*q + (j - 16) for j >= 16, so one epilogue warp (32 TMEM lanes) owns both halves of 16
+// features. This maps an A row to its row in the natural [64 gate | 64 up] staging order.
+__device__ __forceinline__ int glu_stage_row(int r) {
+  const int q = r >> 5, j = r & 31;
+  return (j < 16) ? (q * 16 + j) : (64 + q * 16 + (j - 16));
+}
+
+// ------------------------------------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_constant__ LaunchArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t smem_base = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = args.err;
+
+  int* tab = reinterpret_cast<int*>(smem + kOffTab);
+  Tables T;
+  T.gcnt = tab;
+  T.goff = tab + kMaxGroups;
+  T.gw = tab + 2 * kMaxGroups;
+  T.gpre = tab + 3 * kMaxGroups;
+  T.tstart = T.gpre + kMaxGroups + kMaxProblems;
+  T.gbase = T.tstart + kMaxProblems + 1;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full_tma = bars;
+  uint64_t* full_deq = bars + kStages;
+  uint64_t* empty = bars + 2 * kStages;
+  uint64_t* acc_full = bars + 3 * kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_drain = acc_full + 4;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+
+  // ---------------------------------------------------------------- prologue: barriers, TMEM, tile tables
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&full_tma[s], 1);
+        mbar_init(&full_deq[s], kNumDeqWarps);
+        mbar_init(&empty[s], 1);
+      }
+      for (int a = 0; a < 2; ++a) {
+        mbar_init(&acc_full[a], 1);
+        mbar_init(&acc_empty[a], kNumEpiWarps);
+      }
+      mbar_init(mma_drain, 1);
+      fence_mbar_init();
+      for (int p = 0; p < args.nprob; ++p) {
+        const Problem& P = args.p[p];
+        if (P.a_kind == kAInt4K || P.a_kind == kAInt4MN) {
+          tma_prefetch_desc(&P.tmQ);
+          tma_prefetch_desc(&P.tmSZ);
+        } else {
+          tma_prefetch_desc(&P.tmA);
+        }
+        tma_prefetch_desc(&P.tmB);
+        if (P.has_ext) {
+          tma_prefetch_desc(&P.tmAe);
+          tma_prefetch_desc(&P.tmBe);
+        }
+      }
+    }
+    int gbase = 0, total = 0;
+    for (int p = 0; p < args.nprob; ++p) {
+      const Problem& P = args.p[p];
+      if (lane == 0) {
+        T.gbase[p] = gbase;
+        T.tstart[p] = total;
+      }
+      int carry_rows = 0, carry_tiles = 0;
+      const int gp = gbase + p;
+      for (int g0 = 0; g0 < P.ngroups; g0 += 32) {
+        const int g = g0 + lane;
+        int cnt = 0, e = 0, w = 0;
+        if (g < P.ngroups) {
+          e = P.gid_of ? P.gid_of[g] : g;
+          w = P.widx_of ? P.widx_of[g] : e;
+          cnt = P.counts[e];
+        }
+        const int nt = (P.mode == kTokN) ? (cnt + P.BN - 1) / P.BN : 0;
+        int rows_inc = cnt, tiles_inc = nt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int r = __shfl_up_sync(0xffffffffu, rows_inc, o);
+          const int tt = __shfl_up_sync(0xffffffffu, tiles_inc, o);
+          if (lane >= o) {
+            rows_inc += r;
+            tiles_inc += tt;
+          }
+        }
+        if (g < P.ngroups) {
+          T.gcnt[gbase + g] = cnt;
+          T.goff[gbase + g] = P.offsets ? P.offsets[e] : carry_rows + rows_inc - cnt;
+          T.gw[gbase + g] = w;
+          T.gpre[gp + g] = carry_tiles + tiles_inc - nt;
+        }
+        carry_rows += __shfl_sync(0xffffffffu, rows_inc, 31);
+        carry_tiles += __shfl_sync(0xffffffffu, tiles_inc, 31);
+      }
+      if (lane == 0) T.gpre[gp + P.ngroups] = carry_tiles;
+      const int mtiles = mtiles_of(P);
+      total += (P.mode == kTokN) ? mtiles * carry_tiles : mtiles * P.ngroups;
+      gbase += P.ngroups;
+    }
+    if (lane == 0) T.tstart[args.nprob] = total;
+  } else if (warp == 1) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total_tiles = T.tstart[args.nprob];
+
+  if (warp == 0) {
+    // ============================================================================ TMA producer (one thread)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(args, T, t);
+        const Problem& P = args.p[ti.p];
+        const bool glu = P.epi == kEpiGlu;
+        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, err, kDevErrWaitEmpty)) { ok = false; break; }
+          uint8_t* sA = smem + kOffA + s * kAStageBytes;
+          uint8_t* sB = smem + kOffB + s * kBStageBytes;
+          uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
+          uint8_t* sSZ = smem + kOffSZ + s * kSZStageBytes;
+          uint64_t* fb = &full_tma[s];
+          if (P.mode == kTokN) {
+            const int nb = (ti.n_valid + 63) / 64;
+            const bool ext = P.has_ext && kb == ti.nkb - 1;
+            // weight rows of the two 64-row halves (natural order) / of the 16-row GLU blocks
+            const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
+            const int k = kb * kBK;
+            const CUtensorMap* mA = ext ? &P.tmAe : &P.tmA;
+            const int wrow = ti.widx * (ext ? P.e_wrows : P.a_wrows);
+            uint32_t bytes = nb * 8192;
+            if (ext || P.a_kind == kABf16K || P.a_kind == kABf16MN) bytes += 16384;
+            else bytes += 4096 + 512;
+            mbar_arrive_expect_tx(fb, bytes);
+            if (ext || P.a_kind == kABf16K) {
+              const int x = ext ? 0 : k;
+              if (glu) {
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                  tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fb);
+                  tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fb);
+                }
+              } else {
+                tma_load_2d(sA, mA, x, wrow + r0, fb);
+                tma_load_2d(sA + 8192, mA, x, wrow + r1, fb);
+              }
+            } else if (P.a_kind == kABf16MN) {
+              tma_load_2d(sA, mA, ti.m0, wrow + k, fb);
+              tma_load_2d(sA + 8192, mA, ti.m0 + 64, wrow + k, fb);
+            } else if (P.a_kind == kAInt4K) {
+              tma_load_2d(sQ, &P.tmQ, kb * 32, ti.widx * P.q_rows + r0, fb);
+              tma_load_2d(sQ + 2048, &P.tmQ, kb * 32, ti.widx * P.q_rows + r1, fb);
+              tma_load_2d(sSZ, &P.tmSZ, r0, ti.widx * P.q_groups + kb, fb);
+              tma_load_2d(sSZ + 256, &P.tmSZ, r1, ti.widx * P.q_groups + kb, fb);
+            } else {  // kAInt4MN
+              tma_load_2d(sQ, &P.tmQ, ti.m0 / 2, ti.widx * P.q_rows + k, fb);
+              tma_load_2d(sSZ, &P.tmSZ, k, ti.widx * P.q_groups + ti.m0 / 64, fb);
+              tma_load_2d(sSZ + 256, &P.tmSZ, k, ti.widx * P.q_groups + ti.m0 / 64 + 1, fb);
+            }
+            const CUtensorMap* mB = ext ? &P.tmBe : &P.tmB;
+            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, ext ? 0 : k, ti.n0 + 64 * i, fb);
+          } else {  // kTokK: A = tokens^T (MN-major), B = tokens^T (MN-major)
+            const int krow = ti.n0 + kb * kBK;
+            const int nb = (P.N + 63) / 64;
+            mbar_arrive_expect_tx(fb, 16384 + nb * 8192);
+            tma_load_2d(sA, &P.tmA, P.a_x0 + ti.m0, krow, fb);
+            tma_load_2d(sA + 8192, &P.tmA, P.a_x0 + ti.m0 + 64, krow, fb);
+            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, &P.tmB, P.b_x0 + 64 * i, krow, fb);
+          }
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
+        if (!mbar_wait(&full_tma[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+    }
+  } else if (warp == 1) {
+    // ============================================================================ MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t it = 0, acc_it = 0;
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(args, T, t);
+        if (ti.nkb == 0) continue;
+        const Problem& P = args.p[ti.p];
+        const int acc = acc_it & 1;
+        if (!mbar_wait(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
+        const uint32_t a_mn = (P.mode == kTokK || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
+        const uint32_t b_mn = (P.mode == kTokK) ? 1u : 0u;
+        const uint32_t idesc_main = make_idesc_bf16(n_mma, a_mn, b_mn);
+        const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
+        const uint32_t d_tmem = tmem_base + acc * kMaxBN;
+        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&full_tma[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
+          if (!mbar_wait(&full_deq[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
+          tc_fence_after();
+          const bool ext = P.mode == kTokN && P.has_ext && kb == ti.nkb - 1;
+          const bool amn = a_mn && !ext;
+          const uint32_t sA = smem_base + kOffA + s * kAStageBytes;
+          const uint32_t sB = smem_base + kOffB + s * kBStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = amn ? make_sdesc(sA + kk * 2048, 8192, 1024) : make_sdesc(sA + kk * 32, 16, 1024);
+            const uint64_t bd = b_mn ? make_sdesc(sB + kk * 2048, 8192, 1024) : make_sdesc(sB + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, ext ? idesc_ext : idesc_main, (kb | kk) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        ++acc_it;
+      }
+      if (issued) {  // all MMAs must complete before TMEM is released
+        umma_commit(mma_drain);
+        mbar_wait(mma_drain, 0, err, kDevErrTmaDrain);
+      }
+    }
+  } else if (warp < 2 + kNumDeqWarps) {
+    // ============================================================================ int4 dequant warps
+    const int pt = threadIdx.x - 64;  // 0..127
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = decode_tile(args, T, t);
+      const Problem& P = args.p[ti.p];
+      const bool int4 = P.mode == kTokN && (P.a_kind == kAInt4K || P.a_kind == kAInt4MN);
+      const bool glu = P.epi == kEpiGlu;
+      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait(&full_tma[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
+        const bool ext = P.has_ext && kb == ti.nkb - 1;
+        if (int4 && !ext) {
+          uint8_t* sA = smem + kOffA + s * kAStageBytes;
+          const uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
+          const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + s * kSZStageBytes);
+          if (P.a_kind == kAInt4K) {
+            const int r = pt;
+            const int sr = glu ? glu_stage_row(r) : r;
+            dq64_to_row(sQ + sr * 32, sSZ[sr], sA + (r >> 3) * 1024 + (r & 7) * 128, r & 7);
+          } else {
+            const int kr = pt >> 1, half = pt & 1;
+            dq64_to_row(sQ + kr * 64 + half * 32, sSZ[half * 64 + kr],
+                        sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128, kr & 7);
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_deq[s]);
+      }
+    }
+  } else {
+    // ============================================================================ epilogue warps
+    const int q = warp & 3;         // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;  // accumulator row (A row) owned by this thread
+    uint32_t acc_it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(args, T, t);
+      const Problem& P = args.p[ti.p];
+      if (ti.nkb == 0) {
+        // kTokK group without tokens: its gradient block is zero
+        if (P.mode == kTokK) {
+          const int m = ti.m0 + row;
+          if (m < P.M) {
+            float* C = reinterpret_cast<float*>(P.C) + (long long)ti.g * P.c_gs;
+            for (int n = 0; n < P.N; ++n) C[(long long)m * P.c_sm + (long long)n * P.c_sn] = 0.0f;
+          }
+        }
+        continue;
+      }
+      const int acc = acc_it & 1;
+      if (!mbar_wait(&acc_full[acc], (acc_it >> 1) & 1, err, kDevErrWaitAccFull)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kMaxBN;
+      const int nchunks = (ti.n_valid + 31) / 32;
+      const float alpha = P.alpha;
+      if (P.epi == kEpiGlu) {
+        const bool is_gate = lane < 16;
+        const int f = ti.m0 + q * 16 + (lane & 15);
+        const bool fvalid = f < P.inter;
+        bf16* Cb = reinterpret_cast<bf16*>(P.C);
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tbase + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            // lanes 0-15 take even token columns, lanes 16-31 odd ones; both need gate and up of the column
+            const float mine_e = __uint_as_float(v[2 * jj]), mine_o = __uint_as_float(v[2 * jj + 1]);
+            const float other_e = __shfl_xor_sync(0xffffffffu, mine_e, 16);
+            const float other_o = __shfl_xor_sync(0xffffffffu, mine_o, 16);
+            const int j = 2 * jj + (is_gate ? 0 : 1);
+            const float gacc = is_gate ? mine_e : other_o;
+            const float uacc = is_gate ? other_e : mine_o;
+            const int n = c * 32 + j;
+            if (n < ti.n_valid && fvalid) {
+              const long long tok = ti.n0 + n;
+              const float gb = bf16_round(gacc * alpha);
+              const float ub = bf16_round(uacc * alpha);
+              const float ab = bf16_round(act_fwd(gb, P.act));
+              Cb[tok * P.c_sn + f] = __float2bfloat16_rn(ab * ub);
+              if (P.Hout) {
+                P.Hout[tok * P.h_ld + f] = __float2bfloat16_rn(gb);
+                P.Hout[tok * P.h_ld + P.inter + f] = __float2bfloat16_rn(ub);
+              }
+            }
+          }
+        }
+      } else if (P.epi == kEpiDGlu) {
+        const int m = ti.m0 + row;
+        const bool mvalid = m < P.M;
+        bf16* Cb = reinterpret_cast<bf16*>(P.C);
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tbase + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = c * 32 + j;
+            if (n < ti.n_valid && mvalid) {
+              const long long tok = ti.n0 + n;
+              const float da = bf16_round(__uint_as_float(v[j]) * alpha);
+              const float g = __bfloat162float(P.Hin[tok * P.h_ld + m]);
+              const float u = __bfloat162float(P.Hin[tok * P.h_ld + P.inter + m]);
+              float a, dd;
+              act_and_grad(g, P.act, a, dd);
+              Cb[tok * P.c_sn + m] = __float2bfloat16_rn(da * u * dd);
+              Cb[tok * P.c_sn + P.inter + m] = __float2bfloat16_rn(da * a);
+            }
+          }
+        }
+      } else {
+        const int m = ti.m0 + row;
+        const bool mvalid = m < P.M;
+        const long long gofs = (P.mode == kTokK) ? (long long)ti.g * P.c_gs : 0;
+        const long long nbase = (P.mode == kTokK) ? 0 : ti.n0;
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tbase + c * 32, v);
+          tmem_ld_wait();
+          if (P.epi == kEpiStoreBf16) {
+            bf16* Cb = reinterpret_cast<bf16*>(P.C) + gofs;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = c * 32 + j;
+              if (n < ti.n_valid && mvalid)
+                Cb[(nbase + n) * P.c_sn + (long long)m * P.c_sm] = __float2bfloat16_rn(__uint_as_float(v[j]) * alpha);
+            }
+          } else {
+            float* Cf = reinterpret_cast<float*>(P.C) + gofs;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = c * 32 + j;
+              if (n < ti.n_valid && mvalid) Cf[(nbase + n) * P.c_sn + (long long)m * P.c_sm] = __uint_as_float(v[j]) * alpha;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      ++acc_it;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------ host side
+int launch_gemm(LaunchArgs& args, cudaStream_t stream) {
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  static bool configured[64] = {false};
+  if (dev < 64 && !configured[dev]) {
+    SMELB_CUDA(cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc));
+    configured[dev] = true;
+  }
+  SMELB_CHECK_ARG(args.nprob >= 1 && args.nprob <= kMaxProblems, kErrArg, "gemm: %d problems in one launch",
+                  args.nprob);
+  int total_groups = 0;
+  for (int p = 0; p < args.nprob; ++p) total_groups += args.p[p].ngroups;
+  SMELB_CHECK_ARG(total_groups <= kMaxGroups, kErrShape, "gemm: %d groups in one launch (max %d)", total_groups,
+                  kMaxGroups);
+  args.err = device_status(dev);
+  SMELB_CHECK_ARG(args.err != nullptr, kErrCuda, "gemm: no device status word");
+  const bool timed = gemm_timing_enabled();
+  if (timed) gemm_timing_begin(stream);
+  moe_gemm_kernel<<<num_sms(dev), kThreads, kSmemAlloc, stream>>>(args);
+  SMELB_CUDA(cudaGetLastError());
+  if (timed) gemm_timing_end(stream);
+  count_launch();
+  return kOk;
+}
+
+}  // namespace smelb

@@ -1,0 +1,98 @@
+// Grouped multi-problem GEMM engine for the MoE expert layer (sm_100a: TMA + tcgen05 + TMEM).
+//
+// Every GEMM of the layer is expressed "swap-AB": the weight side is the MMA's A operand (M = 128 output features
+// per tile) and the token side is the B operand (N = tokens of one expert, 16..256 per tile). Experts with few
+// routed tokens then cost N=16-granular MMAs instead of padding to a 128-row M tile.
+//
+// One launch runs up to kMaxProblems independent problems (e.g. frozen int4 experts + selected bf16 experts +
+// shared expert), scheduled as one persistent tile list over all SMs.
+//
+// A operand sources (per problem):
+//   kAInt4K  : frozen experts, int4 group-64 weights W[e][m][k] (forward). TMA stages the packed nibbles and the
+//              (scale, zero) pairs into shared memory; four dequant warps expand them to bf16 in the 128B-swizzled
+//              K-major UMMA layout.
+//   kAInt4MN : frozen experts, int4 weights used transposed, W[e][k][m] (backward dX). Same staging; the dequant
+//              warps write the MN-major UMMA layout.
+//   kABf16K  : bf16 weights [m][k] loaded by TMA (selected experts, shared expert, router, LoRA factors).
+//   kABf16MN : bf16 weights [k][m] loaded by TMA (their transposes in backward).
+// Modes:
+//   kTokN : tokens along N. Groups = experts; group g covers token rows offsets[e] .. offsets[e]+counts[e]-1 of the
+//           token matrix; output C[row][m]. Optional LoRA K-extension: one extra 64-wide k-block whose A comes from
+//           tmAe (per-weight [rows, 64]) and whose B comes from tmBe (per-token [rows, 64]).
+//   kTokK : tokens along K (LoRA weight gradients). Output per group: C[g][m][n] = sum_tokens A^T B with fixed N.
+// Epilogues: bf16 store, GLU (act(gate) * up; tiles hold 64 gate rows + the matching 64 up rows), DGLU (gated
+// MLP backward from saved gate/up), fp32 store.
+#pragma once
+
+#include "common.cuh"
+
+namespace smelb {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kMaxBN = 256;
+constexpr int kStages = 4;
+constexpr int kMaxProblems = 12;
+constexpr int kMaxGroups = 320;  // groups over all problems of one launch
+
+constexpr int kAStageBytes = kBM * kBK * 2;      // 16 KB bf16 A tile
+constexpr int kBStageBytes = kMaxBN * kBK * 2;   // 32 KB bf16 B tile
+constexpr int kQStageBytes = 4096;               // packed int4 staging (128 rows x 32 B or 64 rows x 64 B)
+constexpr int kSZStageBytes = 512;               // (scale, zero) staging: 128 x uint32
+constexpr int kStageBytes = kAStageBytes + kBStageBytes + kQStageBytes + kSZStageBytes;
+constexpr int kXchgBytes = 64 * 32 * 4;          // GLU epilogue exchange buffer (64 rows x 32 columns fp32)
+
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 dequant, warps 6-9 epilogue
+constexpr int kNumDeqWarps = 4;
+constexpr int kNumEpiWarps = 4;
+
+enum Mode : int { kTokN = 0, kTokK = 1 };
+enum AKind : int { kAInt4K = 0, kAInt4MN = 1, kABf16K = 2, kABf16MN = 3 };
+enum Epi : int { kEpiStoreBf16 = 0, kEpiGlu = 1, kEpiDGlu = 2, kEpiStoreF32 = 3 };
+enum Act : int { kActSilu = 0, kActGeluTanh = 1 };
+
+struct alignas(64) Problem {
+  CUtensorMap tmA;   // bf16 A (weights [rows][k] / [k][m], or tokens [rows][m] in kTokK); unused for int4
+  CUtensorMap tmB;   // tokens: kTokN [rows][k] K-major; kTokK [rows][n] (MN-major B)
+  CUtensorMap tmAe;  // LoRA extension, weight side [nW * e_wrows][64]
+  CUtensorMap tmBe;  // LoRA extension, token side [rows][64]
+  CUtensorMap tmQ;   // int4 nibbles (uint8): K-major [nW*rows][K/2]; MN-major [nW*K][M/2]
+  CUtensorMap tmSZ;  // (scale | zero << 16) uint32, transposed: [nW*G][rows]
+
+  int mode, a_kind, epi, act;
+  int M;        // output features (valid rows of A)
+  int K;        // kTokN reduction length (multiple of 64)
+  int N;        // kTokK output columns (multiple of 16, <= 256)
+  int BN;       // kTokN token tile (multiple of 64, <= 256)
+  int a_wrows;  // bf16 A, kTokN: tensor-map rows per weight index (K-major: rows of W; MN-major: K)
+  int a_x0;     // kTokK: column offset into tmA
+  int b_x0;     // kTokK: column offset into tmB
+  int has_ext;
+  int e_wrows;  // ext A rows per weight index
+  int q_rows;   // int4: rows of the stored matrix per weight index (K-major: M-dim rows; MN-major: K rows)
+  int q_groups; // int4: groups per stored row (= stored row length / 64)
+
+  const int* counts;   // tokens per expert id
+  const int* offsets;  // first token row per expert id (nullptr: prefix sum of counts in group order)
+  const int* gid_of;   // group -> expert id (nullptr: identity)
+  const int* widx_of;  // group -> weight index (nullptr: same as expert id)
+  int ngroups;
+
+  void* C;            // output
+  long long c_sm;     // element stride of C along m
+  long long c_sn;     // element stride of C along n (token row for kTokN)
+  long long c_gs;     // kTokK: element stride between groups
+  const bf16* Hin;    // DGLU: saved (gate | up) pre-activations [rows][2*inter]
+  bf16* Hout;         // GLU: optional save of (gate | up) [rows][2*inter]
+  long long h_ld;     // row stride of Hin/Hout
+  int inter;          // gated-MLP intermediate size (offset of up in h)
+  float alpha;        // scale applied to the fp32 accumulator before the store
+};
+
+struct LaunchArgs {
+  Problem p[kMaxProblems];
+  int nprob;
+  int* err;
+};
+
+}  // namespace smelb

@@ -1,0 +1,26 @@
+// Host-side helpers shared by the smelb entry points: per-device status word and SM count, last-error text and
+// TMA tensor-map encoding (cuTensorMapEncodeTiled resolved through the runtime, so nothing links libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace smelb {
+
+int* device_status(int dev);
+
+// Instrumentation: number of kernels launched by the library, and optional CUDA-event timing of the GEMM launches.
+void count_launch();
+bool gemm_timing_enabled();
+void gemm_timing_begin(cudaStream_t st);
+void gemm_timing_end(cudaStream_t st);  // 4-byte device word the kernels record wait timeouts in (allocated once per device)
+int num_sms(int dev);
+
+// 2-D tiled tensor map over a row-major matrix [rows][cols] of `elem_bytes`-sized elements with row pitch
+// `row_bytes`. box = {box_cols, box_rows}. swizzle128 selects the 128-byte swizzle (box_cols * elem_bytes == 128).
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+
+}  // namespace smelb

@@ -1,0 +1,667 @@
+// Memory-bound kernels of the MoE layer: int4 dequant (parity helper) and (scale, zero) repack, router softmax /
+// top-k / renorm and its backward, the deterministic counting-sort dispatch, row gather, the fp32 weighted combine
+// and its backward, the final dX reduction and the per-step LoRA factor packing.
+#include "common.cuh"
+#include "kernels.h"
+#include "host.h"
+
+namespace smelb {
+
+// ============================================================================================ int4 dequant
+// out[r][2j] = lo(q[r][j]) * s + z, out[r][2j+1] = hi(q[r][j]) * s + z with (s, z) of group (2j) / group_size,
+// computed in fp32 and rounded once to the output type.
+template <bool F32>
+__global__ void int4_dequant_kernel(const uint8_t* __restrict__ q, const bf16* __restrict__ scale,
+                                    const bf16* __restrict__ zero, void* __restrict__ out, long long rows, int half_k,
+                                    int groups, int group) {
+  const long long n = rows * half_k;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / half_k;
+    const int j = (int)(i - r * half_k);
+    const int g = (2 * j) / group;
+    const float s = __bfloat162float(scale[r * groups + g]);
+    const float z = __bfloat162float(zero[r * groups + g]);
+    const uint8_t b = q[i];
+    const float lo = fmaf((float)(b & 0xF), s, z);
+    const float hi = fmaf((float)(b >> 4), s, z);
+    if (F32) {
+      float2 v = make_float2(lo, hi);
+      reinterpret_cast<float2*>(out)[i] = v;
+    } else {
+      reinterpret_cast<__nv_bfloat162*>(out)[i] = __floats2bfloat162_rn(lo, hi);
+    }
+  }
+}
+
+int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
+                 bool out_f32, cudaStream_t st) {
+  SMELB_CHECK_ARG(k > 0 && k % 2 == 0 && groups > 0 && k % groups == 0 && (k / groups) % 2 == 0, kErrShape,
+                  "int4_dequant: k=%d groups=%d (need k %% groups == 0 and an even group size)", k, groups);
+  if (rows == 0) return kOk;
+  const long long n = rows * (k / 2);
+  const int threads = 256;
+  const long long blocks = std::min<long long>((n + threads - 1) / threads, 148LL * 16);
+  if (out_f32)
+    int4_dequant_kernel<true><<<(int)blocks, threads, 0, st>>>((const uint8_t*)q, (const bf16*)scale,
+                                                                (const bf16*)zero, out, rows, k / 2, groups,
+                                                                k / groups);
+  else
+    int4_dequant_kernel<false><<<(int)blocks, threads, 0, st>>>((const uint8_t*)q, (const bf16*)scale,
+                                                                 (const bf16*)zero, out, rows, k / 2, groups,
+                                                                 k / groups);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// szT[w][g][r] = scale[w][r][g] | zero[w][r][g] << 16 : the (scale, zero) pairs of one group for consecutive rows are
+// contiguous, which is the order the GEMM producer stages them in.
+__global__ void int4_pack_sz_kernel(const uint16_t* __restrict__ scale, const uint16_t* __restrict__ zero,
+                                    uint32_t* __restrict__ szT, long long nw, int rows, int groups) {
+  const long long n = nw * rows * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long w = i / ((long long)rows * groups);
+    const long long rem = i - w * rows * groups;
+    const int g = (int)(rem / rows), r = (int)(rem - (long long)g * rows);
+    const long long src = (w * rows + r) * groups + g;
+    szT[i] = (uint32_t)scale[src] | ((uint32_t)zero[src] << 16);
+  }
+}
+
+int int4_pack_sz(const void* scale, const void* zero, uint32_t* szT, long long nw, int rows, int groups,
+                 cudaStream_t st) {
+  const long long n = nw * rows * groups;
+  if (n == 0) return kOk;
+  const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+  int4_pack_sz_kernel<<<(int)blocks, 256, 0, st>>>((const uint16_t*)scale, (const uint16_t*)zero, szT, nw, rows,
+                                                   groups);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ router
+// One warp per token: probs = softmax_fp32(logits), top-k by (value desc, expert id asc), renormalised in fp32 over
+// the chosen k (summed in k order), optionally multiplied by per_expert_scale (Gemma 4), stored as bf16 or fp32.
+__global__ void router_topk_kernel(const bf16* __restrict__ logits, long long ld, int T, int E, int K,
+                                   float* __restrict__ probs, void* __restrict__ topv, int topv_f32,
+                                   long long* __restrict__ topi, const bf16* __restrict__ per_expert_scale) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const bf16* lg = logits + (long long)warp * ld;
+  constexpr int kMaxPer = 16;  // E <= 512
+  float v[kMaxPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? __bfloat162float(lg[e]) : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? expf(v[i] - mx) : 0.f;
+    sum += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.0f / sum;
+  float* pr = probs + (long long)warp * E;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      v[i] = v[i] * inv;
+      pr[e] = v[i];
+    } else {
+      v[i] = -INFINITY;
+    }
+  }
+  // top-k: repeated warp arg-max; ties resolved towards the smaller expert id
+  float tv[32];
+  int te[32];
+  for (int k = 0; k < K; ++k) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = lane + 32 * i;
+      if (v[i] > bv || (v[i] == bv && e < be)) {
+        bv = v[i];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
+      if (lane + 32 * i == be) v[i] = -INFINITY;
+    tv[k] = bv;
+    te[k] = be;
+  }
+  if (lane == 0) {
+    float s = 0.f;
+    for (int k = 0; k < K; ++k) s += tv[k];
+    for (int k = 0; k < K; ++k) {
+      float val = tv[k] / s;
+      if (per_expert_scale) val = val * __bfloat162float(per_expert_scale[te[k]]);
+      const long long o = (long long)warp * K + k;
+      if (topv_f32) reinterpret_cast<float*>(topv)[o] = val;
+      else reinterpret_cast<bf16*>(topv)[o] = __float2bfloat16_rn(val);
+      topi[o] = te[k];
+    }
+  }
+}
+
+int router_topk(const void* logits, long long ld, int T, int E, int K, float* probs, void* topv, bool topv_f32,
+                long long* topi, const void* per_expert_scale, cudaStream_t st) {
+  SMELB_CHECK_ARG(E >= 1 && E <= 512 && K >= 1 && K <= 32 && K <= E, kErrShape, "router_topk: E=%d K=%d", E, K);
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const int blocks = (T * 32 + threads - 1) / threads;
+  router_topk_kernel<<<blocks, threads, 0, st>>>((const bf16*)logits, ld, T, E, K, probs, topv, topv_f32 ? 1 : 0,
+                                                 topi, (const bf16*)per_expert_scale);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// Backward of probs -> top-k gather -> renorm (-> optional per-expert scale) -> cast:
+//   t_k = v_k / S, S = sum_j v_j;  dv_k = (dt_k - sum_j dt_j t_j) / S;  dp[e] = dprobs[e] + sum_k [topi_k == e] dv_k;
+//   dl = p * (dp - sum_e dp_e p_e)  (softmax Jacobian), stored in the logits dtype (bf16). dprobs may be null.
+__global__ void router_bwd_kernel(const void* __restrict__ dtopv, int dtopv_f32, const float* __restrict__ dprobs,
+                                  const float* __restrict__ probs, const long long* __restrict__ topi,
+                                  const bf16* __restrict__ per_expert_scale, int T, int E, int K,
+                                  bf16* __restrict__ dlogits, long long ld) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* pr = probs + (long long)warp * E;
+  const float* dpr = dprobs ? dprobs + (long long)warp * E : nullptr;
+  float dv = 0.f;
+  int myk_e = -1;
+  if (lane < K) {
+    float S = 0.f, dot = 0.f;
+    for (int k = 0; k < K; ++k) S += pr[topi[(long long)warp * K + k]];
+    for (int k = 0; k < K; ++k) {
+      const long long o = (long long)warp * K + k;
+      const int e = (int)topi[o];
+      float d = dtopv ? (dtopv_f32 ? reinterpret_cast<const float*>(dtopv)[o]
+                                   : __bfloat162float(reinterpret_cast<const bf16*>(dtopv)[o]))
+                      : 0.f;
+      if (per_expert_scale) d *= __bfloat162float(per_expert_scale[e]);
+      dot += d * (pr[e] / S);
+    }
+    const long long o = (long long)warp * K + lane;
+    myk_e = (int)topi[o];
+    float d = dtopv ? (dtopv_f32 ? reinterpret_cast<const float*>(dtopv)[o]
+                                 : __bfloat162float(reinterpret_cast<const bf16*>(dtopv)[o]))
+                    : 0.f;
+    if (per_expert_scale) d *= __bfloat162float(per_expert_scale[myk_e]);
+    dv = (d - dot) / S;
+  }
+  // sdot = sum_e dp_e p_e
+  float contrib = (lane < K) ? dv * pr[myk_e] : 0.f;
+  if (dpr)
+    for (int e = lane; e < E; e += 32) contrib += dpr[e] * pr[e];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+  const float sdot = contrib;
+  bf16* dl = dlogits + (long long)warp * ld;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    float dp = (dpr && e < E) ? dpr[e] : 0.f;
+    for (int k = 0; k < K; ++k) {
+      const float dvk = __shfl_sync(0xffffffffu, dv, k);
+      const int ek = __shfl_sync(0xffffffffu, myk_e, k);
+      if (ek == e) dp += dvk;
+    }
+    if (e < E) dl[e] = __float2bfloat16_rn(pr[e] * (dp - sdot));
+  }
+}
+
+int router_bwd(const void* dtopv, bool dtopv_f32, const float* dprobs, const float* probs, const long long* topi,
+               const void* per_expert_scale, int T, int E, int K, void* dlogits, long long ld, cudaStream_t st) {
+  SMELB_CHECK_ARG(K >= 1 && K <= 32 && E >= K, kErrShape, "router_bwd: E=%d K=%d", E, K);
+  if (T == 0) return kOk;
+  const int threads = 256;
+  router_bwd_kernel<<<(T * 32 + threads - 1) / threads, threads, 0, st>>>(
+      dtopv, dtopv_f32 ? 1 : 0, dprobs, probs, topi, (const bf16*)per_expert_scale, T, E, K, (bf16*)dlogits, ld);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ dispatch plan
+// Stable counting sort of the flattened expert choices i = t*K + k (a single CTA of 32 warps):
+//   counts[e]          number of i with topi[i] == e
+//   offsets[e]         first row of expert e in the dispatch layout; selected experts' segments are padded to a
+//                      multiple of `pad` rows (zero rows) so LoRA weight-gradient GEMMs can reduce over whole tiles
+//   gcounts[e]         rows of expert e's segment (counts, or the padded count for selected experts)
+//   row_of[i]          dispatch row of choice i (stable: equal experts keep (t, k) order)
+//   src_of[row]        i for real rows, -1 for padding rows (rows < total)
+//   order[j]           reference-compatible stable argsort of topi.reshape(-1) (unpadded positions)
+//   total[0]           rows used by the dispatch layout
+constexpr int kPlanWarps = 32;
+constexpr int kPlanMaxE = 512;
+
+__global__ void __launch_bounds__(kPlanWarps * 32, 1)
+    dispatch_plan_kernel(const long long* __restrict__ topi, long long R, int E, const uint8_t* __restrict__ sel_mask,
+                         int pad, int* __restrict__ counts, int* __restrict__ gcounts, int* __restrict__ offsets,
+                         int* __restrict__ row_of, int* __restrict__ src_of, long long* __restrict__ order,
+                         int* __restrict__ total, int* __restrict__ err) {
+  extern __shared__ int sm[];
+  int* hist = sm;                             // [kPlanWarps][E] per-warp counts, later per-warp running bases
+  int* s_off = sm + kPlanWarps * E;           // [E] padded offsets
+  int* s_offu = s_off + E;                    // [E] unpadded offsets
+  int* s_scan = s_offu + E;                   // [2 * 1024] scan scratch
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const long long chunk = (R + kPlanWarps - 1) / kPlanWarps;
+  const long long c0 = warp * chunk, c1 = min(R, c0 + chunk);
+  for (long long i = c0 + lane; i < c1; i += 32) {
+    const long long e = topi[i];
+    if (e < 0 || e >= E) {
+      dev_fail(err, kDevErrBadIndex);
+      continue;
+    }
+    atomicAdd(&hist[warp * E + (int)e], 1);
+  }
+  __syncthreads();
+  // per-expert totals and per-warp exclusive bases
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kPlanWarps; ++w) {
+      const int c = hist[w * E + e];
+      hist[w * E + e] = run;
+      run += c;
+    }
+    counts[e] = run;
+    const int seg = (sel_mask && sel_mask[e]) ? (run + pad - 1) / pad * pad : run;
+    gcounts[e] = seg;
+    s_scan[e] = seg;
+    s_scan[1024 + e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, accu = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = acc;
+      s_offu[e] = accu;
+      acc += s_scan[e];
+      accu += s_scan[1024 + e];
+    }
+    total[0] = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) offsets[e] = s_off[e];
+  // stable ranks: each warp walks its chunk in order, 32 choices at a time
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (long long b = c0; b < c1; b += 32) {
+    const long long i = b + lane;
+    const bool valid = i < c1;
+    long long e64 = valid ? topi[i] : -1;
+    const int e = (e64 >= 0 && e64 < E) ? (int)e64 : -1;
+    const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int rank = __popc(peers & active & lt_mask);
+      const int base = hist[warp * E + e];
+      const int pos = base + rank;
+      const int row = s_off[e] + pos;
+      row_of[i] = row;
+      src_of[row] = (int)i;
+      order[s_offu[e] + pos] = i;
+    }
+    __syncwarp();
+    if (e >= 0) {
+      const int leader = __ffs(peers & active) - 1;
+      if (lane == leader) hist[warp * E + e] += __popc(peers & active);
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  // padding rows of padded segments
+  for (int e = warp; e < E; e += kPlanWarps) {
+    const int cnt = s_scan[1024 + e], seg = s_scan[e];
+    for (int r = cnt + lane; r < seg; r += 32) src_of[s_off[e] + r] = -1;
+  }
+}
+
+int dispatch_plan(const long long* topi, long long R, int E, const uint8_t* sel_mask, int pad, int* counts,
+                  int* gcounts, int* offsets, int* row_of, int* src_of, long long* order, int* total, cudaStream_t st) {
+  SMELB_CHECK_ARG(E >= 1 && E <= kPlanMaxE, kErrShape, "dispatch_plan: E=%d (max %d)", E, kPlanMaxE);
+  SMELB_CHECK_ARG(pad >= 1 && R >= 0 && R < (1LL << 30), kErrShape, "dispatch_plan: R=%lld pad=%d", R, pad);
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  const int smem = (kPlanWarps * E + 2 * E + 2048) * 4;
+  static bool configured[64] = {false};
+  if (dev < 64 && !configured[dev]) {
+    SMELB_CUDA(cudaFuncSetAttribute(dispatch_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (kPlanWarps * kPlanMaxE + 2 * kPlanMaxE + 2048) * 4));
+    configured[dev] = true;
+  }
+  dispatch_plan_kernel<<<1, kPlanWarps * 32, smem, st>>>(topi, R, E, sel_mask, pad, counts, gcounts, offsets, row_of,
+                                                         src_of, order, total, device_status(dev));
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ gather
+// xs[row] = x[src_of[row] / K] for real rows and zeros for padding rows, rows < total[0]. One warp per row, 16-byte
+// vectors (H % 8 == 0).
+__global__ void gather_rows_kernel(const bf16* __restrict__ x, int H, int K, const int* __restrict__ src_of,
+                                   const int* __restrict__ total, long long max_rows, bf16* __restrict__ xs) {
+  const long long rows = min((long long)total[0], max_rows);
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  const int nv = H / 8;
+  for (long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
+    const int src = src_of[r];
+    uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
+    if (src < 0) {
+      for (int v = lane; v < nv; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    } else {
+      const uint4* s = reinterpret_cast<const uint4*>(x + (long long)(src / K) * H);
+      for (int v = lane; v < nv; v += 32) dst[v] = __ldg(s + v);
+    }
+  }
+}
+
+int gather_rows(const void* x, int H, int K, const int* src_of, const int* total, long long max_rows, void* xs,
+                cudaStream_t st) {
+  SMELB_CHECK_ARG(H % 8 == 0, kErrShape, "gather_rows: H=%d not a multiple of 8", H);
+  if (max_rows == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((max_rows * 32 + threads - 1) / threads, 148LL * 8);
+  gather_rows_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)x, H, K, src_of, total, max_rows, (bf16*)xs);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ combine
+// out[t] = bf16( sum_k fl(y[row_of[t,k]] * topv[t,k]) ) accumulated in fp32 in k order; with a shared expert:
+// out[t] = bf16( that + bf16(y_sh[t] * bf16(sigmoid(gl[t]))) ) (the reference's bf16 op sequence). One warp per
+// token, 8 columns per lane step.
+__global__ void combine_fwd_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
+                                   const void* __restrict__ topv, int topv_f32, int T, int K, int H,
+                                   const bf16* __restrict__ y_sh, const bf16* __restrict__ gl, int has_routed,
+                                   bf16* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
+    float w[32];
+    int rows[32];
+    for (int k = 0; k < K; ++k) {
+      const long long o = t * K + k;
+      w[k] = topv_f32 ? reinterpret_cast<const float*>(topv)[o]
+                      : __bfloat162float(reinterpret_cast<const bf16*>(topv)[o]);
+      rows[k] = has_routed ? row_of[o] : 0;
+    }
+    float sg = 0.f;
+    if (y_sh && gl) {
+      const float g = __bfloat162float(gl[t]);
+      sg = bf16_round(1.0f / (1.0f + expf(-g)));
+    }
+    for (int c = lane * 8; c < H; c += 256) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (has_routed) {
+        for (int k = 0; k < K; ++k) {
+          const uint4 v = *reinterpret_cast<const uint4*>(y + (long long)rows[k] * H + c);
+          const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(p[j]);
+            acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(f.x, w[k]));
+            acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(f.y, w[k]));
+          }
+        }
+      }
+      float res[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) res[j] = bf16_round(acc[j]);
+      if (y_sh) {
+        const uint4 v = *reinterpret_cast<const uint4*>(y_sh + t * H + c);
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(p[j]);
+          const float a = gl ? bf16_round(f.x * sg) : f.x;
+          const float b = gl ? bf16_round(f.y * sg) : f.y;
+          res[2 * j] = has_routed ? res[2 * j] + a : a;
+          res[2 * j + 1] = has_routed ? res[2 * j + 1] + b : b;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(res[2 * j], res[2 * j + 1]);
+      *reinterpret_cast<uint4*>(out + t * H + c) = o;
+    }
+  }
+}
+
+int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f32, int T, int K, int H,
+                const void* y_sh, const void* gl, void* out, cudaStream_t st) {
+  SMELB_CHECK_ARG(H % 8 == 0 && K <= 32, kErrShape, "combine_fwd: H=%d K=%d", H, K);
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>(((long long)T * 32 + threads - 1) / threads, 148LL * 8);
+  combine_fwd_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)y, row_of, topv, topv_f32 ? 1 : 0, T, K, H,
+                                                      (const bf16*)y_sh, (const bf16*)gl, y != nullptr ? 1 : 0,
+                                                      (bf16*)out);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// Backward of the combine, one warp per dispatch row (rows < total):
+//   dy[row] = bf16(g[t] * topv[t,k]); dtopv[t,k] = sum_h g[t,h] * y[row,h] (fp32, stored in topv's dtype);
+//   padding rows get dy = 0.
+__global__ void combine_bwd_rows_kernel(const bf16* __restrict__ g, const bf16* __restrict__ y,
+                                        const int* __restrict__ src_of, const int* __restrict__ total,
+                                        long long max_rows, const void* __restrict__ topv, int topv_f32, int K, int H,
+                                        bf16* __restrict__ dy, void* __restrict__ dtopv) {
+  const long long rows = min((long long)total[0], max_rows);
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
+    const int src = src_of[r];
+    uint4* d = reinterpret_cast<uint4*>(dy + r * H);
+    if (src < 0) {
+      for (int c = lane; c < H / 8; c += 32) d[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const long long t = src / K;
+    const float w = topv_f32 ? reinterpret_cast<const float*>(topv)[src]
+                             : __bfloat162float(reinterpret_cast<const bf16*>(topv)[src]);
+    float dot = 0.f;
+    for (int c = lane; c < H / 8; c += 32) {
+      const uint4 gv = reinterpret_cast<const uint4*>(g + t * H)[c];
+      const uint4 yv = reinterpret_cast<const uint4*>(y + r * H)[c];
+      const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
+      const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv);
+      uint4 o;
+      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 gf = __bfloat1622float2(gp[j]);
+        const float2 yf = __bfloat1622float2(yp[j]);
+        op[j] = __floats2bfloat162_rn(gf.x * w, gf.y * w);
+        dot = fmaf(gf.x, yf.x, dot);
+        dot = fmaf(gf.y, yf.y, dot);
+      }
+      d[c] = o;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0 && dtopv) {
+      if (topv_f32) reinterpret_cast<float*>(dtopv)[src] = dot;
+      else reinterpret_cast<bf16*>(dtopv)[src] = __float2bfloat16_rn(dot);
+    }
+  }
+}
+
+int combine_bwd_rows(const void* g, const void* y, const int* src_of, const int* total, long long max_rows,
+                     const void* topv, bool topv_f32, int K, int H, void* dy, void* dtopv, cudaStream_t st) {
+  SMELB_CHECK_ARG(H % 8 == 0, kErrShape, "combine_bwd: H=%d", H);
+  if (max_rows == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((max_rows * 32 + threads - 1) / threads, 148LL * 8);
+  combine_bwd_rows_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)g, (const bf16*)y, src_of, total, max_rows,
+                                                           topv, topv_f32 ? 1 : 0, K, H, (bf16*)dy, dtopv);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// Shared expert gate backward, one warp per token: dy_sh = bf16(g * s_b) with s_b = bf16(sigmoid(gl));
+// ds = sum_h g * y_sh (fp32); dgl = ds * s_b * (1 - s_b), stored as fp32 for the final dX reduction.
+__global__ void shared_gate_bwd_kernel(const bf16* __restrict__ g, const bf16* __restrict__ y_sh,
+                                       const bf16* __restrict__ gl, int T, int H, bf16* __restrict__ dy_sh,
+                                       float* __restrict__ dgl) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
+    const float sb = bf16_round(1.0f / (1.0f + expf(-__bfloat162float(gl[t]))));
+    float dot = 0.f;
+    for (int c = lane; c < H / 8; c += 32) {
+      const uint4 gv = reinterpret_cast<const uint4*>(g + t * H)[c];
+      const uint4 yv = reinterpret_cast<const uint4*>(y_sh + t * H)[c];
+      const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
+      const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv);
+      uint4 o;
+      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 gf = __bfloat1622float2(gp[j]);
+        const float2 yf = __bfloat1622float2(yp[j]);
+        op[j] = __floats2bfloat162_rn(gf.x * sb, gf.y * sb);
+        dot = fmaf(gf.x, yf.x, dot);
+        dot = fmaf(gf.y, yf.y, dot);
+      }
+      reinterpret_cast<uint4*>(dy_sh + t * H)[c] = o;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0) dgl[t] = bf16_round(bf16_round(dot) * sb * (1.0f - sb));
+  }
+}
+
+int shared_gate_bwd(const void* g, const void* y_sh, const void* gl, int T, int H, void* dy_sh, float* dgl,
+                    cudaStream_t st) {
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>(((long long)T * 32 + threads - 1) / threads, 148LL * 8);
+  shared_gate_bwd_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)g, (const bf16*)y_sh, (const bf16*)gl, T, H,
+                                                          (bf16*)dy_sh, dgl);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// Final dX of the layer, one warp per token, fp32 accumulation then one rounding:
+//   dx[t] = sum_k dxs[row_of[t,k]] + dx_sh[t] + dx_r[t] + dgl[t] * w_sg
+__global__ void dx_reduce_kernel(const bf16* __restrict__ dxs, const int* __restrict__ row_of, int K, int T, int H,
+                                 const bf16* __restrict__ dx_sh, const bf16* __restrict__ dx_r,
+                                 const float* __restrict__ dgl, const bf16* __restrict__ w_sg, bf16* __restrict__ dx) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
+    int rows[32];
+    if (dxs)
+      for (int k = 0; k < K; ++k) rows[k] = row_of[t * K + k];
+    const float dg = dgl ? dgl[t] : 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      auto add = [&](const bf16* src) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src);
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(p[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
+      };
+      if (dxs)
+        for (int k = 0; k < K; ++k) add(dxs + (long long)rows[k] * H + c);
+      if (dx_sh) add(dx_sh + t * H + c);
+      if (dx_r) add(dx_r + t * H + c);
+      if (dgl && w_sg) {
+        const uint4 v = *reinterpret_cast<const uint4*>(w_sg + c);
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(p[j]);
+          acc[2 * j] = fmaf(dg, f.x, acc[2 * j]);
+          acc[2 * j + 1] = fmaf(dg, f.y, acc[2 * j + 1]);
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+      *reinterpret_cast<uint4*>(dx + t * H + c) = o;
+    }
+  }
+}
+
+int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const void* dx_sh, const void* dx_r,
+              const float* dgl, const void* w_sg, void* dx, cudaStream_t st) {
+  SMELB_CHECK_ARG(H % 8 == 0 && K <= 32, kErrShape, "dx_reduce: H=%d K=%d", H, K);
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>(((long long)T * 32 + threads - 1) / threads, 148LL * 8);
+  dx_reduce_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)dxs, row_of, K, T, H, (const bf16*)dx_sh,
+                                                    (const bf16*)dx_r, dgl, (const bf16*)w_sg, (bf16*)dx);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ LoRA factor packing
+// out[j][a][b] (bf16, J x OA x OB) = scale_i * src_i[j*sj + (a - a0)*sa + (b - b0)*sb] inside block i (two blocks),
+// zero elsewhere. Used to build the per-step bf16 operands of the LoRA GEMMs from the fp32 parameters
+// (concatenations, block-diagonal stacks, transposes, scale folding and zero padding to 64 columns).
+__global__ void pack_blocks_kernel(PackSpec spec, bf16* __restrict__ out) {
+  const long long n = (long long)spec.J * spec.OA * spec.OB;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long j = i / ((long long)spec.OA * spec.OB);
+    const long long rem = i - j * spec.OA * spec.OB;
+    const int a = (int)(rem / spec.OB), b = (int)(rem - (long long)a * spec.OB);
+    float v = 0.f;
+#pragma unroll
+    for (int bi = 0; bi < 2; ++bi) {
+      const PackBlock& B = spec.blk[bi];
+      if (B.src && a >= B.a0 && a < B.a0 + B.na && b >= B.b0 && b < B.b0 + B.nb)
+        v = B.scale * B.src[j * B.sj + (long long)(a - B.a0) * B.sa + (long long)(b - B.b0) * B.sb];
+    }
+    out[i] = __float2bfloat16_rn(v);
+  }
+}
+
+int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st) {
+  const long long n = (long long)spec.J * spec.OA * spec.OB;
+  if (n == 0) return kOk;
+  const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 8);
+  pack_blocks_kernel<<<(int)blocks, 256, 0, st>>>(spec, (bf16*)out);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+}  // namespace smelb

@@ -1,0 +1,47 @@
+// Host entry points of the memory-bound MoE kernels (kernels.cu). All return a Status code.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+namespace smelb {
+
+struct PackBlock {
+  const float* src;  // nullptr: block unused
+  long long sj;      // source stride between slots j
+  long long sa, sb;  // source strides along the output's a / b axes
+  int a0, na, b0, nb;
+  float scale;
+};
+struct PackSpec {
+  int J, OA, OB;
+  PackBlock blk[2];
+};
+
+int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
+                 bool out_f32, cudaStream_t st);
+int int4_pack_sz(const void* scale, const void* zero, uint32_t* szT, long long nw, int rows, int groups,
+                 cudaStream_t st);
+int router_topk(const void* logits, long long ld, int T, int E, int K, float* probs, void* topv, bool topv_f32,
+                long long* topi, const void* per_expert_scale, cudaStream_t st);
+int router_bwd(const void* dtopv, bool dtopv_f32, const float* dprobs, const float* probs, const long long* topi,
+               const void* per_expert_scale, int T, int E, int K, void* dlogits, long long ld, cudaStream_t st);
+int dispatch_plan(const long long* topi, long long R, int E, const uint8_t* sel_mask, int pad, int* counts,
+                  int* gcounts, int* offsets, int* row_of, int* src_of, long long* order, int* total, cudaStream_t st);
+int gather_rows(const void* x, int H, int K, const int* src_of, const int* total, long long max_rows, void* xs,
+                cudaStream_t st);
+int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f32, int T, int K, int H,
+                const void* y_sh, const void* gl, void* out, cudaStream_t st);
+int combine_bwd_rows(const void* g, const void* y, const int* src_of, const int* total, long long max_rows,
+                     const void* topv, bool topv_f32, int K, int H, void* dy, void* dtopv, cudaStream_t st);
+int shared_gate_bwd(const void* g, const void* y_sh, const void* gl, int T, int H, void* dy_sh, float* dgl,
+                    cudaStream_t st);
+int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const void* dx_sh, const void* dx_r,
+              const float* dgl, const void* w_sg, void* dx, cudaStream_t st);
+int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st);
+
+int launch_gemm(struct LaunchArgs& args, cudaStream_t stream);
+
+}  // namespace smelb

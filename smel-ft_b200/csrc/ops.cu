@@ -1,0 +1,812 @@
+// C ABI of smelb (include/smelb.h): argument checks, GEMM problem construction and the sequencing of the MoE layer's
+// forward and backward launches.
+#include <cstring>
+
+#include "../../include/smelb.h"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "host.h"
+#include "kernels.h"
+
+namespace smelb {
+const char* last_error();
+long long launch_count();
+void set_gemm_timing(bool on);
+int read_gemm_timing(double* ms, long long* n);
+}
+
+using namespace smelb;
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kW64 = 64;       // column width of the LoRA token-side buffers and extension blocks
+
+// ---------------------------------------------------------------------------------------------- tensor maps
+int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int box_rows) {
+  return make_tmap_2d(m, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols * 2, 64, box_rows, true);
+}
+int tm_q(CUtensorMap* m, const void* q, long long rows, long long cols, bool mn_major) {
+  // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes
+  return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : 32, 64,
+                      false);
+}
+int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows) {
+  return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4, 64, 1, false);
+}
+
+#define TRY(x)               \
+  do {                       \
+    int rc_ = (x);           \
+    if (rc_ != kOk) return rc_; \
+  } while (0)
+
+struct Builder {
+  LaunchArgs args;
+  Builder() {
+    memset(&args, 0, sizeof(args));
+  }
+  Problem& add() {
+    Problem& P = args.p[args.nprob++];
+    memset(&P, 0, sizeof(P));
+    P.alpha = 1.0f;
+    return P;
+  }
+  int launch(cudaStream_t st) { return args.nprob ? launch_gemm(args, st) : kOk; }
+};
+
+void groups(Problem& P, const int* counts, const int* offsets, const int* gid, const int* widx, int n) {
+  P.counts = counts;
+  P.offsets = offsets;
+  P.gid_of = gid;
+  P.widx_of = widx;
+  P.ngroups = n;
+}
+
+// Int4 stored matrix of the bank: [nw][rows][cols] nibbles with (scale, zero) per 64 columns.
+struct Int4Mat {
+  const void* q;
+  const uint32_t* sz;
+  int nw, rows, cols;
+};
+
+// kTokN, A = int4 bank used directly (K-major: M = rows, K = cols) or transposed (MN-major: M = cols, K = rows).
+int set_a_int4(Problem& P, const Int4Mat& W, bool mn_major) {
+  P.a_kind = mn_major ? kAInt4MN : kAInt4K;
+  TRY(tm_q(&P.tmQ, W.q, (long long)W.nw * W.rows, W.cols, mn_major));
+  TRY(tm_sz(&P.tmSZ, W.sz, (long long)W.nw * (W.cols / 64), W.rows));
+  P.q_rows = W.rows;
+  P.q_groups = W.cols / 64;
+  P.M = mn_major ? W.cols : W.rows;
+  P.K = mn_major ? W.rows : W.cols;
+  return kOk;
+}
+
+// kTokN, A = bf16 weights [nw][rows][cols]; K-major uses rows as M, MN-major uses cols as M.
+int set_a_bf16(Problem& P, const void* W, int nw, int rows, int cols, bool mn_major, bool glu) {
+  P.a_kind = mn_major ? kABf16MN : kABf16K;
+  TRY(tm_bf16(&P.tmA, W, (long long)nw * rows, cols, glu ? 16 : 64));
+  P.a_wrows = rows;
+  P.M = mn_major ? cols : rows;
+  P.K = mn_major ? rows : cols;
+  return kOk;
+}
+
+// LoRA K-extension: weight side [nw][e_rows][64], token side [tok_rows][64]
+int set_ext(Problem& P, const void* Wext, int nw, int e_rows, const void* Xext, long long tok_rows, bool glu) {
+  P.has_ext = 1;
+  TRY(tm_bf16(&P.tmAe, Wext, (long long)nw * e_rows, kW64, glu ? 16 : 64));
+  TRY(tm_bf16(&P.tmBe, Xext, tok_rows, kW64, 64));
+  P.e_wrows = e_rows;
+  return kOk;
+}
+
+int set_b_tokens(Problem& P, const void* X, long long rows, int cols, int BN = 256) {
+  P.mode = kTokN;
+  P.BN = BN;
+  return tm_bf16(&P.tmB, X, rows, cols, 64);
+}
+
+void out_bf16(Problem& P, void* C, long long ldc) {
+  P.epi = kEpiStoreBf16;
+  P.C = C;
+  P.c_sn = ldc;
+  P.c_sm = 1;
+}
+
+// kTokK LoRA gradient: C[g][m][n] = alpha * sum_k A[k][a_x0 + m] * B[k][b_x0 + n] over the tokens of group g.
+int set_tokk(Problem& P, const void* Atok, long long rows, int a_cols, int a_x0, int M, const void* Btok, int b_cols,
+             int b_x0, int N, float* C, long long c_sm, long long c_sn, long long c_gs, float alpha) {
+  P.mode = kTokK;
+  P.a_kind = kABf16MN;
+  P.epi = kEpiStoreF32;
+  TRY(tm_bf16(&P.tmA, Atok, rows, a_cols, 64));
+  TRY(tm_bf16(&P.tmB, Btok, rows, b_cols, 64));
+  P.a_x0 = a_x0;
+  P.b_x0 = b_x0;
+  P.M = M;
+  P.N = (N + 15) & ~15;
+  P.C = C;
+  P.c_sm = c_sm;
+  P.c_sn = c_sn;
+  P.c_gs = c_gs;
+  P.alpha = alpha;
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------------------------- LoRA packing
+PackBlock blk(const float* src, long long sj, long long sa, long long sb, int a0, int na, int b0, int nb, float s) {
+  PackBlock b;
+  b.src = src;
+  b.sj = sj;
+  b.sa = sa;
+  b.sb = sb;
+  b.a0 = a0;
+  b.na = na;
+  b.b0 = b0;
+  b.nb = nb;
+  b.scale = s;
+  return b;
+}
+PackBlock no_blk() { return blk(nullptr, 0, 0, 0, 0, 0, 0, 0, 0.f); }
+int pack(int J, int OA, int OB, PackBlock b0, PackBlock b1, void* out, cudaStream_t st) {
+  PackSpec s;
+  s.J = J;
+  s.OA = OA;
+  s.OB = OB;
+  s.blk[0] = b0;
+  s.blk[1] = b1;
+  return pack_blocks(s, out, st);
+}
+
+// LoRA parameter set of one gated MLP family (J slots; J = 1 for the shared expert)
+struct LoraSet {
+  int J, r, H, I;
+  float s;
+  const float *Ag, *Bg, *Au, *Bu, *Ad, *Bd;
+};
+
+// forward operands: xa_w [J,2r,H] = [A_gate; A_up]; gu_ext [J,2I,64] = [[s B_gate, 0], [0, s B_up]];
+// z_w [J,r,I] = A_down; dn_ext [J,H,64] = [s B_down, 0]
+int pack_fwd(const LoraSet& L, void* xa_w, void* gu_ext, void* z_w, void* dn_ext, cudaStream_t st) {
+  const int r = L.r, H = L.H, I = L.I;
+  TRY(pack(L.J, 2 * r, H, blk(L.Ag, (long long)r * H, H, 1, 0, r, 0, H, 1.f),
+           blk(L.Au, (long long)r * H, H, 1, r, r, 0, H, 1.f), xa_w, st));
+  TRY(pack(L.J, 2 * I, kW64, blk(L.Bg, (long long)I * r, r, 1, 0, I, 0, r, L.s),
+           blk(L.Bu, (long long)I * r, r, 1, I, I, r, r, L.s), gu_ext, st));
+  TRY(pack(L.J, r, I, blk(L.Ad, (long long)r * I, I, 1, 0, r, 0, I, 1.f), no_blk(), z_w, st));
+  TRY(pack(L.J, H, kW64, blk(L.Bd, (long long)H * r, r, 1, 0, H, 0, r, L.s), no_blk(), dn_ext, st));
+  return kOk;
+}
+
+// backward operands: dz_w [J,r,H] = s B_down^T; da_ext [J,I,64] = [A_down^T, 0];
+// dxa_w [J,2r,2I] = [[s B_gate^T, 0], [0, s B_up^T]]; dx_ext [J,H,64] = [A_gate^T, A_up^T, 0]
+int pack_bwd(const LoraSet& L, void* dz_w, void* da_ext, void* dxa_w, void* dx_ext, cudaStream_t st) {
+  const int r = L.r, H = L.H, I = L.I;
+  TRY(pack(L.J, r, H, blk(L.Bd, (long long)H * r, 1, r, 0, r, 0, H, L.s), no_blk(), dz_w, st));
+  TRY(pack(L.J, I, kW64, blk(L.Ad, (long long)r * I, 1, I, 0, I, 0, r, 1.f), no_blk(), da_ext, st));
+  TRY(pack(L.J, 2 * r, 2 * I, blk(L.Bg, (long long)I * r, 1, r, 0, r, 0, I, L.s),
+           blk(L.Bu, (long long)I * r, 1, r, r, r, I, I, L.s), dxa_w, st));
+  TRY(pack(L.J, H, kW64, blk(L.Ag, (long long)r * H, 1, H, 0, H, 0, r, 1.f),
+           blk(L.Au, (long long)r * H, 1, H, 0, H, r, r, 1.f), dx_ext, st));
+  return kOk;
+}
+
+struct Flags {
+  bool router, routed, shared, sgate, save, topv32, sel, sel_lora, sh_lora, fz_bf16;
+};
+
+int check_layer(const smelb_moe_layer& L, Flags& f) {
+  f.router = L.flags & SMELB_F_ROUTER;
+  f.routed = L.flags & SMELB_F_ROUTED;
+  f.shared = L.flags & SMELB_F_SHARED;
+  f.sgate = f.shared && (L.flags & SMELB_F_SHARED_GATE);
+  f.save = L.flags & SMELB_F_SAVE;
+  f.topv32 = L.flags & SMELB_F_TOPV_FP32;
+  f.sel = f.routed && L.n_sel > 0;
+  f.sel_lora = f.sel && L.r_sel > 0;
+  f.sh_lora = f.shared && L.r_sh > 0;
+  f.fz_bf16 = L.gu_q == nullptr && L.fz_gu != nullptr;
+  SMELB_CHECK_ARG(L.T >= 0 && L.H > 0 && L.H % 64 == 0, kErrShape, "layer: H=%lld must be a multiple of 64",
+                  (long long)L.H);
+  SMELB_CHECK_ARG(L.act == SMELB_ACT_SILU || L.act == SMELB_ACT_GELU_TANH, kErrArg, "layer: unknown activation %d",
+                  L.act);
+  SMELB_CHECK_ARG(L.act_sh == SMELB_ACT_SILU || L.act_sh == SMELB_ACT_GELU_TANH, kErrArg,
+                  "layer: unknown shared activation %d", L.act_sh);
+  if (f.routed || f.router) {
+    SMELB_CHECK_ARG(L.E >= 1 && L.E <= 512 && L.K >= 1 && L.K <= 32 && L.K <= L.E, kErrShape,
+                    "layer: E=%lld K=%lld", (long long)L.E, (long long)L.K);
+  }
+  if (f.routed) {
+    SMELB_CHECK_ARG(L.I > 0 && L.I % 64 == 0, kErrShape, "layer: I=%lld must be a multiple of 64", (long long)L.I);
+    SMELB_CHECK_ARG(L.n_sel >= 0 && L.n_sel <= L.E, kErrShape, "layer: n_sel=%lld", (long long)L.n_sel);
+    SMELB_CHECK_ARG(L.max_rows >= L.T * L.K + L.n_sel * 64, kErrWorkspace, "layer: max_rows=%lld < T*K + 64*n_sel",
+                    (long long)L.max_rows);
+    SMELB_CHECK_ARG(L.E - L.n_sel + L.n_sel + 2 <= kMaxGroups, kErrShape, "layer: too many experts for one launch");
+  }
+  if (f.shared) SMELB_CHECK_ARG(L.S > 0 && L.S % 64 == 0, kErrShape, "layer: S=%lld must be a multiple of 64",
+                                (long long)L.S);
+  if (f.sel_lora) SMELB_CHECK_ARG(2 * L.r_sel <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sel);
+  if (f.sh_lora) SMELB_CHECK_ARG(2 * L.r_sh <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sh);
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------------------------- layer forward
+int layer_fwd(const smelb_moe_layer& L) {
+  Flags f;
+  TRY(check_layer(L, f));
+  cudaStream_t st = (cudaStream_t)L.stream;
+  const int T = (int)L.T, H = (int)L.H, E = (int)L.E, K = (int)L.K, I = (int)L.I, S = (int)L.S;
+  const int nsel = (int)L.n_sel, nfz = (int)(L.E - L.n_sel), rs = (int)L.r_sel, rh = (int)L.r_sh;
+  const long long R = L.max_rows;
+  if (T == 0) return kOk;
+  const LoraSet ls{nsel, rs, H, I, L.s_sel, L.A_gate, L.B_gate, L.A_up, L.B_up, L.A_down, L.B_down};
+  const LoraSet lh{1, rh, H, S, L.s_sh, L.shA_gate, L.shB_gate, L.shA_up, L.shB_up, L.shA_down, L.shB_down};
+  if (f.sel_lora) TRY(pack_fwd(ls, L.p_xa_w, L.p_gu_ext, L.p_z_w, L.p_dn_ext, st));
+  if (f.sh_lora) TRY(pack_fwd(lh, L.sp_xa_w, L.sp_gu_ext, L.sp_z_w, L.sp_dn_ext, st));
+
+  // L1: everything that reads only x: router logits, shared gate logit, shared LoRA A product
+  {
+    Builder b;
+    if (f.router) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.w_router, 1, E, H, false, false));
+      TRY(set_b_tokens(P, L.x, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.logits, E);
+    }
+    if (f.sgate) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.w_sgate, 1, 1, H, false, false));
+      TRY(set_b_tokens(P, L.x, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.sgate_logit, 1);
+    }
+    if (f.sh_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sp_xa_w, 1, 2 * rh, H, false, false));
+      TRY(set_b_tokens(P, L.x, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.sh_xa, kW64);
+    }
+    TRY(b.launch(st));
+  }
+  if (f.router) TRY(router_topk(L.logits, E, T, E, K, L.probs, L.topv, f.topv32, (long long*)L.topi, nullptr, st));
+  const void* topv = f.router ? L.topv : L.topv_in;
+  const long long* topi = (const long long*)(f.router ? L.topi : L.topi_in);
+
+  if (f.routed) {
+    TRY(dispatch_plan(topi, (long long)T * K, E, L.sel_mask, 64, L.counts, L.gcounts, L.offsets, L.row_of, L.src_of,
+                      (long long*)L.order, L.total, st));
+    TRY(gather_rows(L.x, H, K, L.src_of, L.total, R, L.xs, st));
+  }
+  const Int4Mat gu{L.gu_q, L.gu_sz, E, 2 * I, H};
+  const Int4Mat dn{L.dn_q, L.dn_sz, E, H, I};
+
+  // L2: selected-expert LoRA A product, shared expert gate/up (GLU)
+  {
+    Builder b;
+    if (f.sel_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.p_xa_w, nsel, 2 * rs, H, false, false));
+      TRY(set_b_tokens(P, L.xs, R, H));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      out_bf16(P, L.xa, kW64);
+    }
+    if (f.shared) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sh_gu, 1, 2 * S, H, false, true));
+      TRY(set_b_tokens(P, L.x, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      if (f.sh_lora) TRY(set_ext(P, L.sp_gu_ext, 1, 2 * S, L.sh_xa, T, true));
+      P.epi = kEpiGlu;
+      P.C = L.sh_a;
+      P.c_sn = S;
+      P.c_sm = 1;
+      P.Hout = f.save ? (bf16*)L.sh_h : nullptr;
+      P.h_ld = 2 * S;
+      P.inter = S;
+      P.act = L.act_sh;
+    }
+    TRY(b.launch(st));
+  }
+  // L3: routed gate/up (frozen int4 + selected bf16 with LoRA), shared LoRA A of the down projection
+  {
+    Builder b;
+    if (f.routed && nfz > 0) {
+      Problem& P = b.add();
+      if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, false, true));
+      else TRY(set_a_int4(P, gu, false));
+      TRY(set_b_tokens(P, L.xs, R, H));
+      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+      P.epi = kEpiGlu;
+      P.C = L.a;
+      P.c_sn = I;
+      P.c_sm = 1;
+      P.Hout = f.save ? (bf16*)L.h : nullptr;
+      P.h_ld = 2 * I;
+      P.inter = I;
+      P.act = L.act;
+    }
+    if (f.sel) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sel_gu, nsel, 2 * I, H, false, true));
+      TRY(set_b_tokens(P, L.xs, R, H));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      if (f.sel_lora) TRY(set_ext(P, L.p_gu_ext, nsel, 2 * I, L.xa, R, true));
+      P.epi = kEpiGlu;
+      P.C = L.a;
+      P.c_sn = I;
+      P.c_sm = 1;
+      P.Hout = f.save ? (bf16*)L.h : nullptr;
+      P.h_ld = 2 * I;
+      P.inter = I;
+      P.act = L.act;
+    }
+    if (f.sh_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sp_z_w, 1, rh, S, false, false));
+      TRY(set_b_tokens(P, L.sh_a, T, S));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.sh_z, kW64);
+    }
+    TRY(b.launch(st));
+  }
+  // L4: selected LoRA A of the down projection, shared down projection
+  {
+    Builder b;
+    if (f.sel_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.p_z_w, nsel, rs, I, false, false));
+      TRY(set_b_tokens(P, L.a, R, I));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      out_bf16(P, L.z, kW64);
+    }
+    if (f.shared) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sh_dn, 1, H, S, false, false));
+      TRY(set_b_tokens(P, L.sh_a, T, S));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      if (f.sh_lora) TRY(set_ext(P, L.sp_dn_ext, 1, H, L.sh_z, T, false));
+      out_bf16(P, L.sh_y, H);
+    }
+    TRY(b.launch(st));
+  }
+  // L5: routed down projections
+  if (f.routed) {
+    Builder b;
+    if (nfz > 0) {
+      Problem& P = b.add();
+      if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_dn, E, H, I, false, false));
+      else TRY(set_a_int4(P, dn, false));
+      TRY(set_b_tokens(P, L.a, R, I));
+      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+      out_bf16(P, L.y, H);
+    }
+    if (f.sel) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sel_dn, nsel, H, I, false, false));
+      TRY(set_b_tokens(P, L.a, R, I));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      if (f.sel_lora) TRY(set_ext(P, L.p_dn_ext, nsel, H, L.z, R, false));
+      out_bf16(P, L.y, H);
+    }
+    TRY(b.launch(st));
+  }
+  if (f.routed || f.shared)
+    TRY(combine_fwd(f.routed ? L.y : nullptr, L.row_of, topv, f.topv32, T, K, H, f.shared ? L.sh_y : nullptr,
+                    f.sgate ? L.sgate_logit : nullptr, L.out, st));
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------------------------- layer backward
+int layer_bwd(const smelb_moe_layer& L) {
+  Flags f;
+  TRY(check_layer(L, f));
+  cudaStream_t st = (cudaStream_t)L.stream;
+  const int T = (int)L.T, H = (int)L.H, E = (int)L.E, K = (int)L.K, I = (int)L.I, S = (int)L.S;
+  const int nsel = (int)L.n_sel, nfz = (int)(L.E - L.n_sel), rs = (int)L.r_sel, rh = (int)L.r_sh;
+  const long long R = L.max_rows;
+  const int Epad = (E + 63) / 64 * 64;
+  if (T == 0) return kOk;
+  const LoraSet ls{nsel, rs, H, I, L.s_sel, L.A_gate, L.B_gate, L.A_up, L.B_up, L.A_down, L.B_down};
+  const LoraSet lh{1, rh, H, S, L.s_sh, L.shA_gate, L.shB_gate, L.shA_up, L.shB_up, L.shA_down, L.shB_down};
+  if (f.sel_lora) TRY(pack_bwd(ls, L.p_dz_w, L.p_da_ext, L.p_dxa_w, L.p_dx_ext, st));
+  if (f.sh_lora) TRY(pack_bwd(lh, L.sp_dz_w, L.sp_da_ext, L.sp_dxa_w, L.sp_dx_ext, st));
+  const void* topv = f.router ? L.topv : L.topv_in;
+
+  if (f.routed)
+    TRY(combine_bwd_rows(L.g, L.y, L.src_of, L.total, R, topv, f.topv32, K, H, L.dy, L.dtopv, st));
+  const void* sh_dy = L.g;
+  if (f.sgate) {
+    TRY(shared_gate_bwd(L.g, L.sh_y, L.sgate_logit, T, H, L.sh_dy, L.dgl, st));
+    sh_dy = L.sh_dy;
+  }
+  if (f.router)
+    TRY(router_bwd(L.dtopv, f.topv32, L.dprobs, L.probs, (const long long*)L.topi, nullptr, T, E, K, L.dlogits, Epad,
+                   st));
+  const Int4Mat gu{L.gu_q, L.gu_sz, E, 2 * I, H};
+  const Int4Mat dn{L.dn_q, L.dn_sz, E, H, I};
+
+  // B1: LoRA products of dy with B_down
+  {
+    Builder b;
+    if (f.sel_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.p_dz_w, nsel, rs, H, false, false));
+      TRY(set_b_tokens(P, L.dy, R, H));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      out_bf16(P, L.dz, kW64);
+    }
+    if (f.sh_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sp_dz_w, 1, rh, H, false, false));
+      TRY(set_b_tokens(P, sh_dy, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.sh_dz, kW64);
+    }
+    TRY(b.launch(st));
+  }
+  // B2: da = dy @ W_down (+ LoRA) fused with the gated-MLP backward -> dh
+  {
+    Builder b;
+    if (f.routed && nfz > 0) {
+      Problem& P = b.add();
+      if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_dn, E, H, I, true, false));
+      else TRY(set_a_int4(P, dn, true));
+      TRY(set_b_tokens(P, L.dy, R, H));
+      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+      P.epi = kEpiDGlu;
+      P.C = L.dh;
+      P.c_sn = 2 * I;
+      P.Hin = (const bf16*)L.h;
+      P.h_ld = 2 * I;
+      P.inter = I;
+      P.act = L.act;
+    }
+    if (f.sel) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sel_dn, nsel, H, I, true, false));
+      TRY(set_b_tokens(P, L.dy, R, H));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      if (f.sel_lora) TRY(set_ext(P, L.p_da_ext, nsel, I, L.dz, R, false));
+      P.epi = kEpiDGlu;
+      P.C = L.dh;
+      P.c_sn = 2 * I;
+      P.Hin = (const bf16*)L.h;
+      P.h_ld = 2 * I;
+      P.inter = I;
+      P.act = L.act;
+    }
+    if (f.shared) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sh_dn, 1, H, S, true, false));
+      TRY(set_b_tokens(P, sh_dy, T, H));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      if (f.sh_lora) TRY(set_ext(P, L.sp_da_ext, 1, S, L.sh_dz, T, false));
+      P.epi = kEpiDGlu;
+      P.C = L.sh_dh;
+      P.c_sn = 2 * S;
+      P.Hin = (const bf16*)L.sh_h;
+      P.h_ld = 2 * S;
+      P.inter = S;
+      P.act = L.act_sh;
+    }
+    TRY(b.launch(st));
+  }
+  // B3: LoRA products of dh with B_gate / B_up
+  {
+    Builder b;
+    if (f.sel_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.p_dxa_w, nsel, 2 * rs, 2 * I, false, false));
+      TRY(set_b_tokens(P, L.dh, R, 2 * I));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      out_bf16(P, L.dxa, kW64);
+    }
+    if (f.sh_lora) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sp_dxa_w, 1, 2 * rh, 2 * S, false, false));
+      TRY(set_b_tokens(P, L.sh_dh, T, 2 * S));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.sh_dxa, kW64);
+    }
+    TRY(b.launch(st));
+  }
+  // B4: dX contributions: dh @ W_gate_up (+ LoRA) for routed and shared, dlogits @ W_router
+  {
+    Builder b;
+    if (f.routed && nfz > 0) {
+      Problem& P = b.add();
+      if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, true, false));
+      else TRY(set_a_int4(P, gu, true));
+      TRY(set_b_tokens(P, L.dh, R, 2 * I));
+      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+      out_bf16(P, L.dxs, H);
+    }
+    if (f.sel) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sel_gu, nsel, 2 * I, H, true, false));
+      TRY(set_b_tokens(P, L.dh, R, 2 * I));
+      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+      if (f.sel_lora) TRY(set_ext(P, L.p_dx_ext, nsel, H, L.dxa, R, false));
+      out_bf16(P, L.dxs, H);
+    }
+    if (f.shared) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.sh_gu, 1, 2 * S, H, true, false));
+      TRY(set_b_tokens(P, L.sh_dh, T, 2 * S));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      if (f.sh_lora) TRY(set_ext(P, L.sp_dx_ext, 1, H, L.sh_dxa, T, false));
+      out_bf16(P, L.sh_dx, H);
+    }
+    if (f.router) {
+      Problem& P = b.add();
+      TRY(set_a_bf16(P, L.w_router, 1, E, H, true, false));
+      P.K = Epad;
+      TRY(set_b_tokens(P, L.dlogits, T, Epad));
+      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+      out_bf16(P, L.dx_router, H);
+    }
+    TRY(b.launch(st));
+  }
+  // B5: LoRA weight gradients (tokens along K)
+  {
+    Builder b;
+    if (f.sel_lora) {
+      const int* gc = L.gcounts;
+      auto grp = [&](Problem& P) { groups(P, gc, L.offsets, L.sel_ids, L.sel_slots, nsel); };
+      Problem* P;
+      P = &b.add();
+      TRY(set_tokk(*P, L.xs, R, H, 0, H, L.dxa, kW64, 0, rs, L.gA_gate, 1, H, (long long)rs * H, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.xs, R, H, 0, H, L.dxa, kW64, rs, rs, L.gA_up, 1, H, (long long)rs * H, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.dh, R, 2 * I, 0, I, L.xa, kW64, 0, rs, L.gB_gate, rs, 1, (long long)I * rs, L.s_sel));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.dh, R, 2 * I, I, I, L.xa, kW64, rs, rs, L.gB_up, rs, 1, (long long)I * rs, L.s_sel));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.a, R, I, 0, I, L.dz, kW64, 0, rs, L.gA_down, 1, I, (long long)rs * I, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.dy, R, H, 0, H, L.z, kW64, 0, rs, L.gB_down, rs, 1, (long long)H * rs, L.s_sel));
+      grp(*P);
+    }
+    if (f.sh_lora) {
+      auto grp = [&](Problem& P) { groups(P, L.tok_count, nullptr, nullptr, nullptr, 1); };
+      Problem* P;
+      P = &b.add();
+      TRY(set_tokk(*P, L.x, T, H, 0, H, L.sh_dxa, kW64, 0, rh, L.gshA_gate, 1, H, 0, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.x, T, H, 0, H, L.sh_dxa, kW64, rh, rh, L.gshA_up, 1, H, 0, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.sh_dh, T, 2 * S, 0, S, L.sh_xa, kW64, 0, rh, L.gshB_gate, rh, 1, 0, L.s_sh));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.sh_dh, T, 2 * S, S, S, L.sh_xa, kW64, rh, rh, L.gshB_up, rh, 1, 0, L.s_sh));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, L.sh_a, T, S, 0, S, L.sh_dz, kW64, 0, rh, L.gshA_down, 1, S, 0, 1.f));
+      grp(*P);
+      P = &b.add();
+      TRY(set_tokk(*P, sh_dy, T, H, 0, H, L.sh_z, kW64, 0, rh, L.gshB_down, rh, 1, 0, L.s_sh));
+      grp(*P);
+    }
+    TRY(b.launch(st));
+  }
+  TRY(dx_reduce(f.routed ? L.dxs : nullptr, L.row_of, K, T, H, f.shared ? L.sh_dx : nullptr,
+                f.router ? L.dx_router : nullptr, f.sgate ? L.dgl : nullptr, L.w_sgate, L.dx, st));
+  return kOk;
+}
+
+}  // namespace
+
+// ================================================================================================== C ABI
+extern "C" {
+
+int smelb_version(void) { return kVersion; }
+
+int smelb_last_error(char* buf, size_t len) {
+  const char* e = smelb::last_error();
+  const size_t n = strlen(e);
+  if (buf && len) {
+    const size_t c = n < len - 1 ? n : len - 1;
+    memcpy(buf, e, c);
+    buf[c] = 0;
+  }
+  return (int)n;
+}
+
+int smelb_read_status(int device, int* status, int reset) {
+  SMELB_CHECK_ARG(status != nullptr, kErrArg, "read_status: null output");
+  int prev = 0;
+  SMELB_CUDA(cudaGetDevice(&prev));
+  SMELB_CUDA(cudaSetDevice(device));
+  int* w = device_status(device);
+  SMELB_CHECK_ARG(w != nullptr, kErrCuda, "read_status: no status word");
+  SMELB_CUDA(cudaDeviceSynchronize());
+  SMELB_CUDA(cudaMemcpy(status, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) SMELB_CUDA(cudaMemset(w, 0, sizeof(int)));
+  SMELB_CUDA(cudaSetDevice(prev));
+  return kOk;
+}
+
+int smelb_int4_dequant(const void* q, const void* scale, const void* zero, void* out, int64_t rows, int64_t k,
+                       int64_t groups, int out_fp32, void* stream) {
+  SMELB_CHECK_ARG(q && scale && zero && out, kErrArg, "int4_dequant: null pointer");
+  return int4_dequant(q, scale, zero, out, rows, (int)k, (int)groups, out_fp32 != 0, (cudaStream_t)stream);
+}
+
+int smelb_int4_pack_sz(const void* scale, const void* zero, uint32_t* sz_t, int64_t nw, int64_t rows,
+                       int64_t groups, void* stream) {
+  SMELB_CHECK_ARG(scale && zero && sz_t, kErrArg, "int4_pack_sz: null pointer");
+  return int4_pack_sz(scale, zero, sz_t, nw, (int)rows, (int)groups, (cudaStream_t)stream);
+}
+
+int smelb_router_topk(const void* logits, int64_t ld, int64_t T, int64_t E, int64_t K, float* probs, void* topv,
+                      int topv_fp32, int64_t* topi, const void* per_expert_scale, void* stream) {
+  SMELB_CHECK_ARG(logits && probs && topv && topi, kErrArg, "router_topk: null pointer");
+  return router_topk(logits, ld, (int)T, (int)E, (int)K, probs, topv, topv_fp32 != 0, (long long*)topi,
+                     per_expert_scale, (cudaStream_t)stream);
+}
+
+int smelb_router_bwd(const void* dtopv, int dtopv_fp32, const float* probs, const int64_t* topi,
+                     const void* per_expert_scale, int64_t T, int64_t E, int64_t K, void* dlogits, int64_t ld,
+                     void* stream) {
+  SMELB_CHECK_ARG(probs && topi && dlogits, kErrArg, "router_bwd: null pointer");
+  return router_bwd(dtopv, dtopv_fp32 != 0, nullptr, probs, (const long long*)topi, per_expert_scale, (int)T,
+                    (int)E, (int)K, dlogits, ld, (cudaStream_t)stream);
+}
+
+int smelb_dispatch_plan(const int64_t* topi, int64_t T, int64_t K, int64_t E, const uint8_t* sel_mask, int64_t pad,
+                        int32_t* counts, int32_t* gcounts, int32_t* offsets, int32_t* row_of, int32_t* src_of,
+                        int64_t* order, int32_t* total, void* stream) {
+  SMELB_CHECK_ARG(topi && counts && gcounts && offsets && row_of && src_of && order && total, kErrArg,
+                  "dispatch_plan: null pointer");
+  return dispatch_plan((const long long*)topi, T * K, (int)E, sel_mask, (int)pad, counts, gcounts, offsets, row_of,
+                       src_of, (long long*)order, total, (cudaStream_t)stream);
+}
+
+int smelb_gather_rows(const void* x, int64_t H, int64_t K, const int32_t* src_of, const int32_t* total,
+                      int64_t max_rows, void* xs, void* stream) {
+  SMELB_CHECK_ARG(x && src_of && total && xs, kErrArg, "gather_rows: null pointer");
+  return gather_rows(x, (int)H, (int)K, src_of, total, max_rows, xs, (cudaStream_t)stream);
+}
+
+int smelb_combine_fwd(const void* y, const int32_t* row_of, const void* topv, int topv_fp32, int64_t T, int64_t K,
+                      int64_t H, void* out, void* stream) {
+  SMELB_CHECK_ARG(y && row_of && topv && out, kErrArg, "combine_fwd: null pointer");
+  return combine_fwd(y, row_of, topv, topv_fp32 != 0, (int)T, (int)K, (int)H, nullptr, nullptr, out,
+                     (cudaStream_t)stream);
+}
+
+int smelb_frozen_experts_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E,
+                             const void* gu_q, const uint32_t* gu_sz, const void* dn_q, const uint32_t* dn_sz,
+                             int act, void* h_save, void* a_buf, void* out, void* stream) {
+  SMELB_CHECK_ARG(xs && counts && gu_q && gu_sz && dn_q && dn_sz && a_buf && out, kErrArg,
+                  "frozen_experts_fwd: null pointer");
+  SMELB_CHECK_ARG(H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups, kErrShape,
+                  "frozen_experts_fwd: H=%lld I=%lld E=%lld", (long long)H, (long long)I, (long long)E);
+  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "unknown activation %d", act);
+  if (rows == 0) return kOk;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
+  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, gu, false));
+    TRY(set_b_tokens(P, xs, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiGlu;
+    P.C = a_buf;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)h_save;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(b.launch(st));
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, dn, false));
+    TRY(set_b_tokens(P, a_buf, rows, (int)I));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    out_bf16(P, out, H);
+    TRY(b.launch(st));
+  }
+  return kOk;
+}
+
+int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
+                             const int32_t* counts, int64_t E, const void* gu_q, const uint32_t* gu_sz,
+                             const void* dn_q, const uint32_t* dn_sz, int act, const void* h, void* h_buf,
+                             void* dh_buf, void* dx, void* stream) {
+  SMELB_CHECK_ARG(dy && counts && gu_q && gu_sz && dn_q && dn_sz && dh_buf && dx, kErrArg,
+                  "frozen_experts_bwd: null pointer");
+  SMELB_CHECK_ARG(h || (xs && h_buf), kErrArg, "frozen_experts_bwd: need the saved h or xs and h_buf to recompute");
+  SMELB_CHECK_ARG(H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups, kErrShape,
+                  "frozen_experts_bwd: H=%lld I=%lld E=%lld", (long long)H, (long long)I, (long long)E);
+  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "unknown activation %d", act);
+  if (rows == 0) return kOk;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
+  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
+  if (!h) {
+    // recompute gate/up pre-activations into h_buf (the GLU output goes to dh_buf, overwritten below)
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, gu, false));
+    TRY(set_b_tokens(P, xs, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiGlu;
+    P.C = dh_buf;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)h_buf;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(b.launch(st));
+    h = h_buf;
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, dn, true));
+    TRY(set_b_tokens(P, dy, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiDGlu;
+    P.C = dh_buf;
+    P.c_sn = 2 * I;
+    P.Hin = (const bf16*)h;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(b.launch(st));
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, gu, true));
+    TRY(set_b_tokens(P, dh_buf, rows, (int)(2 * I)));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    out_bf16(P, dx, H);
+    TRY(b.launch(st));
+  }
+  return kOk;
+}
+
+size_t smelb_moe_layer_size(void) { return sizeof(smelb_moe_layer); }
+
+long long smelb_launch_count(void) { return smelb::launch_count(); }
+
+int smelb_gemm_timing(int enable) {
+  smelb::set_gemm_timing(enable != 0);
+  return kOk;
+}
+
+int smelb_gemm_timing_read(double* ms_total, long long* launches) {
+  SMELB_CHECK_ARG(ms_total && launches, kErrArg, "gemm_timing_read: null output");
+  return smelb::read_gemm_timing(ms_total, launches);
+}
+
+int smelb_moe_layer_fwd(const smelb_moe_layer* L) {
+  SMELB_CHECK_ARG(L != nullptr, kErrArg, "moe_layer_fwd: null layer");
+  return layer_fwd(*L);
+}
+
+int smelb_moe_layer_bwd(const smelb_moe_layer* L) {
+  SMELB_CHECK_ARG(L != nullptr, kErrArg, "moe_layer_bwd: null layer");
+  return layer_bwd(*L);
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+"""Generate the golden fixtures of tests/golden/ by running the REFERENCE implementation (smel-ft's smel package) on
+the CPU. Run where the reference source tree is available:
+
+    python tests/golden/make_golden.py --reference /path/to/smel-ft
+
+Outputs (torch.save dicts of CPU tensors):
+  quant.pt     quantize_int4 / dequant_int4_torch(fp32) of seeded weights, an on-grid round trip
+  dispatch.pt  stable argsort / bincount of expert choices with many ties
+  moe_c1.pt    config 1 (tiny Qwen-class MoE block, fp32): inputs, int4 bank, routing, dispatch, forward output,
+               dX and all LoRA gradients of moe_forward with an upstream gradient
+  moe_c1_bf16.pt  the same block run by the reference in bf16 on the CPU
+  frozen_gelu.pt  FrozenExpertsFn forward/backward with GELU-tanh, uneven counts and an empty expert
+                  (the case of the reference test tests/test_gemma4.py:153-169)
+The test-suite never imports the reference; it only reads these files.
+"""
+import argparse
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def lora_tensors(H, I, S, n_sel, r, alpha, gen):
+    """A: PEFT kaiming_uniform(a=sqrt(5)) bound 1/sqrt(in); B ~ N(0, 0.02) so the LoRA contributes."""
+    def a(*s):
+        return (torch.rand(*s, generator=gen) * 2 - 1) / (s[-1] ** 0.5)
+
+    def b(*s):
+        return torch.randn(*s, generator=gen) * 0.02
+
+    ex = {"A_gate": a(n_sel, r, H), "B_gate": b(n_sel, I, r), "A_up": a(n_sel, r, H), "B_up": b(n_sel, I, r),
+          "A_down": a(n_sel, r, I), "B_down": b(n_sel, H, r)}
+    sh = {"A_gate": a(r, H), "B_gate": b(S, r), "A_up": a(r, H), "B_up": b(S, r), "A_down": a(r, S),
+          "B_down": b(H, r)}
+    return ex, sh
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
+    from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
+    from smel.quant import dequant_int4_torch, quantize_int4
+
+    torch.set_num_threads(4)
+
+    # ------------------------------------------------------------------ quant
+    g = torch.Generator().manual_seed(11)
+    w = torch.randn(4, 96, 256, generator=g) * 0.02
+    w[0, 0, :64] = 0.37  # a constant group (scale clamps to 1e-8)
+    pk = quantize_int4(w, 64)
+    deq = dequant_int4_torch(pk["q"], pk["scale"], pk["zero"], torch.float32)
+    gq = torch.randint(0, 16, (4, 8, 128), generator=g)
+    gs = (torch.rand(4, 8, 2, generator=g) + 0.5).bfloat16().float()
+    gz = torch.randn(4, 8, 2, generator=g).bfloat16().float()
+    grid = (gq.reshape(4, 8, 2, 64).float() * gs[..., None] + gz[..., None]).reshape(4, 8, 128)
+    pg = quantize_int4(grid, 64)
+    torch.save({"w": w, "q": pk["q"], "scale": pk["scale"], "zero": pk["zero"], "deq_f32": deq,
+                "grid_w": grid, "grid_q": pg["q"], "grid_scale": pg["scale"], "grid_zero": pg["zero"],
+                "grid_back": dequant_int4_torch(pg["q"], pg["scale"], pg["zero"], torch.float32)},
+               os.path.join(HERE, "quant.pt"))
+
+    # ------------------------------------------------------------------ dispatch (many ties)
+    topi = torch.randint(0, 8, (97, 4), generator=g)
+    topi[10:20] = 3
+    flat = topi.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    torch.save({"topi": topi, "E": 8, "order": order, "tok": order // 4, "counts": torch.bincount(flat, minlength=8)},
+               os.path.join(HERE, "dispatch.pt"))
+
+    # ------------------------------------------------------------------ config 1 (tiny, fp32)
+    H, E, K, I, S, T, r, alpha = 64, 8, 2, 64, 64, 128, 8, 16.0
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, H, generator=g)
+    W = {"mlp.gate.weight": torch.randn(E, H, generator=g) * 0.02,
+         "mlp.shared_expert.gate_proj.weight": torch.randn(S, H, generator=g) * 0.02,
+         "mlp.shared_expert.up_proj.weight": torch.randn(S, H, generator=g) * 0.02,
+         "mlp.shared_expert.down_proj.weight": torch.randn(H, S, generator=g) * 0.02,
+         "mlp.shared_expert_gate.weight": torch.randn(1, H, generator=g) * 0.02}
+    gu = torch.randn(E, 2 * I, H, generator=g) * 0.02
+    dn = torch.randn(E, H, I, generator=g) * 0.02
+    sel = [0, 1]
+    exl, shl = lora_tensors(H, I, S, len(sel), r, alpha, g)
+    gy = torch.randn(T, H, generator=g)
+    bank = Int4Experts(quantize_int4(gu, 64), quantize_int4(dn, 64), dtype=torch.float32)
+
+    def run(dtype):
+        xd = x.to(dtype).clone().requires_grad_(True)
+        Wd = {k: v.to(dtype) for k, v in W.items()}
+        bank_d = Int4Experts(bank.gu, bank.dn, dtype=dtype)
+        ex = LayerExperts(bank_d, sel, gu[sel].to(dtype).clone(), dn[sel].to(dtype).clone(), group=4)
+        le = ExpertsLoRA(sel, H, I, r, alpha)
+        ls = MLPLoRA(H, S, r, alpha)
+        with torch.no_grad():
+            for n, v in exl.items():
+                getattr(le, n).copy_(v)
+            for n, v in shl.items():
+                getattr(ls, n).copy_(v)
+        lora = LayerLoRA(le, ls)
+        rec = {}
+        out = moe_forward(xd, Wd, ex, K, lora, stats=lambda p, v, i: rec.update(probs=p.detach(), topv=v.detach(),
+                                                                              topi=i.detach()))
+        out.backward(gy.to(dtype))
+        res = {"out": out.detach(), "dx": xd.grad.detach(), **rec}
+        for n in exl:
+            res["g_ex_" + n] = getattr(le, n).grad.detach().clone()
+            res["g_sh_" + n] = getattr(ls, n).grad.detach().clone()
+        return res
+
+    res32 = run(torch.float32)
+    flat = res32["topi"].reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    torch.save({"cfg": dict(H=H, E=E, K=K, I=I, S=S, T=T, r=r, alpha=alpha, sel=sel, act="silu"),
+                "x": x, "W": W, "gu": gu, "dn": dn, "gy": gy, "lora_ex": exl, "lora_sh": shl,
+                "gu_q": bank.gu["q"], "gu_scale": bank.gu["scale"], "gu_zero": bank.gu["zero"],
+                "dn_q": bank.dn["q"], "dn_scale": bank.dn["scale"], "dn_zero": bank.dn["zero"],
+                "order": order, "counts": torch.bincount(flat, minlength=E), **res32},
+               os.path.join(HERE, "moe_c1.pt"))
+    res16 = run(torch.bfloat16)
+    torch.save(res16, os.path.join(HERE, "moe_c1_bf16.pt"))
+
+    # route alone on the config-1 inputs, fp32 (routing indices and weights)
+    probs, topv, topi = route(x, W["mlp.gate.weight"], K)
+    torch.save({"probs": probs, "topv": topv, "topi": topi}, os.path.join(HERE, "route_c1.pt"))
+
+    # ------------------------------------------------------------------ frozen experts, GELU-tanh, empty expert
+    g = torch.Generator().manual_seed(5)
+    Ef, Hf, If, N = 6, 32, 24, 50
+    fgu, fdn = torch.randn(Ef, 2 * If, Hf, generator=g) * 0.2, torch.randn(Ef, Hf, If, generator=g) * 0.2
+    counts = [9, 0, 12, 7, 15, 7]
+    xf = torch.randn(N, Hf, generator=g, dtype=torch.float64).float().requires_grad_(True)
+    gyf = torch.randn(N, Hf, generator=g)
+    yf = FrozenExpertsFn.apply(xf, counts, BF16Experts(fgu, fdn), 2, "gelu_tanh")
+    yf.backward(gyf)
+    torch.save({"gu": fgu, "dn": fdn, "counts": torch.tensor(counts), "x": xf.detach(), "gy": gyf, "y": yf.detach(),
+                "dx": xf.grad.detach()}, os.path.join(HERE, "frozen_gelu.pt"))
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

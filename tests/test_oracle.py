@@ -1,0 +1,113 @@
+"""The CPU oracle against golden vectors produced by the reference implementation (tests/golden/make_golden.py)."""
+import numpy as np
+import torch
+
+from oracle import moe_oracle as O
+
+
+def test_quantize_matches_reference_bit_exact(golden):
+    d = golden("quant.pt")
+    pk = O.quantize_int4(d["w"], 64)
+    assert torch.equal(pk["q"], d["q"])
+    assert torch.equal(pk["scale"].view(torch.int16), d["scale"].view(torch.int16))
+    assert torch.equal(pk["zero"].view(torch.int16), d["zero"].view(torch.int16))
+
+
+def test_dequant_fp32_matches_reference_bit_exact(golden):
+    d = golden("quant.pt")
+    w = O.dequant_int4(d["q"], d["scale"], d["zero"], torch.float32)
+    assert torch.equal(w, d["deq_f32"])
+
+
+def test_int4_roundtrip_on_grid(golden):
+    """Known answer (reference tests/test_quant_merge.py:14-23): on-grid weights survive quantize -> dequant up to
+    the bf16 rounding of scale/zero."""
+    d = golden("quant.pt")
+    pk = O.quantize_int4(d["grid_w"], 64)
+    assert torch.equal(pk["q"], d["grid_q"])
+    back = O.dequant_int4(pk["q"], pk["scale"], pk["zero"])
+    assert torch.equal(back, d["grid_back"])
+    assert O.rel_err(back, d["grid_w"]) < 5e-3
+
+
+def test_nibble_order_low_is_even_column():
+    codes = np.arange(16, dtype=np.uint8).reshape(1, 16)
+    q = O.pack_nibbles(codes)
+    assert q.tolist() == [[0x10, 0x32, 0x54, 0x76, 0x98, 0xBA, 0xDC, 0xFE]]
+    assert np.array_equal(O.unpack_nibbles(q), codes)
+
+
+def test_dispatch_matches_reference(golden):
+    d = golden("dispatch.pt")
+    order, tok, counts = O.dispatch(d["topi"].numpy(), d["E"])
+    assert np.array_equal(order, d["order"].numpy())
+    assert np.array_equal(tok, d["tok"].numpy())
+    assert np.array_equal(counts, d["counts"].numpy())
+
+
+def test_dispatch_padded_layout(golden):
+    d = golden("dispatch.pt")
+    topi = d["topi"].numpy()
+    sel = np.zeros(8, dtype=np.uint8)
+    sel[[3, 5]] = 1
+    counts, gcounts, offsets, row_of, src_of = O.dispatch_padded(topi, 8, sel, pad=64)
+    assert np.array_equal(counts, d["counts"].numpy())
+    assert all(gcounts[e] % 64 == 0 for e in (3, 5))
+    # the unpadded rank order is the reference's stable argsort
+    order, _, _ = O.dispatch(topi, 8)
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    for j, i in enumerate(order):
+        e = topi.reshape(-1)[i]
+        assert row_of[i] - offsets[e] == j - starts[e]
+    assert (src_of[row_of] == np.arange(row_of.size)).all()
+    assert (src_of == -1).sum() == int((gcounts - counts).sum())
+
+
+def test_route_matches_reference(golden):
+    d = golden("moe_c1.pt")
+    r = golden("route_c1.pt")
+    probs, topv, topi = O.route(d["x"], d["W"]["mlp.gate.weight"], d["cfg"]["K"])
+    assert torch.allclose(probs, r["probs"], rtol=0, atol=1e-7)
+    # no ties at this seed: indices must match exactly
+    assert torch.equal(topi, r["topi"])
+    assert torch.allclose(topv, r["topv"], rtol=0, atol=1e-6)
+
+
+def _c1_oracle(d, dtype=torch.float64):
+    cfg = d["cfg"]
+    gu = O.dequant_int4(d["gu_q"], d["gu_scale"], d["gu_zero"]).to(dtype)
+    dn = O.dequant_int4(d["dn_q"], d["dn_scale"], d["dn_zero"]).to(dtype)
+    x = d["x"].to(dtype).requires_grad_(True)
+    W = {k: v.to(dtype) for k, v in d["W"].items()}
+    sel = cfg["sel"]
+    lex = {k: v.to(dtype).requires_grad_(True) for k, v in d["lora_ex"].items()}
+    lsh = {k: v.to(dtype).requires_grad_(True) for k, v in d["lora_sh"].items()}
+    scale = cfg["alpha"] / cfg["r"]
+    out, probs, topv, topi = O.moe_layer(x, W, gu, dn, cfg["K"], sel, d["gu"][sel].to(dtype), d["dn"][sel].to(dtype),
+                                         {**lex, "scale": scale}, {**lsh, "scale": scale}, topi=d["topi"])
+    out.backward(d["gy"].to(dtype))
+    return out, x.grad, lex, lsh, topv
+
+
+def test_moe_forward_backward_matches_reference_fp32(golden):
+    """Config 1: the oracle (fp64) reproduces the reference's fp32 output, dX and all LoRA gradients."""
+    d = golden("moe_c1.pt")
+    out, dx, lex, lsh, topv = _c1_oracle(d)
+    assert O.rel_err(out, d["out"]) < 1e-5
+    assert O.rel_err(dx, d["dx"]) < 1e-5
+    assert O.rel_err(topv, d["topv"]) < 1e-6
+    for n in lex:
+        assert O.rel_err(lex[n].grad, d["g_ex_" + n]) < 1e-5, n
+        assert O.rel_err(lsh[n].grad, d["g_sh_" + n]) < 1e-5, n
+
+
+def test_frozen_experts_gelu_backward_matches_reference(golden):
+    d = golden("frozen_gelu.pt")
+    x = d["x"].double().requires_grad_(True)
+    y = O.frozen_experts(x, d["counts"].tolist(), d["gu"].double(), d["dn"].double(), "gelu_tanh")
+    assert O.rel_err(y, d["y"]) < 1e-5
+    y.backward(d["gy"].double())
+    assert O.rel_err(x.grad, d["dx"]) < 1e-5
+    manual = O.frozen_experts_backward(d["x"].double(), d["gy"].double(), d["counts"].tolist(), d["gu"].double(),
+                                       d["dn"].double(), "gelu_tanh")
+    assert O.rel_err(manual, d["dx"]) < 1e-5
