@@ -176,10 +176,12 @@ def run_ours(args, world, rank, local):
     n0 = _lib.launch_count()
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record()
     for _ in range(args.steps):
         step(x, gy)
     e1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ck = clocks.stop()
     launches = _lib.launch_count() - n0

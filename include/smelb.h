@@ -38,9 +38,17 @@ int smelb_version(void);
 /* Copies the text of the last error of the calling thread into buf (NUL-terminated). Returns its length. */
 int smelb_last_error(char* buf, size_t len);
 
+/* Makes `device` (and its primary context) current for this library on the calling thread. Bindings call it with
+ * the framework's current device before the other entry points (e.g. on autograd worker threads). */
+int smelb_set_device(int device);
+
 /* Synchronizes `device` and reads its status word: 0, or the code of the first device-side wait that gave up
  * (a pipeline barrier that was never satisfied) or of an out-of-range expert index. reset != 0 clears it. */
 int smelb_read_status(int device, int* status, int reset);
+
+/* As smelb_read_status, with the location of the first failure: words[0] code, words[1] block, words[2] tile,
+ * words[3] k-block (-1 where not applicable). words has 4 entries. */
+int smelb_read_status_detail(int device, int* words, int reset);
 
 /* ---------------------------------------------------------------------------------------------------- int4 format
  * smel/quant.py:74-94 dequant_int4 / dequant_int4_torch: q uint8 [rows, k/2] (low nibble = even column),

@@ -24,14 +24,14 @@ def _deps_mtime():
     return max(os.path.getmtime(f) for f in files if os.path.isfile(f))
 
 
-def build(force=False, jobs=4, verbose=False, extra=()):
+def build(force=False, jobs=4, verbose=False, extra=(), out=OUT, build_dir=BUILD):
     """Compile every source to an object and link the shared library. Returns the library path."""
-    os.makedirs(BUILD, exist_ok=True)
-    if not force and os.path.exists(OUT) and os.path.getmtime(OUT) >= _deps_mtime():
-        return OUT
+    os.makedirs(build_dir, exist_ok=True)
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= _deps_mtime():
+        return out
 
     def compile_one(src):
-        obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+        obj = os.path.join(build_dir, src.replace(".cu", ".o"))
         cmd = [NVCC, *FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
@@ -42,13 +42,13 @@ def build(force=False, jobs=4, verbose=False, extra=()):
 
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         objs = list(ex.map(compile_one, SOURCES))
-    tmp = OUT + ".tmp"
+    tmp = out + ".tmp"
     cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC", *objs, "-o", tmp]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":

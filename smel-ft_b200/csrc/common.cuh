@@ -49,22 +49,41 @@ void set_last_error(const char* fmt, ...);
     }                                                                                       \
   } while (0)
 
-// Device-side error words (written with atomicCAS so the first failure wins).
+// Device-side status: word 0 holds the first failure code (atomicCAS, first one wins); words 1-3 the block, tile and
+// k-block index where it happened.
 enum DevErr : int {
   kDevErrNone = 0,
-  kDevErrWaitFull = 1,
-  kDevErrWaitEmpty = 2,
-  kDevErrWaitAccFull = 3,
-  kDevErrWaitAccEmpty = 4,
-  kDevErrTmaDrain = 5,
+  kDevErrWaitFull = 1,       // MMA waiting for a token tile
+  kDevErrWaitEmpty = 2,      // token producer waiting for a free slot
+  kDevErrWaitAccFull = 3,    // epilogue waiting for an accumulator
+  kDevErrWaitAccEmpty = 4,   // MMA waiting for a free accumulator
+  kDevErrTmaDrain = 5,       // a producer waiting for its last copies at exit
   kDevErrTooManyGroups = 6,
-  kDevErrBadIndex = 7,
+  kDevErrBadIndex = 7,       // expert index out of range in the dispatch plan
+  kDevErrWaitAFull = 8,      // MMA waiting for a weight tile
+  kDevErrWaitQFull = 9,      // dequant waiting for staged nibbles
+  kDevErrWaitAEmptyDeq = 10, // dequant waiting for a free weight slot
+  kDevErrWaitAEmptyTma = 11, // weight producer waiting for a free weight slot
+  kDevErrWaitQEmpty = 12,    // staging producer waiting for a consumed stage
 };
+constexpr int kStatusWords = 4;
 
 using bf16 = __nv_bfloat16;
 
 __device__ __forceinline__ void dev_fail(int* err, int code) {
-  if (err) atomicCAS(err, 0, code);
+  if (err && atomicCAS(err, 0, code) == 0) {
+    err[1] = blockIdx.x;
+    err[2] = -1;
+    err[3] = -1;
+  }
+}
+
+__device__ __forceinline__ void dev_fail_at(int* err, int code, int tile, int kb) {
+  if (err && atomicCAS(err, 0, code) == 0) {
+    err[1] = blockIdx.x;
+    err[2] = tile;
+    err[3] = kb;
+  }
 }
 
 // ------------------------------------------------------------------------------------------- timers
@@ -92,6 +111,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// arrive `count` times at once
+__device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// raise the current phase's expected transaction bytes without arriving
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -109,22 +138,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait until the phase with the given parity has completed. Returns false (and records `code` in *err) when the
-// wait gives up after SMELB_WAIT_NS, or immediately when another thread has already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
+// Wait until the phase with the given parity has completed. Returns false (and records `code` with the location in
+// the status words) when the wait gives up after SMELB_WAIT_NS. The fast path is a single try_wait; the timed spin
+// lives out of line so it costs the hot loops nothing.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code, int tile, int kb) {
+  const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
-      if (err && *((volatile int*)err) != 0) return false;
-      if (globaltimer_ns() - t0 > SMELB_WAIT_NS) {
-        dev_fail(err, code);
-        return false;
-      }
+    if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > SMELB_WAIT_NS) {
+      dev_fail_at(err, code, tile, kb);
+      return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code, int tile = -1,
+                                          int kb = -1) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, code, tile, kb);
 }
 
 // ------------------------------------------------------------------------------------------- proxy fences
@@ -168,14 +200,15 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 inputs, fp32 accumulate), issued by one thread.
+// No "memory" clobber: operand visibility is ordered by the mbarrier waits and tcgen05 fences, and a clobber would
+// make the compiler reload every memory-resident value (kernel parameters included) after each MMA.
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrive on `bar` once all tcgen05 operations issued so far by this thread have completed.

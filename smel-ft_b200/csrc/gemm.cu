@@ -10,15 +10,16 @@ namespace smelb {
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStages * kAStageBytes;
 constexpr int kOffQ = kOffB + kStages * kBStageBytes;
-constexpr int kOffSZ = kOffQ + kStages * kQStageBytes;
-constexpr int kOffTab = kOffSZ + kStages * kSZStageBytes;
+constexpr int kOffSZ = kOffQ + kQStages * kQStageBytes;
+constexpr int kOffTab = kOffSZ + kQStages * kSZStageBytes;
 constexpr int kTabInts = 3 * kMaxGroups + (kMaxGroups + kMaxProblems) + (kMaxProblems + 1) + kMaxProblems;
 constexpr int kOffBar = (kOffTab + kTabInts * 4 + 7) & ~7;
-constexpr int kNumBars = 3 * kStages + 5;
+constexpr int kNumBars = 3 * kStages + 2 * kQStages + 5;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmem + 16;
 constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment of the dynamic buffer
 static_assert(kSmemAlloc <= 232448, "shared memory budget exceeded");
+static_assert(kThreads <= 1024, "too many threads");
 
 struct TileInfo {
   int p, g, widx, mt, m0, n0, n_valid, nkb;
@@ -167,6 +168,10 @@ __device__ __forceinline__ int glu_stage_row(int r) {
 }
 
 // ------------------------------------------------------------------------------------------ the kernel
+__device__ __forceinline__ bool is_int4(const Problem& P) {
+  return P.mode == kTokN && (P.a_kind == kAInt4K || P.a_kind == kAInt4MN);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_constant__ LaunchArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -183,21 +188,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   T.tstart = T.gpre + kMaxGroups + kMaxProblems;
   T.gbase = T.tstart + kMaxProblems + 1;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full_tma = bars;
-  uint64_t* full_deq = bars + kStages;
-  uint64_t* empty = bars + 2 * kStages;
-  uint64_t* acc_full = bars + 3 * kStages;
+  uint64_t* a_full = bars;                  // weight tile ready (TMA bytes + 4 arrivals, or 4 dequant warps)
+  uint64_t* b_full = a_full + kStages;      // token tile landed
+  uint64_t* empty = b_full + kStages;       // MMAs reading the stage (weight and token tile) are done
+  uint64_t* q_full = empty + kStages;       // packed nibbles + (scale, zero) of 4 k-blocks landed
+  uint64_t* q_empty = q_full + kQStages;    // all 4 k-blocks of the staging stage dequantized
+  uint64_t* acc_full = q_empty + kQStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_drain = acc_full + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + kOffTmem);
 
   // ---------------------------------------------------------------- prologue: barriers, TMEM, tile tables
-  if (warp == 0) {
+  if (warp == kWarpTmaB) {
     if (lane == 0) {
       for (int s = 0; s < kStages; ++s) {
-        mbar_init(&full_tma[s], 1);
-        mbar_init(&full_deq[s], kNumDeqWarps);
+        mbar_init(&a_full[s], kNumDeqWarps);
+        mbar_init(&b_full[s], 1);
         mbar_init(&empty[s], 1);
+      }
+      for (int s = 0; s < kQStages; ++s) {
+        mbar_init(&q_full[s], 1);
+        mbar_init(&q_empty[s], kNumDeqWarps * kQSub);
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&acc_full[a], 1);
@@ -214,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           tma_prefetch_desc(&P.tmA);
         }
         tma_prefetch_desc(&P.tmB);
+        if (P.mode == kTokN) tma_prefetch_desc(&P.tmB32);
         if (P.has_ext) {
           tma_prefetch_desc(&P.tmAe);
           tma_prefetch_desc(&P.tmBe);
@@ -263,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       gbase += P.ngroups;
     }
     if (lane == 0) T.tstart[args.nprob] = total;
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     tmem_alloc(s_tmem, 512);
     tmem_relinquish();
   }
@@ -273,8 +285,48 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   const uint32_t tmem_base = *s_tmem;
   const int total_tiles = T.tstart[args.nprob];
 
-  if (warp == 0) {
-    // ============================================================================ TMA producer (one thread)
+  if (warp == kWarpTmaB) {
+    // ============================================================================ TMA: token ring (one thread)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(args, T, t);
+        const Problem& P = args.p[ti.p];
+        const bool tokk = P.mode == kTokK;
+        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+        const CUtensorMap* mB = &P.tmB;
+        const CUtensorMap* mB32 = &P.tmB32;
+        const CUtensorMap* mBe = &P.tmBe;
+        const int nb = tokk ? (P.N + 63) / 64 : (ti.n_valid + 63) / 64;
+        const int b_x0 = P.b_x0;
+        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
+          uint8_t* sB = smem + kOffB + s * kBStageBytes;
+          uint64_t* fb = &b_full[s];
+          if (!tokk) {
+            const bool ext = kb == ext_kb;
+            if (!ext && ti.n_valid <= 32) {
+              mbar_arrive_expect_tx(fb, 4096);
+              tma_load_2d(sB, mB32, kb * kBK, ti.n0, fb);
+            } else {
+              mbar_arrive_expect_tx(fb, nb * 8192);
+              for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, ext ? mBe : mB, ext ? 0 : kb * kBK, ti.n0 + 64 * i, fb);
+            }
+          } else {  // kTokK: B = tokens^T (MN-major)
+            const int krow = ti.n0 + kb * kBK;
+            mbar_arrive_expect_tx(fb, nb * 8192);
+            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, b_x0 + 64 * i, krow, fb);
+          }
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
+        if (!mbar_wait(&b_full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+    }
+  } else if (warp == kWarpTmaA) {
+    // ============================================================================ TMA: bf16 weight ring (one thread)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
@@ -282,69 +334,91 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         const TileInfo ti = decode_tile(args, T, t);
         const Problem& P = args.p[ti.p];
         const bool glu = P.epi == kEpiGlu;
+        const bool int4 = is_int4(P);
+        const bool tokk = P.mode == kTokK;
+        const int a_kind = P.a_kind;
+        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+        const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
+        const CUtensorMap* mAmain = &P.tmA;
+        const CUtensorMap* mAext = &P.tmAe;
+        const int a_wrows = P.a_wrows, e_wrows = P.e_wrows, a_x0 = P.a_x0;
         for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+          const bool ext = kb == ext_kb;
           const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, err, kDevErrWaitEmpty)) { ok = false; break; }
+          // waited for every k-block (see the note on ring waits), filled only for TMA-sourced weight tiles
+          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyTma, t, kb)) { ok = false; break; }
+          if (int4 && !ext) continue;  // the dequant warps fill this slot
           uint8_t* sA = smem + kOffA + s * kAStageBytes;
-          uint8_t* sB = smem + kOffB + s * kBStageBytes;
+          uint64_t* fa = &a_full[s];
+          mbar_expect_tx(fa, kAStageBytes);
+          if (tokk) {  // A = tokens^T (MN-major)
+            const int krow = ti.n0 + kb * kBK;
+            tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, fa);
+            tma_load_2d(sA + 8192, mAmain, a_x0 + ti.m0 + 64, krow, fa);
+          } else if (ext || a_kind == kABf16K) {
+            const CUtensorMap* mA = ext ? mAext : mAmain;
+            const int wrow = ti.widx * (ext ? e_wrows : a_wrows);
+            const int x = ext ? 0 : kb * kBK;
+            if (glu) {
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fa);
+                tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fa);
+              }
+            } else {
+              tma_load_2d(sA, mA, x, wrow + r0, fa);
+              tma_load_2d(sA + 8192, mA, x, wrow + r1, fa);
+            }
+          } else {  // kABf16MN
+            const int wrow = ti.widx * a_wrows + kb * kBK;
+            tma_load_2d(sA, mAmain, ti.m0, wrow, fa);
+            tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, fa);
+          }
+          mbar_arrive_n(fa, kNumDeqWarps);
+        }
+      }
+      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
+        if (!mbar_wait(&a_full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+    }
+  } else if (warp == kWarpTmaQ) {
+    // ============================================================================ TMA: int4 staging ring (one thread)
+    if (lane == 0) {
+      uint32_t qi = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = decode_tile(args, T, t);
+        const Problem& P = args.p[ti.p];
+        if (!is_int4(P)) continue;
+        const bool glu = P.epi == kEpiGlu;
+        const bool kmajor = P.a_kind == kAInt4K;
+        const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
+        const int nkq = P.K / kBK;
+        const CUtensorMap* mQ = &P.tmQ;
+        const CUtensorMap* mSZ = &P.tmSZ;
+        const int qrow0 = ti.widx * P.q_rows, grow0 = ti.widx * P.q_groups;
+        for (int kq = 0; kq * kQSub < nkq; ++kq, ++qi) {
+          const int s = qi % kQStages;
+          if (!mbar_wait(&q_empty[s], ((qi / kQStages) & 1) ^ 1, err, kDevErrWaitQEmpty, t, kq)) { ok = false; break; }
           uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
           uint8_t* sSZ = smem + kOffSZ + s * kSZStageBytes;
-          uint64_t* fb = &full_tma[s];
-          if (P.mode == kTokN) {
-            const int nb = (ti.n_valid + 63) / 64;
-            const bool ext = P.has_ext && kb == ti.nkb - 1;
-            // weight rows of the two 64-row halves (natural order) / of the 16-row GLU blocks
-            const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
-            const int k = kb * kBK;
-            const CUtensorMap* mA = ext ? &P.tmAe : &P.tmA;
-            const int wrow = ti.widx * (ext ? P.e_wrows : P.a_wrows);
-            uint32_t bytes = nb * 8192;
-            if (ext || P.a_kind == kABf16K || P.a_kind == kABf16MN) bytes += 16384;
-            else bytes += 4096 + 512;
-            mbar_arrive_expect_tx(fb, bytes);
-            if (ext || P.a_kind == kABf16K) {
-              const int x = ext ? 0 : k;
-              if (glu) {
-#pragma unroll
-                for (int qq = 0; qq < 4; ++qq) {
-                  tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fb);
-                  tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fb);
-                }
-              } else {
-                tma_load_2d(sA, mA, x, wrow + r0, fb);
-                tma_load_2d(sA + 8192, mA, x, wrow + r1, fb);
-              }
-            } else if (P.a_kind == kABf16MN) {
-              tma_load_2d(sA, mA, ti.m0, wrow + k, fb);
-              tma_load_2d(sA + 8192, mA, ti.m0 + 64, wrow + k, fb);
-            } else if (P.a_kind == kAInt4K) {
-              tma_load_2d(sQ, &P.tmQ, kb * 32, ti.widx * P.q_rows + r0, fb);
-              tma_load_2d(sQ + 2048, &P.tmQ, kb * 32, ti.widx * P.q_rows + r1, fb);
-              tma_load_2d(sSZ, &P.tmSZ, r0, ti.widx * P.q_groups + kb, fb);
-              tma_load_2d(sSZ + 256, &P.tmSZ, r1, ti.widx * P.q_groups + kb, fb);
-            } else {  // kAInt4MN
-              tma_load_2d(sQ, &P.tmQ, ti.m0 / 2, ti.widx * P.q_rows + k, fb);
-              tma_load_2d(sSZ, &P.tmSZ, k, ti.widx * P.q_groups + ti.m0 / 64, fb);
-              tma_load_2d(sSZ + 256, &P.tmSZ, k, ti.widx * P.q_groups + ti.m0 / 64 + 1, fb);
-            }
-            const CUtensorMap* mB = ext ? &P.tmBe : &P.tmB;
-            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, ext ? 0 : k, ti.n0 + 64 * i, fb);
-          } else {  // kTokK: A = tokens^T (MN-major), B = tokens^T (MN-major)
-            const int krow = ti.n0 + kb * kBK;
-            const int nb = (P.N + 63) / 64;
-            mbar_arrive_expect_tx(fb, 16384 + nb * 8192);
-            tma_load_2d(sA, &P.tmA, P.a_x0 + ti.m0, krow, fb);
-            tma_load_2d(sA + 8192, &P.tmA, P.a_x0 + ti.m0 + 64, krow, fb);
-            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, &P.tmB, P.b_x0 + 64 * i, krow, fb);
+          uint64_t* fb = &q_full[s];
+          mbar_arrive_expect_tx(fb, kQStageBytes + kSZStageBytes);
+          if (kmajor) {
+            tma_load_2d(sQ, mQ, kq * 128, qrow0 + r0, fb);
+            tma_load_2d(sQ + 8192, mQ, kq * 128, qrow0 + r1, fb);
+            tma_load_2d(sSZ, mSZ, r0, grow0 + kq * kQSub, fb);
+            tma_load_2d(sSZ + 1024, mSZ, r1, grow0 + kq * kQSub, fb);
+          } else {
+            tma_load_2d(sQ, mQ, ti.m0 / 2, qrow0 + kq * kQSub * kBK, fb);
+            tma_load_2d(sSZ, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64, fb);
+            tma_load_2d(sSZ + 1024, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64 + 1, fb);
           }
         }
       }
-      // every issued copy must land before the CTA may exit
-      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-        if (!mbar_wait(&full_tma[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+      for (uint32_t j = (qi > (uint32_t)kQStages ? qi - kQStages : 0u); j < qi; ++j)
+        if (!mbar_wait(&q_full[j % kQStages], (j / kQStages) & 1, err, kDevErrTmaDrain)) break;
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ============================================================================ MMA issuer (one thread)
     if (lane == 0) {
       uint32_t it = 0, acc_it = 0;
@@ -353,31 +427,38 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         const TileInfo ti = decode_tile(args, T, t);
         if (ti.nkb == 0) continue;
         const Problem& P = args.p[ti.p];
+        // per-tile constants in registers (the loop below must not touch parameter memory)
+        const bool tokk = P.mode == kTokK;
+        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+        const uint32_t a_mn = (tokk || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
+        const uint32_t b_mn = tokk ? 1u : 0u;
+        const int nkb = ti.nkb;
         const int acc = acc_it & 1;
-        if (!mbar_wait(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty)) break;
+        if (!mbar_wait(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty, t)) break;
         tc_fence_after();
-        const uint32_t n_mma = (uint32_t)((ti.n_valid + 15) & ~15);
-        const uint32_t a_mn = (P.mode == kTokK || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
-        const uint32_t b_mn = (P.mode == kTokK) ? 1u : 0u;
+        // MN-major B (kTokK) must span whole 64-element swizzle atoms; K-major B needs multiples of 16
+        const uint32_t n_mma = tokk ? (uint32_t)((ti.n_valid + 63) & ~63) : (uint32_t)((ti.n_valid + 15) & ~15);
         const uint32_t idesc_main = make_idesc_bf16(n_mma, a_mn, b_mn);
         const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
         const uint32_t d_tmem = tmem_base + acc * kMaxBN;
-        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&full_tma[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
-          if (!mbar_wait(&full_deq[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
+          if (!mbar_wait(&b_full[s], ph, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
+          if (!mbar_wait(&a_full[s], ph, err, kDevErrWaitAFull, t, kb)) { ok = false; break; }
           tc_fence_after();
-          const bool ext = P.mode == kTokN && P.has_ext && kb == ti.nkb - 1;
-          const bool amn = a_mn && !ext;
+          const bool ext = kb == ext_kb;
           const uint32_t sA = smem_base + kOffA + s * kAStageBytes;
           const uint32_t sB = smem_base + kOffB + s * kBStageBytes;
+          const uint32_t idesc = ext ? idesc_ext : idesc_main;
+          // A: K-major steps 32 B per K=16 inside the swizzle atom, MN-major steps two 8-row k-groups (2048 B)
+          const bool amn = a_mn && !ext;
+          const uint64_t a0 = amn ? make_sdesc(sA, 8192, 1024) : make_sdesc(sA, 16, 1024);
+          const uint64_t b0 = b_mn ? make_sdesc(sB, 8192, 1024) : make_sdesc(sB, 16, 1024);
+          const uint32_t astep = amn ? (2048 >> 4) : (32 >> 4), bstep = b_mn ? (2048 >> 4) : (32 >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = amn ? make_sdesc(sA + kk * 2048, 8192, 1024) : make_sdesc(sA + kk * 32, 16, 1024);
-            const uint64_t bd = b_mn ? make_sdesc(sB + kk * 2048, 8192, 1024) : make_sdesc(sB + kk * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, ext ? idesc_ext : idesc_main, (kb | kk) != 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(d_tmem, a0 + (uint64_t)(kk * astep), b0 + (uint64_t)(kk * bstep), idesc, (kb | kk) != 0 ? 1u : 0u);
           issued = true;
           umma_commit(&empty[s]);
         }
@@ -390,39 +471,54 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         mbar_wait(mma_drain, 0, err, kDevErrTmaDrain);
       }
     }
-  } else if (warp < 2 + kNumDeqWarps) {
-    // ============================================================================ int4 dequant warps
-    const int pt = threadIdx.x - 64;  // 0..127
-    uint32_t it = 0;
+  } else if (warp < kWarpEpi0) {
+    // ============================================================================ int4 dequant (two groups)
+    const int grp = (warp - kWarpDeq0) / kNumDeqWarps;
+    const int pt = ((warp - kWarpDeq0) % kNumDeqWarps) * 32 + lane;  // 0..127 within the group
+    uint32_t it = 0, qi = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const TileInfo ti = decode_tile(args, T, t);
       const Problem& P = args.p[ti.p];
-      const bool int4 = P.mode == kTokN && (P.a_kind == kAInt4K || P.a_kind == kAInt4MN);
+      const bool int4 = is_int4(P);
       const bool glu = P.epi == kEpiGlu;
+      const bool kmajor = P.a_kind == kAInt4K;
+      const int nkq = int4 ? P.K / kBK : 0;  // int4 k-blocks of the tile
       for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
         const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait(&full_tma[s], ph, err, kDevErrWaitFull)) { ok = false; break; }
-        const bool ext = P.has_ext && kb == ti.nkb - 1;
-        if (int4 && !ext) {
-          uint8_t* sA = smem + kOffA + s * kAStageBytes;
-          const uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
-          const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + s * kSZStageBytes);
-          if (P.a_kind == kAInt4K) {
-            const int r = pt;
-            const int sr = glu ? glu_stage_row(r) : r;
-            dq64_to_row(sQ + sr * 32, sSZ[sr], sA + (r >> 3) * 1024 + (r & 7) * 128, r & 7);
-          } else {
-            const int kr = pt >> 1, half = pt & 1;
-            dq64_to_row(sQ + kr * 64 + half * 32, sSZ[half * 64 + kr],
-                        sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128, kr & 7);
-          }
-          fence_proxy_async_smem();
+        // every k-block's slot round is waited for, whichever role fills it (see the note on ring waits)
+        if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
+        if (kb >= nkq) continue;  // not an int4 k-block
+        const int j = kb % kQSub;
+        const uint32_t qstage = qi + kb / kQSub;
+        const int qs = qstage % kQStages;
+        // both groups wait on every staging stage (at its first k-block), so no round is skipped
+        if (j == 0 || (int)(it % kNumDeqGroups) == grp)
+          if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
+        if ((int)(it % kNumDeqGroups) != grp) continue;  // the other group takes this k-block
+        uint8_t* sA = smem + kOffA + s * kAStageBytes;
+        const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes;
+        const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes);
+        if (kmajor) {
+          const int r = pt;
+          const int sr = glu ? glu_stage_row(r) : r;
+          dq64_to_row(sQ + sr * 128 + j * 32, sSZ[(sr >> 6) * 256 + j * 64 + (sr & 63)],
+                      sA + (r >> 3) * 1024 + (r & 7) * 128, r & 7);
+        } else {
+          const int kr = pt >> 1, half = pt & 1;
+          dq64_to_row(sQ + (j * 64 + kr) * 64 + half * 32, sSZ[half * 256 + j * 64 + kr],
+                      sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128, kr & 7);
         }
+        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_deq[s]);
+        if (lane == 0) {
+          mbar_arrive(&a_full[s]);
+          // a staging stage counts kQSub arrivals per warp; a short last stage adds the missing ones at its end
+          const int subs = min(kQSub, nkq - (kb / kQSub) * kQSub);
+          mbar_arrive_n(&q_empty[qs], (j == subs - 1) ? 1 + (kQSub - subs) : 1);
+        }
       }
+      qi += (nkq + kQSub - 1) / kQSub;
     }
   } else {
     // ============================================================================ epilogue warps
@@ -444,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         continue;
       }
       const int acc = acc_it & 1;
-      if (!mbar_wait(&acc_full[acc], (acc_it >> 1) & 1, err, kDevErrWaitAccFull)) break;
+      if (!mbar_wait(&acc_full[acc], (acc_it >> 1) & 1, err, kDevErrWaitAccFull, t)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kMaxBN;
       const int nchunks = (ti.n_valid + 31) / 32;
@@ -540,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);

@@ -30,21 +30,38 @@ namespace smelb {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kMaxBN = 256;
-constexpr int kStages = 4;
+#ifndef SMELB_MAX_BN
+#define SMELB_MAX_BN 192
+#endif
+#ifndef SMELB_STAGES
+#define SMELB_STAGES 4
+#endif
+#ifndef SMELB_QSTAGES
+#define SMELB_QSTAGES 2
+#endif
+constexpr int kMaxBN = SMELB_MAX_BN;     // token tile (MMA N) upper bound
+constexpr int kStages = SMELB_STAGES;    // operand ring: a weight tile (16 KB) and a token tile (kMaxBN x 128 B)
+constexpr int kQStages = SMELB_QSTAGES;  // packed-int4 staging ring, 4 k-blocks per stage
+constexpr int kQSub = 4;                 // k-blocks per int4 staging stage (128-byte rows for K-major weights)
 constexpr int kMaxProblems = 12;
 constexpr int kMaxGroups = 320;  // groups over all problems of one launch
 
 constexpr int kAStageBytes = kBM * kBK * 2;      // 16 KB bf16 A tile
-constexpr int kBStageBytes = kMaxBN * kBK * 2;   // 32 KB bf16 B tile
-constexpr int kQStageBytes = 4096;               // packed int4 staging (128 rows x 32 B or 64 rows x 64 B)
-constexpr int kSZStageBytes = 512;               // (scale, zero) staging: 128 x uint32
-constexpr int kStageBytes = kAStageBytes + kBStageBytes + kQStageBytes + kSZStageBytes;
-constexpr int kXchgBytes = 64 * 32 * 4;          // GLU epilogue exchange buffer (64 rows x 32 columns fp32)
+constexpr int kBStageBytes = kMaxBN * kBK * 2;   // bf16 B tile
+constexpr int kQStageBytes = 16384;              // nibbles: 128 rows x 128 B (K-major) or 256 k-rows x 64 B (MN-major)
+constexpr int kSZStageBytes = 2048;              // (scale, zero) pairs: 2 halves x 256 uint32
 
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-5 dequant, warps 6-9 epilogue
-constexpr int kNumDeqWarps = 4;
+// warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3-10 dequant (two groups of four warps taking
+// alternate k-blocks), 11-14 epilogue (one per TMEM lane quarter), 15 TMA (int4 staging ring).
+// Every thread that waits on a ring's "empty" barrier waits on every round of every slot in order (also for k-blocks
+// another role fills): a parity wait issued two rounds ahead of the barrier would pass without waiting.
+constexpr int kNumDeqGroups = 2;
+constexpr int kNumDeqWarps = 4;  // per group
 constexpr int kNumEpiWarps = 4;
+constexpr int kWarpTmaB = 0, kWarpMma = 1, kWarpTmaA = 2, kWarpDeq0 = 3;
+constexpr int kWarpEpi0 = kWarpDeq0 + kNumDeqGroups * kNumDeqWarps;
+constexpr int kWarpTmaQ = kWarpEpi0 + kNumEpiWarps;
+constexpr int kThreads = (kWarpTmaQ + 1) * 32;
 
 enum Mode : int { kTokN = 0, kTokK = 1 };
 enum AKind : int { kAInt4K = 0, kAInt4MN = 1, kABf16K = 2, kABf16MN = 3 };
@@ -53,16 +70,18 @@ enum Act : int { kActSilu = 0, kActGeluTanh = 1 };
 
 struct alignas(64) Problem {
   CUtensorMap tmA;   // bf16 A (weights [rows][k] / [k][m], or tokens [rows][m] in kTokK); unused for int4
-  CUtensorMap tmB;   // tokens: kTokN [rows][k] K-major; kTokK [rows][n] (MN-major B)
+  CUtensorMap tmB;   // tokens: kTokN [rows][k] K-major (64-row box); kTokK [rows][n] (MN-major B)
+  CUtensorMap tmB32; // kTokN tokens with a 32-row box (token tiles of at most 32 rows)
   CUtensorMap tmAe;  // LoRA extension, weight side [nW * e_wrows][64]
   CUtensorMap tmBe;  // LoRA extension, token side [rows][64]
-  CUtensorMap tmQ;   // int4 nibbles (uint8): K-major [nW*rows][K/2]; MN-major [nW*K][M/2]
-  CUtensorMap tmSZ;  // (scale | zero << 16) uint32, transposed: [nW*G][rows]
+  CUtensorMap tmQ;   // int4 nibbles (uint8): K-major [nW*rows][K/2], box 128 B x 64 rows;
+                     //                      MN-major [nW*K][M/2], box 64 B x 256 rows
+  CUtensorMap tmSZ;  // (scale | zero << 16) uint32, transposed [nW*G][rows]: K-major box 64 x 4, MN-major 256 x 1
 
   int mode, a_kind, epi, act;
   int M;        // output features (valid rows of A)
   int K;        // kTokN reduction length (multiple of 64)
-  int N;        // kTokK output columns (multiple of 16, <= 256)
+  int N;        // kTokK output columns stored (<= 256); the MMA runs on N rounded up to 64
   int BN;       // kTokN token tile (multiple of 64, <= 256)
   int a_wrows;  // bf16 A, kTokN: tensor-map rows per weight index (K-major: rows of W; MN-major: K)
   int a_x0;     // kTokK: column offset into tmA

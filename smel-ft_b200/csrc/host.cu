@@ -32,8 +32,8 @@ int* device_status(int dev) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_status[dev]) {
     int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMalloc(&p, kStatusWords * sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, kStatusWords * sizeof(int)) != cudaSuccess) return nullptr;
     g_status[dev] = p;
   }
   return g_status[dev];

@@ -27,12 +27,14 @@ int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int b
   return make_tmap_2d(m, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols * 2, 64, box_rows, true);
 }
 int tm_q(CUtensorMap* m, const void* q, long long rows, long long cols, bool mn_major) {
-  // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes
-  return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : 32, 64,
-                      false);
+  // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes. K-major tiles stage 4 k-blocks per row
+  // (128 B); MN-major tiles stage 4 k-blocks of 64 k-rows x 64 B.
+  return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : 128,
+                      mn_major ? 256 : 64, false);
 }
-int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows) {
-  return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4, 64, 1, false);
+int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows, bool mn_major) {
+  return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4, mn_major ? 256 : 64,
+                      mn_major ? 1 : 4, false);
 }
 
 #define TRY(x)               \
@@ -74,7 +76,7 @@ struct Int4Mat {
 int set_a_int4(Problem& P, const Int4Mat& W, bool mn_major) {
   P.a_kind = mn_major ? kAInt4MN : kAInt4K;
   TRY(tm_q(&P.tmQ, W.q, (long long)W.nw * W.rows, W.cols, mn_major));
-  TRY(tm_sz(&P.tmSZ, W.sz, (long long)W.nw * (W.cols / 64), W.rows));
+  TRY(tm_sz(&P.tmSZ, W.sz, (long long)W.nw * (W.cols / 64), W.rows, mn_major));
   P.q_rows = W.rows;
   P.q_groups = W.cols / 64;
   P.M = mn_major ? W.cols : W.rows;
@@ -101,9 +103,10 @@ int set_ext(Problem& P, const void* Wext, int nw, int e_rows, const void* Xext, 
   return kOk;
 }
 
-int set_b_tokens(Problem& P, const void* X, long long rows, int cols, int BN = 256) {
+int set_b_tokens(Problem& P, const void* X, long long rows, int cols, int BN = kMaxBN) {
   P.mode = kTokN;
-  P.BN = BN;
+  P.BN = BN < kMaxBN ? BN : kMaxBN;
+  TRY(tm_bf16(&P.tmB32, X, rows, cols, 32));
   return tm_bf16(&P.tmB, X, rows, cols, 64);
 }
 
@@ -125,7 +128,7 @@ int set_tokk(Problem& P, const void* Atok, long long rows, int a_cols, int a_x0,
   P.a_x0 = a_x0;
   P.b_x0 = b_x0;
   P.M = M;
-  P.N = (N + 15) & ~15;
+  P.N = N;  // columns stored; the MMA width is rounded up inside the kernel
   P.C = C;
   P.c_sm = c_sm;
   P.c_sn = c_sn;
@@ -228,6 +231,7 @@ int check_layer(const smelb_moe_layer& L, Flags& f) {
                                 (long long)L.S);
   if (f.sel_lora) SMELB_CHECK_ARG(2 * L.r_sel <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sel);
   if (f.sh_lora) SMELB_CHECK_ARG(2 * L.r_sh <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sh);
+  if (f.sel_lora) SMELB_CHECK_ARG(L.r_sel >= 1, kErrShape, "layer: LoRA rank %lld", (long long)L.r_sel);
   return kOk;
 }
 
@@ -623,16 +627,32 @@ int smelb_last_error(char* buf, size_t len) {
   return (int)n;
 }
 
+int smelb_set_device(int device) {
+  static thread_local int current = -1;
+  if (current != device) {
+    SMELB_CUDA(cudaSetDevice(device));
+    current = device;
+  }
+  return kOk;
+}
+
 int smelb_read_status(int device, int* status, int reset) {
-  SMELB_CHECK_ARG(status != nullptr, kErrArg, "read_status: null output");
+  int detail[kStatusWords];
+  const int rc = smelb_read_status_detail(device, detail, reset);
+  if (rc == kOk && status) *status = detail[0];
+  return rc;
+}
+
+int smelb_read_status_detail(int device, int* words, int reset) {
+  SMELB_CHECK_ARG(words != nullptr, kErrArg, "read_status: null output");
   int prev = 0;
   SMELB_CUDA(cudaGetDevice(&prev));
   SMELB_CUDA(cudaSetDevice(device));
   int* w = device_status(device);
   SMELB_CHECK_ARG(w != nullptr, kErrCuda, "read_status: no status word");
   SMELB_CUDA(cudaDeviceSynchronize());
-  SMELB_CUDA(cudaMemcpy(status, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (reset) SMELB_CUDA(cudaMemset(w, 0, sizeof(int)));
+  SMELB_CUDA(cudaMemcpy(words, w, kStatusWords * sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) SMELB_CUDA(cudaMemset(w, 0, kStatusWords * sizeof(int)));
   SMELB_CUDA(cudaSetDevice(prev));
   return kOk;
 }

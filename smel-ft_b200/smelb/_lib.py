@@ -68,6 +68,8 @@ SIGNATURES = {
     "smelb_version": (c_i32, []),
     "smelb_last_error": (c_i32, [ctypes.c_char_p, ctypes.c_size_t]),
     "smelb_read_status": (c_i32, [c_i32, ctypes.POINTER(c_i32), c_i32]),
+    "smelb_set_device": (c_i32, [c_i32]),
+    "smelb_read_status_detail": (c_i32, [c_i32, ctypes.POINTER(c_i32), c_i32]),
     "smelb_int4_dequant": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),
     "smelb_int4_pack_sz": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "smelb_router_topk": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp]),
@@ -111,8 +113,12 @@ def last_error() -> str:
 
 
 def call(name, *args):
-    """Call an entry point and raise SmelbError with the library's message on a non-zero status."""
-    rc = getattr(load(), name)(*args)
+    """Call an entry point on torch's current device and raise SmelbError with the library's message on a non-zero
+    status."""
+    lib = load()
+    if torch.cuda.is_available():
+        lib.smelb_set_device(torch.cuda.current_device())
+    rc = getattr(lib, name)(*args)
     if rc != 0:
         raise SmelbError(f"{name}: {ERRORS.get(rc, rc)}: {last_error()}")
 
@@ -139,6 +145,14 @@ def gemm_timing_read():
     ms, n = ctypes.c_double(0), ctypes.c_longlong(0)
     call("smelb_gemm_timing_read", ctypes.byref(ms), ctypes.byref(n))
     return ms.value, n.value
+
+
+def read_status_detail(device=None, reset=True):
+    """(code, block, tile, k-block) of the first device-side failure (code 0 = none). Synchronizes."""
+    dev = torch.cuda.current_device() if device is None else device
+    w = (c_i32 * 4)()
+    call("smelb_read_status_detail", dev, w, 1 if reset else 0)
+    return tuple(w)
 
 
 def ptr(t):

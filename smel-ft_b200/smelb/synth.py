@@ -46,9 +46,9 @@ def _share_of_top(logits, ranked, n_top, k):
 
 
 def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=32.0, zipf_s=1.1, share=0.5,
-               seed=0, device="cuda", mu=4.0, uniform=False, with_lora=True):
+               seed=0, device="cuda", mu=4.0, uniform=False, with_lora=True, keep_bf16=False):
     """Build one synthetic layer. Returns a dict with x [T, H] bf16, W (router / shared tensors, bf16), ex
-    (LayerExperts), lora (LayerLoRA or None), bank_bf16 (gate_up, down bf16 before quantization), meta."""
+    (LayerExperts), lora (LayerLoRA or None), meta, and with keep_bf16 the bank before quantization (bank_bf16)."""
     dev = torch.device(device)
     g = torch.Generator(device=dev).manual_seed(seed)
 
@@ -110,8 +110,10 @@ def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=3
     lens, cu = packed_lengths(T, seed=seed)
     meta["n_seqs"] = len(lens)
     meta["selected"] = sel
-    return {"x": x.bfloat16().contiguous(), "W": W, "ex": ex, "lora": lora, "bank_bf16": (gu, dn), "meta": meta,
-            "cu_seqlens": cu}
+    out = {"x": x.bfloat16().contiguous(), "W": W, "ex": ex, "lora": lora, "meta": meta, "cu_seqlens": cu}
+    if keep_bf16:
+        out["bank_bf16"] = (gu, dn)
+    return out
 
 
 def flops_per_token(H, E, K, I, S, n_lora_rows_frac=0.0, r=16):
