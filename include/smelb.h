@@ -113,6 +113,20 @@ int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64
                              const void* dn_q, const uint32_t* dn_sz, int act, const void* h, void* h_buf,
                              void* dh_buf, void* dx, void* stream);
 
+/* No counterpart in the reference. smelb_frozen_experts_fwd without caller scratch and without any allocation:
+ * the activated intermediate (bf16 [rows, I]) lives in a file-scope device array of
+ * SMELB_NOALLOC_SCRATCH_BYTES (plus a 256-byte head of wait-timeout status words), so rows * I * 2 may not exceed
+ * SMELB_NOALLOC_SCRATCH_BYTES; larger calls return SMELB_ERR_SHAPE with the limit in smelb_last_error. The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. Every call on a device shares the array, so calls whose kernels overlap on the
+ * GPU (different streams without ordering) race. Each call clears the status head first; a bounded wait that gives
+ * up inside this call is recorded there, not in smelb_read_status. Same arguments as smelb_frozen_experts_fwd
+ * minus a_buf. */
+#define SMELB_NOALLOC_SCRATCH_BYTES 33554432LL
+int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts,
+                                     int64_t E, const void* gu_q, const uint32_t* gu_sz, const void* dn_q,
+                                     const uint32_t* dn_sz, int act, void* h_save, void* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------- the layer
  * smel/moe.py:255-263 moe_forward (route -> routed_experts -> + shared_mlp) and its autograd backward, as two calls.
  * The flags select sub-paths so the same calls also serve route (moe.py:162-167), routed_experts (moe.py:214-252)

@@ -669,4 +669,26 @@ int launch_gemm(LaunchArgs& args, cudaStream_t stream) {
   return kOk;
 }
 
+int launch_gemm_status(LaunchArgs& args, cudaStream_t stream, int* err) {
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  static bool configured[64] = {false};
+  if (dev < 64 && !configured[dev]) {
+    SMELB_CUDA(cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc));
+    configured[dev] = true;
+  }
+  SMELB_CHECK_ARG(args.nprob >= 1 && args.nprob <= kMaxProblems, kErrArg, "gemm: %d problems in one launch",
+                  args.nprob);
+  int total_groups = 0;
+  for (int p = 0; p < args.nprob; ++p) total_groups += args.p[p].ngroups;
+  SMELB_CHECK_ARG(total_groups <= kMaxGroups, kErrShape, "gemm: %d groups in one launch (max %d)", total_groups,
+                  kMaxGroups);
+  SMELB_CHECK_ARG(err != nullptr, kErrArg, "gemm: no status words");
+  args.err = err;
+  moe_gemm_kernel<<<num_sms(dev), kThreads, kSmemAlloc, stream>>>(args);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
 }  // namespace smelb

@@ -43,5 +43,8 @@ int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const voi
 int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st);
 
 int launch_gemm(struct LaunchArgs& args, cudaStream_t stream);
+// Same launch with the wait-timeout status words supplied by the caller (4 ints, device memory) instead of the
+// per-device word launch_gemm allocates on first use; records no timing events.
+int launch_gemm_status(struct LaunchArgs& args, cudaStream_t stream, int* err);
 
 }  // namespace smelb

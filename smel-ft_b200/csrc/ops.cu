@@ -1,6 +1,7 @@
 // C ABI of smelb (include/smelb.h): argument checks, GEMM problem construction and the sequencing of the MoE layer's
 // forward and backward launches.
 #include <cstring>
+#include <mutex>
 
 #include "../../include/smelb.h"
 #include "common.cuh"
@@ -830,3 +831,82 @@ int smelb_moe_layer_bwd(const smelb_moe_layer* L) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------- no-allocation variant
+// smelb_frozen_experts_fwd with its intermediate (the activated gate*up rows, bf16 [rows, I]) and its wait-timeout
+// status words in one file-scope device array instead of caller scratch and the lazily allocated per-device status
+// word. Layout of the array: bytes [0, 256) status words (4 ints used, cleared by every call), bytes
+// [256, 256 + SMELB_NOALLOC_SCRATCH_BYTES) the intermediate. All calls on a device share the array.
+static constexpr size_t kNoAllocHead = 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocHead + SMELB_NOALLOC_SCRATCH_BYTES];
+namespace {
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_scratch on `dev` (the current device), resolved once per device.
+int noalloc_scratch(int dev, unsigned char** out) {
+  SMELB_CHECK_ARG(dev >= 0 && dev < 64, kErrArg, "frozen_experts_fwd_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    SMELB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = (unsigned char*)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return kOk;
+}
+}  // namespace
+
+extern "C" int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, int64_t H, int64_t I,
+                                                const int32_t* counts, int64_t E, const void* gu_q,
+                                                const uint32_t* gu_sz, const void* dn_q, const uint32_t* dn_sz,
+                                                int act, void* h_save, void* out, void* stream) {
+  SMELB_CHECK_ARG(xs && counts && gu_q && gu_sz && dn_q && dn_sz && out, kErrArg,
+                  "frozen_experts_fwd_noalloc: null pointer");
+  SMELB_CHECK_ARG(H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups && rows >= 0, kErrShape,
+                  "frozen_experts_fwd_noalloc: rows=%lld H=%lld I=%lld E=%lld", (long long)rows, (long long)H,
+                  (long long)I, (long long)E);
+  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "unknown activation %d", act);
+  SMELB_CHECK_ARG(rows <= (int64_t)(SMELB_NOALLOC_SCRATCH_BYTES / 2) / (I > 0 ? I : 1), kErrShape,
+                  "frozen_experts_fwd_noalloc: rows*I*2 = %lld bytes exceeds the %lld-byte scratch (max rows %lld "
+                  "at I=%lld)",
+                  (long long)rows * (long long)I * 2, (long long)SMELB_NOALLOC_SCRATCH_BYTES,
+                  (long long)(SMELB_NOALLOC_SCRATCH_BYTES / 2 / I), (long long)I);
+  if (rows == 0) return kOk;
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  unsigned char* scratch = nullptr;
+  TRY(noalloc_scratch(dev, &scratch));
+  cudaStream_t st = (cudaStream_t)stream;
+  int* err = (int*)scratch;
+  void* a_buf = scratch + kNoAllocHead;
+  SMELB_CUDA(cudaMemsetAsync(err, 0, kNoAllocHead, st));
+  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
+  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, gu, false));
+    TRY(set_b_tokens(P, xs, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiGlu;
+    P.C = a_buf;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)h_save;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(launch_gemm_status(b.args, st, err));
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_int4(P, dn, false));
+    TRY(set_b_tokens(P, a_buf, rows, (int)I));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    out_bf16(P, out, H);
+    TRY(launch_gemm_status(b.args, st, err));
+  }
+  return kOk;
+}

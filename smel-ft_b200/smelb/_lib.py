@@ -82,6 +82,8 @@ SIGNATURES = {
                                          c_vp, c_vp, c_vp, c_vp]),
     "smelb_frozen_experts_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp,
                                          c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "smelb_frozen_experts_fwd_noalloc": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp,
+                                                 c_i32, c_vp, c_vp, c_vp]),
     "smelb_moe_layer_size": (ctypes.c_size_t, []),
     "smelb_launch_count": (ctypes.c_longlong, []),
     "smelb_gemm_timing": (c_i32, [c_i32]),
