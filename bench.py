@@ -44,17 +44,24 @@ class Clocks:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
-        self.index, self.proc, self.path = index, None, None
+        self.index, self.proc, self.path, self.skip = index, None, None, 0
 
-    def start(self):
+    def start(self, settle_s=10.0):
+        """Start sampling and return once the first sample is written, so that nvidia-smi's start-up (NVML
+        initialisation) is over before the timed region begins."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "100", "-i", str(self.index)], stdout=open(self.path, "w"),
+                                          "-lms", "50", "-i", str(self.index)], stdout=open(self.path, "w"),
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < settle_s and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
+        self.skip = sum(1 for _ in open(self.path))  # samples taken before the timed region
 
     def stop(self):
         if self.proc is None:
@@ -63,7 +70,9 @@ class Clocks:
         self.proc.wait(timeout=10)
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in open(self.path):
+        for i, line in enumerate(open(self.path)):
+            if i < self.skip:
+                continue
             f = [c.strip() for c in line.split(",")]
             if len(f) < 9:
                 continue
@@ -164,28 +173,60 @@ def run_ours(args, world, rank, local):
         out.backward(gd)
         return xr.grad
 
+    # everything runs on one side stream: a CUDA graph is captured on it, and autograd's gradient accumulation
+    # nodes must live on the stream they are replayed on
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    torch.cuda.set_stream(side)
     for _ in range(args.warmup):
         step(x, gy)
     torch.cuda.synchronize()
     assert smelb.read_status() == 0, "device status word set during warm-up"
 
-    # ---------------- device-resident timing
+    # ---------------- device-resident timing: the whole step (no-grad forward, recompute, backward) is captured once
+    # in a CUDA graph and replayed, so the number is the device's and not the Python host's
+    graph, timing = None, "cuda-graph replay of the whole step"
+    n0 = _lib.launch_count()
+    try:
+        torch.cuda.synchronize()
+        n0 = _lib.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step(x, gy)
+        torch.cuda.synchronize()
+    except Exception as exc:  # not capturable here: time the eager step instead and say so
+        graph, timing = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
+        torch.cuda.synchronize()
+        n0 = _lib.launch_count()
+    per_step_launches = _lib.launch_count() - n0 if graph is not None else None
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step(x, gy)
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
     clocks = Clocks(local)
+    clocks.start()
     barrier(world)
     torch.cuda.synchronize()
-    n0 = _lib.launch_count()
-    clocks.start()
+    n1 = _lib.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     e0.record()
     for _ in range(args.steps):
-        step(x, gy)
+        run_step()
     e1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    ck = clocks.stop()
-    launches = _lib.launch_count() - n0
     barrier(world)
+    ck = clocks.stop()
+    # kernels of this library launched in the timed region (a graph replay launches the captured ones again)
+    launches = per_step_launches * args.steps if graph is not None else _lib.launch_count() - n1
+    assert smelb.read_status() == 0, "device status word set during the timed region"
     # the expert-GEMM launches of the same steps, timed with CUDA events on their stream (separate pass)
     _lib.gemm_timing(True)
     _lib.gemm_timing_read()
@@ -240,7 +281,7 @@ def run_ours(args, world, rank, local):
     res = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random-init weights of the layer shape)",
-           "config": config_json(cfg, layer["meta"], world), "roofline": roof, "e2e": e2e,
+           "config": dict(config_json(cfg, layer["meta"], world), timing=timing), "roofline": roof, "e2e": e2e,
            "gpu_launches": int(launches), "clocks": ck}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(layer, min(cfg["T"], args.cpu_tokens))
@@ -293,7 +334,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=4092)

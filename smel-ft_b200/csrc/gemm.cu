@@ -14,7 +14,7 @@ constexpr int kOffSZ = kOffQ + kQStages * kQStageBytes;
 constexpr int kOffTab = kOffSZ + kQStages * kSZStageBytes;
 constexpr int kTabInts = 3 * kMaxGroups + (kMaxGroups + kMaxProblems) + (kMaxProblems + 1) + kMaxProblems;
 constexpr int kOffBar = (kOffTab + kTabInts * 4 + 7) & ~7;
-constexpr int kNumBars = 3 * kStages + 2 * kQStages + 5;
+constexpr int kNumBars = 2 * kStages + 2 * kQStages + 5;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmem + 16;
 constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment of the dynamic buffer
@@ -119,44 +119,77 @@ __device__ __forceinline__ uint4 dq8_exact(uint32_t w, float s, float z) {
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// 32 packed bytes (64 values sharing one (scale, zero) pair) -> 8 chunks of 8 bf16 written to one 128-byte row of
-// a 128B-swizzled UMMA tile (chunk c lands at chunk position c ^ swz).
-__device__ __forceinline__ void dq64_to_row(const uint8_t* src, uint32_t sz, uint8_t* dst_row, int swz) {
-  const uint4 v0 = *reinterpret_cast<const uint4*>(src);
-  const uint4 v1 = *reinterpret_cast<const uint4*>(src + 16);
+// 32 packed bytes (64 values sharing one (scale, zero) pair) -> 32 words of two bf16 in k order. The bytes are two
+// 16-byte chunks of a staged row: chunk `c0` and `c0 + 1`, each stored at chunk position c ^ swz.
+__device__ __forceinline__ void dq64_fast(const uint8_t* src, int c0, int swz, uint32_t sz, uint32_t (&o)[32]) {
+  const uint4 v0 = *reinterpret_cast<const uint4*>(src + ((c0 ^ swz) << 4));
+  const uint4 v1 = *reinterpret_cast<const uint4*>(src + (((c0 + 1) ^ swz) << 4));
   const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  const __nv_bfloat162 s2 = bits_bf162((sz & 0xFFFFu) | (sz << 16));
+  const __nv_bfloat162 z2 = bits_bf162((sz >> 16) | (sz & 0xFFFF0000u));
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 r = dq8_fast(w[c], s2, z2);
+    o[4 * c] = r.x;
+    o[4 * c + 1] = r.y;
+    o[4 * c + 2] = r.z;
+    o[4 * c + 3] = r.w;
+  }
+}
+
+// The same 64 values through fp32 (groups whose values are not all exact in fp32), out of line: it is rare, and the
+// kernel's instruction footprint matters more than its speed.
+static __device__ __noinline__ void dq64_exact(const uint8_t* src, int c0, int swz, uint32_t sz, uint32_t* o) {
+  const float s = __uint_as_float((sz & 0xFFFFu) << 16);
+  const float z = __uint_as_float(sz & 0xFFFF0000u);
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(src + (((c0 + (c >> 2)) ^ swz) << 4) + (c & 3) * 4);
+    const uint4 r = dq8_exact(w, s, z);
+    o[4 * c] = r.x;
+    o[4 * c + 1] = r.y;
+    o[4 * c + 2] = r.z;
+    o[4 * c + 3] = r.w;
+  }
+}
+
+__device__ __forceinline__ void dq64(const uint8_t* src, int c0, int swz, uint32_t sz, uint32_t (&o)[32]) {
   if (dq_fast_ok(sz)) {
-    const __nv_bfloat162 s2 = bits_bf162((sz & 0xFFFFu) | (sz << 16));
-    const __nv_bfloat162 z2 = bits_bf162((sz >> 16) | (sz & 0xFFFF0000u));
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst_row + ((c ^ swz) << 4)) = dq8_fast(w[c], s2, z2);
+    dq64_fast(src, c0, swz, sz, o);
   } else {
-    const float s = __uint_as_float((sz & 0xFFFFu) << 16);
-    const float z = __uint_as_float(sz & 0xFFFF0000u);
+    uint32_t oc[32];
+    dq64_exact(src, c0, swz, sz, oc);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(dst_row + ((c ^ swz) << 4)) = dq8_exact(w[c], s, z);
+    for (int i = 0; i < 32; ++i) o[i] = oc[i];
   }
 }
 
 // ------------------------------------------------------------------------------------------ epilogue math
+// Activations in fp32 on the bf16-rounded pre-activation, as the reference's bf16 `act` (smel/moe.py:91-107), using
+// the hardware exp2 / reciprocal / tanh approximations: their relative error (~1e-6, and 2^-11 for tanh) is far below
+// the bf16 rounding that follows. Short and inline so the unrolled epilogue columns overlap.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float act_fwd(float x, int act) {
-  if (act == kActSilu) return x / (1.0f + expf(-x));
+  if (act == kActSilu) return __fdividef(x, 1.0f + __expf(-x));
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  return 0.5f * x * (1.0f + tanh_approx(k0 * (x + k1 * x * x * x)));
 }
 
 // (act(g), d act / d g) in fp32
-__device__ __forceinline__ void act_and_grad(float g, int act, float& a, float& d) {
+__device__ __forceinline__ float2 act_and_grad(float g, int act) {
   if (act == kActSilu) {
-    const float sg = 1.0f / (1.0f + expf(-g));
-    a = g * sg;
-    d = sg * (1.0f + g * (1.0f - sg));
-  } else {
-    const float c = 0.7978845608028654f;
-    const float t = tanhf(c * (g + 0.044715f * g * g * g));
-    a = 0.5f * g * (1.0f + t);
-    d = 0.5f * (1.0f + t) + 0.5f * g * (1.0f - t * t) * c * (1.0f + 3.0f * 0.044715f * g * g);
+    const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+    return make_float2(g * sg, sg * (1.0f + g * (1.0f - sg)));
   }
+  const float c = 0.7978845608028654f;
+  const float t = tanh_approx(c * (g + 0.044715f * g * g * g));
+  return make_float2(0.5f * g * (1.0f + t),
+                     0.5f * (1.0f + t) + 0.5f * g * (1.0f - t * t) * c * (1.0f + 3.0f * 0.044715f * g * g));
 }
 
 // GLU tiles interleave gate and up in 16-row blocks: A row 32*q + j holds gate feature f0 + 16*q + j for j < 16
@@ -188,9 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   T.tstart = T.gpre + kMaxGroups + kMaxProblems;
   T.gbase = T.tstart + kMaxProblems + 1;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* a_full = bars;                  // weight tile ready (TMA bytes + 4 arrivals, or 4 dequant warps)
-  uint64_t* b_full = a_full + kStages;      // token tile landed
-  uint64_t* empty = b_full + kStages;       // MMAs reading the stage (weight and token tile) are done
+  // full: the stage's token tile landed (1 arrival + bytes) and its weight tile is ready (TMA bytes + 4 arrivals,
+  // or 4 dequant-warp arrivals)
+  uint64_t* full = bars;
+  uint64_t* empty = full + kStages;         // MMAs reading the stage (weight and token tile) are done
   uint64_t* q_full = empty + kStages;       // packed nibbles + (scale, zero) of 4 k-blocks landed
   uint64_t* q_empty = q_full + kQStages;    // all 4 k-blocks of the staging stage dequantized
   uint64_t* acc_full = q_empty + kQStages;
@@ -202,13 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   if (warp == kWarpTmaB) {
     if (lane == 0) {
       for (int s = 0; s < kStages; ++s) {
-        mbar_init(&a_full[s], kNumDeqWarps);
-        mbar_init(&b_full[s], 1);
+        mbar_init(&full[s], kNumDeqWarps + 2);  // token TMA + weight TMA + the owning dequant group
         mbar_init(&empty[s], 1);
       }
       for (int s = 0; s < kQStages; ++s) {
         mbar_init(&q_full[s], 1);
-        mbar_init(&q_empty[s], kNumDeqWarps * kQSub);
+        mbar_init(&q_empty[s], kNumDeqGroups * kNumDeqWarps);
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&acc_full[a], 1);
@@ -304,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           const int s = it % kStages;
           if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
           uint8_t* sB = smem + kOffB + s * kBStageBytes;
-          uint64_t* fb = &b_full[s];
+          uint64_t* fb = &full[s];
           if (!tokk) {
             const bool ext = kb == ext_kb;
             if (!ext && ti.n_valid <= 32) {
@@ -323,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       }
       // every issued copy must land before the CTA may exit
       for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-        if (!mbar_wait(&b_full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
     }
   } else if (warp == kWarpTmaA) {
     // ============================================================================ TMA: bf16 weight ring (one thread)
@@ -345,12 +378,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
           const bool ext = kb == ext_kb;
           const int s = it % kStages;
-          // waited for every k-block (see the note on ring waits), filled only for TMA-sourced weight tiles
+          // waited for and arrived on in every round (see the note on ring waits), filled for TMA-sourced tiles
           if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyTma, t, kb)) { ok = false; break; }
-          if (int4 && !ext) continue;  // the dequant warps fill this slot
+          uint64_t* fa = &full[s];
+          if (int4 && !ext) {  // the dequant warps fill this slot; the arrival keeps this thread gating every round
+            mbar_arrive(fa);
+            continue;
+          }
           uint8_t* sA = smem + kOffA + s * kAStageBytes;
-          uint64_t* fa = &a_full[s];
-          mbar_expect_tx(fa, kAStageBytes);
+          mbar_arrive_expect_tx(fa, kAStageBytes);
           if (tokk) {  // A = tokens^T (MN-major)
             const int krow = ti.n0 + kb * kBK;
             tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, fa);
@@ -374,11 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             tma_load_2d(sA, mAmain, ti.m0, wrow, fa);
             tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, fa);
           }
-          mbar_arrive_n(fa, kNumDeqWarps);
         }
       }
       for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-        if (!mbar_wait(&a_full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
     }
   } else if (warp == kWarpTmaQ) {
     // ============================================================================ TMA: int4 staging ring (one thread)
@@ -419,62 +454,82 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         if (!mbar_wait(&q_full[j % kQStages], (j / kQStages) & 1, err, kDevErrTmaDrain)) break;
     }
   } else if (warp == kWarpMma) {
-    // ============================================================================ MMA issuer (one thread)
-    if (lane == 0) {
-      uint32_t it = 0, acc_it = 0;
-      bool ok = true, issued = false;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(args, T, t);
-        if (ti.nkb == 0) continue;
-        const Problem& P = args.p[ti.p];
-        // per-tile constants in registers (the loop below must not touch parameter memory)
-        const bool tokk = P.mode == kTokK;
-        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
-        const uint32_t a_mn = (tokk || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
-        const uint32_t b_mn = tokk ? 1u : 0u;
-        const int nkb = ti.nkb;
-        const int acc = acc_it & 1;
-        if (!mbar_wait(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty, t)) break;
+    // ============================================================================ MMA issuer (whole warp)
+    // The loop runs warp-uniform and each tcgen05 instruction goes out through one elected lane.
+    uint32_t it = 0, acc_it = 0;
+    bool ok = true, issued = false;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = decode_tile(args, T, t);
+      if (ti.nkb == 0) continue;
+      const Problem& P = args.p[ti.p];
+      // per-tile constants in registers (the loop below must not touch parameter memory)
+      const bool tokk = P.mode == kTokK;
+      const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+      const bool a_tm = P.mode == kTokN && P.a_kind == kAInt4K;  // weight tile in tensor memory
+      const uint32_t a_mn = (tokk || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
+      const uint32_t b_mn = tokk ? 1u : 0u;
+      const int nkb = ti.nkb;
+      const int acc = acc_it & 1;
+      if (!mbar_wait_warp(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty, t)) break;
+      tc_fence_after();
+      // MN-major B (kTokK) must span whole 64-element swizzle atoms; K-major B needs multiples of 16
+      const uint32_t n_mma = tokk ? (uint32_t)((ti.n_valid + 63) & ~63) : (uint32_t)((ti.n_valid + 15) & ~15);
+      const uint32_t idesc_main = make_idesc_bf16(n_mma, a_tm ? 0u : a_mn, b_mn);
+      const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
+      const uint32_t d_tmem = tmem_base + acc * kTmemAcc;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait_warp(&full[s], ph, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
         tc_fence_after();
-        // MN-major B (kTokK) must span whole 64-element swizzle atoms; K-major B needs multiples of 16
-        const uint32_t n_mma = tokk ? (uint32_t)((ti.n_valid + 63) & ~63) : (uint32_t)((ti.n_valid + 15) & ~15);
-        const uint32_t idesc_main = make_idesc_bf16(n_mma, a_mn, b_mn);
-        const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
-        const uint32_t d_tmem = tmem_base + acc * kMaxBN;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&b_full[s], ph, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
-          if (!mbar_wait(&a_full[s], ph, err, kDevErrWaitAFull, t, kb)) { ok = false; break; }
-          tc_fence_after();
-          const bool ext = kb == ext_kb;
-          const uint32_t sA = smem_base + kOffA + s * kAStageBytes;
-          const uint32_t sB = smem_base + kOffB + s * kBStageBytes;
-          const uint32_t idesc = ext ? idesc_ext : idesc_main;
+        const bool ext = kb == ext_kb;
+        const uint32_t sA = smem_base + kOffA + s * kAStageBytes;
+        const uint32_t sB = smem_base + kOffB + s * kBStageBytes;
+        const uint64_t b0 = b_mn ? make_sdesc(sB, 8192, 1024) : make_sdesc(sB, 16, 1024);
+        const uint32_t bstep = b_mn ? (2048 >> 4) : (32 >> 4);
+        // operands are computed warp-uniform; one elected lane issues the k-block's four MMAs and the commit that
+        // frees the stage
+        if (a_tm && !ext) {
+          const uint32_t a_tmem = tmem_base + kTmemA0 + s * 32;
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16_ts(d_tmem, a_tmem + kk * 8, b0 + (uint64_t)(kk * bstep), idesc_main, (kb | kk) != 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+        } else {
           // A: K-major steps 32 B per K=16 inside the swizzle atom, MN-major steps two 8-row k-groups (2048 B)
           const bool amn = a_mn && !ext;
+          const uint32_t idesc = ext ? idesc_ext : idesc_main;
           const uint64_t a0 = amn ? make_sdesc(sA, 8192, 1024) : make_sdesc(sA, 16, 1024);
-          const uint64_t b0 = b_mn ? make_sdesc(sB, 8192, 1024) : make_sdesc(sB, 16, 1024);
-          const uint32_t astep = amn ? (2048 >> 4) : (32 >> 4), bstep = b_mn ? (2048 >> 4) : (32 >> 4);
+          const uint32_t astep = amn ? (2048 >> 4) : (32 >> 4);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(d_tmem, a0 + (uint64_t)(kk * astep), b0 + (uint64_t)(kk * bstep), idesc, (kb | kk) != 0 ? 1u : 0u);
-          issued = true;
-          umma_commit(&empty[s]);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16(d_tmem, a0 + (uint64_t)(kk * astep), b0 + (uint64_t)(kk * bstep), idesc,
+                       (kb | kk) != 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
         }
-        if (!ok) break;
-        umma_commit(&acc_full[acc]);
-        ++acc_it;
+        __syncwarp();
+        issued = true;
       }
-      if (issued) {  // all MMAs must complete before TMEM is released
-        umma_commit(mma_drain);
-        mbar_wait(mma_drain, 0, err, kDevErrTmaDrain);
-      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[acc]);
+      __syncwarp();
+      ++acc_it;
+    }
+    if (issued) {  // all MMAs must complete before TMEM is released
+      if (elect_one()) umma_commit(mma_drain);
+      __syncwarp();
+      mbar_wait_warp(mma_drain, 0, err, kDevErrTmaDrain);
     }
   } else if (warp < kWarpEpi0) {
     // ============================================================================ int4 dequant (two groups)
     const int grp = (warp - kWarpDeq0) / kNumDeqWarps;
     const int pt = ((warp - kWarpDeq0) % kNumDeqWarps) * 32 + lane;  // 0..127 within the group
+    const int lq = warp & 3;                                         // TMEM lane quarter this warp may access
+    const int trow = lq * 32 + lane;                                 // weight-tile row this thread stores to TMEM
     uint32_t it = 0, qi = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
@@ -486,36 +541,60 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int nkq = int4 ? P.K / kBK : 0;  // int4 k-blocks of the tile
       for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
         const int s = it % kStages;
-        // every k-block's slot round is waited for, whichever role fills it (see the note on ring waits)
-        if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
-        if (kb >= nkq) continue;  // not an int4 k-block
+        const bool mine = (int)(it % kNumDeqGroups) == grp;  // ring slots of one parity belong to one group
+        const bool q4 = kb < nkq;                            // an int4 k-block (staged nibbles)
         const int j = kb % kQSub;
         const uint32_t qstage = qi + kb / kQSub;
         const int qs = qstage % kQStages;
-        // both groups wait on every staging stage (at its first k-block), so no round is skipped
-        if (j == 0 || (int)(it % kNumDeqGroups) == grp)
+        const int subs = min(kQSub, nkq - (kb / kQSub) * kQSub);  // k-blocks of this staging stage
+        const uint32_t it0 = it - j;                               // ring index of the stage's first k-block
+        // the first and last k-block of the stage this group owns (-1: none, a 1-k-block stage of the other group)
+        const int jfirst = ((int)(it0 % kNumDeqGroups) == grp) ? 0 : (subs > 1 ? 1 : -1);
+        const int jlast = jfirst < 0 ? -1 : jfirst + 2 * ((subs - 1 - jfirst) / 2);
+        if (q4 && j == 0 && jfirst < 0) {
+          // take part in the stage's round without owning any of its k-blocks
           if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
-        if ((int)(it % kNumDeqGroups) != grp) continue;  // the other group takes this k-block
-        uint8_t* sA = smem + kOffA + s * kAStageBytes;
-        const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes;
-        const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes);
-        if (kmajor) {
-          const int r = pt;
-          const int sr = glu ? glu_stage_row(r) : r;
-          dq64_to_row(sQ + sr * 128 + j * 32, sSZ[(sr >> 6) * 256 + j * 64 + (sr & 63)],
-                      sA + (r >> 3) * 1024 + (r & 7) * 128, r & 7);
-        } else {
-          const int kr = pt >> 1, half = pt & 1;
-          dq64_to_row(sQ + (j * 64 + kr) * 64 + half * 32, sSZ[half * 256 + j * 64 + kr],
-                      sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128, kr & 7);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&q_empty[qs]);
         }
-        fence_proxy_async_smem();
+        if (!mine) continue;
+        if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
+        if (q4) {
+          if (j == jfirst)
+            if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
+          uint8_t* sA = smem + kOffA + s * kAStageBytes;
+          const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes;
+          const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes);
+          // K-major: weight row trow -> TMEM lane trow, 64 bf16 in columns kTmemA0 + 32 s .. +31; the nibble rows
+          // are staged with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)).
+          // MN-major: k-row kr, half `half` of the 128 output features -> one 128-byte row of the swizzled smem tile.
+          const int sr = glu ? glu_stage_row(trow) : trow;
+          const int kr = pt >> 1, half = pt & 1;
+          const uint8_t* src = kmajor ? sQ + sr * 128 : sQ + (j * 64 + kr) * 64 + half * 32;
+          const int c0 = kmajor ? 2 * j : 0;
+          const int swz = kmajor ? (sr & 7) : 0;
+          const uint32_t sz = kmajor ? sSZ[(sr >> 6) * 256 + j * 64 + (sr & 63)] : sSZ[half * 256 + j * 64 + kr];
+          uint32_t o[32];
+          dq64(src, c0, swz, sz, o);
+          if (kmajor) {
+            tc_fence_after();  // the MMAs that read this TMEM stage completed (empty wait above)
+            __syncwarp();      // tcgen05.st is warp-collective: reconverge after the per-row dequant branch
+            tmem_st32(tmem_base + ((uint32_t)(lq * 32) << 16) + kTmemA0 + s * 32, o);
+            tmem_st_wait();
+            tc_fence_before();
+          } else {
+            uint8_t* dst = sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(dst + ((c ^ (kr & 7)) << 4)) =
+                  make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            fence_proxy_async_smem();
+          }
+        }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&a_full[s]);
-          // a staging stage counts kQSub arrivals per warp; a short last stage adds the missing ones at its end
-          const int subs = min(kQSub, nkq - (kb / kQSub) * kQSub);
-          mbar_arrive_n(&q_empty[qs], (j == subs - 1) ? 1 + (kQSub - subs) : 1);
+          mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates every round
+          if (q4 && j == jlast) mbar_arrive(&q_empty[qs]);
         }
       }
       qi += (nkq + kQSub - 1) / kQSub;
@@ -542,88 +621,97 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int acc = acc_it & 1;
       if (!mbar_wait(&acc_full[acc], (acc_it >> 1) & 1, err, kDevErrWaitAccFull, t)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kMaxBN;
-      const int nchunks = (ti.n_valid + 31) / 32;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * kTmemAcc;
+      const int n_valid = ti.n_valid;
       const float alpha = P.alpha;
-      if (P.epi == kEpiGlu) {
+      const int epi = P.epi, act = P.act;
+      // Columns are read from TMEM in chunks of 16 (8 for DGLU) with short unrolled bodies: the kernel's instruction
+      // footprint, shared by all warp roles, is what limits the epilogue, not its arithmetic.
+      if (epi == kEpiGlu) {
+        // lanes 0-15 own gate rows and take even token columns, lanes 16-31 own up rows and take odd ones; both need
+        // gate and up of their column (one shuffle across the half-warps)
         const bool is_gate = lane < 16;
         const int f = ti.m0 + q * 16 + (lane & 15);
         const bool fvalid = f < P.inter;
-        bf16* Cb = reinterpret_cast<bf16*>(P.C);
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c * 32, v);
+        const long long ldc = P.c_sn, ldh = P.h_ld;
+        const int inter = P.inter;
+        bf16* cp = reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + f;
+        bf16* hp = P.Hout ? P.Hout + (long long)ti.n0 * ldh + f : nullptr;
+        const int par = is_gate ? 0 : 1;
+        for (int c = 0; c < n_valid; c += 16) {
+          uint32_t v[16];
+          __syncwarp();
+          tmem_ld16(tbase + c, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            // lanes 0-15 take even token columns, lanes 16-31 odd ones; both need gate and up of the column
+          for (int jj = 0; jj < 8; ++jj) {
             const float mine_e = __uint_as_float(v[2 * jj]), mine_o = __uint_as_float(v[2 * jj + 1]);
             const float other_e = __shfl_xor_sync(0xffffffffu, mine_e, 16);
             const float other_o = __shfl_xor_sync(0xffffffffu, mine_o, 16);
-            const int j = 2 * jj + (is_gate ? 0 : 1);
             const float gacc = is_gate ? mine_e : other_o;
             const float uacc = is_gate ? other_e : mine_o;
-            const int n = c * 32 + j;
-            if (n < ti.n_valid && fvalid) {
-              const long long tok = ti.n0 + n;
+            const int n = c + 2 * jj + par;
+            if (n < n_valid && fvalid) {
               const float gb = bf16_round(gacc * alpha);
               const float ub = bf16_round(uacc * alpha);
-              const float ab = bf16_round(act_fwd(gb, P.act));
-              Cb[tok * P.c_sn + f] = __float2bfloat16_rn(ab * ub);
-              if (P.Hout) {
-                P.Hout[tok * P.h_ld + f] = __float2bfloat16_rn(gb);
-                P.Hout[tok * P.h_ld + P.inter + f] = __float2bfloat16_rn(ub);
+              const float ab = bf16_round(act_fwd(gb, act));
+              cp[(long long)n * ldc] = __float2bfloat16_rn(ab * ub);
+              if (hp) {
+                hp[(long long)n * ldh] = __float2bfloat16_rn(gb);
+                hp[(long long)n * ldh + inter] = __float2bfloat16_rn(ub);
               }
             }
           }
         }
-      } else if (P.epi == kEpiDGlu) {
+      } else if (epi == kEpiDGlu) {
         const int m = ti.m0 + row;
         const bool mvalid = m < P.M;
-        bf16* Cb = reinterpret_cast<bf16*>(P.C);
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c * 32, v);
+        const long long ldc = P.c_sn, ldh = P.h_ld;
+        const int inter = P.inter;
+        bf16* cp = reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + m;
+        const bf16* hp = P.Hin + (long long)ti.n0 * ldh + m;
+        for (int c = 0; c < n_valid; c += 8) {
+          uint32_t v[8];
+          __syncwarp();
+          tmem_ld8(tbase + c, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = c * 32 + j;
-            if (n < ti.n_valid && mvalid) {
-              const long long tok = ti.n0 + n;
+          for (int j = 0; j < 8; ++j) {
+            const int n = c + j;
+            if (n < n_valid && mvalid) {
               const float da = bf16_round(__uint_as_float(v[j]) * alpha);
-              const float g = __bfloat162float(P.Hin[tok * P.h_ld + m]);
-              const float u = __bfloat162float(P.Hin[tok * P.h_ld + P.inter + m]);
-              float a, dd;
-              act_and_grad(g, P.act, a, dd);
-              Cb[tok * P.c_sn + m] = __float2bfloat16_rn(da * u * dd);
-              Cb[tok * P.c_sn + P.inter + m] = __float2bfloat16_rn(da * a);
+              const float gv = __bfloat162float(hp[(long long)n * ldh]);
+              const float uv = __bfloat162float(hp[(long long)n * ldh + inter]);
+              const float2 ad = act_and_grad(gv, act);
+              cp[(long long)n * ldc] = __float2bfloat16_rn(da * uv * ad.y);
+              cp[(long long)n * ldc + inter] = __float2bfloat16_rn(da * ad.x);
             }
           }
         }
       } else {
         const int m = ti.m0 + row;
         const bool mvalid = m < P.M;
-        const long long gofs = (P.mode == kTokK) ? (long long)ti.g * P.c_gs : 0;
-        const long long nbase = (P.mode == kTokK) ? 0 : ti.n0;
-        for (int c = 0; c < nchunks; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c * 32, v);
+        const long long ldc = P.c_sn;
+        const long long base = ((P.mode == kTokK) ? (long long)ti.g * P.c_gs : (long long)ti.n0 * ldc) +
+                               (long long)m * P.c_sm;
+        const bool f32 = epi != kEpiStoreBf16;
+        for (int c = 0; c < n_valid; c += 16) {
+          uint32_t v[16];
+          __syncwarp();
+          tmem_ld16(tbase + c, v);
           tmem_ld_wait();
-          if (P.epi == kEpiStoreBf16) {
-            bf16* Cb = reinterpret_cast<bf16*>(P.C) + gofs;
+          if (!mvalid) continue;
+          const int nn = min(16, n_valid - c);
+          if (f32) {
+            float* cp = reinterpret_cast<float*>(P.C) + base + (long long)c * ldc;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = c * 32 + j;
-              if (n < ti.n_valid && mvalid)
-                Cb[(nbase + n) * P.c_sn + (long long)m * P.c_sm] = __float2bfloat16_rn(__uint_as_float(v[j]) * alpha);
-            }
+            for (int j = 0; j < 16; ++j)
+              if (j < nn) cp[(long long)j * ldc] = __uint_as_float(v[j]) * alpha;
           } else {
-            float* Cf = reinterpret_cast<float*>(P.C) + gofs;
+            bf16* cp = reinterpret_cast<bf16*>(P.C) + base + (long long)c * ldc;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = c * 32 + j;
-              if (n < ti.n_valid && mvalid) Cf[(nbase + n) * P.c_sn + (long long)m * P.c_sm] = __uint_as_float(v[j]) * alpha;
-            }
+            for (int j = 0; j < 16; ++j)
+              if (j < nn) cp[(long long)j * ldc] = __float2bfloat16_rn(__uint_as_float(v[j]) * alpha);
           }
         }
       }

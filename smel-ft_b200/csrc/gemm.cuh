@@ -48,13 +48,21 @@ constexpr int kMaxGroups = 320;  // groups over all problems of one launch
 
 constexpr int kAStageBytes = kBM * kBK * 2;      // 16 KB bf16 A tile
 constexpr int kBStageBytes = kMaxBN * kBK * 2;   // bf16 B tile
+// Tensor memory (512 columns x 128 lanes of 32 bit): two fp32 accumulators of kMaxBN columns, then one 32-column
+// bf16 weight tile per ring stage for the int4 K-major path (the dequant warps store it, the MMA reads A from it).
+constexpr int kTmemAcc = kMaxBN;
+constexpr int kTmemA0 = 2 * kMaxBN;
+static_assert(kTmemA0 + 4 * 32 <= 512 && kTmemA0 + SMELB_STAGES * 32 <= 512, "tensor memory budget exceeded");
 constexpr int kQStageBytes = 16384;              // nibbles: 128 rows x 128 B (K-major) or 256 k-rows x 64 B (MN-major)
 constexpr int kSZStageBytes = 2048;              // (scale, zero) pairs: 2 halves x 256 uint32
 
 // warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3-10 dequant (two groups of four warps taking
 // alternate k-blocks), 11-14 epilogue (one per TMEM lane quarter), 15 TMA (int4 staging ring).
-// Every thread that waits on a ring's "empty" barrier waits on every round of every slot in order (also for k-blocks
-// another role fills): a parity wait issued two rounds ahead of the barrier would pass without waiting.
+// Ring waits: a thread that waits on a barrier round must also be one of the arrivals that the barrier's NEXT round
+// of the paired barrier needs (it "gates" the ring), otherwise it can fall two phases behind and its parity wait
+// then aliases onto a later phase. So the token TMA, the weight TMA and the owning dequant group arrive on "full"
+// in every round they wait on "empty" (the weight TMA also for int4 slots it does not fill); ring slots of one
+// parity belong to one dequant group; every dequant warp waits on and releases every int4 staging stage once.
 constexpr int kNumDeqGroups = 2;
 constexpr int kNumDeqWarps = 4;  // per group
 constexpr int kNumEpiWarps = 4;

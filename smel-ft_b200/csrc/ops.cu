@@ -29,9 +29,10 @@ int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int b
 }
 int tm_q(CUtensorMap* m, const void* q, long long rows, long long cols, bool mn_major) {
   // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes. K-major tiles stage 4 k-blocks per row
-  // (128 B); MN-major tiles stage 4 k-blocks of 64 k-rows x 64 B.
+  // (128 B, 128-byte swizzle so the dequant warps' row reads are free of bank conflicts); MN-major tiles stage
+  // 4 k-blocks of 64 k-rows x 64 B.
   return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : 128,
-                      mn_major ? 256 : 64, false);
+                      mn_major ? 256 : 64, !mn_major);
 }
 int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows, bool mn_major) {
   return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4, mn_major ? 256 : 64,
