@@ -88,6 +88,13 @@ int smelb_dispatch_plan(const int64_t* topi, int64_t T, int64_t K, int64_t E, co
                         int32_t* counts, int32_t* gcounts, int32_t* offsets, int32_t* row_of, int32_t* src_of,
                         int64_t* order, int32_t* total, void* stream);
 
+/* The same plan computed by many CTAs (same outputs, bit for bit). workspace: int32 scratch of workspace_ints
+ * elements (up to 148 * E are used; with fewer than 2 * E it falls back to the one-CTA plan). */
+int smelb_dispatch_plan_ws(const int64_t* topi, int64_t T, int64_t K, int64_t E, const uint8_t* sel_mask,
+                           int64_t pad, int32_t* counts, int32_t* gcounts, int32_t* offsets, int32_t* row_of,
+                           int32_t* src_of, int64_t* order, int32_t* total, int32_t* workspace,
+                           int64_t workspace_ints, void* stream);
+
 /* xs[row] = x[src_of[row] / K] (zeros on padding rows) for rows < total[0]. x bf16 [T, H], xs bf16 [max_rows, H]. */
 int smelb_gather_rows(const void* x, int64_t H, int64_t K, const int32_t* src_of, const int32_t* total,
                       int64_t max_rows, void* xs, void* stream);

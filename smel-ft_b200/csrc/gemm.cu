@@ -1,6 +1,6 @@
-// Persistent grouped multi-problem GEMM for sm_100a: a TMA producer warp, a single-thread tcgen05.mma issuer with
-// TMEM accumulators (double-buffered across tiles), four int4 dequant warps and four epilogue warps. See gemm.cuh
-// for the operand conventions.
+// Persistent grouped multi-problem GEMM for sm_100a: TMA producer warps, a warp-elected tcgen05.mma issuer with TMEM
+// accumulators (double-buffered across tiles), two groups of four int4 dequant warps and a team of epilogue warps.
+// See gemm.cuh for the operand conventions and the warp roles.
 #include "gemm.cuh"
 #include "host.h"
 
@@ -601,8 +601,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     }
   } else {
     // ============================================================================ epilogue warps
-    const int q = warp & 3;         // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;  // accumulator row (A row) owned by this thread
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;              // accumulator row (A row) owned by this thread
+    const int sub = (warp - kWarpEpi0) >> 2;    // which of the quarter's kEpiSubs warps: takes chunks sub, sub + kEpiSubs, ...
     uint32_t acc_it = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const TileInfo ti = decode_tile(args, T, t);
@@ -613,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           const int m = ti.m0 + row;
           if (m < P.M) {
             float* C = reinterpret_cast<float*>(P.C) + (long long)ti.g * P.c_gs;
-            for (int n = 0; n < P.N; ++n) C[(long long)m * P.c_sm + (long long)n * P.c_sn] = 0.0f;
+            for (int n = sub; n < P.N; n += kEpiSubs) C[(long long)m * P.c_sm + (long long)n * P.c_sn] = 0.0f;
           }
         }
         continue;
@@ -638,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         bf16* cp = reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + f;
         bf16* hp = P.Hout ? P.Hout + (long long)ti.n0 * ldh + f : nullptr;
         const int par = is_gate ? 0 : 1;
-        for (int c = 0; c < n_valid; c += 16) {
+        for (int c = 16 * sub; c < n_valid; c += 16 * kEpiSubs) {
           uint32_t v[16];
           __syncwarp();
           tmem_ld16(tbase + c, v);
@@ -670,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         const int inter = P.inter;
         bf16* cp = reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + m;
         const bf16* hp = P.Hin + (long long)ti.n0 * ldh + m;
-        for (int c = 0; c < n_valid; c += 8) {
+        for (int c = 8 * sub; c < n_valid; c += 8 * kEpiSubs) {
           uint32_t v[8];
           __syncwarp();
           tmem_ld8(tbase + c, v);
@@ -688,6 +689,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             }
           }
         }
+      } else if (epi == kEpiStoreBf16 && P.mode == kTokN && P.c_sm == 1 && (P.M & 1) == 0 && (P.c_sn & 1) == 0 &&
+                 (reinterpret_cast<uintptr_t>(P.C) & 3) == 0) {
+        // bf16 rows [token][feature] with the features of adjacent lanes adjacent in memory: lane pairs exchange half
+        // of their columns (one shuffle per column pair) and each lane stores packed feature pairs as 32-bit words,
+        // the even lane for the chunk's first 8 tokens, the odd lane for the last 8.
+        const int m = ti.m0 + row;
+        const int m0 = m & ~1;
+        const bool odd = lane & 1;
+        const bool mvalid = m0 < P.M;
+        const long long ldc = P.c_sn;
+        uint32_t* cp = reinterpret_cast<uint32_t*>(reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + m0);
+        const long long ldw = ldc >> 1;  // row pitch in 32-bit words
+        for (int c = 16 * sub; c < n_valid; c += 16 * kEpiSubs) {
+          uint32_t v[16];
+          __syncwarp();
+          tmem_ld16(tbase + c, v);
+          tmem_ld_wait();
+          const int tb = c + (odd ? 8 : 0);  // first token this lane stores
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            // the even lane sends column 8 + j and keeps column j; the odd lane sends column j and keeps 8 + j
+            const float mine = __uint_as_float(odd ? v[8 + j] : v[j]);
+            const float send = __uint_as_float(odd ? v[j] : v[8 + j]);
+            const float other = __shfl_xor_sync(0xffffffffu, send, 1);
+            const float lo = odd ? other : mine, hi = odd ? mine : other;  // features m0, m0 + 1
+            if (mvalid && tb + j < n_valid) cp[(long long)(tb + j) * ldw] = bf162_bits(__floats2bfloat162_rn(lo * alpha, hi * alpha));
+          }
+        }
       } else {
         const int m = ti.m0 + row;
         const bool mvalid = m < P.M;
@@ -695,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         const long long base = ((P.mode == kTokK) ? (long long)ti.g * P.c_gs : (long long)ti.n0 * ldc) +
                                (long long)m * P.c_sm;
         const bool f32 = epi != kEpiStoreBf16;
-        for (int c = 0; c < n_valid; c += 16) {
+        for (int c = 16 * sub; c < n_valid; c += 16 * kEpiSubs) {
           uint32_t v[16];
           __syncwarp();
           tmem_ld16(tbase + c, v);

@@ -56,8 +56,10 @@ static_assert(kTmemA0 + 4 * 32 <= 512 && kTmemA0 + SMELB_STAGES * 32 <= 512, "te
 constexpr int kQStageBytes = 16384;              // nibbles: 128 rows x 128 B (K-major) or 256 k-rows x 64 B (MN-major)
 constexpr int kSZStageBytes = 2048;              // (scale, zero) pairs: 2 halves x 256 uint32
 
-// warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3-10 dequant (two groups of four warps taking
-// alternate k-blocks), 11-14 epilogue (one per TMEM lane quarter), 15 TMA (int4 staging ring).
+// warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3 TMA (int4 staging ring), 4-11 dequant (two
+// groups of four warps taking alternate k-blocks), then the epilogue: kEpiSubs warps per TMEM lane quarter, which
+// split a tile's accumulator columns between them in 16-column chunks (several warps per quarter hide the latency
+// of the per-element conversion and store chains).
 // Ring waits: a thread that waits on a barrier round must also be one of the arrivals that the barrier's NEXT round
 // of the paired barrier needs (it "gates" the ring), otherwise it can fall two phases behind and its parity wait
 // then aliases onto a later phase. So the token TMA, the weight TMA and the owning dequant group arrive on "full"
@@ -65,11 +67,14 @@ constexpr int kSZStageBytes = 2048;              // (scale, zero) pairs: 2 halve
 // parity belong to one dequant group; every dequant warp waits on and releases every int4 staging stage once.
 constexpr int kNumDeqGroups = 2;
 constexpr int kNumDeqWarps = 4;  // per group
-constexpr int kNumEpiWarps = 4;
-constexpr int kWarpTmaB = 0, kWarpMma = 1, kWarpTmaA = 2, kWarpDeq0 = 3;
+#ifndef SMELB_EPI_SUBS
+#define SMELB_EPI_SUBS 3
+#endif
+constexpr int kEpiSubs = SMELB_EPI_SUBS;
+constexpr int kNumEpiWarps = 4 * kEpiSubs;
+constexpr int kWarpTmaB = 0, kWarpMma = 1, kWarpTmaA = 2, kWarpTmaQ = 3, kWarpDeq0 = 4;
 constexpr int kWarpEpi0 = kWarpDeq0 + kNumDeqGroups * kNumDeqWarps;
-constexpr int kWarpTmaQ = kWarpEpi0 + kNumEpiWarps;
-constexpr int kThreads = (kWarpTmaQ + 1) * 32;
+constexpr int kThreads = (kWarpEpi0 + kNumEpiWarps) * 32;
 
 enum Mode : int { kTokN = 0, kTokK = 1 };
 enum AKind : int { kAInt4K = 0, kAInt4MN = 1, kABf16K = 2, kABf16MN = 3 };

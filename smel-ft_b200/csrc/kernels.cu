@@ -254,6 +254,7 @@ int router_bwd(const void* dtopv, bool dtopv_f32, const float* dprobs, const flo
 //   total[0]           rows used by the dispatch layout
 constexpr int kPlanWarps = 32;
 constexpr int kPlanMaxE = 512;
+constexpr long long kPlanStageMax = 49152;  // choices staged in shared memory as uint16 expert ids
 
 __global__ void __launch_bounds__(kPlanWarps * 32, 1)
     dispatch_plan_kernel(const long long* __restrict__ topi, long long R, int E, const uint8_t* __restrict__ sel_mask,
@@ -264,19 +265,38 @@ __global__ void __launch_bounds__(kPlanWarps * 32, 1)
   int* hist = sm;                             // [kPlanWarps][E] per-warp counts, later per-warp running bases
   int* s_off = sm + kPlanWarps * E;           // [E] padded offsets
   int* s_offu = s_off + E;                    // [E] unpadded offsets
-  int* s_scan = s_offu + E;                   // [2 * 1024] scan scratch
+  int* s_seg = s_offu + E;                    // [E] padded segment lengths
+  int* s_cnt = s_seg + E;                     // [E] counts
+  uint16_t* s_eid = reinterpret_cast<uint16_t*>(s_cnt + E);  // [R] expert ids (0xFFFF: invalid), when staged
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool staged = R <= kPlanStageMax;
   for (int i = threadIdx.x; i < kPlanWarps * E; i += blockDim.x) hist[i] = 0;
+  if (staged) {
+    // coalesced, independent loads: the whole choice list lands in shared memory once
+    for (long long i = threadIdx.x; i < R; i += blockDim.x) {
+      const long long e = topi[i];
+      if (e < 0 || e >= E) dev_fail(err, kDevErrBadIndex);
+      s_eid[i] = (e < 0 || e >= E) ? (uint16_t)0xFFFF : (uint16_t)e;
+    }
+  }
   __syncthreads();
+  auto eid = [&](long long i) -> int {
+    if (staged) {
+      const int e = s_eid[i];
+      return e == 0xFFFF ? -1 : e;
+    }
+    const long long e = topi[i];
+    return (e >= 0 && e < E) ? (int)e : -1;
+  };
   const long long chunk = (R + kPlanWarps - 1) / kPlanWarps;
   const long long c0 = warp * chunk, c1 = min(R, c0 + chunk);
   for (long long i = c0 + lane; i < c1; i += 32) {
-    const long long e = topi[i];
-    if (e < 0 || e >= E) {
-      dev_fail(err, kDevErrBadIndex);
+    const int e = eid(i);
+    if (e < 0) {
+      if (!staged) dev_fail(err, kDevErrBadIndex);
       continue;
     }
-    atomicAdd(&hist[warp * E + (int)e], 1);
+    atomicAdd(&hist[warp * E + e], 1);
   }
   __syncthreads();
   // per-expert totals and per-warp exclusive bases
@@ -290,19 +310,36 @@ __global__ void __launch_bounds__(kPlanWarps * 32, 1)
     counts[e] = run;
     const int seg = (sel_mask && sel_mask[e]) ? (run + pad - 1) / pad * pad : run;
     gcounts[e] = seg;
-    s_scan[e] = seg;
-    s_scan[1024 + e] = run;
+    s_seg[e] = seg;
+    s_cnt[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, accu = 0;
-    for (int e = 0; e < E; ++e) {
+  if (warp == 0) {
+    // exclusive scans of the segment lengths and counts: each lane sums a run of consecutive experts
+    const int per = (E + 31) / 32;
+    const int e0 = lane * per, e1 = min(E, e0 + per);
+    int a = 0, au = 0;
+    for (int e = e0; e < e1; ++e) {
+      a += s_seg[e];
+      au += s_cnt[e];
+    }
+    int ia = a, iau = au;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, ia, o), xu = __shfl_up_sync(0xffffffffu, iau, o);
+      if (lane >= o) {
+        ia += x;
+        iau += xu;
+      }
+    }
+    int acc = ia - a, accu = iau - au;
+    for (int e = e0; e < e1; ++e) {
       s_off[e] = acc;
       s_offu[e] = accu;
-      acc += s_scan[e];
-      accu += s_scan[1024 + e];
+      acc += s_seg[e];
+      accu += s_cnt[e];
     }
-    total[0] = acc;
+    if (lane == 31) total[0] = ia;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) offsets[e] = s_off[e];
@@ -310,15 +347,12 @@ __global__ void __launch_bounds__(kPlanWarps * 32, 1)
   const unsigned lt_mask = (1u << lane) - 1u;
   for (long long b = c0; b < c1; b += 32) {
     const long long i = b + lane;
-    const bool valid = i < c1;
-    long long e64 = valid ? topi[i] : -1;
-    const int e = (e64 >= 0 && e64 < E) ? (int)e64 : -1;
+    const int e = i < c1 ? eid(i) : -1;
     const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     if (e >= 0) {
       const int rank = __popc(peers & active & lt_mask);
-      const int base = hist[warp * E + e];
-      const int pos = base + rank;
+      const int pos = hist[warp * E + e] + rank;
       const int row = s_off[e] + pos;
       row_of[i] = row;
       src_of[row] = (int)i;
@@ -334,7 +368,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32, 1)
   __syncthreads();
   // padding rows of padded segments
   for (int e = warp; e < E; e += kPlanWarps) {
-    const int cnt = s_scan[1024 + e], seg = s_scan[e];
+    const int cnt = s_cnt[e], seg = s_seg[e];
     for (int r = cnt + lane; r < seg; r += 32) src_of[s_off[e] + r] = -1;
   }
 }
@@ -345,15 +379,154 @@ int dispatch_plan(const long long* topi, long long R, int E, const uint8_t* sel_
   SMELB_CHECK_ARG(pad >= 1 && R >= 0 && R < (1LL << 30), kErrShape, "dispatch_plan: R=%lld pad=%d", R, pad);
   int dev = 0;
   SMELB_CUDA(cudaGetDevice(&dev));
-  const int smem = (kPlanWarps * E + 2 * E + 2048) * 4;
+  const long long staged = R <= kPlanStageMax ? R : 0;
+  const int smem = (int)((kPlanWarps * E + 4 * E) * 4 + ((staged * 2 + 15) & ~15LL));
   static bool configured[64] = {false};
   if (dev < 64 && !configured[dev]) {
     SMELB_CUDA(cudaFuncSetAttribute(dispatch_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (kPlanWarps * kPlanMaxE + 2 * kPlanMaxE + 2048) * 4));
+                                    (int)((kPlanWarps * kPlanMaxE + 4 * kPlanMaxE) * 4 + kPlanStageMax * 2)));
     configured[dev] = true;
   }
   dispatch_plan_kernel<<<1, kPlanWarps * 32, smem, st>>>(topi, R, E, sel_mask, pad, counts, gcounts, offsets, row_of,
                                                          src_of, order, total, device_status(dev));
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// Multi-CTA variant of the same plan for callers that can lend scratch (nb x E ints): pass 1 counts each CTA's
+// contiguous chunk of choices, pass 2 derives every CTA's base per expert from the earlier chunks' counts, the
+// (padded) segment offsets, and then ranks its chunk warp by warp in order, so the result equals the single-CTA plan.
+constexpr int kPlanMtWarps = 8;
+
+__global__ void __launch_bounds__(256) plan_count_kernel(const long long* __restrict__ topi, long long R, int E,
+                                                         long long chunk, int* __restrict__ cnt, int* __restrict__ err) {
+  __shared__ int hist[kPlanMaxE];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const long long c0 = blockIdx.x * chunk, c1 = min(R, c0 + chunk);
+  for (long long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+    const long long e = topi[i];
+    if (e < 0 || e >= E) {
+      dev_fail(err, kDevErrBadIndex);
+      continue;
+    }
+    atomicAdd(&hist[(int)e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[(long long)blockIdx.x * E + e] = hist[e];
+}
+
+__global__ void __launch_bounds__(kPlanMtWarps * 32) plan_rank_kernel(
+    const long long* __restrict__ topi, long long R, int E, long long chunk, const uint8_t* __restrict__ sel_mask,
+    int pad, const int* __restrict__ cnt, int* __restrict__ counts, int* __restrict__ gcounts,
+    int* __restrict__ offsets, int* __restrict__ row_of, int* __restrict__ src_of, long long* __restrict__ order,
+    int* __restrict__ total) {
+  __shared__ int base[kPlanMaxE], tot[kPlanMaxE], seg[kPlanMaxE], s_off[kPlanMaxE], s_offu[kPlanMaxE];
+  __shared__ int wcnt[kPlanMtWarps][kPlanMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = gridDim.x, b = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int bs = 0, t = 0;
+    for (int bb = 0; bb < nb; ++bb) {
+      const int c = cnt[(long long)bb * E + e];
+      bs += bb < b ? c : 0;
+      t += c;
+    }
+    base[e] = bs;
+    tot[e] = t;
+    seg[e] = (sel_mask && sel_mask[e]) ? (t + pad - 1) / pad * pad : t;
+    for (int w = 0; w < kPlanMtWarps; ++w) wcnt[w][e] = 0;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int per = (E + 31) / 32;
+    const int e0 = lane * per, e1 = min(E, e0 + per);
+    int a = 0, au = 0;
+    for (int e = e0; e < e1; ++e) {
+      a += seg[e];
+      au += tot[e];
+    }
+    int ia = a, iau = au;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, ia, o), xu = __shfl_up_sync(0xffffffffu, iau, o);
+      if (lane >= o) {
+        ia += x;
+        iau += xu;
+      }
+    }
+    int acc = ia - a, accu = iau - au;
+    for (int e = e0; e < e1; ++e) {
+      s_off[e] = acc;
+      s_offu[e] = accu;
+      acc += seg[e];
+      accu += tot[e];
+    }
+    if (b == 0 && lane == 31) total[0] = ia;
+  }
+  // this CTA's chunk, split into kPlanMtWarps consecutive sub-chunks
+  const long long c0 = b * chunk, c1 = min(R, c0 + chunk);
+  const long long sub = (c1 - c0 + kPlanMtWarps - 1) / kPlanMtWarps;
+  const long long w0 = min(c1, c0 + warp * sub), w1 = min(c1, w0 + sub);
+  for (long long i = w0 + lane; i < w1; i += 32) {
+    const long long e = topi[i];
+    if (e >= 0 && e < E) atomicAdd(&wcnt[warp][(int)e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    if (b == 0) {
+      counts[e] = tot[e];
+      gcounts[e] = seg[e];
+      offsets[e] = s_off[e];
+    }
+    int run = base[e];
+    for (int w = 0; w < kPlanMtWarps; ++w) {
+      const int c = wcnt[w][e];
+      wcnt[w][e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (long long r0 = w0; r0 < w1; r0 += 32) {
+    const long long i = r0 + lane;
+    long long e64 = i < w1 ? topi[i] : -1;
+    const int e = (e64 >= 0 && e64 < E) ? (int)e64 : -1;
+    const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int pos = wcnt[warp][e] + __popc(peers & active & lt_mask);
+      const int row = s_off[e] + pos;
+      row_of[i] = row;
+      src_of[row] = (int)i;
+      order[s_offu[e] + pos] = i;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers & active) - 1) wcnt[warp][e] += __popc(peers & active);
+    __syncwarp();
+  }
+  // padding rows of the padded segments of this CTA's experts
+  for (int e = b; e < E; e += nb)
+    for (int r = tot[e] + threadIdx.x; r < seg[e]; r += blockDim.x) src_of[s_off[e] + r] = -1;
+}
+
+int dispatch_plan_mt(const long long* topi, long long R, int E, const uint8_t* sel_mask, int pad, int* counts,
+                     int* gcounts, int* offsets, int* row_of, int* src_of, long long* order, int* total, int* scratch,
+                     long long scratch_ints, cudaStream_t st) {
+  SMELB_CHECK_ARG(E >= 1 && E <= kPlanMaxE, kErrShape, "dispatch_plan: E=%d (max %d)", E, kPlanMaxE);
+  SMELB_CHECK_ARG(pad >= 1 && R >= 0 && R < (1LL << 30), kErrShape, "dispatch_plan: R=%lld pad=%d", R, pad);
+  long long nb = std::min<long long>(148, std::max<long long>(1, R / 256));
+  nb = std::min<long long>(nb, scratch_ints / E);
+  if (nb < 2) return dispatch_plan(topi, R, E, sel_mask, pad, counts, gcounts, offsets, row_of, src_of, order, total, st);
+  const long long chunk = (R + nb - 1) / nb;
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  plan_count_kernel<<<(int)nb, 256, 0, st>>>(topi, R, E, chunk, scratch, device_status(dev));
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  plan_rank_kernel<<<(int)nb, kPlanMtWarps * 32, 0, st>>>(topi, R, E, chunk, sel_mask, pad, scratch, counts, gcounts,
+                                                          offsets, row_of, src_of, order, total);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -652,6 +825,61 @@ __global__ void pack_blocks_kernel(PackSpec spec, bf16* __restrict__ out) {
     }
     out[i] = __float2bfloat16_rn(v);
   }
+}
+
+__device__ __forceinline__ uint32_t pk_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+// One thread per 8 consecutive outputs of a row (j, a) of one of the batch's outputs (OB % 8 == 0): the block
+// descriptions are read once per thread into registers and the 8 values leave as one 16-byte store.
+__global__ void pack_batch_kernel(const __grid_constant__ PackBatch b) {
+  const long long nvec = b.start[b.n] / 8;
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < nvec; t += (long long)gridDim.x * blockDim.x) {
+    const long long i = t * 8;
+    int k = 0;
+    while (k + 1 < b.n && i >= b.start[k + 1]) ++k;
+    const int OA = b.spec[k].OA, OB = b.spec[k].OB;
+    const long long li = i - b.start[k];
+    const int row = (int)(li / OB), c0 = (int)(li - (long long)row * OB);
+    const int j = row / OA, a = row - j * OA;
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = 0.f;
+#pragma unroll
+    for (int bi = 0; bi < 2; ++bi) {
+      const PackBlock B = b.spec[k].blk[bi];
+      if (!B.src || a < B.a0 || a >= B.a0 + B.na) continue;
+      const float* src = B.src + j * B.sj + (long long)(a - B.a0) * B.sa;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int c = c0 + q;
+        if (c >= B.b0 && c < B.b0 + B.nb) v[q] = B.scale * src[(long long)(c - B.b0) * B.sb];
+      }
+    }
+    uint4 o;
+    o.x = pk_bits(__floats2bfloat162_rn(v[0], v[1]));
+    o.y = pk_bits(__floats2bfloat162_rn(v[2], v[3]));
+    o.z = pk_bits(__floats2bfloat162_rn(v[4], v[5]));
+    o.w = pk_bits(__floats2bfloat162_rn(v[6], v[7]));
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(b.out[k]) + li) = o;
+  }
+}
+
+int pack_batch(PackBatch& b, cudaStream_t st) {
+  b.start[0] = 0;
+  b.rstart[0] = 0;
+  for (int k = 0; k < b.n; ++k) {
+    b.start[k + 1] = b.start[k] + (long long)b.spec[k].J * b.spec[k].OA * b.spec[k].OB;
+    b.rstart[k + 1] = b.rstart[k] + b.spec[k].J * b.spec[k].OA;
+  }
+  if (b.n == 0 || b.start[b.n] == 0) return kOk;
+  for (int k = 0; k < b.n; ++k)
+    SMELB_CHECK_ARG(b.spec[k].OB % 8 == 0 && (reinterpret_cast<uintptr_t>(b.out[k]) & 15) == 0, kErrShape,
+                    "pack: output %d row length %d (needs a multiple of 8, 16-byte aligned)", k, b.spec[k].OB);
+  const long long nvec = b.start[b.n] / 8;
+  const int blocks = (int)std::min<long long>(148 * 8, (nvec + 255) / 256);
+  pack_batch_kernel<<<blocks, 256, 0, st>>>(b);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
 }
 
 int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st) {

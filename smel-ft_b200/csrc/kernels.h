@@ -19,6 +19,15 @@ struct PackSpec {
   int J, OA, OB;
   PackBlock blk[2];
 };
+// Several pack outputs in one launch (the LoRA operands of one layer call).
+constexpr int kMaxPacks = 8;
+struct PackBatch {
+  int n;
+  PackSpec spec[kMaxPacks];
+  void* out[kMaxPacks];
+  long long start[kMaxPacks + 1];  // prefix of the output element counts
+  int rstart[kMaxPacks + 1];       // prefix of the output rows (J * OA)
+};
 
 int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
                  bool out_f32, cudaStream_t st);
@@ -30,6 +39,10 @@ int router_bwd(const void* dtopv, bool dtopv_f32, const float* dprobs, const flo
                const void* per_expert_scale, int T, int E, int K, void* dlogits, long long ld, cudaStream_t st);
 int dispatch_plan(const long long* topi, long long R, int E, const uint8_t* sel_mask, int pad, int* counts,
                   int* gcounts, int* offsets, int* row_of, int* src_of, long long* order, int* total, cudaStream_t st);
+// The same plan on many CTAs, with `scratch` (>= 2 * E ints useful; nb x E used) lent by the caller.
+int dispatch_plan_mt(const long long* topi, long long R, int E, const uint8_t* sel_mask, int pad, int* counts,
+                     int* gcounts, int* offsets, int* row_of, int* src_of, long long* order, int* total, int* scratch,
+                     long long scratch_ints, cudaStream_t st);
 int gather_rows(const void* x, int H, int K, const int* src_of, const int* total, long long max_rows, void* xs,
                 cudaStream_t st);
 int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f32, int T, int K, int H,
@@ -41,6 +54,7 @@ int shared_gate_bwd(const void* g, const void* y_sh, const void* gl, int T, int 
 int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const void* dx_sh, const void* dx_r,
               const float* dgl, const void* w_sg, void* dx, cudaStream_t st);
 int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st);
+int pack_batch(PackBatch& batch, cudaStream_t st);  // launches nothing when the batch is empty
 
 int launch_gemm(struct LaunchArgs& args, cudaStream_t stream);
 // Same launch with the wait-timeout status words supplied by the caller (4 ints, device memory) instead of the

@@ -154,14 +154,17 @@ PackBlock blk(const float* src, long long sj, long long sa, long long sb, int a0
   return b;
 }
 PackBlock no_blk() { return blk(nullptr, 0, 0, 0, 0, 0, 0, 0, 0.f); }
-int pack(int J, int OA, int OB, PackBlock b0, PackBlock b1, void* out, cudaStream_t st) {
-  PackSpec s;
+// appends one output to the batch (launched once for all LoRA operands of a layer call)
+int pack(int J, int OA, int OB, PackBlock b0, PackBlock b1, void* out, PackBatch& batch) {
+  SMELB_CHECK_ARG(batch.n < kMaxPacks, kErrArg, "LoRA pack batch full");
+  PackSpec& s = batch.spec[batch.n];
   s.J = J;
   s.OA = OA;
   s.OB = OB;
   s.blk[0] = b0;
   s.blk[1] = b1;
-  return pack_blocks(s, out, st);
+  batch.out[batch.n++] = out;
+  return kOk;
 }
 
 // LoRA parameter set of one gated MLP family (J slots; J = 1 for the shared expert)
@@ -173,7 +176,7 @@ struct LoraSet {
 
 // forward operands: xa_w [J,2r,H] = [A_gate; A_up]; gu_ext [J,2I,64] = [[s B_gate, 0], [0, s B_up]];
 // z_w [J,r,I] = A_down; dn_ext [J,H,64] = [s B_down, 0]
-int pack_fwd(const LoraSet& L, void* xa_w, void* gu_ext, void* z_w, void* dn_ext, cudaStream_t st) {
+int pack_fwd(const LoraSet& L, void* xa_w, void* gu_ext, void* z_w, void* dn_ext, PackBatch& st) {
   const int r = L.r, H = L.H, I = L.I;
   TRY(pack(L.J, 2 * r, H, blk(L.Ag, (long long)r * H, H, 1, 0, r, 0, H, 1.f),
            blk(L.Au, (long long)r * H, H, 1, r, r, 0, H, 1.f), xa_w, st));
@@ -186,7 +189,7 @@ int pack_fwd(const LoraSet& L, void* xa_w, void* gu_ext, void* z_w, void* dn_ext
 
 // backward operands: dz_w [J,r,H] = s B_down^T; da_ext [J,I,64] = [A_down^T, 0];
 // dxa_w [J,2r,2I] = [[s B_gate^T, 0], [0, s B_up^T]]; dx_ext [J,H,64] = [A_gate^T, A_up^T, 0]
-int pack_bwd(const LoraSet& L, void* dz_w, void* da_ext, void* dxa_w, void* dx_ext, cudaStream_t st) {
+int pack_bwd(const LoraSet& L, void* dz_w, void* da_ext, void* dxa_w, void* dx_ext, PackBatch& st) {
   const int r = L.r, H = L.H, I = L.I;
   TRY(pack(L.J, r, H, blk(L.Bd, (long long)H * r, 1, r, 0, r, 0, H, L.s), no_blk(), dz_w, st));
   TRY(pack(L.J, I, kW64, blk(L.Ad, (long long)r * I, 1, I, 0, I, 0, r, 1.f), no_blk(), da_ext, st));
@@ -248,8 +251,13 @@ int layer_fwd(const smelb_moe_layer& L) {
   if (T == 0) return kOk;
   const LoraSet ls{nsel, rs, H, I, L.s_sel, L.A_gate, L.B_gate, L.A_up, L.B_up, L.A_down, L.B_down};
   const LoraSet lh{1, rh, H, S, L.s_sh, L.shA_gate, L.shB_gate, L.shA_up, L.shB_up, L.shA_down, L.shB_down};
-  if (f.sel_lora) TRY(pack_fwd(ls, L.p_xa_w, L.p_gu_ext, L.p_z_w, L.p_dn_ext, st));
-  if (f.sh_lora) TRY(pack_fwd(lh, L.sp_xa_w, L.sp_gu_ext, L.sp_z_w, L.sp_dn_ext, st));
+  {
+    PackBatch pb;
+    pb.n = 0;
+    if (f.sel_lora) TRY(pack_fwd(ls, L.p_xa_w, L.p_gu_ext, L.p_z_w, L.p_dn_ext, pb));
+    if (f.sh_lora) TRY(pack_fwd(lh, L.sp_xa_w, L.sp_gu_ext, L.sp_z_w, L.sp_dn_ext, pb));
+    TRY(pack_batch(pb, st));
+  }
 
   // L1: everything that reads only x: router logits, shared gate logit, shared LoRA A product
   {
@@ -282,8 +290,9 @@ int layer_fwd(const smelb_moe_layer& L) {
   const long long* topi = (const long long*)(f.router ? L.topi : L.topi_in);
 
   if (f.routed) {
-    TRY(dispatch_plan(topi, (long long)T * K, E, L.sel_mask, 64, L.counts, L.gcounts, L.offsets, L.row_of, L.src_of,
-                      (long long*)L.order, L.total, st));
+    // the dispatch buffer xs is written only by the gather that follows, so the plan may use it as scratch
+    TRY(dispatch_plan_mt(topi, (long long)T * K, E, L.sel_mask, 64, L.counts, L.gcounts, L.offsets, L.row_of,
+                         L.src_of, (long long*)L.order, L.total, (int*)L.xs, (long long)R * H / 2, st));
     TRY(gather_rows(L.x, H, K, L.src_of, L.total, R, L.xs, st));
   }
   const Int4Mat gu{L.gu_q, L.gu_sz, E, 2 * I, H};
@@ -417,8 +426,13 @@ int layer_bwd(const smelb_moe_layer& L) {
   if (T == 0) return kOk;
   const LoraSet ls{nsel, rs, H, I, L.s_sel, L.A_gate, L.B_gate, L.A_up, L.B_up, L.A_down, L.B_down};
   const LoraSet lh{1, rh, H, S, L.s_sh, L.shA_gate, L.shB_gate, L.shA_up, L.shB_up, L.shA_down, L.shB_down};
-  if (f.sel_lora) TRY(pack_bwd(ls, L.p_dz_w, L.p_da_ext, L.p_dxa_w, L.p_dx_ext, st));
-  if (f.sh_lora) TRY(pack_bwd(lh, L.sp_dz_w, L.sp_da_ext, L.sp_dxa_w, L.sp_dx_ext, st));
+  {
+    PackBatch pb;
+    pb.n = 0;
+    if (f.sel_lora) TRY(pack_bwd(ls, L.p_dz_w, L.p_da_ext, L.p_dxa_w, L.p_dx_ext, pb));
+    if (f.sh_lora) TRY(pack_bwd(lh, L.sp_dz_w, L.sp_da_ext, L.sp_dxa_w, L.sp_dx_ext, pb));
+    TRY(pack_batch(pb, st));
+  }
   const void* topv = f.router ? L.topv : L.topv_in;
 
   if (f.routed)
@@ -693,6 +707,16 @@ int smelb_dispatch_plan(const int64_t* topi, int64_t T, int64_t K, int64_t E, co
                   "dispatch_plan: null pointer");
   return dispatch_plan((const long long*)topi, T * K, (int)E, sel_mask, (int)pad, counts, gcounts, offsets, row_of,
                        src_of, (long long*)order, total, (cudaStream_t)stream);
+}
+
+int smelb_dispatch_plan_ws(const int64_t* topi, int64_t T, int64_t K, int64_t E, const uint8_t* sel_mask,
+                           int64_t pad, int32_t* counts, int32_t* gcounts, int32_t* offsets, int32_t* row_of,
+                           int32_t* src_of, int64_t* order, int32_t* total, int32_t* workspace,
+                           int64_t workspace_ints, void* stream) {
+  SMELB_CHECK_ARG(topi && counts && gcounts && offsets && row_of && src_of && order && total && workspace, kErrArg,
+                  "dispatch_plan_ws: null pointer");
+  return dispatch_plan_mt((const long long*)topi, T * K, (int)E, sel_mask, (int)pad, counts, gcounts, offsets, row_of,
+                          src_of, (long long*)order, total, workspace, workspace_ints, (cudaStream_t)stream);
 }
 
 int smelb_gather_rows(const void* x, int64_t H, int64_t K, const int32_t* src_of, const int32_t* total,

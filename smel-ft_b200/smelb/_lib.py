@@ -76,6 +76,8 @@ SIGNATURES = {
     "smelb_router_bwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "smelb_dispatch_plan": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                     c_vp, c_vp]),
+    "smelb_dispatch_plan_ws": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                       c_vp, c_i64, c_vp]),
     "smelb_gather_rows": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "smelb_combine_fwd": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "smelb_frozen_experts_fwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i32,

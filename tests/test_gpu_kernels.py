@@ -84,13 +84,19 @@ def test_router_topk_bit_exact_given_logits(dev):
     assert (diff <= v_ref.float().abs() * 2 ** -7).all()
 
 
-def test_dispatch_plan_bit_exact(dev, golden):
+@pytest.mark.parametrize("entry", ["smelb_dispatch_plan", "smelb_dispatch_plan_ws"])
+def test_dispatch_plan_bit_exact(dev, golden, entry):
+    """One-CTA plan and the many-CTA plan (the layer's) against the oracle's stable sort, bit for bit."""
     from smelb import _lib
-    for T, K, E, seed in ((97, 4, 8, 0), (4092, 8, 256, 1), (1, 8, 256, 2), (3000, 2, 16, 3)):
+    for T, K, E, seed in ((97, 4, 8, 0), (4092, 8, 256, 1), (1, 8, 256, 2), (3000, 2, 16, 3), (4092, 8, 256, 4),
+                          (16384, 8, 128, 5)):
         g = torch.Generator().manual_seed(seed)
         topi = torch.randint(0, E, (T, K), generator=g)
         if seed == 3:
             topi[:, 0] = 5  # one very hot expert
+        if seed == 4:  # Zipf-like skew: a few experts take most choices
+            w = 1.0 / torch.arange(1, E + 1, dtype=torch.float64) ** 1.1
+            topi = torch.multinomial(w.expand(T, E), K, replacement=False, generator=g)
         sel = np.zeros(E, dtype=np.uint8)
         sel[[1, 5, E - 1]] = 1
         counts, gcounts, offsets, row_of, src_of = O.dispatch_padded(topi.numpy(), E, sel, 64)
@@ -101,9 +107,13 @@ def test_dispatch_plan_bit_exact(dev, golden):
              (("counts", E), ("gcounts", E), ("offsets", E), ("row_of", T * K), ("src_of", R), ("total", 1))}
         order_d = torch.empty(T * K, dtype=torch.int64, device=dev)
         sel_d = torch.from_numpy(sel).to(dev)
-        _lib.call("smelb_dispatch_plan", tg.data_ptr(), T, K, E, sel_d.data_ptr(), 64, b["counts"].data_ptr(),
-                  b["gcounts"].data_ptr(), b["offsets"].data_ptr(), b["row_of"].data_ptr(), b["src_of"].data_ptr(),
-                  order_d.data_ptr(), b["total"].data_ptr(), _lib.stream_ptr())
+        args = [tg.data_ptr(), T, K, E, sel_d.data_ptr(), 64, b["counts"].data_ptr(), b["gcounts"].data_ptr(),
+                b["offsets"].data_ptr(), b["row_of"].data_ptr(), b["src_of"].data_ptr(), order_d.data_ptr(),
+                b["total"].data_ptr()]
+        if entry == "smelb_dispatch_plan_ws":
+            ws = torch.full((148 * E,), -3, dtype=torch.int32, device=dev)
+            args += [ws.data_ptr(), ws.numel()]
+        _lib.call(entry, *args, _lib.stream_ptr())
         assert b["counts"].cpu().numpy().tolist() == counts.tolist()
         assert b["gcounts"].cpu().numpy().tolist() == gcounts.tolist()
         assert b["offsets"].cpu().numpy().tolist() == offsets.tolist()
