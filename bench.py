@@ -275,9 +275,15 @@ def run_ours(args, world, rank, local):
     gemm_ms_step = gemm_ms / args.steps
     achieved = flops_step / (gemm_ms_step / 1e3) / 1e12
     peak = pk["bf16_tflops"]
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "moe_gemm_traffic.json")
+    if os.path.exists(tpath):  # DRAM bytes of the GEMM launches of one step, from the committed ncu capture
+        tj = json.load(open(tpath))
+        traffic = {"bytes_per_launch": round(tj["traffic_bytes_per_step"] / tj["launches_per_step"]),
+                   "bytes_per_step": round(tj["traffic_bytes_per_step"]), "source": tj["source"]}
     roof = {"bound": "tensor", "kernel": "moe_gemm_kernel (all expert / router / LoRA GEMMs of the step)",
             "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-            "peak_kind": f"{pk_kind} bf16 burst", "traffic": None,
+            "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic,
             "gemm_ms_per_step": round(gemm_ms_step, 4), "gemm_launches_per_step": gemm_n // max(args.steps, 1),
             "algorithmic_flops_per_step": flops_step,
             "layer_frac_of_roofline": round((flops_step / (ms_step / 1e3) / 1e12) / peak, 4)}

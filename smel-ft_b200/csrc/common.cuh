@@ -152,6 +152,9 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+#ifndef SMELB_BACKOFF_MAX_NS
+#define SMELB_BACKOFF_MAX_NS 512u
+#endif
 #ifndef SMELB_SUSPEND_NS
 #define SMELB_SUSPEND_NS 100000u  // upper bound of one suspended try_wait (100 us); the wake-up is on completion
 #endif
@@ -161,12 +164,17 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
 // (out of line) suspends in try_wait instead of spinning, and checks the clock between suspensions.
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code, int tile, int kb) {
   const uint64_t t0 = globaltimer_ns();
+  uint32_t sleep_ns = 0;
   while (true) {
     if (mbar_try_wait_suspend(bar, parity, SMELB_SUSPEND_NS)) return true;
     if (globaltimer_ns() - t0 > SMELB_WAIT_NS) {
       dev_fail_at(err, code, tile, kb);
       return false;
     }
+    // back off so that a waiting warp leaves its scheduler's issue slots to the warps that work: a few quick polls,
+    // then sleeps growing to SMELB_BACKOFF_MAX_NS
+    if (sleep_ns) __nanosleep(sleep_ns);
+    sleep_ns = sleep_ns ? min(2 * sleep_ns, (uint32_t)SMELB_BACKOFF_MAX_NS) : 32u;
   }
 }
 
