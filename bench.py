@@ -128,7 +128,8 @@ def config_json(cfg, meta, world):
             "lora_rank": cfg["r"], "routing": f"zipf s=1.1 over a seeded permutation, top-12 gate share "
             f"{meta.get('share', 0):.3f}", "seed": meta.get("seed"),
             "l2": "weights 0.53 GB > L2 126 MB: each step streams the banks from HBM",
-            "parallelism": "single" if world == 1 else f"replicas x{world} (weak scaling)"}
+            "parallelism": "single" if world == 1 else
+            f"ep{world}: experts split over {world} GPUs, {cfg['T']} tokens per GPU (weak scaling)"}
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline
@@ -156,21 +157,36 @@ def run_ours(args, world, rank, local):
     from smelb.synth import flops_per_token, qwen_layer
     dev = torch.device("cuda", local)
     cfg = layer_config(args)
-    layer = qwen_layer(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"], n_sel=cfg["n_sel"],
-                       r=cfg["r"], alpha=cfg["alpha"], seed=rank, device=dev)
+    ep_mode = world > 1
+    # with several GPUs the layer is expert parallel: one layer (same weights on every rank, built from one seed) whose
+    # experts are split over the ranks, and every rank brings its own cfg["T"] tokens (weak scaling)
+    layer = qwen_layer(T=cfg["T"] * world, H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"],
+                       n_sel=cfg["n_sel"], r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
     W, ex, lora, K = layer["W"], layer["ex"], layer["lora"], cfg["K"]
-    params = list(lora.parameters())
-    x = layer["x"]
-    gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(9), device=dev).bfloat16()
+    x = layer["x"][rank * cfg["T"]:(rank + 1) * cfg["T"]].contiguous()
+    gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(9 + rank), device=dev).bfloat16()
+    if ep_mode:
+        from smelb import ep
+        ex_run, lora_run = ep.shard_layer(ex, lora, rank, world)
+    else:
+        ex_run, lora_run = ex, lora
+    params = list(lora_run.parameters()) if ep_mode else list(lora.parameters())
+
+    def layer_call(xd):
+        if ep_mode:
+            return ep.moe_forward_ep(xd, W, ex_run, K, lora_run)
+        return smelb.moe_forward(xd, W, ex_run, K, lora_run)
 
     def step(xd, gd):
         for p in params:
             p.grad = None
         with torch.no_grad():
-            smelb.moe_forward(xd, W, ex, K, lora)
+            layer_call(xd)
         xr = xd.detach().requires_grad_(True)
-        out = smelb.moe_forward(xr, W, ex, K, lora)
+        out = layer_call(xr)
         out.backward(gd)
+        if ep_mode:
+            ep.allreduce_shared_grads(lora_run)
         return xr.grad
 
     # everything runs on one side stream: a CUDA graph is captured on it, and autograd's gradient accumulation
@@ -210,7 +226,12 @@ def run_ours(args, world, rank, local):
     # in a CUDA graph and replayed, so the number is the device's and not the Python host's
     graph, timing = None, "cuda-graph replay of the whole step"
     n0 = _lib.launch_count()
+    if ep_mode:
+        graph, timing = None, ("eager (expert parallel: the per-call row counts are needed on the host as the "
+                               "all-to-all split sizes, so the step is not graph-captured)")
     try:
+        if ep_mode:
+            raise RuntimeError("skip")
         torch.cuda.synchronize()
         n0 = _lib.launch_count()
         graph = torch.cuda.CUDAGraph()
@@ -218,7 +239,8 @@ def run_ours(args, world, rank, local):
             step(x, gy)
         torch.cuda.synchronize()
     except Exception as exc:  # not capturable here: time the eager step instead and say so
-        graph, timing = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
+        if not ep_mode:
+            graph, timing = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
         torch.cuda.synchronize()
         n0 = _lib.launch_count()
     per_step_launches = _lib.launch_count() - n0 if graph is not None else None

@@ -103,6 +103,17 @@ int smelb_gather_rows(const void* x, int64_t H, int64_t K, const int32_t* src_of
 int smelb_combine_fwd(const void* y, const int32_t* row_of, const void* topv, int topv_fp32, int64_t T, int64_t K,
                       int64_t H, void* out, void* stream);
 
+/* Backward of smelb_combine_fwd for rows r < total[0] (src_of[r] = choice t*K+k, -1 on padding rows):
+ * dy[r] = bf16(g[t] * topv[t,k]) (zeros on padding rows) and dtopv[t,k] = sum_h g[t,h] * y[r,h] in fp32 (stored as
+ * bf16, or fp32 if topv_fp32). dtopv may be NULL. The autograd of moe.py:248-252. */
+int smelb_combine_bwd(const void* g, const void* y, const int32_t* src_of, const int32_t* total, int64_t max_rows,
+                      const void* topv, int topv_fp32, int64_t K, int64_t H, void* dy, void* dtopv, void* stream);
+
+/* Backward of smelb_gather_rows: dx[t] = bf16(sum_k fp32(dxs[row_of[t,k]])) in k order (the autograd of the
+ * x[tok] gather, moe.py:221). */
+int smelb_gather_rows_bwd(const void* dxs, const int32_t* row_of, int64_t T, int64_t K, int64_t H, void* dx,
+                          void* stream);
+
 /* ---------------------------------------------------------------------------------------------------- experts
  * smel/moe.py:110-126 FrozenExpertsFn.forward / frozen_experts_forward: xs bf16 [rows, H] grouped by expert with
  * counts (device int32 [E], sum = rows); int4 bank gate_up (q [E, 2I, H/2], sz_t [E, H/64, 2I]) and down

@@ -732,6 +732,21 @@ int smelb_combine_fwd(const void* y, const int32_t* row_of, const void* topv, in
                      (cudaStream_t)stream);
 }
 
+int smelb_combine_bwd(const void* g, const void* y, const int32_t* src_of, const int32_t* total, int64_t max_rows,
+                      const void* topv, int topv_fp32, int64_t K, int64_t H, void* dy, void* dtopv, void* stream) {
+  SMELB_CHECK_ARG(g && y && src_of && total && topv && dy, kErrArg, "combine_bwd: null pointer");
+  SMELB_CHECK_ARG(K >= 1 && K <= 32 && H % 8 == 0, kErrShape, "combine_bwd: K=%lld H=%lld", (long long)K, (long long)H);
+  return combine_bwd_rows(g, y, src_of, total, max_rows, topv, topv_fp32 != 0, (int)K, (int)H, dy, dtopv,
+                          (cudaStream_t)stream);
+}
+
+int smelb_gather_rows_bwd(const void* dxs, const int32_t* row_of, int64_t T, int64_t K, int64_t H, void* dx,
+                          void* stream) {
+  SMELB_CHECK_ARG(dxs && row_of && dx, kErrArg, "gather_rows_bwd: null pointer");
+  SMELB_CHECK_ARG(K >= 1 && K <= 32, kErrShape, "gather_rows_bwd: K=%lld", (long long)K);
+  return dx_reduce(dxs, row_of, (int)K, (int)T, (int)H, nullptr, nullptr, nullptr, nullptr, dx, (cudaStream_t)stream);
+}
+
 int smelb_frozen_experts_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E,
                              const void* gu_q, const uint32_t* gu_sz, const void* dn_q, const uint32_t* dn_sz,
                              int act, void* h_save, void* a_buf, void* out, void* stream) {

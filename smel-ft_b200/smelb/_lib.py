@@ -80,6 +80,8 @@ SIGNATURES = {
                                        c_vp, c_i64, c_vp]),
     "smelb_gather_rows": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "smelb_combine_fwd": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "smelb_combine_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "smelb_gather_rows_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "smelb_frozen_experts_fwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i32,
                                          c_vp, c_vp, c_vp, c_vp]),
     "smelb_frozen_experts_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp,
