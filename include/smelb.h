@@ -114,6 +114,24 @@ int smelb_combine_bwd(const void* g, const void* y, const int32_t* src_of, const
 int smelb_gather_rows_bwd(const void* dxs, const int32_t* row_of, int64_t T, int64_t K, int64_t H, void* dx,
                           void* stream);
 
+/* ---------------------------------------------------------------------------------------------------- row norms
+ * smel/norm.py rmsnorm / add_rmsnorm (torch form smel/layer_runner.py:110-130), bf16 rows [rows, C] (C % 8 == 0),
+ * fp32 math, one rounding to bf16:
+ *   h_add == NULL: y = x * rstd * w';  h_add != NULL: s_out = bf16(h_add + x), y = s_out * rstd * w'
+ *   w' = 1 (w_mode 0, w may be NULL), w (1, Gemma 4) or 1 + w (2, Qwen3.5/3.6); rstd = rsqrt(mean(v^2) + eps).
+ * post_scale (bf16 [C]) / post_mul (0: none) add the Gemma 4 router prologue of smel/moe.py:170-176 in its bf16
+ * steps: y = bf16(bf16(bf16(v * rstd) * post_scale) * post_mul) (w_mode 0). rstd_out (fp32 [rows]) may be NULL. */
+int smelb_rmsnorm_fwd(const void* x, const void* h_add, const void* w, int w_mode, const void* post_scale,
+                      float post_mul, float eps, int64_t rows, int64_t C, void* s_out, void* y, float* rstd_out,
+                      void* stream);
+
+/* Backward of smelb_rmsnorm_fwd with frozen weights: dx = rstd * (g - xhat * mean(g * xhat)) + ds, g = dy * w'
+ * (through the post chain's bf16 steps when given), xhat = x * rstd. x is the normed input (s_out for the fused
+ * add); ds (the gradient reaching the sum from its other use) may be NULL. */
+int smelb_rmsnorm_bwd(const void* dy, const void* x, const void* w, int w_mode, const void* post_scale,
+                      float post_mul, const float* rstd, const void* ds, int64_t rows, int64_t C, void* dx,
+                      void* stream);
+
 /* ---------------------------------------------------------------------------------------------------- experts
  * smel/moe.py:110-126 FrozenExpertsFn.forward / frozen_experts_forward: xs bf16 [rows, H] grouped by expert with
  * counts (device int32 [E], sum = rows); int4 bank gate_up (q [E, 2I, H/2], sz_t [E, H/64, 2I]) and down
@@ -220,6 +238,7 @@ typedef struct smelb_moe_layer {
   const void* fz_dn;        /* [E, H, I] */
   int32_t act_sh;           /* activation of the shared expert / dense MLP (SMELB_ACT_*) */
   int32_t reserved;
+  const void* per_expert_scale; /* bf16 [E] multiplier of the renormalised top-k weights (Gemma 4), or NULL */
 } smelb_moe_layer;
 
 /* Instrumentation. smelb_launch_count: kernels launched by this library so far (all entry points).

@@ -224,6 +224,17 @@ def moe_layer(x, W, bank_gu, bank_dn, top_k, sel_ids=(), sel_gu=None, sel_dn=Non
         topi = topk_stable(probs, top_k)
     top = probs.gather(1, topi)
     topv = (top / top.sum(dim=-1, keepdim=True)).to(x.dtype)
+    routed_out = routed(x, topv, topi, bank_gu, bank_dn, sel_ids, sel_gu, sel_dn, lora_ex, act_name)
+    pre = "mlp.shared_expert."
+    sh = mlp(x, W[pre + "gate_proj.weight"].to(x.dtype), W[pre + "up_proj.weight"].to(x.dtype),
+             W[pre + "down_proj.weight"].to(x.dtype), lora_sh, "silu")
+    sh = sh * torch.sigmoid(F.linear(x, W["mlp.shared_expert_gate.weight"].to(x.dtype)))  # moe.py:197-201
+    return routed_out + sh, probs, topv, topi
+
+
+def routed(x, topv, topi, bank_gu, bank_dn, sel_ids=(), sel_gu=None, sel_dn=None, lora_ex=None, act_name="silu"):
+    """smel/moe.py:214-252 routed_experts: stable dispatch by expert, frozen experts from the dequantized bank,
+    selected experts with LoRA, then the fp32 weighted sum over k in k order, in the dtype of x."""
     N, H = x.shape
     K = topi.shape[1]
     E = bank_gu.shape[0]
@@ -257,11 +268,56 @@ def moe_layer(x, W, bank_gu, bank_dn, top_k, sel_ids=(), sel_gu=None, sel_dn=Non
     inv[torch.from_numpy(order)] = torch.arange(order.shape[0])
     yk = y[inv].view(N, K, H)
     routed = (yk.float() * topv.float().unsqueeze(-1)).sum(1).to(x.dtype)  # moe.py:248-252
-    pre = "mlp.shared_expert."
-    sh = mlp(x, W[pre + "gate_proj.weight"].to(x.dtype), W[pre + "up_proj.weight"].to(x.dtype),
-             W[pre + "down_proj.weight"].to(x.dtype), lora_sh, "silu")
-    sh = sh * torch.sigmoid(F.linear(x, W["mlp.shared_expert_gate.weight"].to(x.dtype)))  # moe.py:197-201
-    return routed + sh, probs, topv, topi
+    return routed
+
+
+# ============================================================================================== Gemma 4 block
+def rmsnorm(x, w, eps, plus_one=True):
+    """smel/layer_runner.py:110-121 (torch form of smel/norm.py rmsnorm): fp32 math, one rounding to x's dtype."""
+    xf = x.double() if x.dtype == torch.float64 else x.float()
+    if plus_one:
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+        return (xf * (1.0 + w.to(xf.dtype))).type_as(x)
+    xf = xf * torch.pow(xf.pow(2).mean(-1, keepdim=True) + eps, -0.5)
+    return (xf if w is None else xf * w.to(xf.dtype)).type_as(x)
+
+
+def add_rmsnorm(h, x, w, eps, plus_one=True):
+    """smel/layer_runner.py:124-130: (h + x, rmsnorm(h + x))."""
+    s = h + x
+    return s, rmsnorm(s, w, eps, plus_one)
+
+
+def route_gemma4(h, W, top_k, eps, topi=None):
+    """smel/moe.py:170-180: weightless RMSNorm of h (rounded to h's dtype), x router.scale x H^-0.5, router.proj
+    logits, fp32 softmax, top-k (value desc, id asc; or forced), renormalised, x per_expert_scale[topi]; topv fp32."""
+    hf = h.float() if h.dtype != torch.float64 else h
+    x = (hf * torch.pow(hf.pow(2).mean(-1, keepdim=True) + eps, -0.5)).type_as(h)
+    x = x * W["router.scale"].to(h.dtype) * h.shape[-1] ** -0.5
+    logits = F.linear(x, W["router.proj.weight"].to(h.dtype))
+    probs = torch.softmax(logits, dim=-1, dtype=torch.float32 if h.dtype != torch.float64 else torch.float64)
+    if topi is None:
+        topi = topk_stable(probs, top_k)
+    topv = probs.gather(1, topi)
+    topv = topv / topv.sum(dim=-1, keepdim=True)
+    return probs, topv * W["router.per_expert_scale"].to(topv.dtype)[topi], topi
+
+
+def moe_block_gemma4(h, xm, W, bank_gu, bank_dn, top_k, eps, sel_ids=(), sel_gu=None, sel_dn=None, lora_ex=None,
+                     lora_sh=None, act_name="gelu_tanh", topi=None):
+    """smel/layer_runner.py:252-261 (the Gemma 4 MoE block after the attention residual): dense MLP with the "shared"
+    LoRA on xm and its post norm, route_gemma4 on h, routed experts on the pre-FFN-2 norm of h and their post norm,
+    h + rmsnorm(m + e), times layer_scalar. Returns (out, probs, topv, topi)."""
+    dt = h.dtype
+    m = mlp(xm, W["mlp.gate_proj.weight"].to(dt), W["mlp.up_proj.weight"].to(dt), W["mlp.down_proj.weight"].to(dt),
+            lora_sh, act_name)
+    m = rmsnorm(m, W["post_feedforward_layernorm_1.weight"], eps, False)
+    probs, topv, topi = route_gemma4(h, W, top_k, eps, topi)
+    xe = rmsnorm(h, W["pre_feedforward_layernorm_2.weight"], eps, False)
+    e = routed(xe, topv, topi, bank_gu, bank_dn, sel_ids, sel_gu, sel_dn, lora_ex, act_name)
+    e = rmsnorm(e, W["post_feedforward_layernorm_2.weight"], eps, False)
+    out = (h + rmsnorm(m + e, W["post_feedforward_layernorm.weight"], eps, False)) * W["layer_scalar"].to(dt)
+    return out, probs, topv, topi
 
 
 # ============================================================================================== metrics

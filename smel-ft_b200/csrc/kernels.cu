@@ -532,6 +532,138 @@ int dispatch_plan_mt(const long long* topi, long long R, int E, const uint8_t* s
   return kOk;
 }
 
+// ============================================================================================ row norms
+// RMSNorm of bf16 rows in fp32 (smel/norm.py:1-20 and its torch form smel/layer_runner.py:110-130), one warp per row:
+//   v = x, or with a residual input h: s = bf16(h + x) (stored) and v = s;
+//   rstd = rsqrt(mean(v^2) + eps);  y = bf16(v * rstd * w')  with w' = 1 (w_mode 0), w (1) or 1 + w (2).
+// The Gemma 4 router prologue (smel/moe.py:170-176) is w_mode 0 plus a post chain in the reference's bf16 steps:
+//   y = bf16(bf16(bf16(v * rstd) * scale[c]) * post_mul)   (post_scale != null and/or post_mul != 0).
+// Backward (frozen norm weights): g = dy * w' (with the post chain: g = bf16(bf16(dy * post_mul) * scale)),
+//   dx = rstd * (g - xhat * mean(g * xhat)) [+ ds], xhat = v * rstd.
+__device__ __forceinline__ void ld8(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* q = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(q[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void st8(bf16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* q = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) q[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ float weff(const bf16* w, int w_mode, int c) {
+  if (w_mode == 0) return 1.f;
+  const float f = __bfloat162float(w[c]);
+  return w_mode == 2 ? 1.f + f : f;
+}
+
+__global__ void rmsnorm_fwd_kernel(const NormArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; r < a.rows; r += nw) {
+    const long long o = r * a.C;
+    float ss = 0.f;
+    for (int c = lane * 8; c < a.C; c += 256) {
+      float v[8];
+      ld8(a.x + o + c, v);
+      if (a.h) {
+        float hv[8];
+        ld8(a.h + o + c, hv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = bf16_round(hv[j] + v[j]);  // the residual stream is rounded
+        st8(a.s + o + c, v);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float rs = rsqrtf(ss / (float)a.C + a.eps);
+    if (a.rstd && lane == 0) a.rstd[r] = rs;
+    const bf16* src = a.h ? a.s : a.x;
+    for (int c = lane * 8; c < a.C; c += 256) {
+      float v[8];
+      ld8(src + o + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float y = v[j] * rs * weff(a.w, a.w_mode, c + j);
+        if (a.post_scale) y = bf16_round(bf16_round(y) * __bfloat162float(a.post_scale[c + j]));
+        if (a.post_mul != 0.f) y = bf16_round(y) * a.post_mul;
+        v[j] = y;
+      }
+      st8(a.y + o + c, v);
+    }
+  }
+}
+
+__global__ void rmsnorm_bwd_kernel(const NormBwdArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+  auto gval = [&](float dy, int c) {
+    float g = dy;
+    if (a.post_mul != 0.f) g = bf16_round(g * a.post_mul);
+    if (a.post_scale) g = bf16_round(g * __bfloat162float(a.post_scale[c]));
+    return g * weff(a.w, a.w_mode, c);
+  };
+  for (long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; r < a.rows; r += nw) {
+    const long long o = r * a.C;
+    const float rs = a.rstd[r];
+    float dot = 0.f;
+    for (int c = lane * 8; c < a.C; c += 256) {
+      float d[8], v[8];
+      ld8(a.dy + o + c, d);
+      ld8(a.x + o + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot = fmaf(gval(d[j], c + j), v[j] * rs, dot);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float mc = dot / (float)a.C;
+    for (int c = lane * 8; c < a.C; c += 256) {
+      float d[8], v[8], e[8];
+      ld8(a.dy + o + c, d);
+      ld8(a.x + o + c, v);
+      if (a.ds) ld8(a.ds + o + c, e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float dx = rs * (gval(d[j], c + j) - v[j] * rs * mc);
+        if (a.ds) dx += e[j];
+        d[j] = dx;
+      }
+      st8(a.dx + o + c, d);
+    }
+  }
+}
+
+int rmsnorm_fwd(const NormArgs& a, cudaStream_t st) {
+  SMELB_CHECK_ARG(a.C % 8 == 0 && a.C > 0, kErrShape, "rmsnorm: %d columns (a multiple of 8)", a.C);
+  SMELB_CHECK_ARG(!a.h || a.s, kErrArg, "rmsnorm: the fused add needs its sum output");
+  SMELB_CHECK_ARG(a.w_mode == 0 || a.w, kErrArg, "rmsnorm: w_mode %d without a weight", a.w_mode);
+  if (a.rows == 0) return kOk;
+  const long long blocks = std::min<long long>((a.rows * 32 + 255) / 256, 148LL * 16);
+  rmsnorm_fwd_kernel<<<(int)blocks, 256, 0, st>>>(a);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st) {
+  SMELB_CHECK_ARG(a.C % 8 == 0 && a.C > 0, kErrShape, "rmsnorm_bwd: %d columns (a multiple of 8)", a.C);
+  SMELB_CHECK_ARG(a.w_mode == 0 || a.w, kErrArg, "rmsnorm_bwd: w_mode %d without a weight", a.w_mode);
+  if (a.rows == 0) return kOk;
+  const long long blocks = std::min<long long>((a.rows * 32 + 255) / 256, 148LL * 16);
+  rmsnorm_bwd_kernel<<<(int)blocks, 256, 0, st>>>(a);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
 // ============================================================================================ gather
 // xs[row] = x[src_of[row] / K] for real rows and zeros for padding rows, rows < total[0]. One warp per row, 16-byte
 // vectors (H % 8 == 0).

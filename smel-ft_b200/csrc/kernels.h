@@ -1,12 +1,15 @@
 // Host entry points of the memory-bound MoE kernels (kernels.cu). All return a Status code.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdint>
 
 namespace smelb {
+
+using bf16 = __nv_bfloat16;
 
 struct PackBlock {
   const float* src;  // nullptr: block unused
@@ -55,6 +58,38 @@ int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const voi
               const float* dgl, const void* w_sg, void* dx, cudaStream_t st);
 int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st);
 int pack_batch(PackBatch& batch, cudaStream_t st);  // launches nothing when the batch is empty
+
+struct NormArgs {
+  const bf16* x;
+  const bf16* h;           // residual input of the fused add, or null
+  const bf16* w;           // norm weight, or null (w_mode 0)
+  const bf16* post_scale;  // router prologue scale vector, or null
+  float post_mul;          // router prologue scalar (0: none)
+  int w_mode;
+  float eps;
+  long long rows;
+  int C;
+  bf16* s;                 // fused add output (h + x), with h
+  bf16* y;
+  float* rstd;             // per-row rstd, or null
+};
+
+struct NormBwdArgs {
+  const bf16* dy;
+  const bf16* x;           // the normed input (the fused add's sum s for add_rmsnorm)
+  const bf16* w;
+  const bf16* post_scale;
+  float post_mul;
+  int w_mode;
+  const float* rstd;
+  const bf16* ds;          // gradient reaching the sum from its other use, or null
+  long long rows;
+  int C;
+  bf16* dx;
+};
+
+int rmsnorm_fwd(const NormArgs& a, cudaStream_t st);
+int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st);
 
 int launch_gemm(struct LaunchArgs& args, cudaStream_t stream);
 // Same launch with the wait-timeout status words supplied by the caller (4 ints, device memory) instead of the

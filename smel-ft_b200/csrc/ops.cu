@@ -285,7 +285,8 @@ int layer_fwd(const smelb_moe_layer& L) {
     }
     TRY(b.launch(st));
   }
-  if (f.router) TRY(router_topk(L.logits, E, T, E, K, L.probs, L.topv, f.topv32, (long long*)L.topi, nullptr, st));
+  if (f.router)
+    TRY(router_topk(L.logits, E, T, E, K, L.probs, L.topv, f.topv32, (long long*)L.topi, L.per_expert_scale, st));
   const void* topv = f.router ? L.topv : L.topv_in;
   const long long* topi = (const long long*)(f.router ? L.topi : L.topi_in);
 
@@ -443,7 +444,8 @@ int layer_bwd(const smelb_moe_layer& L) {
     sh_dy = L.sh_dy;
   }
   if (f.router)
-    TRY(router_bwd(L.dtopv, f.topv32, L.dprobs, L.probs, (const long long*)L.topi, nullptr, T, E, K, L.dlogits, Epad,
+    TRY(router_bwd(L.dtopv, f.topv32, L.dprobs, L.probs, (const long long*)L.topi, L.per_expert_scale, T, E, K,
+                   L.dlogits, Epad,
                    st));
   const Int4Mat gu{L.gu_q, L.gu_sz, E, 2 * I, H};
   const Int4Mat dn{L.dn_q, L.dn_sz, E, H, I};
@@ -745,6 +747,26 @@ int smelb_gather_rows_bwd(const void* dxs, const int32_t* row_of, int64_t T, int
   SMELB_CHECK_ARG(dxs && row_of && dx, kErrArg, "gather_rows_bwd: null pointer");
   SMELB_CHECK_ARG(K >= 1 && K <= 32, kErrShape, "gather_rows_bwd: K=%lld", (long long)K);
   return dx_reduce(dxs, row_of, (int)K, (int)T, (int)H, nullptr, nullptr, nullptr, nullptr, dx, (cudaStream_t)stream);
+}
+
+int smelb_rmsnorm_fwd(const void* x, const void* h_add, const void* w, int w_mode, const void* post_scale,
+                      float post_mul, float eps, int64_t rows, int64_t C, void* s_out, void* y, float* rstd_out,
+                      void* stream) {
+  SMELB_CHECK_ARG(x && y, kErrArg, "rmsnorm_fwd: null pointer");
+  SMELB_CHECK_ARG(w_mode >= 0 && w_mode <= 2, kErrArg, "rmsnorm_fwd: w_mode %d", w_mode);
+  NormArgs a{(const bf16*)x, (const bf16*)h_add, (const bf16*)w, (const bf16*)post_scale, post_mul, w_mode, eps,
+             (long long)rows, (int)C, (bf16*)s_out, (bf16*)y, rstd_out};
+  return rmsnorm_fwd(a, (cudaStream_t)stream);
+}
+
+int smelb_rmsnorm_bwd(const void* dy, const void* x, const void* w, int w_mode, const void* post_scale,
+                      float post_mul, const float* rstd, const void* ds, int64_t rows, int64_t C, void* dx,
+                      void* stream) {
+  SMELB_CHECK_ARG(dy && x && rstd && dx, kErrArg, "rmsnorm_bwd: null pointer");
+  SMELB_CHECK_ARG(w_mode >= 0 && w_mode <= 2, kErrArg, "rmsnorm_bwd: w_mode %d", w_mode);
+  NormBwdArgs a{(const bf16*)dy, (const bf16*)x, (const bf16*)w, (const bf16*)post_scale, post_mul, w_mode, rstd,
+                (const bf16*)ds, (long long)rows, (int)C, (bf16*)dx};
+  return rmsnorm_bwd(a, (cudaStream_t)stream);
 }
 
 int smelb_frozen_experts_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E,

@@ -1,8 +1,10 @@
 """smelb: the SMEL FT MoE expert layer (smel/moe.py, smel/quant.py int4 group-64, smel/lora.py) on B200 (sm_100a).
 
 Drop-in names for the reference modules:
-    smel.moe  -> smelb.moe   (BF16Experts, Int4Experts, LayerExperts, FrozenExpertsFn, route, routed_experts,
-                              mlp_lora, shared_mlp, moe_forward)
+    smel.moe  -> smelb.moe   (BF16Experts, Int4Experts, LayerExperts, FrozenExpertsFn, route, route_gemma4,
+                              routed_experts, mlp_lora, shared_mlp, moe_forward)
+    smel.norm / layer_runner norms -> smelb.norm (rmsnorm, add_rmsnorm); the Gemma 4 MoE block of
+                              layer_runner.py:249-261 -> smelb.moe.moe_block_gemma4
     smel.quant-> smelb.quant (quantize_int4, dequant_int4, dequant_int4_torch, rel_err)
     smel.lora -> smelb.lora  (ExpertsLoRA, MLPLoRA, LayerLoRA, BlockLoRA)
 All compute runs in libsmelb.so (hand-written CUDA for sm_100a) through the C ABI in include/smelb.h.
@@ -10,13 +12,15 @@ All compute runs in libsmelb.so (hand-written CUDA for sm_100a) through the C AB
 from . import _lib
 from ._lib import SmelbError, read_status
 from .lora import BlockLoRA, ExpertsLoRA, LayerLoRA, MLPLoRA
-from .moe import (BF16Experts, FrozenExpertsFn, Int4Experts, LayerExperts, mlp_lora, moe_forward, route,
-                  routed_experts, shared_mlp)
+from .moe import (BF16Experts, FrozenExpertsFn, Int4Experts, LayerExperts, mlp_lora, moe_block_gemma4, moe_forward,
+                  route, route_gemma4, routed_experts, shared_mlp)
+from .norm import add_rmsnorm, rmsnorm
 from .quant import dequant_int4, dequant_int4_torch, quantize_int4, rel_err
 
 __all__ = ["BF16Experts", "BlockLoRA", "ExpertsLoRA", "FrozenExpertsFn", "Int4Experts", "LayerExperts", "LayerLoRA",
-           "MLPLoRA", "SmelbError", "dequant_int4", "dequant_int4_torch", "mlp_lora", "moe_forward", "quantize_int4",
-           "read_status", "rel_err", "route", "routed_experts", "shared_mlp"]
+           "MLPLoRA", "SmelbError", "add_rmsnorm", "dequant_int4", "dequant_int4_torch", "mlp_lora", "moe_block_gemma4",
+           "moe_forward", "quantize_int4", "read_status", "rel_err", "rmsnorm", "route", "route_gemma4",
+           "routed_experts", "shared_mlp"]
 
 
 def load_library():

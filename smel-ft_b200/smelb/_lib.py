@@ -56,6 +56,7 @@ _LAYER_FIELDS = [
     ("gshA_gate", c_vp), ("gshB_gate", c_vp), ("gshA_up", c_vp), ("gshB_up", c_vp), ("gshA_down", c_vp),
     ("gshB_down", c_vp),
     ("dprobs", c_vp), ("fz_gu", c_vp), ("fz_dn", c_vp), ("act_sh", c_i32), ("reserved", c_i32),
+    ("per_expert_scale", c_vp),
 ]
 
 
@@ -80,6 +81,9 @@ SIGNATURES = {
                                        c_vp, c_i64, c_vp]),
     "smelb_gather_rows": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "smelb_combine_fwd": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "smelb_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, ctypes.c_float, ctypes.c_float, c_i64, c_i64, c_vp,
+                                  c_vp, c_vp, c_vp]),
+    "smelb_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, ctypes.c_float, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "smelb_combine_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "smelb_gather_rows_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "smelb_frozen_experts_fwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i32,

@@ -332,6 +332,23 @@ def route(x2d, gate_w, top_k):
     return probs, topv, topi
 
 
+def route_gemma4(h, W, top_k, eps):
+    """Gemma 4 router on the residual stream (moe.py:170-180): the weightless RMSNorm of h times router.scale times
+    H^-0.5 (bf16 steps), router.proj logits, fp32 softmax, top-k renormalised in fp32 and multiplied by
+    router.per_expert_scale of the chosen experts. Returns (probs fp32 [N, E], topv fp32 [N, K], topi int64 [N, K]);
+    differentiable w.r.t. h through topv and probs."""
+    from . import norm
+    h = _bf16(h, "route_gemma4: h")
+    x = norm.router_prologue_gemma4(h, W["router.scale"], eps)
+    proj = W["router.proj.weight"]
+    cfg = _Cfg(_lib.F_ROUTER | _lib.F_TOPV_FP32, x, top_k, proj.shape[0])
+    cfg.topv_dtype = torch.float32
+    cfg.t["w_router"] = _bf16(proj, "route_gemma4: router.proj.weight")
+    cfg.t["per_expert_scale"] = _bf16(W["router.per_expert_scale"], "route_gemma4: router.per_expert_scale")
+    _, probs, topv, topi = _apply(cfg, x)
+    return probs, topv, topi
+
+
 def routed_experts(x2d, topv, topi, ex: LayerExperts, lora=None):
     """Weighted sum of the routed experts for every token; differentiable w.r.t. x2d, topv and the LoRA parameters
     (moe.py:214-252)."""
@@ -393,6 +410,26 @@ def moe_forward(x2d, W, ex: LayerExperts, top_k: int, lora_layer=None, stats=Non
     if stats is not None:
         stats(probs, topv, topi)
     return out
+
+
+def moe_block_gemma4(h, xm, W, ex: LayerExperts, top_k: int, eps: float, act="gelu_tanh", lora_layer=None,
+                     stats=None):
+    """The Gemma 4 MoE block of smel/layer_runner.py:249-261 after the attention residual: the dense MLP (with the
+    layer's "shared" LoRA) on xm and the routed experts on the pre-FFN-2 norm of h run in parallel, each with its
+    post norm, and  h + rmsnorm(m + e)  scaled by layer_scalar. Norms are Gemma's x * rstd * w."""
+    from . import norm
+    lora_sh = lora_layer.shared if lora_layer is not None else None
+    lora_ex = lora_layer.experts if lora_layer is not None else None
+    m = mlp_lora(xm, W["mlp.gate_proj.weight"], W["mlp.up_proj.weight"], W["mlp.down_proj.weight"], lora_sh, act,
+                 W.get("mlp.gate_up_proj.weight"))
+    m = norm.rmsnorm(m, W["post_feedforward_layernorm_1.weight"], eps, False)
+    probs, topv, topi = route_gemma4(h, W, top_k, eps)
+    if stats is not None:
+        stats(probs, topv, topi)
+    e = routed_experts(norm.rmsnorm(h, W["pre_feedforward_layernorm_2.weight"], eps, False), topv, topi, ex, lora_ex)
+    e = norm.rmsnorm(e, W["post_feedforward_layernorm_2.weight"], eps, False)
+    _, y = norm.add_rmsnorm(m, e, W["post_feedforward_layernorm.weight"], eps, False)
+    return (h + y) * W["layer_scalar"]
 
 
 class FrozenExpertsFn(torch.autograd.Function):

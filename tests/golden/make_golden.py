@@ -11,6 +11,9 @@ Outputs (torch.save dicts of CPU tensors):
   moe_c1_bf16.pt  the same block run by the reference in bf16 on the CPU
   frozen_gelu.pt  FrozenExpertsFn forward/backward with GELU-tanh, uneven counts and an empty expert
                   (the case of the reference test tests/test_gemma4.py:153-169)
+  gemma_block.pt  the Gemma 4 MoE block of smel/layer_runner.py:252-261 (dense GeGLU MLP with LoRA, route_gemma4,
+                  int4 + LoRA routed experts, the four Gemma norms, layer_scalar) in fp32: inputs, outputs, routing,
+                  dh, dxm and all LoRA gradients
 The test-suite never imports the reference; it only reads these files.
 """
 import argparse
@@ -138,6 +141,48 @@ def main():
     yf.backward(gyf)
     torch.save({"gu": fgu, "dn": fdn, "counts": torch.tensor(counts), "x": xf.detach(), "gy": gyf, "y": yf.detach(),
                 "dx": xf.grad.detach()}, os.path.join(HERE, "frozen_gelu.pt"))
+
+    # ------------------------------------------------------------------ Gemma 4 MoE block (layer_runner.py:252-261)
+    from smel.layer_runner import rmsnorm as ref_rmsnorm
+    from smel.moe import mlp_lora, route_gemma4, routed_experts
+    H, E, K, I, S, T, r, alpha, eps = 64, 8, 2, 64, 128, 96, 8, 16.0, 1e-6
+    sel = [2, 5]
+    g = torch.Generator().manual_seed(31)
+    rn = lambda *sh, std=1.0: torch.randn(*sh, generator=g) * std  # noqa: E731
+    W = {"router.scale": 1.0 + rn(H, std=0.2), "router.proj.weight": rn(E, H, std=0.3),
+         "router.per_expert_scale": 0.5 + torch.rand(E, generator=g),
+         "mlp.gate_proj.weight": rn(S, H, std=0.05), "mlp.up_proj.weight": rn(S, H, std=0.05),
+         "mlp.down_proj.weight": rn(H, S, std=0.05),
+         "post_feedforward_layernorm_1.weight": 1.0 + rn(H, std=0.1),
+         "pre_feedforward_layernorm_2.weight": 1.0 + rn(H, std=0.1),
+         "post_feedforward_layernorm_2.weight": 1.0 + rn(H, std=0.1),
+         "post_feedforward_layernorm.weight": 1.0 + rn(H, std=0.1), "layer_scalar": torch.tensor([0.7])}
+    gu, dn = rn(E, 2 * I, H, std=0.05), rn(E, H, I, std=0.05)
+    qgu, qdn = quantize_int4(gu, 64), quantize_int4(dn, 64)
+    ex = LayerExperts(Int4Experts(qgu, qdn, dtype=torch.float32), sel, gu[sel].clone(), dn[sel].clone(),
+                      act="gelu_tanh")
+    lex_t, lsh_t = lora_tensors(H, I, S, len(sel), r, alpha, g)
+    lex_m, lsh_m = ExpertsLoRA(sel, H, I, r, alpha), MLPLoRA(H, S, r, alpha)
+    with torch.no_grad():
+        for n in ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down"):
+            getattr(lex_m, n).copy_(lex_t[n])
+            getattr(lsh_m, n).copy_(lsh_t[n])
+    h, xm, gy = rn(T, H).requires_grad_(True), rn(T, H).requires_grad_(True), rn(T, H)
+    m = mlp_lora(xm, W["mlp.gate_proj.weight"], W["mlp.up_proj.weight"], W["mlp.down_proj.weight"], lsh_m,
+                 "gelu_tanh", None)
+    m = ref_rmsnorm(m, W["post_feedforward_layernorm_1.weight"], eps, False)
+    probs, topv, topi = route_gemma4(h, W, K, eps)
+    e = routed_experts(ref_rmsnorm(h, W["pre_feedforward_layernorm_2.weight"], eps, False), topv, topi, ex, lex_m)
+    e = ref_rmsnorm(e, W["post_feedforward_layernorm_2.weight"], eps, False)
+    out = (h + ref_rmsnorm(m + e, W["post_feedforward_layernorm.weight"], eps, False)) * W["layer_scalar"]
+    out.backward(gy)
+    torch.save({"cfg": dict(H=H, E=E, K=K, I=I, S=S, T=T, r=r, alpha=alpha, eps=eps, sel=sel, act="gelu_tanh"),
+                "W": W, "gu": gu, "dn": dn, "gu_q": qgu["q"], "gu_scale": qgu["scale"], "gu_zero": qgu["zero"],
+                "dn_q": qdn["q"], "dn_scale": qdn["scale"], "dn_zero": qdn["zero"], "lora_ex": lex_t,
+                "lora_sh": lsh_t, "h": h.detach(), "xm": xm.detach(), "gy": gy, "out": out.detach(),
+                "probs": probs.detach(), "topv": topv.detach(), "topi": topi, "dh": h.grad, "dxm": xm.grad,
+                "g_lora_ex": {n: getattr(lex_m, n).grad for n in lex_t},
+                "g_lora_sh": {n: getattr(lsh_m, n).grad for n in lsh_t}}, os.path.join(HERE, "gemma_block.pt"))
     print("golden fixtures written to", HERE)
 
 

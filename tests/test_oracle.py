@@ -111,3 +111,45 @@ def test_frozen_experts_gelu_backward_matches_reference(golden):
     manual = O.frozen_experts_backward(d["x"].double(), d["gy"].double(), d["counts"].tolist(), d["gu"].double(),
                                        d["dn"].double(), "gelu_tanh")
     assert O.rel_err(manual, d["dx"]) < 1e-5
+
+
+def _gemma_oracle(d, dt=torch.float32, topi=None, h=None, xm=None):
+    c = d["cfg"]
+    gu = O.dequant_int4(d["gu_q"], d["gu_scale"], d["gu_zero"], dt)
+    dn = O.dequant_int4(d["dn_q"], d["dn_scale"], d["dn_zero"], dt)
+    s = c["alpha"] / c["r"]
+    lex = {k: v.to(dt).clone().requires_grad_(True) for k, v in d["lora_ex"].items()}
+    lsh = {k: v.to(dt).clone().requires_grad_(True) for k, v in d["lora_sh"].items()}
+    h = (d["h"] if h is None else h).to(dt).clone().requires_grad_(True)
+    xm = (d["xm"] if xm is None else xm).to(dt).clone().requires_grad_(True)
+    W = {k: v.to(dt) for k, v in d["W"].items()}
+    out, probs, topv, topi = O.moe_block_gemma4(h, xm, W, gu, dn, c["K"], c["eps"], c["sel"], d["gu"][c["sel"]].to(dt),
+                                                d["dn"][c["sel"]].to(dt), {**lex, "scale": s}, {**lsh, "scale": s},
+                                                c["act"], topi)
+    return out, probs, topv, topi, h, xm, lex, lsh
+
+
+def test_gemma_block_matches_reference_fp32(golden):
+    """route_gemma4 + the Gemma 4 MoE block (smel/layer_runner.py:252-261) against the reference's own fp32 run."""
+    d = golden("gemma_block.pt")
+    out, probs, topv, topi, h, xm, lex, lsh = _gemma_oracle(d)
+    assert torch.equal(topi, d["topi"])
+    assert O.rel_err(probs, d["probs"]) < 1e-6 and O.rel_err(topv, d["topv"]) < 1e-6
+    assert O.rel_err(out, d["out"]) < 1e-5
+    out.backward(d["gy"])
+    assert O.rel_err(h.grad, d["dh"]) < 1e-5 and O.rel_err(xm.grad, d["dxm"]) < 1e-5
+    for n in lex:
+        assert O.rel_err(lex[n].grad, d["g_lora_ex"][n]) < 1e-5, n
+        assert O.rel_err(lsh[n].grad, d["g_lora_sh"][n]) < 1e-5, n
+
+
+def test_rmsnorm_oracle_forms():
+    """The three weight modes of smel/layer_runner.py:110-121 and the fused add of :124-130."""
+    g = torch.Generator().manual_seed(3)
+    x, h, w = torch.randn(7, 64, generator=g), torch.randn(7, 64, generator=g), torch.randn(64, generator=g)
+    rstd = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+    assert torch.allclose(O.rmsnorm(x, w, 1e-6, True), x * rstd * (1 + w), atol=1e-6)
+    assert torch.allclose(O.rmsnorm(x, w, 1e-6, False), x * rstd * w, atol=1e-6)
+    assert torch.allclose(O.rmsnorm(x, None, 1e-6, False), x * rstd, atol=1e-6)
+    s, y = O.add_rmsnorm(h, x, w, 1e-6, False)
+    assert torch.equal(s, h + x) and torch.allclose(y, O.rmsnorm(h + x, w, 1e-6, False))
