@@ -319,6 +319,65 @@ def run_ours(args, world, rank, local):
     return res
 
 
+# ------------------------------------------------------------------------------------------ config 4 sweep
+def run_sweep(args, local):
+    """Config 4: the Qwen3.6 layer shape, forward only (no grad), all 256 experts frozen int4 group-64, at 1, 16, 128,
+    1024 and 16384 tokens per call, routing uniform (router N(0, 0.02)) or Zipf s=1.2 (tau = 1). One JSON line per
+    point with the achieved HBM bandwidth and tensor throughput over the algorithmic bytes and FLOPs of the call.
+    Each call is a CUDA-graph replay timed alone between writes of a 256 MB buffer (L2 flushed)."""
+    import smelb
+    from smelb.synth import int4_bank_bytes_per_expert, qwen_layer
+    dev = torch.device("cuda", local)
+    H, E, K, I, S = 2048, 256, 8, 512, 512
+    Ts = [1, 16, 128, 1024, 16384]
+    pk, pk_kind = peaks()
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+    bank_b = int4_bank_bytes_per_expert(H, I)
+    for routing in ("uniform", "zipf s=1.2"):
+        L = qwen_layer(T=max(Ts), H=H, E=E, K=K, I=I, S=S, n_sel=0, with_lora=False, seed=4, device=dev,
+                       uniform=routing == "uniform", zipf_s=1.2, tau=1.0)
+        W, ex = L["W"], L["ex"]
+        for T in Ts:
+            x = L["x"][:T].contiguous()
+            rec = {}
+            with torch.no_grad():
+                smelb.moe_forward(x, W, ex, K, None, stats=lambda p, v, i: rec.update(i=i))
+            touched = int(torch.unique(rec["i"]).numel())
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side), torch.no_grad():
+                for _ in range(3):
+                    smelb.moe_forward(x, W, ex, K, None)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side), torch.no_grad():
+                smelb.moe_forward(x, W, ex, K, None)
+            torch.cuda.synchronize()
+            ms = []
+            for _ in range(max(args.steps, 5)):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                ms.append(e0.elapsed_time(e1))
+            t = statistics.median(ms) / 1e3
+            nbytes = touched * bank_b + 3 * S * H * 2 + E * H * 2 + T * H * 2 * 2
+            flops = T * (2 * K * 3 * H * I + 2 * 3 * H * S + 2 * H * E)
+            gbs, tfl = nbytes / t / 1e9, flops / t / 1e12
+            bound = "hbm" if nbytes / (pk["hbm_gbs"] * 1e9) > flops / (pk["bf16_tflops"] * 1e12) else "tensor"
+            print(json.dumps({"sweep": "config 4 (forward only, all experts int4)", "tokens": T, "routing": routing,
+                              "touched_experts": touched, "ms_per_call": round(t * 1e3, 4),
+                              "tokens_per_s": round(T / t, 1), "algorithmic_bytes": nbytes, "hbm_gbs": round(gbs, 1),
+                              "hbm_frac": round(gbs / pk["hbm_gbs"], 4), "tflops": round(tfl, 2),
+                              "tc_frac": round(tfl / pk["bf16_tflops"], 4), "bound": bound,
+                              "peaks": f"{pk_kind}: {pk['hbm_gbs']} GB/s, {pk['bf16_tflops']} TFLOP/s",
+                              "timing": "median of graph replays, each after an L2 flush"}), flush=True)
+            del g
+            assert smelb.read_status() == 0
+
+
 # ------------------------------------------------------------------------------------------ reference arm
 def run_reference(args, world, rank):
     """The reference's CPU torch path (restated in oracle/cpu_step.py) on the host cores, same metric and config."""
@@ -373,10 +432,15 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=4092, help="tokens per reference-arm step")
     ap.add_argument("--ref-budget-s", type=float, default=150.0, help="stop the reference arm after this long")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="config 4 token-count sweep (one JSON line per point)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
-        if args.impl == "reference":
+        if args.sweep:
+            if rank == 0:
+                run_sweep(args, local)
+            res = None
+        elif args.impl == "reference":
             res = run_reference(args, world, rank)
         else:
             res = run_ours(args, world, rank, local)

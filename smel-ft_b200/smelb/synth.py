@@ -46,7 +46,7 @@ def _share_of_top(logits, ranked, n_top, k):
 
 
 def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=32.0, zipf_s=1.1, share=0.5,
-               seed=0, device="cuda", mu=4.0, uniform=False, with_lora=True, keep_bf16=False):
+               seed=0, device="cuda", mu=4.0, uniform=False, with_lora=True, keep_bf16=False, tau=None):
     """Build one synthetic layer. Returns a dict with x [T, H] bf16, W (router / shared tensors, bf16), ex
     (LayerExperts), lora (LayerLoRA or None), meta, and with keep_bf16 the bank before quantization (bank_bf16)."""
     dev = torch.device(device)
@@ -66,7 +66,7 @@ def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=3
     gu = rnd(E, 2 * I, H).bfloat16()
     dn = rnd(E, H, I).bfloat16()
     perm = torch.randperm(E, generator=torch.Generator().manual_seed(seed + 1))  # perm[0] = rank-1 expert
-    tau = 0.0
+    tau = None if tau is None else float(tau)  # fixed Zipf temperature, or bisected below
     meta = {"seed": seed, "T": T, "H": H, "E": E, "K": K, "I": I, "S": S, "n_sel": n_sel, "r": r, "alpha": alpha}
     if not uniform:
         u = torch.randn(H, generator=g, device=dev)
@@ -75,7 +75,7 @@ def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=3
         rank[perm.to(dev)] = torch.arange(1, E + 1, device=dev, dtype=torch.float32)
         xs = x + mu * u
         lo_t, hi_t = 0.0, 4.0
-        for _ in range(24):  # bisection on tau for the target top-12 share
+        for _ in range(24 if tau is None else 0):  # bisection on tau for the target top-12 share
             tau = 0.5 * (lo_t + hi_t)
             b = -zipf_s * tau * torch.log(rank)
             logits = (xs.bfloat16() @ (wg + (b / mu)[:, None] * u[None]).bfloat16().t())
@@ -84,10 +84,12 @@ def qwen_layer(T=4092, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=3
                 lo_t = tau
             else:
                 hi_t = tau
+        if tau is None:
+            tau = 0.5 * (lo_t + hi_t)
         b = -zipf_s * tau * torch.log(rank)
         wg = wg + (b / mu)[:, None] * u[None]
         x = xs
-        meta.update(tau=tau, share=_share_of_top(x.bfloat16() @ wg.bfloat16().t(), perm.to(dev), n_sel, K),
+        meta.update(tau=float(tau), share=_share_of_top(x.bfloat16() @ wg.bfloat16().t(), perm.to(dev), max(n_sel, 1), K),
                     zipf_s=zipf_s, mu=mu)
     W["mlp.gate.weight"] = wg.bfloat16()
     sel = perm[:n_sel].tolist() if n_sel else []
