@@ -13,7 +13,9 @@ constexpr int kOffQ = kOffB + kStages * kBStageBytes;
 constexpr int kOffSZ = kOffQ + kQStages * kQStageBytes;
 constexpr int kOffTab = kOffSZ + kQStages * kSZStageBytes;
 constexpr int kTabInts = 3 * kMaxGroups + (kMaxGroups + kMaxProblems) + (kMaxProblems + 1) + kMaxProblems;
-constexpr int kOffBar = (kOffTab + kTabInts * 4 + 7) & ~7;
+constexpr int kTileTab = 128;  // decoded tiles of this CTA kept in shared memory (later ones are decoded on the fly)
+constexpr int kOffTiles = (kOffTab + kTabInts * 4 + 15) & ~15;
+constexpr int kOffBar = kOffTiles + kTileTab * 32;
 constexpr int kNumBars = 2 * kStages + 2 * kQStages + 5;
 constexpr int kOffTmem = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmem + 16;
@@ -21,9 +23,10 @@ constexpr int kSmemAlloc = kSmemBytes + 1024;  // slack for 1024-byte alignment 
 static_assert(kSmemAlloc <= 232448, "shared memory budget exceeded");
 static_assert(kThreads <= 1024, "too many threads");
 
-struct TileInfo {
+struct alignas(16) TileInfo {
   int p, g, widx, mt, m0, n0, n_valid, nkb;
 };
+static_assert(sizeof(TileInfo) == 32, "tile table entry");
 
 struct Tables {
   int* gcnt;    // [kMaxGroups] tokens of each group
@@ -74,6 +77,13 @@ __device__ __forceinline__ TileInfo decode_tile(const LaunchArgs& args, const Ta
   }
   ti.widx = T.gw[gb + ti.g];
   return ti;
+}
+
+// The i-th tile of this CTA (global tile t = blockIdx.x + i * gridDim.x): decoded once in the prologue for the first
+// kTileTab tiles, so the warp roles do not each repeat the search.
+__device__ __forceinline__ TileInfo tile_at(const LaunchArgs& args, const Tables& T, const TileInfo* tiles, int i, int t) {
+  if (i < kTileTab) return tiles[i];
+  return decode_tile(args, T, t);
 }
 
 // ------------------------------------------------------------------------------------------ int4 dequant helpers
@@ -231,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_drain = acc_full + 4;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  TileInfo* tiles = reinterpret_cast<TileInfo*>(smem + kOffTiles);
 
   // ---------------------------------------------------------------- prologue: barriers, TMEM, tile tables
   if (warp == kWarpTmaB) {
@@ -317,14 +328,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
   const int total_tiles = T.tstart[args.nprob];
+  {
+    const int mine = total_tiles > (int)blockIdx.x ? (total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    for (int i = threadIdx.x; i < min(mine, kTileTab); i += blockDim.x)
+      tiles[i] = decode_tile(args, T, (int)blockIdx.x + i * (int)gridDim.x);
+  }
+  __syncthreads();
 
   if (warp == kWarpTmaB) {
     // ============================================================================ TMA: token ring (one thread)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(args, T, t);
+      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+        const TileInfo ti = tile_at(args, T, tiles, i, t);
         const Problem& P = args.p[ti.p];
         const bool tokk = P.mode == kTokK;
         const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
@@ -363,8 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(args, T, t);
+      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+        const TileInfo ti = tile_at(args, T, tiles, i, t);
         const Problem& P = args.p[ti.p];
         const bool glu = P.epi == kEpiGlu;
         const bool int4 = is_int4(P);
@@ -420,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     if (lane == 0) {
       uint32_t qi = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileInfo ti = decode_tile(args, T, t);
+      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+        const TileInfo ti = tile_at(args, T, tiles, i, t);
         const Problem& P = args.p[ti.p];
         if (!is_int4(P)) continue;
         const bool glu = P.epi == kEpiGlu;
@@ -455,66 +472,87 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     }
   } else if (warp == kWarpMma) {
     // ============================================================================ MMA issuer (whole warp)
-    // The loop runs warp-uniform and each tcgen05 instruction goes out through one elected lane.
+    // The loop runs warp-uniform and each tcgen05 instruction goes out through one elected lane. Per tile the
+    // operand descriptors of ring stage 0 are built once; a stage adds its byte offset to the start-address field
+    // (shared-memory addresses >> 4 stay below 2^14, so the field never carries). Per k-block: one wait, one fence,
+    // four MMAs and the commit that frees the stage. The LoRA extension (always the tile's last k-block) has its own
+    // step after the main loop.
     uint32_t it = 0, acc_it = 0;
     bool ok = true, issued = false;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = decode_tile(args, T, t);
+    const uint32_t tmem_u = __shfl_sync(0xffffffffu, tmem_base, 0);
+    const uint64_t descA_k = make_sdesc(smem_base + kOffA, 16, 1024), descA_mn = make_sdesc(smem_base + kOffA, 8192, 1024);
+    const uint64_t descB_k = make_sdesc(smem_base + kOffB, 16, 1024), descB_mn = make_sdesc(smem_base + kOffB, 8192, 1024);
+    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
       if (ti.nkb == 0) continue;
       const Problem& P = args.p[ti.p];
-      // per-tile constants in registers (the loop below must not touch parameter memory)
       const bool tokk = P.mode == kTokK;
-      const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+      const bool has_ext = !tokk && P.has_ext;
+      const int nmain = has_ext ? ti.nkb - 1 : ti.nkb;
       const bool a_tm = P.mode == kTokN && P.a_kind == kAInt4K;  // weight tile in tensor memory
-      const uint32_t a_mn = (tokk || P.a_kind == kAInt4MN || P.a_kind == kABf16MN) ? 1u : 0u;
-      const uint32_t b_mn = tokk ? 1u : 0u;
-      const int nkb = ti.nkb;
+      const bool a_mn = tokk || P.a_kind == kAInt4MN || P.a_kind == kABf16MN;
+      // MN-major B (kTokK) must span whole 64-element swizzle atoms; K-major B needs multiples of 16
+      const uint32_t n_mma = tokk ? (uint32_t)((ti.n_valid + 63) & ~63) : (uint32_t)((ti.n_valid + 15) & ~15);
+      const uint32_t idesc = make_idesc_bf16(n_mma, (a_tm || !a_mn) ? 0u : 1u, tokk ? 1u : 0u);
+      const uint64_t b0 = tokk ? descB_mn : descB_k;
+      const uint32_t bstep = tokk ? (2048 >> 4) : (32 >> 4);
+      // A: K-major steps 32 B per K=16 inside the swizzle atom, MN-major steps two 8-row k-groups (2048 B)
+      const uint64_t a0 = a_mn ? descA_mn : descA_k;
+      const uint32_t astep = a_mn ? (2048 >> 4) : (32 >> 4);
       const int acc = acc_it & 1;
       if (!mbar_wait_warp(&acc_empty[acc], ((acc_it >> 1) & 1) ^ 1, err, kDevErrWaitAccEmpty, t)) break;
       tc_fence_after();
-      // MN-major B (kTokK) must span whole 64-element swizzle atoms; K-major B needs multiples of 16
-      const uint32_t n_mma = tokk ? (uint32_t)((ti.n_valid + 63) & ~63) : (uint32_t)((ti.n_valid + 15) & ~15);
-      const uint32_t idesc_main = make_idesc_bf16(n_mma, a_tm ? 0u : a_mn, b_mn);
-      const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
-      const uint32_t d_tmem = tmem_base + acc * kTmemAcc;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (!mbar_wait_warp(&full[s], ph, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
-        tc_fence_after();
-        const bool ext = kb == ext_kb;
-        const uint32_t sA = smem_base + kOffA + s * kAStageBytes;
-        const uint32_t sB = smem_base + kOffB + s * kBStageBytes;
-        const uint64_t b0 = b_mn ? make_sdesc(sB, 8192, 1024) : make_sdesc(sB, 16, 1024);
-        const uint32_t bstep = b_mn ? (2048 >> 4) : (32 >> 4);
-        // operands are computed warp-uniform; one elected lane issues the k-block's four MMAs and the commit that
-        // frees the stage
-        if (a_tm && !ext) {
-          const uint32_t a_tmem = tmem_base + kTmemA0 + s * 32;
+      issued = true;  // from here on MMAs may be in flight: drain them before TMEM is released, also on errors
+      const uint32_t d_tmem = tmem_u + acc * kTmemAcc;
+      if (a_tm) {
+        for (int kb = 0; kb < nmain; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait_warp(&full[s], (it / kStages) & 1, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_tmem = tmem_u + kTmemA0 + s * 32;
+          const uint64_t bs = b0 + (uint64_t)(s * (kBStageBytes >> 4));
           if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16_ts(d_tmem, a_tmem + kk * 8, b0 + (uint64_t)(kk * bstep), idesc_main, (kb | kk) != 0 ? 1u : 0u);
+              umma_f16_ts(d_tmem, a_tmem + kk * 8, bs + (uint64_t)(kk * bstep), idesc, (kb | kk) != 0 ? 1u : 0u);
             umma_commit(&empty[s]);
           }
-        } else {
-          // A: K-major steps 32 B per K=16 inside the swizzle atom, MN-major steps two 8-row k-groups (2048 B)
-          const bool amn = a_mn && !ext;
-          const uint32_t idesc = ext ? idesc_ext : idesc_main;
-          const uint64_t a0 = amn ? make_sdesc(sA, 8192, 1024) : make_sdesc(sA, 16, 1024);
-          const uint32_t astep = amn ? (2048 >> 4) : (32 >> 4);
-          if (elect_one()) {
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_f16(d_tmem, a0 + (uint64_t)(kk * astep), b0 + (uint64_t)(kk * bstep), idesc,
-                       (kb | kk) != 0 ? 1u : 0u);
-            umma_commit(&empty[s]);
-          }
+          __syncwarp();
         }
-        __syncwarp();
-        issued = true;
+      } else {
+        for (int kb = 0; kb < nmain; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait_warp(&full[s], (it / kStages) & 1, err, kDevErrWaitFull, t, kb)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t as = a0 + (uint64_t)(s * (kAStageBytes >> 4));
+          const uint64_t bs = b0 + (uint64_t)(s * (kBStageBytes >> 4));
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_f16(d_tmem, as + (uint64_t)(kk * astep), bs + (uint64_t)(kk * bstep), idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+          __syncwarp();
+        }
       }
       if (!ok) break;
+      if (has_ext) {  // both operands K-major from the ring
+        const int s = it % kStages;
+        if (!mbar_wait_warp(&full[s], (it / kStages) & 1, err, kDevErrWaitFull, t, nmain)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t idesc_ext = make_idesc_bf16(n_mma, 0u, 0u);
+        const uint64_t as = descA_k + (uint64_t)(s * (kAStageBytes >> 4));
+        const uint64_t bs = descB_k + (uint64_t)(s * (kBStageBytes >> 4));
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(d_tmem, as + (uint64_t)(kk * (32 >> 4)), bs + (uint64_t)(kk * (32 >> 4)), idesc_ext,
+                     (nmain | kk) != 0 ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        __syncwarp();
+        ++it;
+      }
       if (elect_one()) umma_commit(&acc_full[acc]);
       __syncwarp();
       ++acc_it;
@@ -526,64 +564,62 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     }
   } else if (warp < kWarpEpi0) {
     // ============================================================================ int4 dequant (two groups)
+    // Group grp owns the ring slots of parity grp and walks only its own k-blocks of each tile. Every dequant warp
+    // takes part in every int4 staging stage once: it waits for the stage with its first owned k-block there and
+    // releases it after its last one; a stage where the group owns nothing (a one-k-block last stage) is waited for
+    // and released on its own.
     const int grp = (warp - kWarpDeq0) / kNumDeqWarps;
     const int pt = ((warp - kWarpDeq0) % kNumDeqWarps) * 32 + lane;  // 0..127 within the group
     const int lq = warp & 3;                                         // TMEM lane quarter this warp may access
     const int trow = lq * 32 + lane;                                 // weight-tile row this thread stores to TMEM
+    const uint32_t tmem_row = tmem_base + ((uint32_t)(lq * 32) << 16) + kTmemA0;
+    static_assert(kNumDeqGroups == 2, "k-block ownership by ring-index parity");
     uint32_t it = 0, qi = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileInfo ti = decode_tile(args, T, t);
+    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
       const Problem& P = args.p[ti.p];
-      const bool int4 = is_int4(P);
-      const bool glu = P.epi == kEpiGlu;
+      const int nkb = ti.nkb;
+      const uint32_t it0 = it;
+      it += nkb;
+      const int kb0 = (int)((it0 & 1u) != (uint32_t)grp);  // first k-block of this tile owned by the group
+      const int nkq = is_int4(P) ? P.K / kBK : 0;          // int4 k-blocks of the tile (staged nibbles)
       const bool kmajor = P.a_kind == kAInt4K;
-      const int nkq = int4 ? P.K / kBK : 0;  // int4 k-blocks of the tile
-      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-        const int s = it % kStages;
-        const bool mine = (int)(it % kNumDeqGroups) == grp;  // ring slots of one parity belong to one group
-        const bool q4 = kb < nkq;                            // an int4 k-block (staged nibbles)
-        const int j = kb % kQSub;
-        const uint32_t qstage = qi + kb / kQSub;
-        const int qs = qstage % kQStages;
-        const int subs = min(kQSub, nkq - (kb / kQSub) * kQSub);  // k-blocks of this staging stage
-        const uint32_t it0 = it - j;                               // ring index of the stage's first k-block
-        // the first and last k-block of the stage this group owns (-1: none, a 1-k-block stage of the other group)
-        const int jfirst = ((int)(it0 % kNumDeqGroups) == grp) ? 0 : (subs > 1 ? 1 : -1);
-        const int jlast = jfirst < 0 ? -1 : jfirst + 2 * ((subs - 1 - jfirst) / 2);
-        if (q4 && j == 0 && jfirst < 0) {
-          // take part in the stage's round without owning any of its k-blocks
-          if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&q_empty[qs]);
-        }
-        if (!mine) continue;
-        if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
-        if (q4) {
-          if (j == jfirst)
+      // K-major: weight row trow -> TMEM lane trow, 64 bf16 in columns kTmemA0 + 32 s .. +31; the nibble rows are
+      // staged with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)).
+      // MN-major: k-row kr, half `half` of the 128 output features -> one 128-byte row of the swizzled smem tile.
+      const int sr = P.epi == kEpiGlu ? glu_stage_row(trow) : trow;
+      const int kr = pt >> 1, half = pt & 1;
+      const int q_off = kmajor ? sr * 128 : kr * 64 + half * 32;                 // + j * 64 * 64 for MN-major
+      const int sz_off = kmajor ? (sr >> 6) * 256 + (sr & 63) : half * 256 + kr;  // + j * 64
+      const int swz = kmajor ? (sr & 7) : 0;
+      for (int kb = kb0; kb < nkb; kb += 2) {
+        const uint32_t r = it0 + kb;
+        const int s = r % kStages;
+        if (!mbar_wait(&empty[s], ((r / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
+        if (kb < nkq) {
+          const int kq = kb / kQSub, j = kb % kQSub;
+          const uint32_t qstage = qi + kq;
+          const int qs = qstage % kQStages;
+          const int subs = min(kQSub, nkq - kq * kQSub);
+          const int jf = j & 1;                               // the group's first k-block in this stage
+          const int jl = jf + 2 * ((subs - 1 - jf) >> 1);     // and its last
+          if (j == jf)
             if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
-          uint8_t* sA = smem + kOffA + s * kAStageBytes;
-          const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes;
-          const uint32_t* sSZ = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes);
-          // K-major: weight row trow -> TMEM lane trow, 64 bf16 in columns kTmemA0 + 32 s .. +31; the nibble rows
-          // are staged with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)).
-          // MN-major: k-row kr, half `half` of the 128 output features -> one 128-byte row of the swizzled smem tile.
-          const int sr = glu ? glu_stage_row(trow) : trow;
-          const int kr = pt >> 1, half = pt & 1;
-          const uint8_t* src = kmajor ? sQ + sr * 128 : sQ + (j * 64 + kr) * 64 + half * 32;
-          const int c0 = kmajor ? 2 * j : 0;
-          const int swz = kmajor ? (sr & 7) : 0;
-          const uint32_t sz = kmajor ? sSZ[(sr >> 6) * 256 + j * 64 + (sr & 63)] : sSZ[half * 256 + j * 64 + kr];
+          const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes + q_off + (kmajor ? 0 : j * 64 * 64);
+          const uint32_t sz = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes)[sz_off + j * 64];
           uint32_t o[32];
-          dq64(src, c0, swz, sz, o);
+          dq64(sQ, kmajor ? 2 * j : 0, swz, sz, o);
+          __syncwarp();
+          if (lane == 0 && j == jl) mbar_arrive(&q_empty[qs]);  // the staged nibbles of this stage are consumed
           if (kmajor) {
             tc_fence_after();  // the MMAs that read this TMEM stage completed (empty wait above)
-            __syncwarp();      // tcgen05.st is warp-collective: reconverge after the per-row dequant branch
-            tmem_st32(tmem_base + ((uint32_t)(lq * 32) << 16) + kTmemA0 + s * 32, o);
+            __syncwarp();      // tcgen05.st is warp-collective
+            tmem_st32(tmem_row + s * 32, o);
             tmem_st_wait();
             tc_fence_before();
           } else {
-            uint8_t* dst = sA + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
+            uint8_t* dst = smem + kOffA + s * kAStageBytes + half * 8192 + (kr >> 3) * 1024 + (kr & 7) * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
               *reinterpret_cast<uint4*>(dst + ((c ^ (kr & 7)) << 4)) =
@@ -592,10 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           }
         }
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates every round
-          if (q4 && j == jlast) mbar_arrive(&q_empty[qs]);
-        }
+        if (lane == 0) mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates
+      }
+      if (!ok) break;
+      if (nkq % kQSub == 1 && ((nkq - 1) & 1) != kb0) {
+        // a one-k-block last stage owned by the other group: take part in its round
+        const uint32_t qstage = qi + nkq / kQSub;
+        const int qs = qstage % kQStages;
+        if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, nkq - 1)) { ok = false; break; }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_empty[qs]);
       }
       qi += (nkq + kQSub - 1) / kQSub;
     }
@@ -605,8 +647,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     const int row = q * 32 + lane;              // accumulator row (A row) owned by this thread
     const int sub = (warp - kWarpEpi0) >> 2;    // which of the quarter's kEpiSubs warps: takes chunks sub, sub + kEpiSubs, ...
     uint32_t acc_it = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(args, T, t);
+    for (int t = blockIdx.x, i = 0; t < total_tiles; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
       const Problem& P = args.p[ti.p];
       if (ti.nkb == 0) {
         // kTokK group without tokens: its gradient block is zero
