@@ -57,6 +57,13 @@ int smelb_read_status_detail(int device, int* words, int reset);
 int smelb_int4_dequant(const void* q, const void* scale, const void* zero, void* out, int64_t rows, int64_t k,
                        int64_t groups, int out_fp32, void* stream);
 
+/* smel/quant.py:14-44 quantize_int4 with group = 64: w [rows, k] (bf16, or fp32 when w_fp32 != 0) -> q uint8
+ * [rows, k/2] (low nibble = even column), scale / zero bf16 [rows, k/64]. Per group the [min, max] range is shrunk
+ * towards its center by each of the n_clip factors in `clip` (host array, 1..8 entries, the reference's
+ * clip_search) and the candidate with the smallest squared error is kept (the earlier one on ties). k % 64 == 0. */
+int smelb_int4_quantize(const void* w, int w_fp32, int64_t rows, int64_t k, const float* clip, int n_clip, void* q,
+                        void* scale, void* zero, void* stream);
+
 /* smel/moe.py:35-55 Int4Experts: builds the (scale | zero << 16) uint32 pairs transposed to [nw, groups, rows],
  * the layout the fused expert GEMMs stage per k-block. scale/zero bf16 [nw, rows, groups]. */
 int smelb_int4_pack_sz(const void* scale, const void* zero, uint32_t* sz_t, int64_t nw, int64_t rows,

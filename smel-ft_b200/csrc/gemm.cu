@@ -456,14 +456,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           uint64_t* fb = &q_full[s];
           mbar_arrive_expect_tx(fb, kQStageBytes + kSZStageBytes);
           if (kmajor) {
-            tma_load_2d(sQ, mQ, kq * 128, qrow0 + r0, fb);
-            tma_load_2d(sQ + 8192, mQ, kq * 128, qrow0 + r1, fb);
+            tma_load_2d(sQ, mQ, kq * kQRowBytes, qrow0 + r0, fb);
+            tma_load_2d(sQ + 64 * kQRowBytes, mQ, kq * kQRowBytes, qrow0 + r1, fb);
             tma_load_2d(sSZ, mSZ, r0, grow0 + kq * kQSub, fb);
-            tma_load_2d(sSZ + 1024, mSZ, r1, grow0 + kq * kQSub, fb);
+            tma_load_2d(sSZ + kSZStageBytes / 2, mSZ, r1, grow0 + kq * kQSub, fb);
           } else {
             tma_load_2d(sQ, mQ, ti.m0 / 2, qrow0 + kq * kQSub * kBK, fb);
             tma_load_2d(sSZ, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64, fb);
-            tma_load_2d(sSZ + 1024, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64 + 1, fb);
+            tma_load_2d(sSZ + kSZStageBytes / 2, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64 + 1, fb);
           }
         }
       }
@@ -586,13 +586,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int nkq = is_int4(P) ? P.K / kBK : 0;          // int4 k-blocks of the tile (staged nibbles)
       const bool kmajor = P.a_kind == kAInt4K;
       // K-major: weight row trow -> TMEM lane trow, 64 bf16 in columns kTmemA0 + 32 s .. +31; the nibble rows are
-      // staged with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)).
+      // staged swizzled (16-byte chunk c of row r at chunk c ^ qswz(r)).
       // MN-major: k-row kr, half `half` of the 128 output features -> one 128-byte row of the swizzled smem tile.
       const int sr = P.epi == kEpiGlu ? glu_stage_row(trow) : trow;
       const int kr = pt >> 1, half = pt & 1;
-      const int q_off = kmajor ? sr * 128 : kr * 64 + half * 32;                 // + j * 64 * 64 for MN-major
-      const int sz_off = kmajor ? (sr >> 6) * 256 + (sr & 63) : half * 256 + kr;  // + j * 64
-      const int swz = kmajor ? (sr & 7) : 0;
+      const int q_off = kmajor ? sr * kQRowBytes : kr * 64 + half * 32;  // + j * 64 * 64 for MN-major
+      const int sz_off = (kmajor ? (sr >> 6) : half) * (kQSub * 64) + (kmajor ? (sr & 63) : kr);  // + j * 64
+      const int swz = kmajor ? qswz(sr) : 0;
       for (int kb = kb0; kb < nkb; kb += 2) {
         const uint32_t r = it0 + kb;
         const int s = r % kStages;

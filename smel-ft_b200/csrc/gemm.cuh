@@ -37,12 +37,14 @@ constexpr int kBK = 64;
 #define SMELB_STAGES 4
 #endif
 #ifndef SMELB_QSTAGES
-#define SMELB_QSTAGES 2
+#define SMELB_QSTAGES 4
 #endif
 constexpr int kMaxBN = SMELB_MAX_BN;     // token tile (MMA N) upper bound
 constexpr int kStages = SMELB_STAGES;    // operand ring: a weight tile (16 KB) and a token tile (kMaxBN x 128 B)
-constexpr int kQStages = SMELB_QSTAGES;  // packed-int4 staging ring, 4 k-blocks per stage
-constexpr int kQSub = 4;                 // k-blocks per int4 staging stage (128-byte rows for K-major weights)
+constexpr int kQStages = SMELB_QSTAGES;  // packed-int4 staging ring
+constexpr int kQSub = 2;                 // k-blocks per int4 staging stage
+constexpr int kQRowBytes = kQSub * 32;   // one staged K-major weight row: kQSub k-blocks of 64 nibbles
+static_assert(kQRowBytes == 64 || kQRowBytes == 128, "staged rows use the 64- or 128-byte swizzle");
 constexpr int kMaxProblems = 12;
 constexpr int kMaxGroups = 320;  // groups over all problems of one launch
 
@@ -53,8 +55,10 @@ constexpr int kBStageBytes = kMaxBN * kBK * 2;   // bf16 B tile
 constexpr int kTmemAcc = kMaxBN;
 constexpr int kTmemA0 = 2 * kMaxBN;
 static_assert(kTmemA0 + 4 * 32 <= 512 && kTmemA0 + SMELB_STAGES * 32 <= 512, "tensor memory budget exceeded");
-constexpr int kQStageBytes = 16384;              // nibbles: 128 rows x 128 B (K-major) or 256 k-rows x 64 B (MN-major)
-constexpr int kSZStageBytes = 2048;              // (scale, zero) pairs: 2 halves x 256 uint32
+constexpr int kQStageBytes = 128 * kQRowBytes;  // nibbles: 128 rows x kQRowBytes (K-major) or kQSub*64 k-rows x 64 B
+constexpr int kSZStageBytes = 2 * kQSub * 64 * 4;  // (scale, zero) pairs: 2 halves x kQSub*64 uint32
+// 16-byte chunk c of staged K-major row r sits at chunk c ^ qswz(r) (the TMA 64- or 128-byte swizzle)
+__host__ __device__ constexpr int qswz(int r) { return kQRowBytes == 128 ? (r & 7) : ((r >> 1) & 3); }
 
 // warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3 TMA (int4 staging ring), 4-11 dequant (two
 // groups of four warps taking alternate k-blocks), then the epilogue: kEpiSubs warps per TMEM lane quarter, which

@@ -125,7 +125,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+                 uint64_t cols, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
   auto fn = encode_fn();
   SMELB_CHECK_ARG(fn != nullptr, kErrCuda, "cuTensorMapEncodeTiled is not available from the driver");
   SMELB_CHECK_ARG(base != nullptr, kErrArg, "tensor map over a null pointer");
@@ -133,13 +133,18 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   SMELB_CHECK_ARG(row_bytes % 16 == 0, kErrShape, "tensor map row pitch %llu not a multiple of 16 bytes",
                   (unsigned long long)row_bytes);
   SMELB_CHECK_ARG((box_cols * elem_bytes) % 16 == 0, kErrShape, "tensor map box inner extent not 16-byte multiple");
+  SMELB_CHECK_ARG(swizzle_bytes == 0 || (int)(box_cols * elem_bytes) == swizzle_bytes, kErrShape,
+                  "tensor map swizzle span %d for a %u-byte box row", swizzle_bytes, box_cols * elem_bytes);
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
   if (rows == 0) rows = 1;  // an empty matrix still needs a valid (never read) map
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   SMELB_CHECK_ARG(r == CUDA_SUCCESS, kErrShape,
                   "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu pitch=%llu box=%ux%u", (int)r,

@@ -19,8 +19,8 @@ void gemm_timing_end(cudaStream_t st);  // 4-byte device word the kernels record
 int num_sms(int dev);
 
 // 2-D tiled tensor map over a row-major matrix [rows][cols] of `elem_bytes`-sized elements with row pitch
-// `row_bytes`. box = {box_cols, box_rows}. swizzle128 selects the 128-byte swizzle (box_cols * elem_bytes == 128).
+// `row_bytes`. box = {box_cols, box_rows}. swizzle_bytes: 0 (none), 64 or 128 (box_cols * elem_bytes equal to it).
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
-                 uint64_t cols, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+                 uint64_t cols, uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
 }  // namespace smelb

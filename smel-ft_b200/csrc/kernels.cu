@@ -54,6 +54,101 @@ int int4_dequant(const void* q, const void* scale, const void* zero, void* out, 
   return kOk;
 }
 
+// ------------------------------------------------------------------------------------------ int4 quantizer
+// smel/quant.py:5-44, one warp per 64-value group (lane l holds columns 2l, 2l+1, so the warp reads the group's
+// 128 or 256 contiguous bytes and writes its 32 packed bytes). Every fp32 step is a separate correctly rounded
+// operation in the reference's order (no contraction into FMAs): the group's [min, max], its center, each clip
+// candidate's range, step = max((hi - lo) / 15, 1e-8) and base = lo both rounded to bf16, codes
+// round_half_even((w - base) / step) clamped to [0, 15], and the squared error of codes * step + base. A later
+// candidate replaces the best one only when its error is strictly smaller. The error sum runs as a butterfly over
+// the warp, so where two candidates' errors agree to within fp32 rounding the choice can differ from the
+// reference's CPU sum order.
+struct ClipList {
+  int n;
+  float c[kMaxClip];
+};
+
+__device__ __forceinline__ float warp_sum_rn(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <bool F32>
+__global__ void int4_quantize_kernel(const void* __restrict__ w, uint8_t* __restrict__ q, uint16_t* __restrict__ scale,
+                                     uint16_t* __restrict__ zero, long long ngroups, ClipList cl) {
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long gi = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; gi < ngroups; gi += nwarps) {
+    float w0, w1;
+    if (F32) {
+      const float2 v = reinterpret_cast<const float2*>(w)[gi * 32 + lane];
+      w0 = v.x;
+      w1 = v.y;
+    } else {
+      const __nv_bfloat162 v = reinterpret_cast<const __nv_bfloat162*>(w)[gi * 32 + lane];
+      w0 = __low2float(v);
+      w1 = __high2float(v);
+    }
+    float mn = fminf(w0, w1), mx = fmaxf(w0, w1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float mid = __fdiv_rn(__fadd_rn(mn, mx), 2.0f);
+    float best_err = 0.0f, best_s = 0.0f, best_z = 0.0f, best_q0 = 0.0f, best_q1 = 0.0f;
+    for (int ci = 0; ci < cl.n; ++ci) {
+      const float c = cl.c[ci];
+      const float lo = __fadd_rn(mid, __fmul_rn(__fsub_rn(mn, mid), c));
+      const float hi = __fadd_rn(mid, __fmul_rn(__fsub_rn(mx, mid), c));
+      const float s = __bfloat162float(__float2bfloat16_rn(fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 15.0f), 1e-8f)));
+      const float z = __bfloat162float(__float2bfloat16_rn(lo));
+      const float q0 = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(w0, z), s)), 0.0f), 15.0f);
+      const float q1 = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(w1, z), s)), 0.0f), 15.0f);
+      const float d0 = __fsub_rn(__fadd_rn(__fmul_rn(q0, s), z), w0);
+      const float d1 = __fsub_rn(__fadd_rn(__fmul_rn(q1, s), z), w1);
+      const float e = warp_sum_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)));
+      if (ci == 0 || e < best_err) {
+        best_err = e;
+        best_s = s;
+        best_z = z;
+        best_q0 = q0;
+        best_q1 = q1;
+      }
+    }
+    q[gi * 32 + lane] = (uint8_t)((int)best_q0 | ((int)best_q1 << 4));
+    if (lane == 0) {
+      scale[gi] = __bfloat16_as_ushort(__float2bfloat16_rn(best_s));
+      zero[gi] = __bfloat16_as_ushort(__float2bfloat16_rn(best_z));
+    }
+  }
+}
+
+int int4_quantize(const void* w, bool w_f32, long long rows, int k, const float* clip, int n_clip, void* q,
+                  void* scale, void* zero, cudaStream_t st) {
+  SMELB_CHECK_ARG(k > 0 && k % 64 == 0, kErrShape, "int4_quantize: k=%d is not a multiple of the group size 64", k);
+  SMELB_CHECK_ARG(n_clip >= 1 && n_clip <= kMaxClip, kErrArg, "int4_quantize: %d clip factors (1..%d)", n_clip,
+                  kMaxClip);
+  SMELB_CHECK_ARG(rows >= 0, kErrShape, "int4_quantize: rows=%lld", rows);
+  if (rows == 0) return kOk;
+  ClipList cl;
+  cl.n = n_clip;
+  for (int i = 0; i < kMaxClip; ++i) cl.c[i] = i < n_clip ? clip[i] : 1.0f;
+  const long long ngroups = rows * (k / 64);
+  const int threads = 256;
+  const long long blocks = std::min<long long>((ngroups + 7) / 8, 148LL * 16);
+  if (w_f32)
+    int4_quantize_kernel<true><<<(int)blocks, threads, 0, st>>>(w, (uint8_t*)q, (uint16_t*)scale, (uint16_t*)zero,
+                                                                 ngroups, cl);
+  else
+    int4_quantize_kernel<false><<<(int)blocks, threads, 0, st>>>(w, (uint8_t*)q, (uint16_t*)scale, (uint16_t*)zero,
+                                                                  ngroups, cl);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
 // szT[w][g][r] = scale[w][r][g] | zero[w][r][g] << 16 : the (scale, zero) pairs of one group for consecutive rows are
 // contiguous, which is the order the GEMM producer stages them in.
 __global__ void int4_pack_sz_kernel(const uint16_t* __restrict__ scale, const uint16_t* __restrict__ zero,

@@ -34,6 +34,10 @@ struct PackBatch {
 
 int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
                  bool out_f32, cudaStream_t st);
+// Group-64 int4 quantizer with the clip search of smel/quant.py:5-44 (up to kMaxClip candidate factors).
+constexpr int kMaxClip = 8;
+int int4_quantize(const void* w, bool w_f32, long long rows, int k, const float* clip, int n_clip, void* q,
+                  void* scale, void* zero, cudaStream_t st);
 int int4_pack_sz(const void* scale, const void* zero, uint32_t* szT, long long nw, int rows, int groups,
                  cudaStream_t st);
 int router_topk(const void* logits, long long ld, int T, int E, int K, float* probs, void* topv, bool topv_f32,

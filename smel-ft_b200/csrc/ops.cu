@@ -25,18 +25,18 @@ constexpr int kW64 = 64;       // column width of the LoRA token-side buffers an
 
 // ---------------------------------------------------------------------------------------------- tensor maps
 int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int box_rows) {
-  return make_tmap_2d(m, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols * 2, 64, box_rows, true);
+  return make_tmap_2d(m, p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols * 2, 64, box_rows, 128);
 }
 int tm_q(CUtensorMap* m, const void* q, long long rows, long long cols, bool mn_major) {
-  // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes. K-major tiles stage 4 k-blocks per row
-  // (128 B, 128-byte swizzle so the dequant warps' row reads are free of bank conflicts); MN-major tiles stage
-  // 4 k-blocks of 64 k-rows x 64 B.
-  return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : 128,
-                      mn_major ? 256 : 64, !mn_major);
+  // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes. K-major tiles stage kQSub k-blocks per
+  // row (kQRowBytes, swizzled over the row so the dequant warps' row reads are free of bank conflicts); MN-major
+  // tiles stage kQSub k-blocks of 64 k-rows x 64 B.
+  return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : kQRowBytes,
+                      mn_major ? kQSub * 64 : 64, mn_major ? 0 : kQRowBytes);
 }
 int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows, bool mn_major) {
-  return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4, mn_major ? 256 : 64,
-                      mn_major ? 1 : 4, false);
+  return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4,
+                      mn_major ? kQSub * 64 : 64, mn_major ? 1 : kQSub, 0);
 }
 
 #define TRY(x)               \
@@ -679,6 +679,12 @@ int smelb_int4_dequant(const void* q, const void* scale, const void* zero, void*
                        int64_t groups, int out_fp32, void* stream) {
   SMELB_CHECK_ARG(q && scale && zero && out, kErrArg, "int4_dequant: null pointer");
   return int4_dequant(q, scale, zero, out, rows, (int)k, (int)groups, out_fp32 != 0, (cudaStream_t)stream);
+}
+
+int smelb_int4_quantize(const void* w, int w_fp32, int64_t rows, int64_t k, const float* clip, int n_clip, void* q,
+                        void* scale, void* zero, void* stream) {
+  SMELB_CHECK_ARG(w && clip && q && scale && zero, kErrArg, "int4_quantize: null pointer");
+  return int4_quantize(w, w_fp32 != 0, rows, (int)k, clip, n_clip, q, scale, zero, (cudaStream_t)stream);
 }
 
 int smelb_int4_pack_sz(const void* scale, const void* zero, uint32_t* sz_t, int64_t nw, int64_t rows,

@@ -73,6 +73,7 @@ SIGNATURES = {
     "smelb_read_status_detail": (c_i32, [c_i32, ctypes.POINTER(c_i32), c_i32]),
     "smelb_int4_dequant": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),
     "smelb_int4_pack_sz": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "smelb_int4_quantize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "smelb_router_topk": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp]),
     "smelb_router_bwd": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "smelb_dispatch_plan": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

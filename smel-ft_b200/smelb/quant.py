@@ -44,15 +44,38 @@ def _quantize_slab(w, group, clip_search):
             "zero": best_base.squeeze(-1).to(torch.bfloat16)}
 
 
+def _quantize_kernel(w, clip_search):
+    """Group-64 banks: one pass of `smelb_int4_quantize` (a warp per group, the candidates evaluated in
+    registers)."""
+    import ctypes
+    K = w.shape[-1]
+    w2 = w if w.dtype in (torch.bfloat16, torch.float32) else w.float()
+    w2 = w2.contiguous()
+    rows = w2.numel() // K
+    lead = w.shape[:-1]
+    q = torch.empty(*lead, K // 2, dtype=torch.uint8, device=w.device)
+    scale = torch.empty(*lead, K // 64, dtype=torch.bfloat16, device=w.device)
+    zero = torch.empty_like(scale)
+    clip = (ctypes.c_float * len(clip_search))(*[float(c) for c in clip_search])
+    _lib.call("smelb_int4_quantize", _lib.ptr(w2), 1 if w2.dtype == torch.float32 else 0, rows, K,
+              ctypes.cast(clip, ctypes.c_void_p), len(clip_search), _lib.ptr(q), _lib.ptr(scale), _lib.ptr(zero),
+              _lib.stream_ptr(w.device))
+    return {"q": q, "scale": scale, "zero": zero}
+
+
 def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=CLIP_SEARCH) -> dict:
     """w [..., K] -> {q uint8 [..., K/2], scale bf16 [..., K/group], zero bf16 [..., K/group]}
     (smel/quant.py:14-44): per group the [min, max] range is shrunk by the clip factor with the smallest squared
-    error. 3-D banks are processed 16 experts at a time to bound the fp32 temporaries."""
+    error. Group 64 (the fused kernels' format) runs the CUDA quantizer; other group sizes run the same steps as
+    torch operations on the GPU, 16 experts at a time for 3-D banks to bound the fp32 temporaries."""
     if not w.is_cuda:
         raise _lib.SmelbError("quantize_int4: smelb quantizes on the GPU; move the weights to CUDA first")
     K = w.shape[-1]
     if K % group or group % 2:
         raise ValueError(f"quantize_int4: K={K} must be a multiple of an even group size (group={group})")
+    clip_search = tuple(clip_search or (1.0,))
+    if group == 64 and len(clip_search) <= 8:
+        return _quantize_kernel(w, clip_search)
     if w.dim() == 3 and w.shape[0] > 16:
         parts = [_quantize_slab(w[i:i + 16], group, clip_search) for i in range(0, w.shape[0], 16)]
         return {k: torch.cat([p[k] for p in parts]) for k in parts[0]}

@@ -62,6 +62,42 @@ def test_quantize_matches_reference(dev, golden):
     assert torch.equal(q_gpu[rows_same], q_ref[rows_same])
 
 
+def _ties_only(pk, ref):
+    """Groups where (scale, zero) differ must be near-ties of the clip search; elsewhere the codes are identical.
+    Returns the fraction of differing groups."""
+    same = (pk["scale"].view(torch.int16) == ref["scale"].view(torch.int16)) & \
+           (pk["zero"].view(torch.int16) == ref["zero"].view(torch.int16))
+    flat = same.reshape(-1)
+    qa, qb = pk["q"].reshape(-1, 32), ref["q"].reshape(-1, 32)
+    assert torch.equal(qa[flat], qb[flat])
+    return 1.0 - flat.float().mean().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_quantize_kernel_vs_torch_steps(dev, dtype):
+    """The CUDA quantizer (group 64) against the same clip search as torch operations on the GPU
+    (smelb.quant._quantize_slab): identical bytes except on near-ties of the candidates' squared errors. The input
+    holds constant groups (zero range), one-outlier groups and a range of magnitudes."""
+    from smelb import quant
+    g = torch.Generator(device=dev).manual_seed(11)
+    w = torch.randn(20, 96, 512, generator=g, device=dev) * 0.02
+    w[0, :8] = 0.25                                   # constant groups: step clamps to 1e-8
+    w[1, :8, ::64] = 3.0                               # one outlier per group
+    w[2] *= 1e-4
+    w[3] *= 50.0
+    w = w.to(dtype)
+    pk = quant.quantize_int4(w, 64)
+    ref = quant._quantize_slab(w, 64, quant.CLIP_SEARCH)
+    assert pk["q"].shape == ref["q"].shape and pk["scale"].dtype == torch.bfloat16
+    assert _ties_only(pk, ref) < 1e-3
+    # one candidate (no clip search), and the default tuple as a list
+    pk1 = quant.quantize_int4(w, 64, clip_search=(1.0,))
+    ref1 = quant._quantize_slab(w, 64, (1.0,))
+    assert _ties_only(pk1, ref1) == 0.0
+    assert _ties_only(quant.quantize_int4(w, 64, clip_search=list(quant.CLIP_SEARCH)), pk) == 0.0
+    _status_ok()
+
+
 def test_router_topk_bit_exact_given_logits(dev):
     """Given identical bf16 logits the routing indices are bit-exact (ties -> smaller expert id) and topv equals the
     oracle's renormalised weights cast to bf16 up to one bf16 ulp."""
