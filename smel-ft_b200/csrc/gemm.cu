@@ -1,5 +1,5 @@
 // Persistent grouped multi-problem GEMM for sm_100a: TMA producer warps, a warp-elected tcgen05.mma issuer with TMEM
-// accumulators (double-buffered across tiles), two groups of four int4 dequant warps and a team of epilogue warps.
+// accumulators (double-buffered across tiles), three groups of four int4 dequant warps and a team of epilogue warps.
 // See gemm.cuh for the operand conventions and the warp roles.
 #include "gemm.cuh"
 #include "host.h"
@@ -563,27 +563,38 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       mbar_wait_warp(mma_drain, 0, err, kDevErrTmaDrain);
     }
   } else if (warp < kWarpEpi0) {
-    // ============================================================================ int4 dequant (two groups)
-    // Group grp owns the ring slots of parity grp and walks only its own k-blocks of each tile. Every dequant warp
-    // takes part in every int4 staging stage once: it waits for the stage with its first owned k-block there and
-    // releases it after its last one; a stage where the group owns nothing (a one-k-block last stage) is waited for
-    // and released on its own.
+    // ============================================================================ int4 dequant (three groups)
+    // Group grp owns the k-blocks whose ring index is grp mod kNumDeqGroups and walks only those. Every dequant warp
+    // takes part in every int4 staging stage once, in stage order: it waits for a stage before its k-block there
+    // and releases the stage after it; a stage where the group owns no k-block is waited for and released on its
+    // own when the walk passes it.
     const int grp = (warp - kWarpDeq0) / kNumDeqWarps;
     const int pt = ((warp - kWarpDeq0) % kNumDeqWarps) * 32 + lane;  // 0..127 within the group
     const int lq = warp & 3;                                         // TMEM lane quarter this warp may access
     const int trow = lq * 32 + lane;                                 // weight-tile row this thread stores to TMEM
     const uint32_t tmem_row = tmem_base + ((uint32_t)(lq * 32) << 16) + kTmemA0;
-    static_assert(kNumDeqGroups == 2, "k-block ownership by ring-index parity");
+    static_assert(kNumDeqGroups <= kStages, "a dequant group's empty wait must not alias (see the ring note)");
+    static_assert(kQSub <= kNumDeqGroups, "a group owns at most one k-block of a staging stage");
     uint32_t it = 0, qi = 0;
     bool ok = true;
+    // take part in staging stage `qstage` without owning a k-block of it
+    auto pass_stage = [&](uint32_t qstage, int t, int kb) -> bool {
+      const int qs = qstage % kQStages;
+      if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) return false;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[qs]);
+      return true;
+    };
     for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
       const TileInfo ti = tile_at(args, T, tiles, i, t);
       const Problem& P = args.p[ti.p];
       const int nkb = ti.nkb;
       const uint32_t it0 = it;
       it += nkb;
-      const int kb0 = (int)((it0 & 1u) != (uint32_t)grp);  // first k-block of this tile owned by the group
+      // first k-block of this tile owned by the group
+      const int kb0 = (int)(((uint32_t)grp + kNumDeqGroups - it0 % kNumDeqGroups) % kNumDeqGroups);
       const int nkq = is_int4(P) ? P.K / kBK : 0;          // int4 k-blocks of the tile (staged nibbles)
+      const int nstages = (nkq + kQSub - 1) / kQSub;
       const bool kmajor = P.a_kind == kAInt4K;
       // K-major: weight row trow -> TMEM lane trow, 64 bf16 in columns kTmemA0 + 32 s .. +31; the nibble rows are
       // staged swizzled (16-byte chunk c of row r at chunk c ^ qswz(r)).
@@ -593,25 +604,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int q_off = kmajor ? sr * kQRowBytes : kr * 64 + half * 32;  // + j * 64 * 64 for MN-major
       const int sz_off = (kmajor ? (sr >> 6) : half) * (kQSub * 64) + (kmajor ? (sr & 63) : kr);  // + j * 64
       const int swz = kmajor ? qswz(sr) : 0;
-      for (int kb = kb0; kb < nkb; kb += 2) {
+      int qdone = 0;  // staging stages of this tile the warp has released
+      for (int kb = kb0; kb < nkb; kb += kNumDeqGroups) {
         const uint32_t r = it0 + kb;
         const int s = r % kStages;
+        const bool q4 = kb < nkq;
+        const int kq = kb / kQSub;
+        if (q4)
+          for (; qdone < kq && ok; ++qdone) ok = pass_stage(qi + qdone, t, kb);
+        if (!ok) break;
         if (!mbar_wait(&empty[s], ((r / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyDeq, t, kb)) { ok = false; break; }
-        if (kb < nkq) {
-          const int kq = kb / kQSub, j = kb % kQSub;
+        if (q4) {
+          const int j = kb % kQSub;
           const uint32_t qstage = qi + kq;
           const int qs = qstage % kQStages;
-          const int subs = min(kQSub, nkq - kq * kQSub);
-          const int jf = j & 1;                               // the group's first k-block in this stage
-          const int jl = jf + 2 * ((subs - 1 - jf) >> 1);     // and its last
-          if (j == jf)
-            if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
+          if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
           const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes + q_off + (kmajor ? 0 : j * 64 * 64);
           const uint32_t sz = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes)[sz_off + j * 64];
           uint32_t o[32];
           dq64(sQ, kmajor ? 2 * j : 0, swz, sz, o);
           __syncwarp();
-          if (lane == 0 && j == jl) mbar_arrive(&q_empty[qs]);  // the staged nibbles of this stage are consumed
+          if (lane == 0) mbar_arrive(&q_empty[qs]);  // the group's only k-block of this stage: nibbles consumed
+          qdone = kq + 1;
           if (kmajor) {
             tc_fence_after();  // the MMAs that read this TMEM stage completed (empty wait above)
             __syncwarp();      // tcgen05.st is warp-collective
@@ -630,16 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates
       }
-      if (!ok) break;
-      if (nkq % kQSub == 1 && ((nkq - 1) & 1) != kb0) {
-        // a one-k-block last stage owned by the other group: take part in its round
-        const uint32_t qstage = qi + nkq / kQSub;
-        const int qs = qstage % kQStages;
-        if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, nkq - 1)) { ok = false; break; }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&q_empty[qs]);
-      }
-      qi += (nkq + kQSub - 1) / kQSub;
+      for (; qdone < nstages && ok; ++qdone) ok = pass_stage(qi + qdone, t, nkb);
+      qi += nstages;
     }
   } else {
     // ============================================================================ epilogue warps
