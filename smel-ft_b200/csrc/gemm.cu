@@ -336,25 +336,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   __syncthreads();
 
   if (warp == kWarpTmaB) {
-    // ============================================================================ TMA: token ring (one thread)
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
-        const TileInfo ti = tile_at(args, T, tiles, i, t);
-        const Problem& P = args.p[ti.p];
-        const bool tokk = P.mode == kTokK;
-        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
-        const CUtensorMap* mB = &P.tmB;
-        const CUtensorMap* mB32 = &P.tmB32;
-        const CUtensorMap* mBe = &P.tmBe;
-        const int nb = tokk ? (P.N + 63) / 64 : (ti.n_valid + 63) / 64;
-        const int b_x0 = P.b_x0;
-        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
-          uint8_t* sB = smem + kOffB + s * kBStageBytes;
-          uint64_t* fb = &full[s];
+    // ============================================================================ TMA: token ring (whole warp)
+    // The producer loops run warp-uniform and each copy goes out through one elected lane: issued from a lone lane
+    // of a diverged warp the same loop spent several hundred cycles per k-block (measured), which made these
+    // warps the slowest stage of the pipeline.
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
+      const Problem& P = args.p[ti.p];
+      const bool tokk = P.mode == kTokK;
+      const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+      const CUtensorMap* mB = &P.tmB;
+      const CUtensorMap* mB32 = &P.tmB32;
+      const CUtensorMap* mBe = &P.tmBe;
+      const int nb = tokk ? (P.N + 63) / 64 : (ti.n_valid + 63) / 64;
+      const int b_x0 = P.b_x0;
+      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait_warp(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
+        uint8_t* sB = smem + kOffB + s * kBStageBytes;
+        uint64_t* fb = &full[s];
+        if (elect_one()) {
           if (!tokk) {
             const bool ext = kb == ext_kb;
             if (!ext && ti.n_valid <= 32) {
@@ -362,7 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
               tma_load_2d(sB, mB32, kb * kBK, ti.n0, fb);
             } else {
               mbar_arrive_expect_tx(fb, nb * 8192);
-              for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, ext ? mBe : mB, ext ? 0 : kb * kBK, ti.n0 + 64 * i, fb);
+              for (int i = 0; i < nb; ++i)
+                tma_load_2d(sB + i * 8192, ext ? mBe : mB, ext ? 0 : kb * kBK, ti.n0 + 64 * i, fb);
             }
           } else {  // kTokK: B = tokens^T (MN-major)
             const int krow = ti.n0 + kb * kBK;
@@ -370,90 +374,92 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, b_x0 + 64 * i, krow, fb);
           }
         }
+        __syncwarp();
       }
-      // every issued copy must land before the CTA may exit
-      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
     }
+    // every issued copy must land before the CTA may exit
+    for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
+      if (!mbar_wait_warp(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
   } else if (warp == kWarpTmaA) {
-    // ============================================================================ TMA: bf16 weight ring (one thread)
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
-        const TileInfo ti = tile_at(args, T, tiles, i, t);
-        const Problem& P = args.p[ti.p];
-        const bool glu = P.epi == kEpiGlu;
-        const bool int4 = is_int4(P);
-        const bool tokk = P.mode == kTokK;
-        const int a_kind = P.a_kind;
-        const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
-        const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
-        const CUtensorMap* mAmain = &P.tmA;
-        const CUtensorMap* mAext = &P.tmAe;
-        const int a_wrows = P.a_wrows, e_wrows = P.e_wrows, a_x0 = P.a_x0;
-        for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-          const bool ext = kb == ext_kb;
-          const int s = it % kStages;
-          // waited for and arrived on in every round (see the note on ring waits), filled for TMA-sourced tiles
-          if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyTma, t, kb)) { ok = false; break; }
-          uint64_t* fa = &full[s];
-          if (int4 && !ext) {  // the dequant warps fill this slot; the arrival keeps this thread gating every round
+    // ============================================================================ TMA: bf16 weight ring (whole warp)
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
+      const Problem& P = args.p[ti.p];
+      const bool glu = P.epi == kEpiGlu;
+      const bool int4 = is_int4(P);
+      const bool tokk = P.mode == kTokK;
+      const int a_kind = P.a_kind;
+      const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
+      const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
+      const CUtensorMap* mAmain = &P.tmA;
+      const CUtensorMap* mAext = &P.tmAe;
+      const int a_wrows = P.a_wrows, e_wrows = P.e_wrows, a_x0 = P.a_x0;
+      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
+        const bool ext = kb == ext_kb;
+        const int s = it % kStages;
+        // waited for and arrived on in every round (see the note on ring waits), filled for TMA-sourced tiles
+        if (!mbar_wait_warp(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyTma, t, kb)) { ok = false; break; }
+        uint64_t* fa = &full[s];
+        if (elect_one()) {
+          if (int4 && !ext) {  // the dequant warps fill this slot; the arrival keeps this warp gating every round
             mbar_arrive(fa);
-            continue;
-          }
-          uint8_t* sA = smem + kOffA + s * kAStageBytes;
-          mbar_arrive_expect_tx(fa, kAStageBytes);
-          if (tokk) {  // A = tokens^T (MN-major)
-            const int krow = ti.n0 + kb * kBK;
-            tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, fa);
-            tma_load_2d(sA + 8192, mAmain, a_x0 + ti.m0 + 64, krow, fa);
-          } else if (ext || a_kind == kABf16K) {
-            const CUtensorMap* mA = ext ? mAext : mAmain;
-            const int wrow = ti.widx * (ext ? e_wrows : a_wrows);
-            const int x = ext ? 0 : kb * kBK;
-            if (glu) {
+          } else {
+            uint8_t* sA = smem + kOffA + s * kAStageBytes;
+            mbar_arrive_expect_tx(fa, kAStageBytes);
+            if (tokk) {  // A = tokens^T (MN-major)
+              const int krow = ti.n0 + kb * kBK;
+              tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, fa);
+              tma_load_2d(sA + 8192, mAmain, a_x0 + ti.m0 + 64, krow, fa);
+            } else if (ext || a_kind == kABf16K) {
+              const CUtensorMap* mA = ext ? mAext : mAmain;
+              const int wrow = ti.widx * (ext ? e_wrows : a_wrows);
+              const int x = ext ? 0 : kb * kBK;
+              if (glu) {
 #pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fa);
-                tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fa);
+                for (int qq = 0; qq < 4; ++qq) {
+                  tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fa);
+                  tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fa);
+                }
+              } else {
+                tma_load_2d(sA, mA, x, wrow + r0, fa);
+                tma_load_2d(sA + 8192, mA, x, wrow + r1, fa);
               }
-            } else {
-              tma_load_2d(sA, mA, x, wrow + r0, fa);
-              tma_load_2d(sA + 8192, mA, x, wrow + r1, fa);
+            } else {  // kABf16MN
+              const int wrow = ti.widx * a_wrows + kb * kBK;
+              tma_load_2d(sA, mAmain, ti.m0, wrow, fa);
+              tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, fa);
             }
-          } else {  // kABf16MN
-            const int wrow = ti.widx * a_wrows + kb * kBK;
-            tma_load_2d(sA, mAmain, ti.m0, wrow, fa);
-            tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, fa);
           }
         }
+        __syncwarp();
       }
-      for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
     }
+    for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
+      if (!mbar_wait_warp(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
   } else if (warp == kWarpTmaQ) {
-    // ============================================================================ TMA: int4 staging ring (one thread)
-    if (lane == 0) {
-      uint32_t qi = 0;
-      bool ok = true;
-      for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
-        const TileInfo ti = tile_at(args, T, tiles, i, t);
-        const Problem& P = args.p[ti.p];
-        if (!is_int4(P)) continue;
-        const bool glu = P.epi == kEpiGlu;
-        const bool kmajor = P.a_kind == kAInt4K;
-        const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
-        const int nkq = P.K / kBK;
-        const CUtensorMap* mQ = &P.tmQ;
-        const CUtensorMap* mSZ = &P.tmSZ;
-        const int qrow0 = ti.widx * P.q_rows, grow0 = ti.widx * P.q_groups;
-        for (int kq = 0; kq * kQSub < nkq; ++kq, ++qi) {
-          const int s = qi % kQStages;
-          if (!mbar_wait(&q_empty[s], ((qi / kQStages) & 1) ^ 1, err, kDevErrWaitQEmpty, t, kq)) { ok = false; break; }
-          uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
-          uint8_t* sSZ = smem + kOffSZ + s * kSZStageBytes;
-          uint64_t* fb = &q_full[s];
+    // ============================================================================ TMA: int4 staging ring (whole warp)
+    uint32_t qi = 0;
+    bool ok = true;
+    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
+      const TileInfo ti = tile_at(args, T, tiles, i, t);
+      const Problem& P = args.p[ti.p];
+      if (!is_int4(P)) continue;
+      const bool glu = P.epi == kEpiGlu;
+      const bool kmajor = P.a_kind == kAInt4K;
+      const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
+      const int nkq = P.K / kBK;
+      const CUtensorMap* mQ = &P.tmQ;
+      const CUtensorMap* mSZ = &P.tmSZ;
+      const int qrow0 = ti.widx * P.q_rows, grow0 = ti.widx * P.q_groups;
+      for (int kq = 0; kq * kQSub < nkq; ++kq, ++qi) {
+        const int s = qi % kQStages;
+        if (!mbar_wait_warp(&q_empty[s], ((qi / kQStages) & 1) ^ 1, err, kDevErrWaitQEmpty, t, kq)) { ok = false; break; }
+        uint8_t* sQ = smem + kOffQ + s * kQStageBytes;
+        uint8_t* sSZ = smem + kOffSZ + s * kSZStageBytes;
+        uint64_t* fb = &q_full[s];
+        if (elect_one()) {
           mbar_arrive_expect_tx(fb, kQStageBytes + kSZStageBytes);
           if (kmajor) {
             tma_load_2d(sQ, mQ, kq * kQRowBytes, qrow0 + r0, fb);
@@ -466,10 +472,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             tma_load_2d(sSZ + kSZStageBytes / 2, mSZ, kq * kQSub * kBK, grow0 + ti.m0 / 64 + 1, fb);
           }
         }
+        __syncwarp();
       }
-      for (uint32_t j = (qi > (uint32_t)kQStages ? qi - kQStages : 0u); j < qi; ++j)
-        if (!mbar_wait(&q_full[j % kQStages], (j / kQStages) & 1, err, kDevErrTmaDrain)) break;
     }
+    for (uint32_t j = (qi > (uint32_t)kQStages ? qi - kQStages : 0u); j < qi; ++j)
+      if (!mbar_wait_warp(&q_full[j % kQStages], (j / kQStages) & 1, err, kDevErrTmaDrain)) break;
   } else if (warp == kWarpMma) {
     // ============================================================================ MMA issuer (whole warp)
     // The loop runs warp-uniform and each tcgen05 instruction goes out through one elected lane. Per tile the
