@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   if (warp == kWarpTmaB) {
     if (lane == 0) {
       for (int s = 0; s < kStages; ++s) {
-        mbar_init(&full[s], kNumDeqWarps + 2);  // token TMA + weight TMA + the owning dequant group
+        mbar_init(&full[s], kNumDeqWarps + 1);  // the owning TMA producer + the owning dequant group
         mbar_init(&empty[s], 1);
       }
       for (int s = 0; s < kQStages; ++s) {
@@ -335,83 +335,65 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   }
   __syncthreads();
 
-  if (warp == kWarpTmaB) {
-    // ============================================================================ TMA: token ring (whole warp)
-    // The producer loops run warp-uniform and each copy goes out through one elected lane: issued from a lone lane
-    // of a diverged warp the same loop spent several hundred cycles per k-block (measured), which made these
-    // warps the slowest stage of the pipeline.
+  if (warp == kWarpTmaB || warp == kWarpTmaA) {
+    // ============================================================================ TMA producers (two warps)
+    // Producer `prod` owns the ring slots of parity prod (so it waits on and arrives at every round of its slots):
+    // per owned k-block it waits for the slot, then one elected lane arms the slot's `full` barrier with the byte
+    // count and issues the token tile and, where the weight tile comes by TMA (bf16 weights, the LoRA extension, the
+    // token-side A of kTokK), the weight tile too. Each producer pays one wait and one arrival per two k-blocks.
+    // The loops run warp-uniform with elected issue: from a lone lane of a diverged warp the same loop was several
+    // times slower (measured).
+    static_assert(kStages % 2 == 0, "a producer owns the ring slots of one parity");
+    const uint32_t prod = warp == kWarpTmaB ? 0u : 1u;
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
       const TileInfo ti = tile_at(args, T, tiles, i, t);
       const Problem& P = args.p[ti.p];
+      const uint32_t it0 = it;
+      it += ti.nkb;
       const bool tokk = P.mode == kTokK;
+      const bool glu = P.epi == kEpiGlu;
+      const bool int4 = is_int4(P);
+      const int a_kind = P.a_kind;
       const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
       const CUtensorMap* mB = &P.tmB;
       const CUtensorMap* mB32 = &P.tmB32;
       const CUtensorMap* mBe = &P.tmBe;
-      const int nb = tokk ? (P.N + 63) / 64 : (ti.n_valid + 63) / 64;
-      const int b_x0 = P.b_x0;
-      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-        const int s = it % kStages;
-        if (!mbar_wait_warp(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
-        uint8_t* sB = smem + kOffB + s * kBStageBytes;
-        uint64_t* fb = &full[s];
-        if (elect_one()) {
-          if (!tokk) {
-            const bool ext = kb == ext_kb;
-            if (!ext && ti.n_valid <= 32) {
-              mbar_arrive_expect_tx(fb, 4096);
-              tma_load_2d(sB, mB32, kb * kBK, ti.n0, fb);
-            } else {
-              mbar_arrive_expect_tx(fb, nb * 8192);
-              for (int i = 0; i < nb; ++i)
-                tma_load_2d(sB + i * 8192, ext ? mBe : mB, ext ? 0 : kb * kBK, ti.n0 + 64 * i, fb);
-            }
-          } else {  // kTokK: B = tokens^T (MN-major)
-            const int krow = ti.n0 + kb * kBK;
-            mbar_arrive_expect_tx(fb, nb * 8192);
-            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, b_x0 + 64 * i, krow, fb);
-          }
-        }
-        __syncwarp();
-      }
-    }
-    // every issued copy must land before the CTA may exit
-    for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-      if (!mbar_wait_warp(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
-  } else if (warp == kWarpTmaA) {
-    // ============================================================================ TMA: bf16 weight ring (whole warp)
-    uint32_t it = 0;
-    bool ok = true;
-    for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
-      const TileInfo ti = tile_at(args, T, tiles, i, t);
-      const Problem& P = args.p[ti.p];
-      const bool glu = P.epi == kEpiGlu;
-      const bool int4 = is_int4(P);
-      const bool tokk = P.mode == kTokK;
-      const int a_kind = P.a_kind;
-      const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
-      const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
       const CUtensorMap* mAmain = &P.tmA;
       const CUtensorMap* mAext = &P.tmAe;
+      const int nb = tokk ? (P.N + 63) / 64 : (ti.n_valid + 63) / 64;
+      const int b_x0 = P.b_x0;
+      const int r0 = ti.m0, r1 = glu ? P.inter + ti.m0 : ti.m0 + 64;
       const int a_wrows = P.a_wrows, e_wrows = P.e_wrows, a_x0 = P.a_x0;
-      for (int kb = 0; kb < ti.nkb; ++kb, ++it) {
-        const bool ext = kb == ext_kb;
-        const int s = it % kStages;
-        // waited for and arrived on in every round (see the note on ring waits), filled for TMA-sourced tiles
-        if (!mbar_wait_warp(&empty[s], ((it / kStages) & 1) ^ 1, err, kDevErrWaitAEmptyTma, t, kb)) { ok = false; break; }
-        uint64_t* fa = &full[s];
+      for (int kb = (int)((it0 & 1u) != prod); kb < ti.nkb; kb += 2) {
+        const uint32_t r = it0 + kb;
+        const int s = r % kStages;
+        if (!mbar_wait_warp(&empty[s], ((r / kStages) & 1) ^ 1, err, kDevErrWaitEmpty, t, kb)) { ok = false; break; }
         if (elect_one()) {
-          if (int4 && !ext) {  // the dequant warps fill this slot; the arrival keeps this warp gating every round
-            mbar_arrive(fa);
+          uint64_t* f = &full[s];
+          uint8_t* sB = smem + kOffB + s * kBStageBytes;
+          uint8_t* sA = smem + kOffA + s * kAStageBytes;
+          const bool ext = kb == ext_kb;
+          const bool a_tma = ext || !int4;  // the weight tile comes by TMA (else the dequant warps fill it)
+          const bool b32 = !tokk && !ext && ti.n_valid <= 32;
+          mbar_arrive_expect_tx(f, (b32 ? 4096 : nb * 8192) + (a_tma ? kAStageBytes : 0));
+          // token tile
+          if (tokk) {  // B = tokens^T (MN-major)
+            const int krow = ti.n0 + kb * kBK;
+            for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, b_x0 + 64 * i, krow, f);
+          } else if (b32) {
+            tma_load_2d(sB, mB32, kb * kBK, ti.n0, f);
           } else {
-            uint8_t* sA = smem + kOffA + s * kAStageBytes;
-            mbar_arrive_expect_tx(fa, kAStageBytes);
+            for (int i = 0; i < nb; ++i)
+              tma_load_2d(sB + i * 8192, ext ? mBe : mB, ext ? 0 : kb * kBK, ti.n0 + 64 * i, f);
+          }
+          // weight tile
+          if (a_tma) {
             if (tokk) {  // A = tokens^T (MN-major)
               const int krow = ti.n0 + kb * kBK;
-              tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, fa);
-              tma_load_2d(sA + 8192, mAmain, a_x0 + ti.m0 + 64, krow, fa);
+              tma_load_2d(sA, mAmain, a_x0 + ti.m0, krow, f);
+              tma_load_2d(sA + 8192, mAmain, a_x0 + ti.m0 + 64, krow, f);
             } else if (ext || a_kind == kABf16K) {
               const CUtensorMap* mA = ext ? mAext : mAmain;
               const int wrow = ti.widx * (ext ? e_wrows : a_wrows);
@@ -419,25 +401,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
               if (glu) {
 #pragma unroll
                 for (int qq = 0; qq < 4; ++qq) {
-                  tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, fa);
-                  tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, fa);
+                  tma_load_2d(sA + qq * 4096, mA, x, wrow + r0 + 16 * qq, f);
+                  tma_load_2d(sA + qq * 4096 + 2048, mA, x, wrow + r1 + 16 * qq, f);
                 }
               } else {
-                tma_load_2d(sA, mA, x, wrow + r0, fa);
-                tma_load_2d(sA + 8192, mA, x, wrow + r1, fa);
+                tma_load_2d(sA, mA, x, wrow + r0, f);
+                tma_load_2d(sA + 8192, mA, x, wrow + r1, f);
               }
             } else {  // kABf16MN
               const int wrow = ti.widx * a_wrows + kb * kBK;
-              tma_load_2d(sA, mAmain, ti.m0, wrow, fa);
-              tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, fa);
+              tma_load_2d(sA, mAmain, ti.m0, wrow, f);
+              tma_load_2d(sA + 8192, mAmain, ti.m0 + 64, wrow, f);
             }
           }
         }
         __syncwarp();
       }
     }
+    // every copy this warp issued must land before the CTA may exit
     for (uint32_t j = (it > (uint32_t)kStages ? it - kStages : 0u); j < it; ++j)
-      if (!mbar_wait_warp(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
+      if ((j & 1u) == prod)
+        if (!mbar_wait_warp(&full[j % kStages], (j / kStages) & 1, err, kDevErrTmaDrain)) break;
   } else if (warp == kWarpTmaQ) {
     // ============================================================================ TMA: int4 staging ring (whole warp)
     uint32_t qi = 0;
@@ -589,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int qs = qstage % kQStages;
       if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) return false;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&q_empty[qs]);
+      if (elect_one()) mbar_arrive(&q_empty[qs]);
       return true;
     };
     for (int t = blockIdx.x, i = 0; t < total_tiles && ok; t += gridDim.x, ++i) {
@@ -631,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           uint32_t o[32];
           dq64(sQ, kmajor ? 2 * j : 0, swz, sz, o);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&q_empty[qs]);  // the group's only k-block of this stage: nibbles consumed
+          if (elect_one()) mbar_arrive(&q_empty[qs]);  // the group's only k-block of this stage: nibbles consumed
           qdone = kq + 1;
           if (kmajor) {
             tc_fence_after();  // the MMAs that read this TMEM stage completed (empty wait above)
@@ -649,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates
+        if (elect_one()) mbar_arrive(&full[s]);  // also for k-blocks whose weight tile comes by TMA: the owner gates
       }
       for (; qdone < nstages && ok; ++qdone) ok = pass_stage(qi + qdone, t, nkb);
       qi += nstages;
@@ -801,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (elect_one()) mbar_arrive(&acc_empty[acc]);
       ++acc_it;
     }
   }

@@ -60,14 +60,16 @@ constexpr int kSZStageBytes = 2 * kQSub * 64 * 4;  // (scale, zero) pairs: 2 hal
 // 16-byte chunk c of staged K-major row r sits at chunk c ^ qswz(r) (the TMA 64- or 128-byte swizzle)
 __host__ __device__ constexpr int qswz(int r) { return kQRowBytes == 128 ? (r & 7) : ((r >> 1) & 3); }
 
-// warp roles: 0 TMA (token ring), 1 MMA, 2 TMA (bf16 weight ring), 3 TMA (int4 staging ring), 4-15 dequant (three
+// warp roles: 0 and 2 TMA producers (token and TMA-sourced weight tiles of alternate k-blocks), 1 MMA, 3 TMA (int4
+// staging ring), 4-15 dequant (three
 // groups of four warps; group g takes the k-blocks whose ring index is g mod 3), then the epilogue: kEpiSubs warps
 // per TMEM lane quarter, which split a tile's accumulator columns between them in 16-column chunks (several warps
 // per quarter hide the latency of the per-element conversion and store chains).
 // Ring waits: a thread that waits on a barrier round must also be one of the arrivals that the barrier's NEXT round
 // of the paired barrier needs (it "gates" the ring), otherwise it can fall two phases behind and its parity wait
-// then aliases onto a later phase. So the token TMA, the weight TMA and the owning dequant group arrive on "full"
-// in every round they wait on "empty" (the weight TMA also for int4 slots it does not fill). A dequant group waits
+// then aliases onto a later phase. So the owning TMA producer (fixed per slot: slot parity) and the owning dequant
+// group arrive on "full" in every round they wait on "empty" (the group also for slots whose weight tile comes by
+// TMA, the producer also for int4 slots where it loads only the token tile). A dequant group waits
 // only for the round before each round it owns, and that round cannot complete without its arrival; a group at
 // ring index r has passed r - 3, whose wait saw r - 7 consumed, so its wait for r - 4 cannot alias either (this
 // needs kNumDeqGroups <= kStages). Every dequant warp waits on and releases every int4 staging stage once.
