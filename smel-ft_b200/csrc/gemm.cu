@@ -711,6 +711,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         bf16* cp = reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + m;
         const bf16* hp = P.Hin + (long long)ti.n0 * ldh + m;
         for (int c = 8 * sub; c < n_valid; c += 8 * kEpiSubs) {
+          // all of the chunk's saved pre-activations are loaded before any store: interleaved with the stores (which
+          // the compiler cannot prove disjoint from them) every column would pay a full memory latency
+          bf16 hg[8], hu[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int n = c + j;
+            const bool ok = n < n_valid && mvalid;
+            hg[j] = ok ? __ldg(hp + (long long)n * ldh) : __float2bfloat16_rn(0.0f);
+            hu[j] = ok ? __ldg(hp + (long long)n * ldh + inter) : __float2bfloat16_rn(0.0f);
+          }
           uint32_t v[8];
           __syncwarp();
           tmem_ld8(tbase + c, v);
@@ -720,10 +730,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             const int n = c + j;
             if (n < n_valid && mvalid) {
               const float da = bf16_round(__uint_as_float(v[j]) * alpha);
-              const float gv = __bfloat162float(hp[(long long)n * ldh]);
-              const float uv = __bfloat162float(hp[(long long)n * ldh + inter]);
-              const float2 ad = act_and_grad(gv, act);
-              cp[(long long)n * ldc] = __float2bfloat16_rn(da * uv * ad.y);
+              const float2 ad = act_and_grad(__bfloat162float(hg[j]), act);
+              cp[(long long)n * ldc] = __float2bfloat16_rn(da * __bfloat162float(hu[j]) * ad.y);
               cp[(long long)n * ldc + inter] = __float2bfloat16_rn(da * ad.x);
             }
           }
