@@ -286,20 +286,30 @@ class _MoELayerFn(torch.autograd.Function):
         t.update(_alloc_fwd(cfg, dev, save))
         L = _struct(cfg, t)
         _lib.call("smelb_moe_layer_fwd", ctypes.byref(L))
-        ctx.cfg, ctx.t, ctx.dtypes = cfg, t, [None if p is None else p.dtype for p in params]
-        ctx.has_topv_in = topv_in is not None
         outs = (t["out"], t.get("probs", x.new_empty(0)), t.get("topv", x.new_empty(0)),
                 t.get("topi", x.new_empty(0, dtype=torch.long)))
+        # The function's own outputs are saved through save_for_backward and kept out of ctx: a plain reference
+        # from ctx to an output forms a cycle through the output's grad_fn, which keeps the whole step's buffers
+        # alive until Python's cycle collector runs (the caching allocator then grows and calls the driver).
+        ctx.out_keys = [k for k in ("probs", "topv", "topi") if k in t]
+        ctx.save_for_backward(*[t[k] for k in ctx.out_keys])
+        ctx.out_shape = tuple(t["out"].shape)
+        ctx.t = {k: v for k, v in t.items() if k not in ("out", "probs", "topv", "topi")}
+        ctx.cfg, ctx.dtypes = cfg, [None if p is None else p.dtype for p in params]
+        ctx.has_topv_in = topv_in is not None
         ctx.mark_non_differentiable(outs[3])
         return outs
 
     @staticmethod
     def backward(ctx, g_out, g_probs, g_topv, g_topi):
         cfg, t = ctx.cfg, dict(ctx.t)
+        t.update(zip(ctx.out_keys, ctx.saved_tensors))
         dev = t["x"].device
         b = _alloc_bwd(cfg, dev)
         t.update(b)
-        t["g"] = (g_out if g_out is not None else torch.zeros_like(t["out"])).to(torch.bfloat16).contiguous()
+        if g_out is None:
+            g_out = torch.zeros(ctx.out_shape, dtype=torch.bfloat16, device=dev)
+        t["g"] = g_out.to(torch.bfloat16).contiguous()
         if cfg.flags & _lib.F_ROUTER:
             if g_probs is not None and g_probs.numel():
                 t["dprobs"] = g_probs.float().contiguous()
