@@ -202,24 +202,53 @@ def run_ours(args, world, rank, local):
     # ---------------- end to end through the public API with host buffers
     xh = x.cpu().pin_memory()
     gh = gy.cpu().pin_memory()
-    dxh = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
-    xd, gd = torch.empty_like(x), torch.empty_like(gy)
-    # measured first, before the graph capture and the clock sampler: this loop is host-bound (Python, autograd and
-    # kernel launches every step), so nothing else may compete for the host while it runs
+    dxh = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(x) for _ in range(2)]
+    gd = [torch.empty_like(gy) for _ in range(2)]
+    # Every step copies its inputs from pinned host memory and reads its dX back. The copies run on their own
+    # stream, double-buffered as an input pipeline would: step i+1's inputs upload while step i computes, and step
+    # i's dX downloads while step i+1 computes. Measured first, before the graph capture and the clock sampler: the
+    # loop drives Python, autograd and the launches every step, so nothing else may compete for the host.
+    copy_s = torch.cuda.Stream(dev)
+    up_done = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]   # step finished with buffer b (inputs consumed, dX produced)
+    down_done = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        b = i % 2
+        with torch.cuda.stream(copy_s):
+            if i >= 2:
+                copy_s.wait_event(used[b])
+            xd[b].copy_(xh, non_blocking=True)
+            gd[b].copy_(gh, non_blocking=True)
+            up_done[b].record(copy_s)
+
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    e0.record()
-    for _ in range(args.steps):
-        xd.copy_(xh, non_blocking=True)
-        gd.copy_(gh, non_blocking=True)
-        dx = step(xd, gd)
-        dxh.copy_(dx, non_blocking=True)
-    e1.record()
+    e0.record(copy_s)
+    side.wait_event(e0)
+    upload(0)
+    dxs = [None, None]
+    for i in range(args.steps):
+        b = i % 2
+        if i + 1 < args.steps:
+            upload(i + 1)
+        side.wait_event(up_done[b])
+        if i >= 2:
+            side.wait_event(down_done[b])  # the host copy of dX two steps back has left this buffer's slot
+        dxs[b] = step(xd[b], gd[b])
+        used[b].record(side)
+        with torch.cuda.stream(copy_s):
+            copy_s.wait_event(used[b])
+            dxh[b].copy_(dxs[b], non_blocking=True)
+            down_done[b].record(copy_s)
+    side.wait_stream(copy_s)
+    e1.record(side)
     torch.cuda.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
     e2e = {"value": world * cfg["T"] * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
-           "h2d_bytes_per_step": xh.numel() * 2 + gh.numel() * 2, "d2h_bytes_per_step": dxh.numel() * 2}
+           "h2d_bytes_per_step": xh.numel() * 2 + gh.numel() * 2, "d2h_bytes_per_step": dxh[0].numel() * 2}
     assert smelb.read_status() == 0, "device status word set during the end-to-end loop"
 
     # ---------------- device-resident timing: the whole step (no-grad forward, recompute, backward) is captured once
