@@ -6,8 +6,10 @@ Qwen3.6-35B-A3B layer shape (config 2), as one JSON line on rank 0.
 One step = the layer-major training unit of the reference (smel/layer_runner.py:319-364): a no-grad forward of the
 micro-batch, then a recompute under autograd and the backward (dX plus all LoRA gradients), on 4092 tokens of seeded
 synthetic input (Zipf-skewed routing, 244 int4 + 12 bf16 LoRA experts, shared expert with LoRA).
-With N > 1 (torchrun) every rank runs its own replica on its own tokens (weak scaling); the step time is the maximum
-over ranks. `--impl reference` times the CPU restatement of the reference's torch path on the host cores instead.
+With N > 1 (torchrun) every rank brings its own 4092 tokens (weak scaling) and the step time is the maximum over
+ranks: by default (`--parallel dp`) every GPU holds the whole layer and the LoRA gradients are all-reduced every step;
+`--parallel ep` splits the experts over the GPUs instead (smelb.ep, row all-to-alls over NCCL).
+`--impl reference` times the CPU restatement of the reference's torch path on the host cores instead.
 """
 import argparse
 import json
@@ -121,7 +123,7 @@ def layer_config(args):
     return dict(T=args.tokens, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=32.0)
 
 
-def config_json(cfg, meta, world):
+def config_json(cfg, meta, world, parallel="dp"):
     return {"workload": "qwen3.6-35b-a3b moe layer (config 2): fwd + recompute + bwd", "tokens": cfg["T"],
             "hidden": cfg["H"], "experts": cfg["E"], "top_k": cfg["K"], "expert_inter": cfg["I"],
             "shared_inter": cfg["S"], "frozen": "int4 group-64", "lora_experts": cfg["n_sel"],
@@ -129,7 +131,9 @@ def config_json(cfg, meta, world):
             f"{meta.get('share', 0):.3f}", "seed": meta.get("seed"),
             "l2": "weights 0.53 GB > L2 126 MB: each step streams the banks from HBM",
             "parallelism": "single" if world == 1 else
-            f"ep{world}: experts split over {world} GPUs, {cfg['T']} tokens per GPU (weak scaling)"}
+            (f"ep{world}: experts split over {world} GPUs, {cfg['T']} tokens per GPU (weak scaling)" if parallel == "ep"
+             else f"dp{world}: the whole layer on each of {world} GPUs, {cfg['T']} tokens per GPU (weak scaling), "
+                  f"LoRA gradients all-reduced every step")}
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline
@@ -157,9 +161,12 @@ def run_ours(args, world, rank, local):
     from smelb.synth import flops_per_token, qwen_layer
     dev = torch.device("cuda", local)
     cfg = layer_config(args)
-    ep_mode = world > 1
-    # with several GPUs the layer is expert parallel: one layer (same weights on every rank, built from one seed) whose
-    # experts are split over the ranks, and every rank brings its own cfg["T"] tokens (weak scaling)
+    ep_mode = world > 1 and args.parallel == "ep"
+    dp_mode = world > 1 and args.parallel == "dp"
+    # With several GPUs every rank brings its own cfg["T"] tokens (weak scaling) of one layer (same weights on every
+    # rank, built from one seed). dp: every GPU holds the whole layer (0.53 GB of weights, a small part of its HBM)
+    # and the LoRA gradients are summed over the ranks every step (one NCCL all-reduce of the flattened gradients);
+    # ep: the experts are split over the ranks (smelb.ep: count and row all-to-alls over NCCL).
     layer = qwen_layer(T=cfg["T"] * world, H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"],
                        n_sel=cfg["n_sel"], r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
     W, ex, lora, K = layer["W"], layer["ex"], layer["lora"], cfg["K"]
@@ -189,6 +196,23 @@ def run_ours(args, world, rank, local):
             ep.allreduce_shared_grads(lora_run)
         return xr.grad
 
+    flat = {}
+
+    def dp_sync():
+        """Data parallel: sum the LoRA gradients over the ranks (one all-reduce of their concatenation)."""
+        if not dp_mode:
+            return
+        grads = [p.grad for p in params if p.grad is not None]
+        if "buf" not in flat:
+            flat["buf"] = torch.empty(sum(g.numel() for g in grads), dtype=torch.float32, device=dev)
+        buf = flat["buf"]
+        torch.cat([g.reshape(-1).float() for g in grads], out=buf)
+        torch.distributed.all_reduce(buf)
+        o = 0
+        for g in grads:
+            g.view(-1).copy_(buf[o:o + g.numel()])
+            o += g.numel()
+
     # everything runs on one side stream: a CUDA graph is captured on it, and autograd's gradient accumulation
     # nodes must live on the stream they are replayed on
     side = torch.cuda.Stream(dev)
@@ -196,6 +220,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.set_stream(side)
     for _ in range(args.warmup):
         step(x, gy)
+        dp_sync()
     torch.cuda.synchronize()
     assert smelb.read_status() == 0, "device status word set during warm-up"
 
@@ -238,6 +263,7 @@ def run_ours(args, world, rank, local):
         if i >= 2:
             side.wait_event(down_done[b])  # the host copy of dX two steps back has left this buffer's slot
         dxs[b] = step(xd[b], gd[b])
+        dp_sync()
         used[b].record(side)
         with torch.cuda.stream(copy_s):
             copy_s.wait_event(used[b])
@@ -279,6 +305,7 @@ def run_ours(args, world, rank, local):
             graph.replay()
         else:
             step(x, gy)
+        dp_sync()
 
     for _ in range(args.warmup):
         run_step()
@@ -341,7 +368,8 @@ def run_ours(args, world, rank, local):
     res = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random-init weights of the layer shape)",
-           "config": dict(config_json(cfg, layer["meta"], world), timing=timing), "roofline": roof, "e2e": e2e,
+           "config": dict(config_json(cfg, layer["meta"], world, args.parallel), timing=timing), "roofline": roof,
+           "e2e": e2e,
            "gpu_launches": int(launches), "clocks": ck}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(layer, min(cfg["T"], args.cpu_tokens))
@@ -462,6 +490,8 @@ def main():
     ap.add_argument("--ref-budget-s", type=float, default=150.0, help="stop the reference arm after this long")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="config 4 token-count sweep (one JSON line per point)")
+    ap.add_argument("--parallel", default="dp", choices=["dp", "ep"],
+                    help="with N > 1: data-parallel replicas of the layer (dp) or experts split over the GPUs (ep)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
