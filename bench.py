@@ -196,22 +196,15 @@ def run_ours(args, world, rank, local):
             ep.allreduce_shared_grads(lora_run)
         return xr.grad
 
-    flat = {}
+    grad_sum = None
+    if dp_mode:
+        from smelb import dp
+        grad_sum = dp.GradAllReduce(params)
 
     def dp_sync():
         """Data parallel: sum the LoRA gradients over the ranks (one all-reduce of their concatenation)."""
-        if not dp_mode:
-            return
-        grads = [p.grad for p in params if p.grad is not None]
-        if "buf" not in flat:
-            flat["buf"] = torch.empty(sum(g.numel() for g in grads), dtype=torch.float32, device=dev)
-        buf = flat["buf"]
-        torch.cat([g.reshape(-1).float() for g in grads], out=buf)
-        torch.distributed.all_reduce(buf)
-        o = 0
-        for g in grads:
-            g.view(-1).copy_(buf[o:o + g.numel()])
-            o += g.numel()
+        if grad_sum is not None:
+            grad_sum()
 
     # everything runs on one side stream: a CUDA graph is captured on it, and autograd's gradient accumulation
     # nodes must live on the stream they are replayed on
