@@ -369,6 +369,67 @@ def run_ours(args, world, rank, local):
     return res
 
 
+# ------------------------------------------------------------------------------------------ layer streaming
+def run_stream(args, local, n_layers=4):
+    """Layer-major forward over a stack of config-2 layers (smel/layer_runner.py:319-330 with stream.py:90-110): each
+    layer's packed tensors come from pinned host memory through smelb.stream.LayerSource (two layers on the GPU,
+    the next one uploading while the current one computes), against the same stack kept resident. One JSON line per
+    mode: tokens/s of one pass over the stack, the bytes uploaded per pass and the time the compute stream waited."""
+    import smelb
+    from smelb.stream import LayerSource
+    from smelb.synth import qwen_layer
+    dev = torch.device("cuda", local)
+    cfg = layer_config(args)
+    host, x = {}, None
+    for l in range(n_layers):
+        L = qwen_layer(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"], n_sel=cfg["n_sel"],
+                       r=cfg["r"], alpha=cfg["alpha"], seed=20 + l, device=dev, with_lora=False)
+        ex = L["ex"]
+        t = dict(L["W"])
+        t.update({"experts.gate_up." + k: v for k, v in ex.frozen.gu.items()})
+        t.update({"experts.down." + k: v for k, v in ex.frozen.dn.items()})
+        t.update({"experts.sel.gate_up": ex.sel_gate_up, "experts.sel.down": ex.sel_down,
+                  "experts.sel.ids": ex.sel_ids.clone()})
+        host[l] = {k: v.cpu() for k, v in t.items()}
+        x = L["x"] if x is None else x
+        del L, ex, t
+    torch.cuda.empty_cache()
+    for mode in ("streamed", "resident"):
+        src = LayerSource(host, device=dev, resident=(mode == "resident"), max_on_gpu=2, timing=True)
+
+        def one_pass():
+            h = x
+            for l in range(n_layers):
+                dense, ex = src.get(l)
+                src.prefetch((l + 1) % n_layers)
+                h = smelb.moe_forward(h, dense, ex, cfg["K"], None)
+            return h
+
+        with torch.no_grad():
+            for _ in range(2):
+                one_pass()
+            torch.cuda.synchronize()
+            src.wait_ms()
+            src.stats.update(bytes=0, loads=0, wait_ms=0.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                one_pass()
+            e1.record()
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        line = {"stream": f"layer-major forward over {n_layers} config-2 layers", "mode": mode,
+                "layers": n_layers, "tokens": cfg["T"], "ms_per_pass": round(ms, 3),
+                "tokens_per_s_per_layer": round(cfg["T"] * n_layers / (ms / 1e3), 1),
+                "h2d_gb_per_pass": round(src.stats["bytes"] / args.steps / 1e9, 3),
+                "h2d_gbs": round(src.stats["bytes"] / args.steps / (ms / 1e3) / 1e9, 1),
+                "compute_wait_ms_per_pass": round(src.wait_ms() / args.steps, 3)}
+        print(json.dumps(line), flush=True)
+        src.close()
+        del src
+        torch.cuda.empty_cache()
+
+
 # ------------------------------------------------------------------------------------------ config 4 sweep
 def run_sweep(args, local):
     """Config 4: the Qwen3.6 layer shape, forward only (no grad), all 256 experts frozen int4 group-64, at 1, 16, 128,
@@ -483,14 +544,16 @@ def main():
     ap.add_argument("--ref-budget-s", type=float, default=150.0, help="stop the reference arm after this long")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="config 4 token-count sweep (one JSON line per point)")
+    ap.add_argument("--stream", action="store_true",
+                    help="layer-major forward over a stack of layers streamed from pinned host memory vs resident")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"],
                     help="with N > 1: data-parallel replicas of the layer (dp) or experts split over the GPUs (ep)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
-        if args.sweep:
+        if args.sweep or args.stream:
             if rank == 0:
-                run_sweep(args, local)
+                (run_sweep if args.sweep else run_stream)(args, local)
             res = None
         elif args.impl == "reference":
             res = run_reference(args, world, rank)
