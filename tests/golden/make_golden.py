@@ -14,6 +14,9 @@ Outputs (torch.save dicts of CPU tensors):
   gemma_block.pt  the Gemma 4 MoE block of smel/layer_runner.py:252-261 (dense GeGLU MLP with LoRA, route_gemma4,
                   int4 + LoRA routed experts, the four Gemma norms, layer_scalar) in fp32: inputs, outputs, routing,
                   dh, dxm and all LoRA gradients
+  pack.pt      smel/pack.py: pack_layer of a small checkpoint layer (dense fp32 tensors, an A_log, an integer
+               tensor, the fused bank, two selected experts) and merge_experts / merge_mlp with LoRA deltas
+               (python tests/golden/make_golden.py --only pack writes just this file)
 The test-suite never imports the reference; it only reads these files.
 """
 import argparse
@@ -43,8 +46,12 @@ def lora_tensors(H, I, S, n_sel, r, alpha, gen):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default=None, choices=[None, "pack"])
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    if args.only == "pack":
+        make_pack()
+        return
     from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
     from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
     from smel.quant import dequant_int4_torch, quantize_int4
@@ -183,7 +190,39 @@ def main():
                 "probs": probs.detach(), "topv": topv.detach(), "topi": topi, "dh": h.grad, "dxm": xm.grad,
                 "g_lora_ex": {n: getattr(lex_m, n).grad for n in lex_t},
                 "g_lora_sh": {n: getattr(lsh_m, n).grad for n in lsh_t}}, os.path.join(HERE, "gemma_block.pt"))
+    make_pack()
     print("golden fixtures written to", HERE)
+
+
+def make_pack():
+    from smel.lora import ExpertsLoRA, MLPLoRA
+    from smel.pack import merge_experts, merge_mlp, pack_layer
+    g = torch.Generator().manual_seed(21)
+    E, H, I, S, r = 6, 128, 64, 64, 8
+    t = {"mlp.gate.weight": torch.randn(E, H, generator=g) * 0.05,
+         "mlp.shared_expert.gate_proj.weight": torch.randn(S, H, generator=g) * 0.02,
+         "mlp.shared_expert.up_proj.weight": torch.randn(S, H, generator=g) * 0.02,
+         "mlp.shared_expert.down_proj.weight": torch.randn(H, S, generator=g) * 0.02,
+         "linear_attn.A_log": torch.randn(4, generator=g),
+         "step.count": torch.arange(3, dtype=torch.int64),
+         "mlp.experts.gate_up_proj": torch.randn(E, 2 * I, H, generator=g) * 0.02,
+         "mlp.experts.down_proj": torch.randn(E, H, I, generator=g) * 0.02}
+    sel = [4, 1]
+    packed = pack_layer(t, sel, 64)
+    lex = ExpertsLoRA(sel, H, I, r, 16.0)
+    lsh = MLPLoRA(H, S, r, 16.0)
+    with torch.no_grad():
+        for m in (lex, lsh):
+            for n in ("B_gate", "B_up", "B_down"):
+                getattr(m, n).copy_(torch.randn(getattr(m, n).shape, generator=g) * 0.05)
+    mgu, mdn = merge_experts(t["mlp.experts.gate_up_proj"].bfloat16(), t["mlp.experts.down_proj"].bfloat16(), lex)
+    mg, mu, md = merge_mlp(t["mlp.shared_expert.gate_proj.weight"].bfloat16(),
+                           t["mlp.shared_expert.up_proj.weight"].bfloat16(),
+                           t["mlp.shared_expert.down_proj.weight"].bfloat16(), lsh)
+    torch.save({"t": t, "sel": sel, "packed": packed,
+                "lora_ex": {n: p.detach().clone() for n, p in lex.named_parameters()},
+                "lora_sh": {n: p.detach().clone() for n, p in lsh.named_parameters()}, "r": r, "alpha": 16.0,
+                "merged_gu": mgu, "merged_dn": mdn, "merged_mlp": (mg, mu, md)}, os.path.join(HERE, "pack.pt"))
 
 
 if __name__ == "__main__":
