@@ -744,7 +744,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         const int m = ti.m0 + row;
         const int m0 = m & ~1;
         const bool odd = lane & 1;
-        const bool mvalid = m0 < P.M;
+        // features [M, m_pad) are stored as zeros (the 64-wide LoRA blocks whose unused columns must read as 0)
+        const bool mvalid = m0 < max(P.M, P.m_pad);
+        const bool lo_ok = m0 < P.M, hi_ok = m0 + 1 < P.M;
         const long long ldc = P.c_sn;
         uint32_t* cp = reinterpret_cast<uint32_t*>(reinterpret_cast<bf16*>(P.C) + (long long)ti.n0 * ldc + m0);
         const long long ldw = ldc >> 1;  // row pitch in 32-bit words
@@ -761,12 +763,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             const float send = __uint_as_float(odd ? v[j] : v[8 + j]);
             const float other = __shfl_xor_sync(0xffffffffu, send, 1);
             const float lo = odd ? other : mine, hi = odd ? mine : other;  // features m0, m0 + 1
-            if (mvalid && tb + j < n_valid) cp[(long long)(tb + j) * ldw] = bf162_bits(__floats2bfloat162_rn(lo * alpha, hi * alpha));
+            if (mvalid && tb + j < n_valid)
+              cp[(long long)(tb + j) * ldw] =
+                  bf162_bits(__floats2bfloat162_rn(lo_ok ? lo * alpha : 0.0f, hi_ok ? hi * alpha : 0.0f));
           }
         }
       } else {
         const int m = ti.m0 + row;
-        const bool mvalid = m < P.M;
+        const bool mvalid = m < max(P.M, P.m_pad);
+        const float am = m < P.M ? alpha : 0.0f;  // rows [M, m_pad) are stored as zeros
         const long long ldc = P.c_sn;
         const long long base = ((P.mode == kTokK) ? (long long)ti.g * P.c_gs : (long long)ti.n0 * ldc) +
                                (long long)m * P.c_sm;
@@ -787,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
             bf16* cp = reinterpret_cast<bf16*>(P.C) + base + (long long)c * ldc;
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (j < nn) cp[(long long)j * ldc] = __float2bfloat16_rn(__uint_as_float(v[j]) * alpha);
+              if (j < nn) cp[(long long)j * ldc] = __float2bfloat16_rn(am != 0.0f ? __uint_as_float(v[j]) * am : 0.0f);
           }
         }
       }

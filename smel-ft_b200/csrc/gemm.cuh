@@ -127,6 +127,7 @@ struct alignas(64) Problem {
   long long h_ld;     // row stride of Hin/Hout
   int inter;          // gated-MLP intermediate size (offset of up in h)
   float alpha;        // scale applied to the fp32 accumulator before the store
+  int m_pad;          // bf16 [token][feature] stores: features [M, m_pad) are written as zeros (0: none)
 };
 
 struct LaunchArgs {

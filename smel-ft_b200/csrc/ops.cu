@@ -282,6 +282,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.x, T, H));
       groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
       out_bf16(P, L.sh_xa, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     TRY(b.launch(st));
   }
@@ -308,6 +309,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.xs, R, H));
       groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
       out_bf16(P, L.xa, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     if (f.shared) {
       Problem& P = b.add();
@@ -365,6 +367,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.sh_a, T, S));
       groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
       out_bf16(P, L.sh_z, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     TRY(b.launch(st));
   }
@@ -377,6 +380,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.a, R, I));
       groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
       out_bf16(P, L.z, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     if (f.shared) {
       Problem& P = b.add();
@@ -459,6 +463,7 @@ int layer_bwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.dy, R, H));
       groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
       out_bf16(P, L.dz, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     if (f.sh_lora) {
       Problem& P = b.add();
@@ -466,6 +471,7 @@ int layer_bwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, sh_dy, T, H));
       groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
       out_bf16(P, L.sh_dz, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     TRY(b.launch(st));
   }
@@ -525,6 +531,7 @@ int layer_bwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.dh, R, 2 * I));
       groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
       out_bf16(P, L.dxa, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     if (f.sh_lora) {
       Problem& P = b.add();
@@ -532,6 +539,7 @@ int layer_bwd(const smelb_moe_layer& L) {
       TRY(set_b_tokens(P, L.sh_dh, T, 2 * S));
       groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
       out_bf16(P, L.sh_dxa, kW64);
+      P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     TRY(b.launch(st));
   }

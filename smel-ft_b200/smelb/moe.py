@@ -195,7 +195,6 @@ def _alloc_fwd(cfg, dev, save):
     b = {"out": torch.empty(T, H, dtype=torch.bfloat16, device=dev),
          "tok_count": torch.full((1,), T, dtype=torch.int32, device=dev)}
     e = lambda *s, dtype=torch.bfloat16: torch.empty(*s, dtype=dtype, device=dev)  # noqa: E731
-    z = lambda *s, dtype=torch.bfloat16: torch.zeros(*s, dtype=dtype, device=dev)  # noqa: E731
     if f & _lib.F_ROUTER:
         b.update(logits=e(T, E), probs=e(T, E, dtype=torch.float32), topv=e(T, K, dtype=cfg.topv_dtype),
                  topi=e(T, K, dtype=torch.int64))
@@ -210,7 +209,8 @@ def _alloc_fwd(cfg, dev, save):
         if save:
             b["h"] = e(R, 2 * I)
         if n and r:
-            b.update(xa=z(R, _W64), z=z(R, _W64), p_xa_w=e(n, 2 * r, H), p_gu_ext=e(n, 2 * I, _W64),
+            # the 64-wide LoRA blocks: the GEMMs write every row of the selected segments, padding columns as zeros
+            b.update(xa=e(R, _W64), z=e(R, _W64), p_xa_w=e(n, 2 * r, H), p_gu_ext=e(n, 2 * I, _W64),
                      p_z_w=e(n, r, I), p_dn_ext=e(n, H, _W64))
     else:
         cfg.max_rows = 0
@@ -219,7 +219,7 @@ def _alloc_fwd(cfg, dev, save):
         if save:
             b["sh_h"] = e(T, 2 * S)
         if rh:
-            b.update(sh_xa=z(T, _W64), sh_z=z(T, _W64), sp_xa_w=e(1, 2 * rh, H), sp_gu_ext=e(1, 2 * S, _W64),
+            b.update(sh_xa=e(T, _W64), sh_z=e(T, _W64), sp_xa_w=e(1, 2 * rh, H), sp_gu_ext=e(1, 2 * S, _W64),
                      sp_z_w=e(1, rh, S), sp_dn_ext=e(1, H, _W64))
     return b
 
@@ -234,12 +234,13 @@ def _alloc_bwd(cfg, dev):
         R = cfg.max_rows
         b.update(dy=e(R, H), dh=e(R, 2 * I), dxs=e(R, H), dtopv=e(T, K, dtype=cfg.topv_dtype))
         if n and r:
-            b.update(dz=z(R, _W64), dxa=z(R, _W64), p_dz_w=e(n, r, H), p_da_ext=e(n, I, _W64),
+            b.update(dz=e(R, _W64), dxa=e(R, _W64), p_dz_w=e(n, r, H), p_da_ext=e(n, I, _W64),
                      p_dxa_w=e(n, 2 * r, 2 * I), p_dx_ext=e(n, H, _W64))
             for name, shp in zip(_LORA_NAMES, ((n, r, H), (n, I, r), (n, r, H), (n, I, r), (n, r, I), (n, H, r))):
                 b["g" + name] = e(*shp, dtype=torch.float32)
     if f & _lib.F_ROUTER:
-        b.update(dlogits=z(T, (E + 63) // 64 * 64), dx_router=e(T, H))
+        Ep = (E + 63) // 64 * 64  # padding columns (E % 64 != 0) must read as zero; the router backward writes the rest
+        b.update(dlogits=(e if Ep == E else z)(T, Ep), dx_router=e(T, H))
         if "dtopv" not in b:
             b["dtopv"] = e(T, K, dtype=cfg.topv_dtype)
     if f & _lib.F_SHARED:
@@ -247,7 +248,7 @@ def _alloc_bwd(cfg, dev):
         if f & _lib.F_SHARED_GATE:
             b.update(sh_dy=e(T, H), dgl=e(T, dtype=torch.float32))
         if rh:
-            b.update(sh_dz=z(T, _W64), sh_dxa=z(T, _W64), sp_dz_w=e(1, rh, H), sp_da_ext=e(1, S, _W64),
+            b.update(sh_dz=e(T, _W64), sh_dxa=e(T, _W64), sp_dz_w=e(1, rh, H), sp_da_ext=e(1, S, _W64),
                      sp_dxa_w=e(1, 2 * rh, 2 * S), sp_dx_ext=e(1, H, _W64))
             for name, shp in zip(_LORA_NAMES, ((rh, H), (S, rh), (rh, H), (S, rh), (rh, S), (H, rh))):
                 b["gsh" + name] = e(*shp, dtype=torch.float32)

@@ -175,6 +175,18 @@ def test_moe_forward_medium_zipf(dev):
     _check_layer(L, dev)
 
 
+def test_moe_forward_after_nan_poisoned_allocator(dev):
+    """The layer's scratch buffers come uninitialised from torch's caching allocator (the 64-wide LoRA blocks rely on
+    the GEMMs writing every row they later read, padding columns as zeros). Fill the allocator's free blocks with
+    NaNs first, so any buffer region read before it is written shows up in the comparison."""
+    from smelb.synth import qwen_layer
+    L = qwen_layer(T=520, H=512, E=32, K=4, I=256, S=256, n_sel=4, r=16, seed=4, device=dev)
+    torch.cuda.synchronize()
+    junk = [torch.full((1 << 26,), float("nan"), dtype=torch.float32, device=dev) for _ in range(8)]
+    del junk
+    _check_layer(L, dev)
+
+
 def test_moe_forward_gemma_like_shapes(dev):
     """Intermediate sizes that are not multiples of 128 (704-like: 5.5 tiles) and GELU-tanh."""
     from smelb.synth import qwen_layer
