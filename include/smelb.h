@@ -248,6 +248,39 @@ typedef struct smelb_moe_layer {
   const void* per_expert_scale; /* bf16 [E] multiplier of the renormalised top-k weights (Gemma 4), or NULL */
 } smelb_moe_layer;
 
+/* ---------------------------------------------------------------------------------------------------- int8 rows
+ * smel/quant.py:97-105 quantize_int8_rows / dequant_int8_rows: symmetric int8 per row of w (bf16, or fp32 when
+ * w_fp32) [rows, H]: s = max(amax|w| / 127, 1e-12) (fp32), q = clamp(round_half_even(w / s), -127, 127) (int8
+ * [rows, H]), scale = bf16(s) [rows]; dequant: out [rows, H] = q * scale rounded once to bf16, or fp32 when
+ * out_fp32. */
+int smelb_int8_rows_quantize(const void* w, int w_fp32, int64_t rows, int64_t H, void* q, void* scale, void* stream);
+int smelb_int8_rows_dequant(const void* q, const void* scale, int64_t rows, int64_t H, void* out, int out_fp32,
+                            void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- chunked CE
+ * smel/loss.py:130-156 chunked_ce / _ChunkedCE.forward, each token chunk one pass of smel/loss.py:50-92 _ce_chunk
+ * over the vocabulary chunks: the cross-entropy of the hidden rows h (bf16 [N, H], H % 64 == 0) against tgt
+ * (int64 [N]) over a frozen LM head, the gradient accumulated online under the log-sum-exp's running maximum.
+ * Head: bf16 rows w [V, H], or int8 rows q [V, H] with a bf16 scale per row q_scale [V] (smel/quant.py:97-105);
+ * pass exactly one of the two. softcap > 0 caps the logits as cap * tanh(z / cap) (smel/loss.py:34-35), gradient
+ * included. Outputs: loss_rows (fp32 [N]) = lse - target logit per row (a target outside [0, V) contributes lse);
+ * loss (fp32 [1]) = sum(loss_rows) / denom; gh (bf16 [N, H]) = d loss / d h, or NULL for the loss alone.
+ * workspace: 256-byte aligned, smelb_chunked_ce_workspace_bytes(min(N, token_chunk), H, min(V, vocab_chunk), int8)
+ * bytes. */
+int64_t smelb_chunked_ce_workspace_bytes(int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8);
+int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, const void* w, const void* q,
+                     const void* q_scale, int64_t V, int64_t vocab_chunk, int64_t token_chunk, float softcap,
+                     float denom, float* loss_rows, float* loss, void* gh, void* workspace, int64_t workspace_bytes,
+                     void* stream);
+
+/* smel/loss.py:45-47 LMHead.logits: out (fp32 [N, V]) = cap(float(bf16(h @ W^T))) chunk by chunk over the
+ * vocabulary; the head as for smelb_chunked_ce. workspace: 256-byte aligned,
+ * smelb_lm_logits_workspace_bytes(N, H, min(V, vocab_chunk), int8) bytes. */
+int64_t smelb_lm_logits_workspace_bytes(int64_t N, int64_t H, int64_t vocab_chunk, int int8);
+int smelb_lm_logits(const void* h, int64_t N, int64_t H, const void* w, const void* q, const void* q_scale, int64_t V,
+                    int64_t vocab_chunk, float softcap, float* out, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+
 /* Instrumentation. smelb_launch_count: kernels launched by this library so far (all entry points).
  * smelb_gemm_timing(1) records a CUDA event pair on the launching stream around every expert-GEMM launch;
  * smelb_gemm_timing_read synchronizes on them and returns the summed duration (ms) and the number of launches

@@ -1,6 +1,8 @@
 // Memory-bound kernels of the MoE layer: int4 dequant (parity helper) and (scale, zero) repack, router softmax /
 // top-k / renorm and its backward, the deterministic counting-sort dispatch, row gather, the fp32 weighted combine
 // and its backward, the final dX reduction and the per-step LoRA factor packing.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "host.h"
@@ -1126,6 +1128,244 @@ int pack_blocks(const PackSpec& spec, void* out, cudaStream_t st) {
   if (n == 0) return kOk;
   const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 8);
   pack_blocks_kernel<<<(int)blocks, 256, 0, st>>>(spec, (bf16*)out);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+
+// ============================================================================================ chunked CE
+// The per-row steps of smel/loss.py:50-92 (_ce_chunk) for one vocabulary chunk, in the reference's order: the
+// (capped) logits z, the chunk maximum, the new running maximum nm and the rescale r = exp(m - nm), the softmax
+// numerators exp(z - nm) summed into s = s * r + sum, then (for the gradient) multiplied by the cap's derivative
+// 1 - (z / cap)^2 and rounded to bf16 as the reference's p.to(h.dtype). The target's logit, the cap's derivative
+// there and its head row are taken from the chunk that holds the target.
+__device__ __forceinline__ float ce_cap(float z, float cap) { return cap > 0.f ? cap * tanhf(z / cap) : z; }
+
+template <bool kMax>
+__device__ __forceinline__ float block_reduce_256(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = kMax ? fmaxf(v, u) : v + u;
+  }
+  __syncthreads();  // red may still be read by the previous reduction
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) v = kMax ? fmaxf(v, red[i]) : v + red[i];
+  return v;
+}
+
+__global__ void set_count_kernel(int* p, int v) { *p = v; }
+
+__global__ void ce_init_kernel(CeState st, long long n, int H) {
+  const long long tot = n * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
+    st.acc[i] = 0.f;
+    st.tgt_row[i] = 0.f;
+    if (i < n) {
+      st.m[i] = -INFINITY;
+      st.s[i] = 0.f;
+      st.r[i] = 0.f;
+      st.tlog[i] = 0.f;
+      st.tdrv[i] = 1.f;
+    }
+  }
+}
+
+// One block per token row. The row's logits are read twice (maximum, then exponentials) and overwritten in place by p.
+__global__ void __launch_bounds__(256) ce_rows_kernel(bf16* __restrict__ lg, int ld, int Vc, long long v0,
+                                                     const long long* __restrict__ tgt, float cap, int need_grad,
+                                                     const bf16* __restrict__ wc, int H, CeState st) {
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  bf16* l = lg + row * ld;
+  const long long t = tgt[row];
+  const bool has_t = t >= v0 && t < v0 + Vc;
+  const int c = has_t ? (int)(t - v0) : 0;
+  const float zt = has_t ? ce_cap(__bfloat162float(l[c]), cap) : 0.f;  // read before any thread writes p
+  float cm = -INFINITY;
+  for (int v = threadIdx.x; v < Vc; v += 256) cm = fmaxf(cm, ce_cap(__bfloat162float(l[v]), cap));
+  cm = block_reduce_256<true>(cm, red);
+  const float m_old = st.m[row];
+  const float nm = fmaxf(m_old, cm);
+  const float r = expf(m_old - nm);
+  float sum = 0.f;
+  for (int v = threadIdx.x; v < ld; v += 256) {
+    float e = 0.f, pv = 0.f;
+    if (v < Vc) {
+      const float z = ce_cap(__bfloat162float(l[v]), cap);
+      e = expf(z - nm);
+      pv = cap > 0.f ? e * (1.f - (z / cap) * (z / cap)) : e;
+    }
+    sum += e;
+    if (need_grad) l[v] = __float2bfloat16_rn(pv);
+  }
+  sum = block_reduce_256<false>(sum, red);
+  if (threadIdx.x == 0) {
+    st.s[row] = st.s[row] * r + sum;
+    st.m[row] = nm;
+    st.r[row] = r;
+    if (has_t) {
+      st.tlog[row] = zt;
+      if (cap > 0.f) st.tdrv[row] = 1.f - (zt / cap) * (zt / cap);
+    }
+  }
+  if (has_t && need_grad)
+    for (int i = threadIdx.x; i < H; i += 256) st.tgt_row[row * H + i] = __bfloat162float(wc[(long long)c * H + i]);
+}
+
+__global__ void ce_acc_kernel(const float* __restrict__ parts, int nparts, CeState st, long long n, int H) {
+  const long long tot = n * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
+    float pw = parts[i];
+    for (int q = 1; q < nparts; ++q) pw += parts[q * tot + i];
+    st.acc[i] = st.acc[i] * st.r[i / H] + pw;
+  }
+}
+
+__global__ void ce_finish_kernel(CeState st, long long n, int H, float denom, float* __restrict__ loss_rows,
+                                 bf16* __restrict__ gh) {
+  const long long tot = n * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / H;
+    if (gh) gh[i] = __float2bfloat16_rn((st.acc[i] / st.s[row] - st.tdrv[row] * st.tgt_row[i]) / denom);
+    if (i < n) loss_rows[i] = st.m[i] + logf(st.s[i]) - st.tlog[i];
+  }
+}
+
+__global__ void __launch_bounds__(256) ce_loss_sum_kernel(const float* __restrict__ loss_rows, long long n,
+                                                         float denom, float* __restrict__ loss) {
+  __shared__ float red[8];
+  float v = 0.f;
+  for (long long i = threadIdx.x; i < n; i += 256) v += loss_rows[i];
+  v = block_reduce_256<false>(v, red);
+  if (threadIdx.x == 0) *loss = v / denom;
+}
+
+template <typename OutT>
+__global__ void int8_rows_dequant_kernel(const int8_t* __restrict__ q, const bf16* __restrict__ scale,
+                                         long long rows, int H, OutT* __restrict__ out) {
+  const long long tot = rows * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
+    const float v = (float)q[i] * __bfloat162float(scale[i / H]);  // exact in fp32 (8-bit times 8-bit mantissas)
+    if constexpr (std::is_same<OutT, float>::value) out[i] = v;
+    else out[i] = __float2bfloat16_rn(v);
+  }
+}
+
+__global__ void ce_logits_out_kernel(const bf16* __restrict__ lg, int ld, int Vc, long long n, float cap,
+                                     float* __restrict__ out, long long ldo) {
+  const long long tot = n * Vc;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / Vc;
+    const int v = (int)(i - row * Vc);
+    out[row * ldo + v] = ce_cap(__bfloat162float(lg[row * ld + v]), cap);
+  }
+}
+
+// smel/quant.py:97-101: s = max(amax|w| / 127, 1e-12) in fp32, q = clamp(rint(w / s), -127, 127) (round half to
+// even, as torch.round), the scale stored as bf16. One block per row.
+__global__ void __launch_bounds__(256) int8_rows_quantize_kernel(const void* __restrict__ w, int w_fp32, int H,
+                                                                int8_t* __restrict__ q, bf16* __restrict__ scale) {
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  const float* wf = reinterpret_cast<const float*>(w) + row * H;
+  const bf16* wb = reinterpret_cast<const bf16*>(w) + row * H;
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < H; i += 256) mx = fmaxf(mx, fabsf(w_fp32 ? wf[i] : __bfloat162float(wb[i])));
+  mx = block_reduce_256<true>(mx, red);
+  const float s = fmaxf(mx / 127.f, 1e-12f);
+  for (int i = threadIdx.x; i < H; i += 256) {
+    const float v = rintf((w_fp32 ? wf[i] : __bfloat162float(wb[i])) / s);
+    q[row * H + i] = (int8_t)fminf(fmaxf(v, -127.f), 127.f);
+  }
+  if (threadIdx.x == 0) scale[row] = __float2bfloat16_rn(s);
+}
+
+static int grid_for(long long work) {
+  return (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, 148LL * 16));
+}
+
+int set_count(int* p, int v, cudaStream_t s) {
+  set_count_kernel<<<1, 1, 0, s>>>(p, v);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_init(const CeState& st, long long n, int H, cudaStream_t s) {
+  if (n == 0) return kOk;
+  ce_init_kernel<<<grid_for(n * H), 256, 0, s>>>(st, n, H);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_rows(void* lg, int ld, int Vc, long long v0, const long long* tgt, float softcap, bool need_grad,
+            const void* wc, int H, const CeState& st, long long n, cudaStream_t s) {
+  SMELB_CHECK_ARG(Vc > 0 && ld >= Vc && n <= 2147483647LL, kErrShape, "ce_rows: Vc=%d ld=%d", Vc, ld);
+  if (n == 0) return kOk;
+  ce_rows_kernel<<<(int)n, 256, 0, s>>>((bf16*)lg, ld, Vc, v0, tgt, softcap, need_grad ? 1 : 0, (const bf16*)wc, H,
+                                        st);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_acc(const float* parts, int nparts, const CeState& st, long long n, int H, cudaStream_t s) {
+  if (n == 0) return kOk;
+  ce_acc_kernel<<<grid_for(n * H), 256, 0, s>>>(parts, nparts, st, n, H);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_finish(const CeState& st, long long n, int H, float denom, float* loss_rows, void* gh, cudaStream_t s) {
+  if (n == 0) return kOk;
+  ce_finish_kernel<<<grid_for(n * H), 256, 0, s>>>(st, n, H, denom, loss_rows, (bf16*)gh);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_logits_out(const void* lg, int ld, int Vc, long long n, float softcap, float* out, long long ldo,
+                  cudaStream_t s) {
+  if (n == 0) return kOk;
+  ce_logits_out_kernel<<<grid_for(n * Vc), 256, 0, s>>>((const bf16*)lg, ld, Vc, n, softcap, out, ldo);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int ce_loss_sum(const float* loss_rows, long long n, float denom, float* loss, cudaStream_t s) {
+  ce_loss_sum_kernel<<<1, 256, 0, s>>>(loss_rows, n, denom, loss);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int int8_rows_quantize(const void* w, bool w_fp32, long long rows, int H, void* q, void* scale, cudaStream_t s) {
+  SMELB_CHECK_ARG(rows <= 2147483647LL && H > 0, kErrShape, "int8_rows_quantize: rows=%lld H=%d", rows, H);
+  if (rows == 0) return kOk;
+  int8_rows_quantize_kernel<<<(int)rows, 256, 0, s>>>(w, w_fp32 ? 1 : 0, H, (int8_t*)q, (bf16*)scale);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int int8_rows_dequant(const void* q, const void* scale, long long rows, int H, void* out, cudaStream_t s,
+                      bool out_fp32) {
+  if (rows == 0) return kOk;
+  if (out_fp32)
+    int8_rows_dequant_kernel<float><<<grid_for(rows * H), 256, 0, s>>>((const int8_t*)q, (const bf16*)scale, rows, H,
+                                                                       (float*)out);
+  else
+    int8_rows_dequant_kernel<bf16><<<grid_for(rows * H), 256, 0, s>>>((const int8_t*)q, (const bf16*)scale, rows, H,
+                                                                      (bf16*)out);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;

@@ -92,6 +92,35 @@ struct NormBwdArgs {
   bf16* dx;
 };
 
+// Chunked cross-entropy over a frozen LM head (smel/loss.py:50-92), the per-row steps around the two GEMMs of a
+// vocabulary chunk. State per row: running max m, running sum s, the last rescale factor r, the target's (capped)
+// logit, the cap's derivative at the target, the fp32 gradient accumulator [n, H] and the target's head row.
+struct CeState {
+  float *m, *s, *r, *tlog, *tdrv;
+  float *acc, *tgt_row;  // [n, H]
+};
+int ce_init(const CeState& st, long long n, int H, cudaStream_t s);
+// *p = v on the stream (the device-side token count the GEMM reads)
+int set_count(int* p, int v, cudaStream_t s);
+// lg: bf16 logits [n, ld] of the chunk's Vc columns (vocabulary rows v0 .. v0 + Vc - 1), overwritten in place by p,
+// the softmax numerators times the cap's derivative (bf16, zero in columns Vc .. ld - 1) when need_grad.
+int ce_rows(void* lg, int ld, int Vc, long long v0, const long long* tgt, float softcap, bool need_grad,
+            const void* wc, int H, const CeState& st, long long n, cudaStream_t s);
+// acc = acc * r + sum of the nparts fp32 partial products [nparts][n, H] (the chunk's p @ W, split along the chunk)
+int ce_acc(const float* parts, int nparts, const CeState& st, long long n, int H, cudaStream_t s);
+// loss_rows = m + log s - tlog; gh (bf16, may be NULL) = (acc / s - tdrv * tgt_row) / denom
+int ce_finish(const CeState& st, long long n, int H, float denom, float* loss_rows, void* gh, cudaStream_t s);
+// out[row, v] (fp32, row pitch ldo) = cap(float(lg[row, v])) for the chunk's Vc columns
+int ce_logits_out(const void* lg, int ld, int Vc, long long n, float softcap, float* out, long long ldo,
+                  cudaStream_t s);
+// loss = sum(loss_rows) / denom (one block, fixed order)
+int ce_loss_sum(const float* loss_rows, long long n, float denom, float* loss, cudaStream_t s);
+// w (bf16 or fp32 [rows, H]) -> int8 rows q [rows, H] + bf16 scale [rows] (smel/quant.py:97-101)
+int int8_rows_quantize(const void* w, bool w_fp32, long long rows, int H, void* q, void* scale, cudaStream_t s);
+// int8 rows (symmetric, bf16 scale per row) -> bf16 or fp32: q * scale rounded once (smel/quant.py:104-105)
+int int8_rows_dequant(const void* q, const void* scale, long long rows, int H, void* out, cudaStream_t s,
+                      bool out_fp32 = false);
+
 int rmsnorm_fwd(const NormArgs& a, cudaStream_t st);
 int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st);
 

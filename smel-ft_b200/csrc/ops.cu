@@ -986,3 +986,236 @@ extern "C" int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, in
   }
   return kOk;
 }
+
+// ---------------------------------------------------------------------------------------------------- chunked CE
+// smel/loss.py:130-146 _ChunkedCE.forward over token chunks, each one pass of smel/loss.py:50-92 _ce_chunk over the
+// vocabulary chunks. Per (token chunk, vocabulary chunk):
+//   [int8 head: dequantize the chunk's rows to bf16]
+//   GEMM 1  lg[n, Vcp] = bf16(h @ Wc^T)                         (A = Wc K-major, tokens as B, the MoE GEMM engine)
+//   rows    online max / sum, target capture, p = exp(z - m) * cap'(z) in bf16 over lg in place
+//   GEMM 2  part[s][n, H] = p[:, ks] @ Wc[ks]                  (A = Wc MN-major, the chunk split along k into
+//                                                               nsplit fp32 partials so the tiles fill the SMs)
+//   acc     acc = acc * r + sum_s part[s]
+// then loss_rows and gh for the token chunk, and the loss over all rows at the end.
+namespace {
+
+constexpr int kCeMaxSplit = 4;
+
+size_t ce_align(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct CeLayout {
+  size_t tok, lg, parts, acc, tgt_row, m, s, r, tlog, tdrv, wc, total;
+};
+
+CeLayout ce_layout(long long n, long long H, long long vocab_chunk, bool int8) {
+  const long long vcp = (vocab_chunk + 63) / 64 * 64;
+  CeLayout L{};
+  size_t o = 0;
+  L.tok = o;      o += ce_align(4);
+  L.lg = o;       o += ce_align((size_t)n * vcp * 2);
+  L.parts = o;    o += ce_align((size_t)kCeMaxSplit * n * H * 4);
+  L.acc = o;      o += ce_align((size_t)n * H * 4);
+  L.tgt_row = o;  o += ce_align((size_t)n * H * 4);
+  L.m = o;        o += ce_align((size_t)n * 4);
+  L.s = o;        o += ce_align((size_t)n * 4);
+  L.r = o;        o += ce_align((size_t)n * 4);
+  L.tlog = o;     o += ce_align((size_t)n * 4);
+  L.tdrv = o;     o += ce_align((size_t)n * 4);
+  L.wc = o;       o += int8 ? ce_align((size_t)vocab_chunk * H * 2) : 0;
+  L.total = o;
+  return L;
+}
+
+// Number of k-splits of GEMM 2 whose tiles best fill whole waves of the SMs (fewest splits on a tie).
+int ce_splits(long long n, long long H, int vcp, int sms) {
+  const long long tiles = ((H + 127) / 128) * ((n + kMaxBN - 1) / kMaxBN);
+  int best = 1;
+  double best_fill = 0.0;
+  for (int s = 1; s <= kCeMaxSplit && 64 * s <= vcp; ++s) {
+    const long long t = tiles * s;
+    const double fill = (double)t / (double)(((t + sms - 1) / sms) * sms);
+    if (fill > best_fill + 1e-9) {
+      best_fill = fill;
+      best = s;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+int smelb_int8_rows_quantize(const void* w, int w_fp32, int64_t rows, int64_t H, void* q, void* scale,
+                              void* stream) {
+  SMELB_CHECK_ARG(w && q && scale, kErrArg, "int8_rows_quantize: null pointer");
+  SMELB_CHECK_ARG(H > 0 && H <= (1 << 30), kErrShape, "int8_rows_quantize: H=%lld", (long long)H);
+  return int8_rows_quantize(w, w_fp32 != 0, rows, (int)H, q, scale, (cudaStream_t)stream);
+}
+
+int smelb_int8_rows_dequant(const void* q, const void* scale, int64_t rows, int64_t H, void* out, int out_fp32,
+                            void* stream) {
+  SMELB_CHECK_ARG(q && scale && out, kErrArg, "int8_rows_dequant: null pointer");
+  SMELB_CHECK_ARG(H > 0 && H <= (1 << 30), kErrShape, "int8_rows_dequant: H=%lld", (long long)H);
+  return int8_rows_dequant(q, scale, rows, (int)H, out, (cudaStream_t)stream, out_fp32 != 0);
+}
+
+int64_t smelb_chunked_ce_workspace_bytes(int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8) {
+  if (token_chunk <= 0 || H <= 0 || vocab_chunk <= 0) return 0;
+  return (int64_t)ce_layout(token_chunk, H, vocab_chunk, int8 != 0).total;
+}
+
+int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, const void* w, const void* q,
+                     const void* q_scale, int64_t V, int64_t vocab_chunk, int64_t token_chunk, float softcap,
+                     float denom, float* loss_rows, float* loss, void* gh, void* workspace, int64_t workspace_bytes,
+                     void* stream) {
+  SMELB_CHECK_ARG(tgt && loss_rows && loss && workspace && (N == 0 || h), kErrArg, "chunked_ce: null pointer");
+  SMELB_CHECK_ARG((w != nullptr) != (q != nullptr) && (q == nullptr || q_scale != nullptr), kErrArg,
+                  "chunked_ce: pass exactly one of the bf16 head (w) or the int8 head (q, q_scale)");
+  SMELB_CHECK_ARG(H > 0 && H % 64 == 0 && H <= 65536, kErrShape, "chunked_ce: H=%lld (a multiple of 64 is required)",
+                  (long long)H);
+  SMELB_CHECK_ARG(N >= 0 && V > 0 && vocab_chunk > 0 && vocab_chunk <= (1 << 24) && token_chunk > 0 && V < (1LL << 40),
+                  kErrShape, "chunked_ce: N=%lld V=%lld vocab_chunk=%lld token_chunk=%lld", (long long)N,
+                  (long long)V, (long long)vocab_chunk, (long long)token_chunk);
+  SMELB_CHECK_ARG(softcap >= 0.f, kErrArg, "chunked_ce: softcap=%g", (double)softcap);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool int8 = q != nullptr;
+  const bool need_grad = gh != nullptr;
+  const long long tc = std::min<long long>(token_chunk, std::max<long long>(N, 1));
+  const long long vc_max = std::min<long long>(vocab_chunk, V);
+  const CeLayout lay = ce_layout(tc, H, vc_max, int8);
+  SMELB_CHECK_ARG(workspace_bytes >= (int64_t)lay.total, kErrWorkspace,
+                  "chunked_ce: workspace %lld bytes, %lld needed", (long long)workspace_bytes, (long long)lay.total);
+  SMELB_CHECK_ARG(((uintptr_t)workspace & 255) == 0 && ((uintptr_t)h & 15) == 0 && (int8 || ((uintptr_t)w & 15) == 0),
+                  kErrArg, "chunked_ce: workspace must be 256-byte aligned, h and w 16-byte aligned");
+  char* ws = (char*)workspace;
+  int* tok = (int*)(ws + lay.tok);
+  bf16* lg = (bf16*)(ws + lay.lg);
+  float* parts = (float*)(ws + lay.parts);
+  CeState S{(float*)(ws + lay.m),   (float*)(ws + lay.s),   (float*)(ws + lay.r),      (float*)(ws + lay.tlog),
+            (float*)(ws + lay.tdrv), (float*)(ws + lay.acc), (float*)(ws + lay.tgt_row)};
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  const int sms = num_sms(dev);
+  for (long long t0 = 0; t0 < N; t0 += tc) {
+    const long long n = std::min<long long>(tc, N - t0);
+    const bf16* hc = (const bf16*)h + t0 * H;
+    const long long* tg = (const long long*)tgt + t0;
+    TRY(set_count(tok, (int)n, st));
+    TRY(ce_init(S, n, (int)H, st));
+    for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
+      const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
+      const int vcp = (Vc + 63) / 64 * 64;
+      const void* wc;
+      if (int8) {
+        TRY(int8_rows_dequant((const int8_t*)q + v0 * H, (const bf16*)q_scale + v0, Vc, (int)H, ws + lay.wc, st));
+        wc = ws + lay.wc;
+      } else {
+        wc = (const bf16*)w + v0 * H;
+      }
+      {
+        Builder b;
+        Problem& P = b.add();
+        TRY(set_a_bf16(P, wc, 1, Vc, (int)H, false, false));
+        TRY(set_b_tokens(P, hc, n, (int)H));
+        groups(P, tok, nullptr, nullptr, nullptr, 1);
+        out_bf16(P, lg, vcp);
+        TRY(b.launch(st));
+      }
+      TRY(ce_rows(lg, vcp, Vc, v0, tg, softcap, need_grad, wc, (int)H, S, n, st));
+      if (!need_grad) continue;
+      const int ns = ce_splits(n, H, vcp, sms);
+      const int kstep = ((vcp / 64 + ns - 1) / ns) * 64;
+      int np = 0;
+      {
+        Builder b;
+        for (int k0 = 0; k0 < vcp; k0 += kstep, ++np) {
+          const int kk = std::min(kstep, vcp - k0);
+          const int rows = std::min(Vc, k0 + kk) - k0;  // >= 1: only the last 63 columns of vcp can lie past Vc
+          Problem& P = b.add();
+          TRY(set_a_bf16(P, (const bf16*)wc + (long long)k0 * H, 1, rows, (int)H, true, false));
+          P.K = kk;
+          P.mode = kTokN;
+          P.BN = kMaxBN;
+          TRY(make_tmap_2d(&P.tmB32, lg + k0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, kk, (uint64_t)vcp * 2, 64, 32,
+                           128));
+          TRY(make_tmap_2d(&P.tmB, lg + k0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, kk, (uint64_t)vcp * 2, 64, 64,
+                           128));
+          groups(P, tok, nullptr, nullptr, nullptr, 1);
+          P.epi = kEpiStoreF32;
+          P.C = parts + (long long)np * n * H;
+          P.c_sn = H;
+          P.c_sm = 1;
+        }
+        TRY(b.launch(st));
+      }
+      TRY(ce_acc(parts, np, S, n, (int)H, st));
+    }
+    TRY(ce_finish(S, n, (int)H, denom, loss_rows + t0, need_grad ? (bf16*)gh + t0 * H : nullptr, st));
+  }
+  return ce_loss_sum(loss_rows, N, denom, loss, st);
+}
+
+namespace {
+// workspace of smelb_lm_logits: the token count, the chunk's bf16 logits [N, Vcp] and (int8 head) its bf16 rows
+struct LogitsLayout {
+  size_t tok, lg, wc, total;
+};
+LogitsLayout logits_layout(long long N, long long H, long long vocab_chunk, bool int8) {
+  const long long vcp = (vocab_chunk + 63) / 64 * 64;
+  LogitsLayout L{};
+  L.tok = 0;
+  L.lg = ce_align(4);
+  L.wc = L.lg + ce_align((size_t)N * vcp * 2);
+  L.total = L.wc + (int8 ? ce_align((size_t)vocab_chunk * H * 2) : 0);
+  return L;
+}
+}  // namespace
+
+int64_t smelb_lm_logits_workspace_bytes(int64_t N, int64_t H, int64_t vocab_chunk, int int8) {
+  if (N <= 0 || H <= 0 || vocab_chunk <= 0) return 0;
+  return (int64_t)logits_layout(N, H, vocab_chunk, int8 != 0).total;
+}
+
+int smelb_lm_logits(const void* h, int64_t N, int64_t H, const void* w, const void* q, const void* q_scale, int64_t V,
+                    int64_t vocab_chunk, float softcap, float* out, void* workspace, int64_t workspace_bytes,
+                    void* stream) {
+  SMELB_CHECK_ARG(out && workspace && (N == 0 || h), kErrArg, "lm_logits: null pointer");
+  SMELB_CHECK_ARG((w != nullptr) != (q != nullptr) && (q == nullptr || q_scale != nullptr), kErrArg,
+                  "lm_logits: pass exactly one of the bf16 head (w) or the int8 head (q, q_scale)");
+  SMELB_CHECK_ARG(H > 0 && H % 64 == 0 && H <= 65536 && N >= 0 && N <= (1LL << 31) - 1 && V > 0 && vocab_chunk > 0 &&
+                      vocab_chunk <= (1 << 24),
+                  kErrShape, "lm_logits: N=%lld H=%lld V=%lld vocab_chunk=%lld", (long long)N, (long long)H,
+                  (long long)V, (long long)vocab_chunk);
+  SMELB_CHECK_ARG(softcap >= 0.f, kErrArg, "lm_logits: softcap=%g", (double)softcap);
+  if (N == 0) return kOk;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool int8 = q != nullptr;
+  const LogitsLayout lay = logits_layout(N, H, std::min<long long>(vocab_chunk, V), int8);
+  SMELB_CHECK_ARG(workspace_bytes >= (int64_t)lay.total, kErrWorkspace, "lm_logits: workspace %lld bytes, %lld needed",
+                  (long long)workspace_bytes, (long long)lay.total);
+  SMELB_CHECK_ARG(((uintptr_t)workspace & 255) == 0 && ((uintptr_t)h & 15) == 0 && (int8 || ((uintptr_t)w & 15) == 0),
+                  kErrArg, "lm_logits: workspace must be 256-byte aligned, h and w 16-byte aligned");
+  char* ws = (char*)workspace;
+  int* tok = (int*)(ws + lay.tok);
+  bf16* lg = (bf16*)(ws + lay.lg);
+  TRY(set_count(tok, (int)N, st));
+  for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
+    const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
+    const int vcp = (Vc + 63) / 64 * 64;
+    const void* wc;
+    if (int8) {
+      TRY(int8_rows_dequant((const int8_t*)q + v0 * H, (const bf16*)q_scale + v0, Vc, (int)H, ws + lay.wc, st));
+      wc = ws + lay.wc;
+    } else {
+      wc = (const bf16*)w + v0 * H;
+    }
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_bf16(P, wc, 1, Vc, (int)H, false, false));
+    TRY(set_b_tokens(P, h, N, (int)H));
+    groups(P, tok, nullptr, nullptr, nullptr, 1);
+    out_bf16(P, lg, vcp);
+    TRY(b.launch(st));
+    TRY(ce_logits_out(lg, vcp, Vc, N, softcap, out + v0, V, st));
+  }
+  return kOk;
+}

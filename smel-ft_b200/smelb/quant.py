@@ -1,4 +1,5 @@
-"""SMEL FT's group-wise asymmetric int4 format (smel/quant.py:1-94), on CUDA.
+"""SMEL FT's group-wise asymmetric int4 format (smel/quant.py:1-94) and the int8 rows of the LM head
+(smel/quant.py:97-105), on CUDA.
 
 Format: w [..., K] -> q uint8 [..., K/2] (two nibbles per byte, the low nibble holds the even column),
 scale / zero bf16 [..., K/group]; w ~= q * scale + zero. Dequantization computes q * scale + zero in fp32 and rounds
@@ -111,6 +112,36 @@ def pack_sz(scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:
     out = torch.empty(nw, groups, rows, device=scale.device, dtype=torch.int32)
     _lib.call("smelb_int4_pack_sz", _lib.ptr(scale), _lib.ptr(zero), _lib.ptr(out), nw, rows, groups,
               _lib.stream_ptr(scale.device))
+    return out
+
+
+def quantize_int8_rows(w: torch.Tensor) -> dict:
+    """Symmetric per-row int8 for the LM head (smel/quant.py:97-101), on the GPU: w [..., H] (bf16 or fp32) ->
+    {q int8 [..., H], scale bf16 [...]}, s = max(amax|w| / 127, 1e-12), q = clamp(round(w / s), -127, 127)."""
+    if not w.is_cuda:
+        raise _lib.SmelbError("quantize_int8_rows: smelb quantizes on the GPU; move the weights to CUDA first")
+    w2 = w if w.dtype in (torch.bfloat16, torch.float32) else w.float()
+    w2 = w2.contiguous()
+    H = w2.shape[-1]
+    rows = w2.numel() // max(H, 1)
+    q = torch.empty(w2.shape, dtype=torch.int8, device=w.device)
+    scale = torch.empty(w2.shape[:-1], dtype=torch.bfloat16, device=w.device)
+    _lib.call("smelb_int8_rows_quantize", _lib.ptr(w2), 1 if w2.dtype == torch.float32 else 0, rows, H, _lib.ptr(q),
+              _lib.ptr(scale), _lib.stream_ptr(w.device))
+    return {"q": q, "scale": scale}
+
+
+def dequant_int8_rows(q: torch.Tensor, scale: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """q * scale in `dtype` (bf16 or fp32) on the GPU (smel/quant.py:104-105)."""
+    if dtype not in (torch.bfloat16, torch.float32):
+        raise _lib.SmelbError(f"dequant_int8_rows: output dtype {dtype} not supported (bf16 or fp32)")
+    if q.dtype != torch.int8 or scale.dtype != torch.bfloat16:
+        raise _lib.SmelbError("dequant_int8_rows: expects int8 q and a bf16 scale")
+    q, scale = q.contiguous(), scale.contiguous()
+    H = q.shape[-1]
+    out = torch.empty(q.shape, dtype=dtype, device=q.device)
+    _lib.call("smelb_int8_rows_dequant", _lib.ptr(q), _lib.ptr(scale), q.numel() // max(H, 1), H, _lib.ptr(out),
+              1 if dtype == torch.float32 else 0, _lib.stream_ptr(q.device))
     return out
 
 

@@ -17,6 +17,10 @@ Outputs (torch.save dicts of CPU tensors):
   pack.pt      smel/pack.py: pack_layer of a small checkpoint layer (dense fp32 tensors, an A_log, an integer
                tensor, the fused bank, two selected experts) and merge_experts / merge_mlp with LoRA deltas
                (python tests/golden/make_golden.py --only pack writes just this file)
+  ce.pt        smel/loss.py chunked_ce in bf16 on the CPU (loss and dL/dh) for a bf16 head with ragged vocabulary
+               and token chunks, the same head as int8 rows (with quantize_int8_rows' q / scale), and a softcapped
+               head (the cases of the reference tests tests/test_data_loss.py:68-85, tests/test_gemma4.py:266-277,
+               in bf16) (--only ce)
 The test-suite never imports the reference; it only reads these files.
 """
 import argparse
@@ -46,11 +50,14 @@ def lora_tensors(H, I, S, n_sel, r, alpha, gen):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", default=None, choices=[None, "pack"])
+    ap.add_argument("--only", default=None, choices=[None, "pack", "ce"])
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     if args.only == "pack":
         make_pack()
+        return
+    if args.only == "ce":
+        make_ce()
         return
     from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
     from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
@@ -223,6 +230,45 @@ def make_pack():
                 "lora_ex": {n: p.detach().clone() for n, p in lex.named_parameters()},
                 "lora_sh": {n: p.detach().clone() for n, p in lsh.named_parameters()}, "r": r, "alpha": 16.0,
                 "merged_gu": mgu, "merged_dn": mdn, "merged_mlp": (mg, mu, md)}, os.path.join(HERE, "pack.pt"))
+
+
+def make_ce():
+    from smel.loss import LMHead, chunked_ce
+    torch.set_num_threads(4)
+    g = torch.Generator().manual_seed(31)
+    cases = {}
+    # bf16 head, ragged last vocabulary chunk (952 rows) and token chunk (8 rows)
+    V, H, N = 3000, 128, 200
+    W = (torch.randn(V, H, generator=g) * 0.05).bfloat16()
+    h = torch.randn(N, H, generator=g).bfloat16()
+    tgt = torch.randint(0, V, (N,), generator=g)
+    for name, int8 in (("bf16", False), ("int8", True)):
+        head = LMHead.from_weight(W, int8=int8, vocab_chunk=1024)
+        hh = h.clone().requires_grad_(True)
+        loss = chunked_ce(hh, head, tgt, denom=N, token_chunk=64)
+        loss.backward()
+        c = {"h": h, "tgt": tgt, "V": V, "vocab_chunk": 1024, "token_chunk": 64, "softcap": 0.0, "denom": float(N),
+             "loss": loss.detach(), "grad": hh.grad.clone()}
+        if int8:
+            c["q"], c["scale"] = head.q["q"], head.q["scale"]
+        else:
+            c["w"] = W
+        cases[name] = c
+    # softcapped head (Gemma), logits well into the cap's curve
+    V, H, N = 3000, 64, 120
+    W = (torch.randn(V, H, generator=g) * 0.5).bfloat16()
+    h = (torch.randn(N, H, generator=g) * 3).bfloat16()
+    tgt = torch.randint(0, V, (N,), generator=g)
+    head = LMHead.from_weight(W, vocab_chunk=700, softcap=30.0)
+    hh = h.clone().requires_grad_(True)
+    loss = chunked_ce(hh, head, tgt, denom=N, token_chunk=50)
+    loss.backward()
+    cases["softcap"] = {"h": h, "tgt": tgt, "w": W, "V": V, "vocab_chunk": 700, "token_chunk": 50, "softcap": 30.0,
+                        "denom": float(N), "loss": loss.detach(), "grad": hh.grad.clone()}
+    # the loss alone (need_grad=False path)
+    with torch.no_grad():
+        cases["softcap"]["loss_nograd"] = chunked_ce(h, head, tgt, denom=N, token_chunk=50, need_grad=False)
+    torch.save(cases, os.path.join(HERE, "ce.pt"))
 
 
 if __name__ == "__main__":

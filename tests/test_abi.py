@@ -15,7 +15,7 @@ HEADER = os.path.join(ROOT, "include", "smelb.h")
 def declared():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|size_t|void|long long)\s+(smelb_\w+)\s*\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|size_t|void|long long)\s+(smelb_\w+)\s*\(", src, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
