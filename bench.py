@@ -430,6 +430,74 @@ def run_stream(args, local, n_layers=4):
         torch.cuda.empty_cache()
 
 
+# ------------------------------------------------------------------------------------------ chunked CE
+def run_ce(args, local):
+    """The step after the layer stack in training (smel/loss.py chunked_ce): cross-entropy loss and dL/dh over a
+    frozen LM head of the Qwen3.6 shape (hidden 2048, vocabulary 248320) on 4092 supervised rows, bf16 and int8
+    heads, at the reference's default chunking (vocabulary 32768, tokens 1024) and with all rows in one token chunk.
+    One JSON line per case: rows/s, the two GEMMs' share, and TFLOP/s of the 4 N V H algorithmic FLOPs against the
+    measured bf16 peak; the CPU oracle on a bounded sample of rows for scale."""
+    import smelb
+    from smelb import _lib
+    dev = torch.device("cuda", local)
+    N, H, V = args.tokens, 2048, 248320
+    g = torch.Generator(device=dev).manual_seed(11)
+    W = (torch.randn(V, H, device=dev, generator=g) * 0.02).bfloat16()
+    h = torch.randn(N, H, device=dev, generator=g).bfloat16().requires_grad_(True)
+    tgt = torch.randint(0, V, (N,), device=dev, generator=g)
+    pk, src = peaks()
+    flops = 4.0 * N * V * H
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import ce_oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        rows = min(N, 1024)
+        hc, tc_, wc = h.detach()[:rows].cpu(), tgt[:rows].cpu(), W.cpu()
+        t0 = time.perf_counter()
+        ce_oracle.chunked_ce(hc, tc_, float(rows), w=wc, vocab_chunk=32768, token_chunk=1024)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(rows / dt, 2), "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{rows} rows of the same head (bf16, chunks 32768 x 1024), loss + gradient, {dt:.2f} s"}
+    for int8 in (False, True):
+        head = smelb.LMHead.from_weight(W, int8=int8, vocab_chunk=32768)
+        for tc in (1024, N):
+            def step():
+                h.grad = None
+                smelb.chunked_ce(h, head, tgt, float(N), tc).backward()
+            for _ in range(max(3, args.warmup)):
+                step()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n0 = _lib.launch_count()
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            launches = (_lib.launch_count() - n0) / args.steps
+            _lib.gemm_timing(True)
+            step()
+            gms, gn = _lib.gemm_timing_read()
+            _lib.gemm_timing(False)
+            tf = flops / (ms / 1e3) / 1e12
+            line = {"metric": "chunked CE loss + dL/dh rows/s (Qwen3.6 LM head)", "value": round(N / (ms / 1e3), 1),
+                    "unit": "rows/s", "ms_per_step": round(ms, 3), "steps": args.steps, "dtype": "bf16",
+                    "data": "synthetic", "higher_is_better": True,
+                    "config": {"workload": "chunked_ce fwd+grad", "rows": N, "hidden": H, "vocab": V,
+                               "head": "int8 rows" if int8 else "bf16", "vocab_chunk": 32768, "token_chunk": tc},
+                    "gpu_launches": launches,
+                    "gemm_ms": round(gms, 3), "gemm_launches": gn,
+                    "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk["bf16_tflops"],
+                                 "unit": "TFLOP/s", "frac": round(tf / pk["bf16_tflops"], 3),
+                                 "note": f"4 N V H flops (two GEMMs) over the whole step, {src} peak; GEMMs alone "
+                                         f"{flops / (gms / 1e3) / 1e12:.0f} TFLOP/s"},
+                    "cpu_baseline": cpu}
+            print(json.dumps(line), flush=True)
+        del head
+        torch.cuda.empty_cache()
+
+
 # ------------------------------------------------------------------------------------------ config 4 sweep
 def run_sweep(args, local):
     """Config 4: the Qwen3.6 layer shape, forward only (no grad), all 256 experts frozen int4 group-64, at 1, 16, 128,
@@ -546,14 +614,16 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="config 4 token-count sweep (one JSON line per point)")
     ap.add_argument("--stream", action="store_true",
                     help="layer-major forward over a stack of layers streamed from pinned host memory vs resident")
+    ap.add_argument("--ce", action="store_true",
+                    help="chunked cross-entropy over the Qwen3.6 LM head (one JSON line per head / chunking)")
     ap.add_argument("--parallel", default="dp", choices=["dp", "ep"],
                     help="with N > 1: data-parallel replicas of the layer (dp) or experts split over the GPUs (ep)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
-        if args.sweep or args.stream:
+        if args.sweep or args.stream or args.ce:
             if rank == 0:
-                (run_sweep if args.sweep else run_stream)(args, local)
+                (run_sweep if args.sweep else run_stream if args.stream else run_ce)(args, local)
             res = None
         elif args.impl == "reference":
             res = run_reference(args, world, rank)

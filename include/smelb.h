@@ -265,9 +265,11 @@ int smelb_int8_rows_dequant(const void* q, const void* scale, int64_t rows, int6
  * pass exactly one of the two. softcap > 0 caps the logits as cap * tanh(z / cap) (smel/loss.py:34-35), gradient
  * included. Outputs: loss_rows (fp32 [N]) = lse - target logit per row (a target outside [0, V) contributes lse);
  * loss (fp32 [1]) = sum(loss_rows) / denom; gh (bf16 [N, H]) = d loss / d h, or NULL for the loss alone.
- * workspace: 256-byte aligned, smelb_chunked_ce_workspace_bytes(min(N, token_chunk), H, min(V, vocab_chunk), int8)
- * bytes. */
-int64_t smelb_chunked_ce_workspace_bytes(int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8);
+ * workspace: 256-byte aligned, smelb_chunked_ce_workspace_bytes(N, token_chunk, H, min(V, vocab_chunk), int8,
+ * gh != NULL) bytes. The vocabulary chunks are the outer loop (an int8 head is dequantised once per call), so the
+ * online state of all N rows lives in the workspace; token_chunk bounds the [token_chunk, vocab_chunk] logit tile. */
+int64_t smelb_chunked_ce_workspace_bytes(int64_t N, int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8,
+                                         int need_grad);
 int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, const void* w, const void* q,
                      const void* q_scale, int64_t V, int64_t vocab_chunk, int64_t token_chunk, float softcap,
                      float denom, float* loss_rows, float* loss, void* gh, void* workspace, int64_t workspace_bytes,

@@ -1162,10 +1162,12 @@ __device__ __forceinline__ float block_reduce_256(float v, float* red) {
 __global__ void set_count_kernel(int* p, int v) { *p = v; }
 
 __global__ void ce_init_kernel(CeState st, long long n, int H) {
-  const long long tot = n * H;
+  const long long tot = st.acc ? n * H : n;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
-    st.acc[i] = 0.f;
-    st.tgt_row[i] = 0.f;
+    if (st.acc) {
+      st.acc[i] = 0.f;
+      st.tgt_row[i] = 0.f;
+    }
     if (i < n) {
       st.m[i] = -INFINITY;
       st.s[i] = 0.f;
@@ -1176,33 +1178,56 @@ __global__ void ce_init_kernel(CeState st, long long n, int H) {
   }
 }
 
-// One block per token row. The row's logits are read twice (maximum, then exponentials) and overwritten in place by p.
+// One block per token row; 16-byte accesses (ld is a multiple of 64, the rows 128-byte aligned). The row's logits
+// are read twice (maximum, then exponentials) and overwritten in place by p. The cap is monotonic, so the chunk
+// maximum of the capped logits is the cap of the raw maximum.
 __global__ void __launch_bounds__(256) ce_rows_kernel(bf16* __restrict__ lg, int ld, int Vc, long long v0,
                                                      const long long* __restrict__ tgt, float cap, int need_grad,
                                                      const bf16* __restrict__ wc, int H, CeState st) {
   __shared__ float red[8];
   const long long row = blockIdx.x;
   bf16* l = lg + row * ld;
+  uint4* lv = reinterpret_cast<uint4*>(l);
+  const int nvec = ld >> 3;
   const long long t = tgt[row];
   const bool has_t = t >= v0 && t < v0 + Vc;
   const int c = has_t ? (int)(t - v0) : 0;
   const float zt = has_t ? ce_cap(__bfloat162float(l[c]), cap) : 0.f;  // read before any thread writes p
-  float cm = -INFINITY;
-  for (int v = threadIdx.x; v < Vc; v += 256) cm = fmaxf(cm, ce_cap(__bfloat162float(l[v]), cap));
-  cm = block_reduce_256<true>(cm, red);
+  float raw = -INFINITY;
+  for (int j = threadIdx.x; j < nvec; j += 256) {
+    const uint4 u = lv[j];
+    const bf16* b = reinterpret_cast<const bf16*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (8 * j + e < Vc) raw = fmaxf(raw, __bfloat162float(b[e]));
+  }
+  raw = block_reduce_256<true>(raw, red);
+  const float cm = ce_cap(raw, cap);
   const float m_old = st.m[row];
   const float nm = fmaxf(m_old, cm);
   const float r = expf(m_old - nm);
   float sum = 0.f;
-  for (int v = threadIdx.x; v < ld; v += 256) {
-    float e = 0.f, pv = 0.f;
-    if (v < Vc) {
-      const float z = ce_cap(__bfloat162float(l[v]), cap);
-      e = expf(z - nm);
-      pv = cap > 0.f ? e * (1.f - (z / cap) * (z / cap)) : e;
+  for (int j = threadIdx.x; j < nvec; j += 256) {
+    const uint4 u = lv[j];
+    const bf16* b = reinterpret_cast<const bf16*>(&u);
+    uint4 o;
+    __nv_bfloat162* ow = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float pv[2];
+#pragma unroll
+      for (int f = 0; f < 2; ++f) {
+        pv[f] = 0.f;
+        if (8 * j + e + f < Vc) {
+          const float z = ce_cap(__bfloat162float(b[e + f]), cap);
+          const float ex = expf(z - nm);
+          sum += ex;
+          pv[f] = cap > 0.f ? ex * (1.f - (z / cap) * (z / cap)) : ex;
+        }
+      }
+      ow[e >> 1] = __floats2bfloat162_rn(pv[0], pv[1]);
     }
-    sum += e;
-    if (need_grad) l[v] = __float2bfloat16_rn(pv);
+    if (need_grad) lv[j] = o;
   }
   sum = block_reduce_256<false>(sum, red);
   if (threadIdx.x == 0) {
@@ -1299,7 +1324,7 @@ int set_count(int* p, int v, cudaStream_t s) {
 
 int ce_init(const CeState& st, long long n, int H, cudaStream_t s) {
   if (n == 0) return kOk;
-  ce_init_kernel<<<grid_for(n * H), 256, 0, s>>>(st, n, H);
+  ce_init_kernel<<<grid_for(st.acc ? n * H : n), 256, 0, s>>>(st, n, H);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -1307,7 +1332,8 @@ int ce_init(const CeState& st, long long n, int H, cudaStream_t s) {
 
 int ce_rows(void* lg, int ld, int Vc, long long v0, const long long* tgt, float softcap, bool need_grad,
             const void* wc, int H, const CeState& st, long long n, cudaStream_t s) {
-  SMELB_CHECK_ARG(Vc > 0 && ld >= Vc && n <= 2147483647LL, kErrShape, "ce_rows: Vc=%d ld=%d", Vc, ld);
+  SMELB_CHECK_ARG(Vc > 0 && ld >= Vc && ld % 8 == 0 && n <= 2147483647LL && ((uintptr_t)lg & 15) == 0, kErrShape,
+                  "ce_rows: Vc=%d ld=%d", Vc, ld);
   if (n == 0) return kOk;
   ce_rows_kernel<<<(int)n, 256, 0, s>>>((bf16*)lg, ld, Vc, v0, tgt, softcap, need_grad ? 1 : 0, (const bf16*)wc, H,
                                         st);

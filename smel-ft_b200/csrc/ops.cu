@@ -988,15 +988,17 @@ extern "C" int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, in
 }
 
 // ---------------------------------------------------------------------------------------------------- chunked CE
-// smel/loss.py:130-146 _ChunkedCE.forward over token chunks, each one pass of smel/loss.py:50-92 _ce_chunk over the
-// vocabulary chunks. Per (token chunk, vocabulary chunk):
-//   [int8 head: dequantize the chunk's rows to bf16]
+// smel/loss.py:130-146 _ChunkedCE.forward with smel/loss.py:50-92 _ce_chunk: one pass over the vocabulary, the
+// online state (running max / sum, target logit and row, fp32 gradient accumulator) kept for every row. The loops
+// run vocabulary-outer, token-chunk-inner, so an int8 head is dequantised once per call and each vocabulary chunk's
+// rows are read while they are hot; every row still sees the vocabulary chunks in the reference's order, so the
+// per-row results are the reference's token chunk by token chunk. Per (vocabulary chunk, token chunk):
 //   GEMM 1  lg[n, Vcp] = bf16(h @ Wc^T)                         (A = Wc K-major, tokens as B, the MoE GEMM engine)
 //   rows    online max / sum, target capture, p = exp(z - m) * cap'(z) in bf16 over lg in place
 //   GEMM 2  part[s][n, H] = p[:, ks] @ Wc[ks]                  (A = Wc MN-major, the chunk split along k into
 //                                                               nsplit fp32 partials so the tiles fill the SMs)
 //   acc     acc = acc * r + sum_s part[s]
-// then loss_rows and gh for the token chunk, and the loss over all rows at the end.
+// then loss_rows and gh for every row, and the loss.
 namespace {
 
 constexpr int kCeMaxSplit = 4;
@@ -1007,21 +1009,22 @@ struct CeLayout {
   size_t tok, lg, parts, acc, tgt_row, m, s, r, tlog, tdrv, wc, total;
 };
 
-CeLayout ce_layout(long long n, long long H, long long vocab_chunk, bool int8) {
-  const long long vcp = (vocab_chunk + 63) / 64 * 64;
+// N rows of state, token chunks of tc rows, vocabulary chunks of vc rows
+CeLayout ce_layout(long long N, long long tc, long long H, long long vc, bool int8, bool grad) {
+  const long long vcp = (vc + 63) / 64 * 64;
   CeLayout L{};
   size_t o = 0;
   L.tok = o;      o += ce_align(4);
-  L.lg = o;       o += ce_align((size_t)n * vcp * 2);
-  L.parts = o;    o += ce_align((size_t)kCeMaxSplit * n * H * 4);
-  L.acc = o;      o += ce_align((size_t)n * H * 4);
-  L.tgt_row = o;  o += ce_align((size_t)n * H * 4);
-  L.m = o;        o += ce_align((size_t)n * 4);
-  L.s = o;        o += ce_align((size_t)n * 4);
-  L.r = o;        o += ce_align((size_t)n * 4);
-  L.tlog = o;     o += ce_align((size_t)n * 4);
-  L.tdrv = o;     o += ce_align((size_t)n * 4);
-  L.wc = o;       o += int8 ? ce_align((size_t)vocab_chunk * H * 2) : 0;
+  L.lg = o;       o += ce_align((size_t)tc * vcp * 2);
+  L.parts = o;    o += grad ? ce_align((size_t)kCeMaxSplit * tc * H * 4) : 0;
+  L.acc = o;      o += grad ? ce_align((size_t)N * H * 4) : 0;
+  L.tgt_row = o;  o += grad ? ce_align((size_t)N * H * 4) : 0;
+  L.m = o;        o += ce_align((size_t)N * 4);
+  L.s = o;        o += ce_align((size_t)N * 4);
+  L.r = o;        o += ce_align((size_t)N * 4);
+  L.tlog = o;     o += ce_align((size_t)N * 4);
+  L.tdrv = o;     o += ce_align((size_t)N * 4);
+  L.wc = o;       o += int8 ? ce_align((size_t)vc * H * 2) : 0;
   L.total = o;
   return L;
 }
@@ -1042,6 +1045,11 @@ int ce_splits(long long n, long long H, int vcp, int sms) {
   return best;
 }
 
+CeState ce_state_at(const CeState& S, long long t0, long long H) {
+  return CeState{S.m + t0,    S.s + t0,    S.r + t0, S.tlog + t0, S.tdrv + t0,
+                 S.acc ? S.acc + t0 * H : nullptr, S.tgt_row ? S.tgt_row + t0 * H : nullptr};
+}
+
 }  // namespace
 
 int smelb_int8_rows_quantize(const void* w, int w_fp32, int64_t rows, int64_t H, void* q, void* scale,
@@ -1058,9 +1066,10 @@ int smelb_int8_rows_dequant(const void* q, const void* scale, int64_t rows, int6
   return int8_rows_dequant(q, scale, rows, (int)H, out, (cudaStream_t)stream, out_fp32 != 0);
 }
 
-int64_t smelb_chunked_ce_workspace_bytes(int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8) {
-  if (token_chunk <= 0 || H <= 0 || vocab_chunk <= 0) return 0;
-  return (int64_t)ce_layout(token_chunk, H, vocab_chunk, int8 != 0).total;
+int64_t smelb_chunked_ce_workspace_bytes(int64_t N, int64_t token_chunk, int64_t H, int64_t vocab_chunk, int int8,
+                                         int need_grad) {
+  if (N <= 0 || token_chunk <= 0 || H <= 0 || vocab_chunk <= 0) return 256;
+  return (int64_t)ce_layout(N, std::min<int64_t>(token_chunk, N), H, vocab_chunk, int8 != 0, need_grad != 0).total;
 }
 
 int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, const void* w, const void* q,
@@ -1072,16 +1081,18 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
                   "chunked_ce: pass exactly one of the bf16 head (w) or the int8 head (q, q_scale)");
   SMELB_CHECK_ARG(H > 0 && H % 64 == 0 && H <= 65536, kErrShape, "chunked_ce: H=%lld (a multiple of 64 is required)",
                   (long long)H);
-  SMELB_CHECK_ARG(N >= 0 && V > 0 && vocab_chunk > 0 && vocab_chunk <= (1 << 24) && token_chunk > 0 && V < (1LL << 40),
+  SMELB_CHECK_ARG(N >= 0 && N <= (1LL << 31) - 1 && V > 0 && vocab_chunk > 0 && vocab_chunk <= (1 << 24) &&
+                      token_chunk > 0 && V < (1LL << 40),
                   kErrShape, "chunked_ce: N=%lld V=%lld vocab_chunk=%lld token_chunk=%lld", (long long)N,
                   (long long)V, (long long)vocab_chunk, (long long)token_chunk);
   SMELB_CHECK_ARG(softcap >= 0.f, kErrArg, "chunked_ce: softcap=%g", (double)softcap);
   cudaStream_t st = (cudaStream_t)stream;
+  if (N == 0) return ce_loss_sum(loss_rows, 0, denom, loss, st);
   const bool int8 = q != nullptr;
   const bool need_grad = gh != nullptr;
-  const long long tc = std::min<long long>(token_chunk, std::max<long long>(N, 1));
+  const long long tc = std::min<long long>(token_chunk, N);
   const long long vc_max = std::min<long long>(vocab_chunk, V);
-  const CeLayout lay = ce_layout(tc, H, vc_max, int8);
+  const CeLayout lay = ce_layout(N, tc, H, vc_max, int8, need_grad);
   SMELB_CHECK_ARG(workspace_bytes >= (int64_t)lay.total, kErrWorkspace,
                   "chunked_ce: workspace %lld bytes, %lld needed", (long long)workspace_bytes, (long long)lay.total);
   SMELB_CHECK_ARG(((uintptr_t)workspace & 255) == 0 && ((uintptr_t)h & 15) == 0 && (int8 || ((uintptr_t)w & 15) == 0),
@@ -1089,27 +1100,32 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
   char* ws = (char*)workspace;
   int* tok = (int*)(ws + lay.tok);
   bf16* lg = (bf16*)(ws + lay.lg);
-  float* parts = (float*)(ws + lay.parts);
-  CeState S{(float*)(ws + lay.m),   (float*)(ws + lay.s),   (float*)(ws + lay.r),      (float*)(ws + lay.tlog),
-            (float*)(ws + lay.tdrv), (float*)(ws + lay.acc), (float*)(ws + lay.tgt_row)};
+  float* parts = need_grad ? (float*)(ws + lay.parts) : nullptr;
+  const CeState S{(float*)(ws + lay.m),    (float*)(ws + lay.s),   (float*)(ws + lay.r), (float*)(ws + lay.tlog),
+                  (float*)(ws + lay.tdrv), need_grad ? (float*)(ws + lay.acc) : nullptr,
+                  need_grad ? (float*)(ws + lay.tgt_row) : nullptr};
   int dev = 0;
   SMELB_CUDA(cudaGetDevice(&dev));
   const int sms = num_sms(dev);
-  for (long long t0 = 0; t0 < N; t0 += tc) {
-    const long long n = std::min<long long>(tc, N - t0);
-    const bf16* hc = (const bf16*)h + t0 * H;
-    const long long* tg = (const long long*)tgt + t0;
-    TRY(set_count(tok, (int)n, st));
-    TRY(ce_init(S, n, (int)H, st));
-    for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
-      const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
-      const int vcp = (Vc + 63) / 64 * 64;
-      const void* wc;
-      if (int8) {
-        TRY(int8_rows_dequant((const int8_t*)q + v0 * H, (const bf16*)q_scale + v0, Vc, (int)H, ws + lay.wc, st));
-        wc = ws + lay.wc;
-      } else {
-        wc = (const bf16*)w + v0 * H;
+  TRY(ce_init(S, N, (int)H, st));
+  int tok_now = -1;  // the value the device-side token count holds
+  for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
+    const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
+    const int vcp = (Vc + 63) / 64 * 64;
+    const void* wc;
+    if (int8) {
+      TRY(int8_rows_dequant((const int8_t*)q + v0 * H, (const bf16*)q_scale + v0, Vc, (int)H, ws + lay.wc, st));
+      wc = ws + lay.wc;
+    } else {
+      wc = (const bf16*)w + v0 * H;
+    }
+    for (long long t0 = 0; t0 < N; t0 += tc) {
+      const long long n = std::min<long long>(tc, N - t0);
+      const bf16* hc = (const bf16*)h + t0 * H;
+      const CeState Sc = ce_state_at(S, t0, H);
+      if (tok_now != (int)n) {
+        TRY(set_count(tok, (int)n, st));
+        tok_now = (int)n;
       }
       {
         Builder b;
@@ -1120,7 +1136,7 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
         out_bf16(P, lg, vcp);
         TRY(b.launch(st));
       }
-      TRY(ce_rows(lg, vcp, Vc, v0, tg, softcap, need_grad, wc, (int)H, S, n, st));
+      TRY(ce_rows(lg, vcp, Vc, v0, (const long long*)tgt + t0, softcap, need_grad, wc, (int)H, Sc, n, st));
       if (!need_grad) continue;
       const int ns = ce_splits(n, H, vcp, sms);
       const int kstep = ((vcp / 64 + ns - 1) / ns) * 64;
@@ -1147,10 +1163,10 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
         }
         TRY(b.launch(st));
       }
-      TRY(ce_acc(parts, np, S, n, (int)H, st));
+      TRY(ce_acc(parts, np, Sc, n, (int)H, st));
     }
-    TRY(ce_finish(S, n, (int)H, denom, loss_rows + t0, need_grad ? (bf16*)gh + t0 * H : nullptr, st));
   }
+  TRY(ce_finish(S, N, (int)H, denom, loss_rows, need_grad ? gh : nullptr, st));
   return ce_loss_sum(loss_rows, N, denom, loss, st);
 }
 

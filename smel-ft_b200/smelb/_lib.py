@@ -95,7 +95,7 @@ SIGNATURES = {
                                                  c_i32, c_vp, c_vp, c_vp]),
     "smelb_int8_rows_quantize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "smelb_int8_rows_dequant": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_vp]),
-    "smelb_chunked_ce_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i32]),
+    "smelb_chunked_ce_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i32, c_i32]),
     "smelb_chunked_ce": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_f32, c_f32, c_vp,
                                  c_vp, c_vp, c_vp, c_i64, c_vp]),
     "smelb_lm_logits_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i32]),

@@ -4,13 +4,14 @@ Same interface as the reference: LMHead (bf16 rows or int8 rows, vocab_chunk, op
 chunked_ce(h, head, tgt, denom, token_chunk, need_grad), whose backward returns the gradient computed in the forward
 pass (the head is frozen). The [N, V] logits are never materialised.
 
-B200 design (libsmelb.so, smelb_chunked_ce): per token chunk, one pass over the vocabulary chunks; per chunk the
-logits come from the MoE layer's tcgen05 GEMM engine (head rows as the MMA's M side, tokens as N) in bf16, a row
+B200 design (libsmelb.so, smelb_chunked_ce): one pass over the vocabulary chunks, each applied to every token chunk
+in turn (the online state of all rows is kept, so an int8 head is dequantised once per call); per chunk the logits
+come from the MoE layer's tcgen05 GEMM engine (head rows as the MMA's M side, tokens as N) in bf16, a row
 kernel does the online max / sum, takes the target's logit and head row, and overwrites the logits in place with the
 softmax numerators times the cap's derivative (bf16, as the reference's p.to(h.dtype)); a second GEMM multiplies them
 by the same head rows (MN-major, split along the chunk into fp32 partials that fill the SMs) and a last kernel
-rescales the fp32 gradient accumulator. An int8 head is dequantised chunk by chunk into a bf16 buffer of the
-workspace. Only the hidden dtype bf16 is supported (the reference's training dtype).
+rescales the fp32 gradient accumulator. An int8 head's chunk is dequantised into a bf16 buffer of the workspace.
+Only the hidden dtype bf16 is supported (the reference's training dtype).
 """
 import torch
 
@@ -98,7 +99,7 @@ def _run(h, head: LMHead, tgt, denom, token_chunk, need_grad):
     tgt = tgt.to(device=h.device, dtype=torch.int64).contiguous()
     tc = max(1, min(int(token_chunk), N))
     vc = min(head.vocab_chunk, head.vocab)
-    nb = int(_lib.load().smelb_chunked_ce_workspace_bytes(tc, H, vc, 1 if int8 else 0))
+    nb = int(_lib.load().smelb_chunked_ce_workspace_bytes(N, tc, H, vc, 1 if int8 else 0, 1 if need_grad else 0))
     ws = torch.empty(nb, dtype=torch.uint8, device=h.device)
     rows = torch.empty(N, dtype=torch.float32, device=h.device)
     loss = torch.empty((), dtype=torch.float32, device=h.device)
