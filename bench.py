@@ -469,10 +469,12 @@ def run_ce(args, local):
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             n0 = _lib.launch_count()
+            torch.cuda.nvtx.range_push(f"timed_ce_{'int8' if int8 else 'bf16'}_{tc}")
             e0.record()
             for _ in range(args.steps):
                 step()
             e1.record()
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / args.steps
             launches = (_lib.launch_count() - n0) / args.steps

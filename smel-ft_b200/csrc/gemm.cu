@@ -53,8 +53,15 @@ __device__ __forceinline__ TileInfo decode_tile(const LaunchArgs& args, const Ta
   ti.p = p;
   if (P.mode == kTokN) {
     const int gp = gb + p;  // gpre holds ngroups + 1 entries per problem
-    const int ntg = local / mtiles;
-    ti.mt = local - ntg * mtiles;
+    int ntg;
+    if (P.n_inner) {
+      const int ntt = T.gpre[gp + P.ngroups];  // token tiles of the problem
+      ti.mt = local / ntt;
+      ntg = local - ti.mt * ntt;
+    } else {
+      ntg = local / mtiles;
+      ti.mt = local - ntg * mtiles;
+    }
     int lo = 0, hi = P.ngroups;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;

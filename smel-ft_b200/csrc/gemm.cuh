@@ -128,6 +128,8 @@ struct alignas(64) Problem {
   int inter;          // gated-MLP intermediate size (offset of up in h)
   float alpha;        // scale applied to the fp32 accumulator before the store
   int m_pad;          // bf16 [token][feature] stores: features [M, m_pad) are written as zeros (0: none)
+  int n_inner;        // kTokN tile order: 0 = the weight (M) tiles of one token tile are consecutive, 1 = the token
+                      // tiles of one weight tile are consecutive (a weight tile read once from HBM, then from L2)
 };
 
 struct LaunchArgs {

@@ -1159,7 +1159,11 @@ __device__ __forceinline__ float block_reduce_256(float v, float* red) {
   return v;
 }
 
-__global__ void set_count_kernel(int* p, int v) { *p = v; }
+// p[i] = min(step, total - i * step) for the nchunks chunks of `total` rows (the device-side token counts the GEMMs read)
+__global__ void set_counts_kernel(int* p, int nchunks, int step, long long total) {
+  for (int i = threadIdx.x; i < nchunks; i += blockDim.x)
+    p[i] = (int)std::min<long long>(step, total - (long long)i * step);
+}
 
 __global__ void ce_init_kernel(CeState st, long long n, int H) {
   const long long tot = st.acc ? n * H : n;
@@ -1243,12 +1247,27 @@ __global__ void __launch_bounds__(256) ce_rows_kernel(bf16* __restrict__ lg, int
     for (int i = threadIdx.x; i < H; i += 256) st.tgt_row[row * H + i] = __bfloat162float(wc[(long long)c * H + i]);
 }
 
-__global__ void ce_acc_kernel(const float* __restrict__ parts, int nparts, CeState st, long long n, int H) {
-  const long long tot = n * H;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
-    float pw = parts[i];
-    for (int q = 1; q < nparts; ++q) pw += parts[q * tot + i];
-    st.acc[i] = st.acc[i] * st.r[i / H] + pw;
+// float4 over [n, H] (H % 4 == 0; the arrays are 16-byte aligned)
+__global__ void ce_acc_kernel(const float4* __restrict__ parts, int nparts, CeState st, long long n, int H) {
+  const int h4 = H >> 2;
+  const long long tot4 = n * h4;
+  float4* acc = reinterpret_cast<float4*>(st.acc);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot4; i += (long long)gridDim.x * blockDim.x) {
+    float4 pw = parts[i];
+    for (int q = 1; q < nparts; ++q) {
+      const float4 u = parts[q * tot4 + i];
+      pw.x += u.x;
+      pw.y += u.y;
+      pw.z += u.z;
+      pw.w += u.w;
+    }
+    const float r = st.r[i / h4];
+    float4 a = acc[i];
+    a.x = a.x * r + pw.x;
+    a.y = a.y * r + pw.y;
+    a.z = a.z * r + pw.z;
+    a.w = a.w * r + pw.w;
+    acc[i] = a;
   }
 }
 
@@ -1315,8 +1334,8 @@ static int grid_for(long long work) {
   return (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, 148LL * 16));
 }
 
-int set_count(int* p, int v, cudaStream_t s) {
-  set_count_kernel<<<1, 1, 0, s>>>(p, v);
+int set_counts(int* p, int nchunks, int step, long long total, cudaStream_t s) {
+  set_counts_kernel<<<1, 256, 0, s>>>(p, nchunks, step, total);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -1343,8 +1362,10 @@ int ce_rows(void* lg, int ld, int Vc, long long v0, const long long* tgt, float 
 }
 
 int ce_acc(const float* parts, int nparts, const CeState& st, long long n, int H, cudaStream_t s) {
+  SMELB_CHECK_ARG(H % 4 == 0 && ((uintptr_t)parts & 15) == 0 && ((uintptr_t)st.acc & 15) == 0, kErrShape,
+                  "ce_acc: H=%d (multiple of 4) and 16-byte aligned arrays required", H);
   if (n == 0) return kOk;
-  ce_acc_kernel<<<grid_for(n * H), 256, 0, s>>>(parts, nparts, st, n, H);
+  ce_acc_kernel<<<grid_for(n * H / 4), 256, 0, s>>>(reinterpret_cast<const float4*>(parts), nparts, st, n, H);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;

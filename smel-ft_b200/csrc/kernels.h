@@ -100,8 +100,8 @@ struct CeState {
   float *acc, *tgt_row;  // [n, H]
 };
 int ce_init(const CeState& st, long long n, int H, cudaStream_t s);
-// *p = v on the stream (the device-side token count the GEMM reads)
-int set_count(int* p, int v, cudaStream_t s);
+// p[i] = min(step, total - i * step), i < nchunks (the device-side token counts of the GEMMs, one per chunk)
+int set_counts(int* p, int nchunks, int step, long long total, cudaStream_t s);
 // lg: bf16 logits [n, ld] of the chunk's Vc columns (vocabulary rows v0 .. v0 + Vc - 1), overwritten in place by p,
 // the softmax numerators times the cap's derivative (bf16, zero in columns Vc .. ld - 1) when need_grad.
 int ce_rows(void* lg, int ld, int Vc, long long v0, const long long* tgt, float softcap, bool need_grad,

@@ -1014,7 +1014,7 @@ CeLayout ce_layout(long long N, long long tc, long long H, long long vc, bool in
   const long long vcp = (vc + 63) / 64 * 64;
   CeLayout L{};
   size_t o = 0;
-  L.tok = o;      o += ce_align(4);
+  L.tok = o;      o += ce_align((size_t)4 * ((N + tc - 1) / tc));  // one token count per token chunk
   L.lg = o;       o += ce_align((size_t)tc * vcp * 2);
   L.parts = o;    o += grad ? ce_align((size_t)kCeMaxSplit * tc * H * 4) : 0;
   L.acc = o;      o += grad ? ce_align((size_t)N * H * 4) : 0;
@@ -1108,7 +1108,7 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
   SMELB_CUDA(cudaGetDevice(&dev));
   const int sms = num_sms(dev);
   TRY(ce_init(S, N, (int)H, st));
-  int tok_now = -1;  // the value the device-side token count holds
+  TRY(set_counts(tok, (int)((N + tc - 1) / tc), (int)tc, N, st));
   for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
     const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
     const int vcp = (Vc + 63) / 64 * 64;
@@ -1123,17 +1123,15 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
       const long long n = std::min<long long>(tc, N - t0);
       const bf16* hc = (const bf16*)h + t0 * H;
       const CeState Sc = ce_state_at(S, t0, H);
-      if (tok_now != (int)n) {
-        TRY(set_count(tok, (int)n, st));
-        tok_now = (int)n;
-      }
+      const int* cnt = tok + t0 / tc;
       {
         Builder b;
         Problem& P = b.add();
         TRY(set_a_bf16(P, wc, 1, Vc, (int)H, false, false));
         TRY(set_b_tokens(P, hc, n, (int)H));
-        groups(P, tok, nullptr, nullptr, nullptr, 1);
+        groups(P, cnt, nullptr, nullptr, nullptr, 1);
         out_bf16(P, lg, vcp);
+        P.n_inner = 1;  // the head tile is shared by the chunk's token tiles through L2
         TRY(b.launch(st));
       }
       TRY(ce_rows(lg, vcp, Vc, v0, (const long long*)tgt + t0, softcap, need_grad, wc, (int)H, Sc, n, st));
@@ -1155,7 +1153,7 @@ int smelb_chunked_ce(const void* h, const int64_t* tgt, int64_t N, int64_t H, co
                            128));
           TRY(make_tmap_2d(&P.tmB, lg + k0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, kk, (uint64_t)vcp * 2, 64, 64,
                            128));
-          groups(P, tok, nullptr, nullptr, nullptr, 1);
+          groups(P, cnt, nullptr, nullptr, nullptr, 1);
           P.epi = kEpiStoreF32;
           P.C = parts + (long long)np * n * H;
           P.c_sn = H;
@@ -1213,7 +1211,7 @@ int smelb_lm_logits(const void* h, int64_t N, int64_t H, const void* w, const vo
   char* ws = (char*)workspace;
   int* tok = (int*)(ws + lay.tok);
   bf16* lg = (bf16*)(ws + lay.lg);
-  TRY(set_count(tok, (int)N, st));
+  TRY(set_counts(tok, 1, (int)N, N, st));
   for (long long v0 = 0; v0 < V; v0 += vocab_chunk) {
     const int Vc = (int)std::min<long long>(vocab_chunk, V - v0);
     const int vcp = (Vc + 63) / 64 * 64;
@@ -1230,6 +1228,7 @@ int smelb_lm_logits(const void* h, int64_t N, int64_t H, const void* w, const vo
     TRY(set_b_tokens(P, h, N, (int)H));
     groups(P, tok, nullptr, nullptr, nullptr, 1);
     out_bf16(P, lg, vcp);
+    P.n_inner = 1;
     TRY(b.launch(st));
     TRY(ce_logits_out(lg, vcp, Vc, N, softcap, out + v0, V, st));
   }
