@@ -73,7 +73,10 @@ __host__ __device__ constexpr int qswz(int r) { return kQRowBytes == 128 ? (r & 
 // only for the round before each round it owns, and that round cannot complete without its arrival; a group at
 // ring index r has passed r - 3, whose wait saw r - 7 consumed, so its wait for r - 4 cannot alias either (this
 // needs kNumDeqGroups <= kStages). Every dequant warp waits on and releases every int4 staging stage once.
-constexpr int kNumDeqGroups = 3;
+#ifndef SMELB_DEQ_GROUPS
+#define SMELB_DEQ_GROUPS 3
+#endif
+constexpr int kNumDeqGroups = SMELB_DEQ_GROUPS;
 constexpr int kNumDeqWarps = 4;  // per group
 #ifndef SMELB_EPI_SUBS
 #define SMELB_EPI_SUBS 3

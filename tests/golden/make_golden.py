@@ -21,6 +21,10 @@ Outputs (torch.save dicts of CPU tensors):
                and token chunks, the same head as int8 rows (with quantize_int8_rows' q / scale), and a softcapped
                head (the cases of the reference tests tests/test_data_loss.py:68-85, tests/test_gemma4.py:266-277,
                in bf16) (--only ce)
+  hf_qwen_block.pt  transformers' own Qwen3_5MoeSparseMoeBlock (the module the reference's tests/test_moe.py:10-36
+               pins moe_forward against) at the reference's tiny config (smel/tiny.py: hidden 256, 32 experts,
+               top-4, expert and shared intermediate 64): weights, inputs, the fp32 and bf16 forward and the input
+               gradients of an upstream gradient (--only hf; needs transformers' qwen3_5_moe module)
 The test-suite never imports the reference; it only reads these files.
 """
 import argparse
@@ -50,7 +54,7 @@ def lora_tensors(H, I, S, n_sel, r, alpha, gen):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", default=None, choices=[None, "pack", "ce"])
+    ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf"])
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     if args.only == "pack":
@@ -58,6 +62,9 @@ def main():
         return
     if args.only == "ce":
         make_ce()
+        return
+    if args.only == "hf":
+        make_hf()
         return
     from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
     from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
@@ -269,6 +276,38 @@ def make_ce():
     with torch.no_grad():
         cases["softcap"]["loss_nograd"] = chunked_ce(h, head, tgt, denom=N, token_chunk=50, need_grad=False)
     torch.save(cases, os.path.join(HERE, "ce.pt"))
+
+
+def make_hf():
+    from smel.tiny import tiny_text_config
+    from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeSparseMoeBlock
+    torch.set_num_threads(4)
+    torch.manual_seed(0)
+    cfg = tiny_text_config()
+    cfg._experts_implementation = "eager"  # the plain per-expert loop of the module (no kernel dispatch)
+    blk = Qwen3_5MoeSparseMoeBlock(cfg).eval()
+    g = torch.Generator().manual_seed(41)
+    with torch.no_grad():
+        for n, p in blk.named_parameters():
+            # as smel/tiny.py build_tiny_model: a non-trivial router, experts N(0, 0.05); shared expert likewise.
+            # Values are rounded to bf16 so that the fixture stores them in bf16 and the fp32 run sees the same ones.
+            p.copy_((torch.randn(p.shape, generator=g) * (0.3 if n == "gate.weight" else 0.05)).bfloat16().float())
+    T, H = 256, blk.gate.weight.shape[1]
+    x = torch.randn(T, H, generator=g).bfloat16().float()
+    gy = torch.randn(T, H, generator=g).bfloat16().float()
+    out = {}
+    for name, dt in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
+        b = blk.to(dt)
+        xx = x.to(dt).detach().clone().requires_grad_(True)
+        y = b(xx[None])
+        y = (y[0] if isinstance(y, tuple) else y)[0]
+        y.backward(gy.to(dt))
+        out[name] = (y.detach().clone(), xx.grad.detach().clone())
+    blk = blk.float()
+    torch.save({"W": {"mlp." + k: v.detach().bfloat16() for k, v in blk.state_dict().items()}, "x": x.bfloat16(),
+                "gy": gy.bfloat16(),
+                "top_k": 4, "sel": [0, 3, 7, 30], "out_fp32": out["fp32"][0], "dx_fp32": out["fp32"][1],
+                "out_bf16": out["bf16"][0], "dx_bf16": out["bf16"][1]}, os.path.join(HERE, "hf_qwen_block.pt"))
 
 
 if __name__ == "__main__":
