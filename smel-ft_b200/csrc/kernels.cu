@@ -799,71 +799,93 @@ int gather_rows(const void* x, int H, int K, const int* src_of, const int* total
 // out[t] = bf16( that + bf16(y_sh[t] * bf16(sigmoid(gl[t]))) ) (the reference's bf16 op sequence). One warp per
 // (token, 256-column block), 8 columns per lane; a block's K expert rows are loaded together before they are summed
 // (in k order), so a few tokens still keep many loads in flight.
+// One warp per unit = (token, slice of nch 256-column chunks): the unit's K row indices and weights are loaded once
+// (eight at a time), then each chunk's eight rows are loaded together and summed in k order. The slice is the whole
+// row when there are enough tokens to fill the GPU and shrinks to one chunk for a handful of tokens (decode).
+constexpr int kCombineMaxChunks = 4;
+
 __global__ void combine_fwd_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
-                                   const void* __restrict__ topv, int topv_f32, int T, int K, int H,
+                                   const void* __restrict__ topv, int topv_f32, int T, int K, int H, int nch,
                                    const bf16* __restrict__ y_sh, const bf16* __restrict__ gl, int has_routed,
                                    bf16* __restrict__ out) {
   const int lane = threadIdx.x & 31;
-  const int nblk = (H + 255) / 256;
+  const int chunks = (H + 255) / 256;
+  const int nsl = (chunks + nch - 1) / nch;  // slices per token
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long u = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; u < (long long)T * nblk; u += nw) {
-    const long long t = u / nblk;
-    const int c = (int)(u - t * nblk) * 256 + lane * 8;
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (has_routed && c < H) {
+  for (long long u = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; u < (long long)T * nsl; u += nw) {
+    const long long t = u / nsl;
+    const int ch0 = (int)(u - t * nsl) * nch;
+    float acc[kCombineMaxChunks][8];
+#pragma unroll
+    for (int q = 0; q < kCombineMaxChunks; ++q)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[q][j] = 0.f;
+    if (has_routed) {
       for (int k0 = 0; k0 < K; k0 += 8) {
-        uint4 v[8];
         float w[8];
+        int rows[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const int k = k0 + kk;
-          if (k < K) {
-            const long long o = t * K + k;
-            w[kk] = topv_f32 ? reinterpret_cast<const float*>(topv)[o]
-                             : __bfloat162float(reinterpret_cast<const bf16*>(topv)[o]);
-            v[kk] = *reinterpret_cast<const uint4*>(y + (long long)row_of[o] * H + c);
-          }
+          const long long o = t * K + k0 + kk;
+          const bool in = k0 + kk < K;
+          w[kk] = !in ? 0.f
+                      : topv_f32 ? reinterpret_cast<const float*>(topv)[o]
+                                 : __bfloat162float(reinterpret_cast<const bf16*>(topv)[o]);
+          rows[kk] = in ? row_of[o] : 0;
         }
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          if (k0 + kk < K) {
-            const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v[kk]);
+        for (int q = 0; q < kCombineMaxChunks; ++q) {
+          const int c = (ch0 + q) * 256 + lane * 8;
+          if (q >= nch || c >= H) break;
+          uint4 v[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 f = __bfloat1622float2(p[j]);
-              acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(f.x, w[kk]));
-              acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(f.y, w[kk]));
+          for (int kk = 0; kk < 8; ++kk)
+            if (k0 + kk < K) v[kk] = *reinterpret_cast<const uint4*>(y + (long long)rows[kk] * H + c);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            if (k0 + kk < K) {
+              const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v[kk]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(p[j]);
+                acc[q][2 * j] = __fadd_rn(acc[q][2 * j], __fmul_rn(f.x, w[kk]));
+                acc[q][2 * j + 1] = __fadd_rn(acc[q][2 * j + 1], __fmul_rn(f.y, w[kk]));
+              }
             }
           }
         }
       }
     }
-    if (c >= H) continue;
     float sg = 0.f;
     if (y_sh && gl) {
       const float g = __bfloat162float(gl[t]);
       sg = bf16_round(1.0f / (1.0f + expf(-g)));
     }
-    float res[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) res[j] = bf16_round(acc[j]);
-    if (y_sh) {
-      const uint4 v = *reinterpret_cast<const uint4*>(y_sh + t * H + c);
-      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+    for (int q = 0; q < kCombineMaxChunks; ++q) {
+      const int c = (ch0 + q) * 256 + lane * 8;
+      if (q >= nch || c >= H) break;
+      float res[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(p[j]);
-        const float a = gl ? bf16_round(f.x * sg) : f.x;
-        const float b = gl ? bf16_round(f.y * sg) : f.y;
-        res[2 * j] = has_routed ? res[2 * j] + a : a;
-        res[2 * j + 1] = has_routed ? res[2 * j + 1] + b : b;
+      for (int j = 0; j < 8; ++j) res[j] = bf16_round(acc[q][j]);
+      if (y_sh) {
+        const uint4 v = *reinterpret_cast<const uint4*>(y_sh + t * H + c);
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(p[j]);
+          const float a = gl ? bf16_round(f.x * sg) : f.x;
+          const float b = gl ? bf16_round(f.y * sg) : f.y;
+          res[2 * j] = has_routed ? res[2 * j] + a : a;
+          res[2 * j + 1] = has_routed ? res[2 * j + 1] + b : b;
+        }
       }
-    }
-    uint4 o;
-    __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
+      uint4 o;
+      __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(res[2 * j], res[2 * j + 1]);
-    *reinterpret_cast<uint4*>(out + t * H + c) = o;
+      for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(res[2 * j], res[2 * j + 1]);
+      *reinterpret_cast<uint4*>(out + t * H + c) = o;
+    }
   }
 }
 
@@ -872,9 +894,14 @@ int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f3
   SMELB_CHECK_ARG(H % 8 == 0 && K <= 32, kErrShape, "combine_fwd: H=%d K=%d", H, K);
   if (T == 0) return kOk;
   const int threads = 256;
-  const long long units = (long long)T * ((H + 255) / 256);
+  const int chunks = (H + 255) / 256;
+  // chunks per unit: as many as keep at least ~8 warps per SM busy, at most kCombineMaxChunks
+  int nch = kCombineMaxChunks;
+  while (nch > 1 && (long long)T * ((chunks + nch - 1) / nch) < 148LL * 8) nch >>= 1;
+  nch = std::min(nch, chunks);
+  const long long units = (long long)T * ((chunks + nch - 1) / nch);
   const long long blocks = std::min<long long>((units * 32 + threads - 1) / threads, 148LL * 8);
-  combine_fwd_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)y, row_of, topv, topv_f32 ? 1 : 0, T, K, H,
+  combine_fwd_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)y, row_of, topv, topv_f32 ? 1 : 0, T, K, H, nch,
                                                       (const bf16*)y_sh, (const bf16*)gl, y != nullptr ? 1 : 0,
                                                       (bf16*)out);
   SMELB_CUDA(cudaGetLastError());
