@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
     const int trow = lq * 32 + lane;                                 // weight-tile row this thread stores to TMEM
     const uint32_t tmem_row = tmem_base + ((uint32_t)(lq * 32) << 16) + kTmemA0;
     static_assert(kNumDeqGroups <= kStages, "a dequant group's empty wait must not alias (see the ring note)");
-    static_assert(kQSub <= kNumDeqGroups, "a group owns at most one k-block of a staging stage");
+    static_assert(kQSub == 2 || kQSub == 4, "staged rows of 64 or 128 bytes");
     uint32_t it = 0, qi = 0;
     bool ok = true;
     // take part in staging stage `qstage` without owning a k-block of it
@@ -602,7 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int q_off = kmajor ? sr * kQRowBytes : kr * 64 + half * 32;  // + j * 64 * 64 for MN-major
       const int sz_off = (kmajor ? (sr >> 6) : half) * (kQSub * 64) + (kmajor ? (sr & 63) : kr);  // + j * 64
       const int swz = kmajor ? qswz(sr) : 0;
-      int qdone = 0;  // staging stages of this tile the warp has released
+      int qdone = 0;   // staging stages of this tile the warp has released
+      int qheld = -1;  // the staging stage the warp has waited for and not released yet
       for (int kb = kb0; kb < nkb; kb += kNumDeqGroups) {
         const uint32_t r = it0 + kb;
         const int s = r % kStages;
@@ -616,14 +617,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           const int j = kb % kQSub;
           const uint32_t qstage = qi + kq;
           const int qs = qstage % kQStages;
-          if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
+          if (qheld != kq) {
+            if (!mbar_wait(&q_full[qs], (qstage / kQStages) & 1, err, kDevErrWaitQFull, t, kb)) { ok = false; break; }
+            qheld = kq;
+          }
           const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes + q_off + (kmajor ? 0 : j * 64 * 64);
           const uint32_t sz = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes)[sz_off + j * 64];
           uint32_t o[32];
           dq64(sQ, kmajor ? 2 * j : 0, swz, sz, o);
-          __syncwarp();
-          if (elect_one()) mbar_arrive(&q_empty[qs]);  // the group's only k-block of this stage: nibbles consumed
-          qdone = kq + 1;
+          // the stage is released after the group's last k-block in it (a group owns one or two of a stage's k-blocks)
+          const int kb_next = kb + kNumDeqGroups;
+          if (kb_next >= nkq || kb_next / kQSub != kq) {
+            __syncwarp();
+            if (elect_one()) mbar_arrive(&q_empty[qs]);
+            qdone = kq + 1;
+            qheld = -1;
+          }
           if (kmajor) {
             tc_fence_after();  // the MMAs that read this TMEM stage completed (empty wait above)
             __syncwarp();      // tcgen05.st is warp-collective

@@ -37,12 +37,18 @@ constexpr int kBK = 64;
 #define SMELB_STAGES 4
 #endif
 #ifndef SMELB_QSTAGES
-#define SMELB_QSTAGES 4
+#define SMELB_QSTAGES 3
 #endif
 constexpr int kMaxBN = SMELB_MAX_BN;     // token tile (MMA N) upper bound
 constexpr int kStages = SMELB_STAGES;    // operand ring: a weight tile (16 KB) and a token tile (kMaxBN x 128 B)
 constexpr int kQStages = SMELB_QSTAGES;  // packed-int4 staging ring
-constexpr int kQSub = 2;                 // k-blocks per int4 staging stage
+#ifndef SMELB_QSUB
+#define SMELB_QSUB 4
+#endif
+// k-blocks per int4 staging stage: 4 makes each staged weight row 128 bytes (4 x 32 bytes of nibbles), so a stage
+// takes half the TMA row requests that 64-byte rows did for the same bytes; a dequant group owns one or two of a
+// stage's k-blocks and releases the stage after its last one.
+constexpr int kQSub = SMELB_QSUB;
 constexpr int kQRowBytes = kQSub * 32;   // one staged K-major weight row: kQSub k-blocks of 64 nibbles
 static_assert(kQRowBytes == 64 || kQRowBytes == 128, "staged rows use the 64- or 128-byte swizzle");
 constexpr int kMaxProblems = 12;
