@@ -25,6 +25,10 @@ Outputs (torch.save dicts of CPU tensors):
                pins moe_forward against) at the reference's tiny config (smel/tiny.py: hidden 256, 32 experts,
                top-4, expert and shared intermediate 64): weights, inputs, the fp32 and bf16 forward and the input
                gradients of an upstream gradient (--only hf; needs transformers' qwen3_5_moe module)
+  hf_gemma_block.pt  the MoE part of transformers' own Gemma4TextDecoderLayer after the attention residual (dense
+               MLP, router, experts, the four feed-forward norms, layer_scalar, called in the order of the module's
+               forward) at the reference's tiny Gemma 4 config (smel/tiny.py: hidden 256, 16 experts, top-4), fp32
+               and bf16 forward and input gradients (--only hf_gemma; needs transformers' gemma4 module)
 The test-suite never imports the reference; it only reads these files.
 """
 import argparse
@@ -54,7 +58,7 @@ def lora_tensors(H, I, S, n_sel, r, alpha, gen):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf"])
+    ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf", "hf_gemma"])
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     if args.only == "pack":
@@ -65,6 +69,9 @@ def main():
         return
     if args.only == "hf":
         make_hf()
+        return
+    if args.only == "hf_gemma":
+        make_hf_gemma()
         return
     from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
     from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
@@ -308,6 +315,57 @@ def make_hf():
                 "gy": gy.bfloat16(),
                 "top_k": 4, "sel": [0, 3, 7, 30], "out_fp32": out["fp32"][0], "dx_fp32": out["fp32"][1],
                 "out_bf16": out["bf16"][0], "dx_bf16": out["bf16"][1]}, os.path.join(HERE, "hf_qwen_block.pt"))
+
+
+def make_hf_gemma():
+    from smel.tiny import tiny_gemma4_config
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4TextDecoderLayer
+    torch.set_num_threads(4)
+    torch.manual_seed(0)
+    cfg = tiny_gemma4_config()
+    cfg._experts_implementation = "eager"  # the plain per-expert loop of the module
+    cfg._attn_implementation = "sdpa"
+    layer = Gemma4TextDecoderLayer(cfg, layer_idx=0).eval()
+    g = torch.Generator().manual_seed(43)
+    with torch.no_grad():
+        for n, p in layer.named_parameters():
+            if n.startswith("self_attn"):
+                continue
+            # as smel/tiny.py build_tiny_gemma4: non-trivial norms and scales (Gemma norms multiply by w directly)
+            if n.endswith("norm.weight") or n.endswith("layernorm.weight") or n.endswith("router.scale"):
+                v = torch.randn(p.shape, generator=g) * 0.2 + 1.0
+            elif n.endswith("per_expert_scale"):
+                v = torch.rand(p.shape, generator=g) + 0.5
+            elif n.endswith("router.proj.weight"):
+                v = torch.randn(p.shape, generator=g) * 0.3
+            else:
+                v = torch.randn(p.shape, generator=g) * 0.05
+            p.copy_(v.bfloat16().float())  # bf16-exact, so the fixture stores bf16 and the fp32 run sees the same
+        layer.layer_scalar.fill_(0.875)
+    T, H = 256, cfg.hidden_size
+    h = torch.randn(T, H, generator=g).bfloat16().float()
+    gy = torch.randn(T, H, generator=g).bfloat16().float()
+
+    def block(L, hh):
+        # the MoE part of Gemma4TextDecoderLayer.forward, after `residual = hidden_states` (attention residual)
+        m = L.post_feedforward_layernorm_1(L.mlp(L.pre_feedforward_layernorm(hh)))
+        _, w, idx = L.router(hh)
+        e = L.post_feedforward_layernorm_2(L.experts(L.pre_feedforward_layernorm_2(hh), idx, w))
+        return (hh + L.post_feedforward_layernorm(m + e)) * L.layer_scalar, idx
+
+    out = {}
+    for name, dt in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
+        L = layer.to(dt)
+        hh = h.to(dt).detach().clone().requires_grad_(True)
+        y, idx = block(L, hh)
+        y.backward(gy.to(dt))
+        out[name] = (y.detach().clone(), hh.grad.detach().clone(), idx.clone())
+    layer = layer.float()
+    W = {k: v.detach().bfloat16() for k, v in layer.state_dict().items() if not k.startswith("self_attn")}
+    torch.save({"W": W, "h": h.bfloat16(), "gy": gy.bfloat16(), "top_k": cfg.top_k_experts,
+                "eps": cfg.rms_norm_eps, "out_fp32": out["fp32"][0], "dh_fp32": out["fp32"][1],
+                "topi_fp32": out["fp32"][2], "out_bf16": out["bf16"][0], "dh_bf16": out["bf16"][1]},
+               os.path.join(HERE, "hf_gemma_block.pt"))
 
 
 if __name__ == "__main__":
