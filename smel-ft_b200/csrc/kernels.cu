@@ -802,7 +802,7 @@ int gather_rows(const void* x, int H, int K, const int* src_of, const int* total
 // One warp per unit = (token, slice of nch 256-column chunks): the unit's K row indices and weights are loaded once
 // (eight at a time), then each chunk's eight rows are loaded together and summed in k order. The slice is the whole
 // row when there are enough tokens to fill the GPU and shrinks to one chunk for a handful of tokens (decode).
-constexpr int kCombineMaxChunks = 4;
+constexpr int kCombineMaxChunks = 2;
 
 __global__ void combine_fwd_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
                                    const void* __restrict__ topv, int topv_f32, int T, int K, int H, int nch,
@@ -895,7 +895,8 @@ int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f3
   if (T == 0) return kOk;
   const int threads = 256;
   const int chunks = (H + 255) / 256;
-  // chunks per unit: as many as keep at least ~8 warps per SM busy, at most kCombineMaxChunks
+  // chunks per unit: as many as keep at least ~8 warps per SM busy, at most kCombineMaxChunks (2: with 4 the
+  // kernel needs 128 registers and half the warps per SM, and runs 5% slower at 4092 tokens)
   int nch = kCombineMaxChunks;
   while (nch > 1 && (long long)T * ((chunks + nch - 1) / nch) < 148LL * 8) nch >>= 1;
   nch = std::min(nch, chunks);
@@ -1022,14 +1023,10 @@ __global__ void dx_reduce_kernel(const bf16* __restrict__ dxs, const int* __rest
   const int lane = threadIdx.x & 31;
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
-    int rows[32];
-    if (dxs)
-      for (int k = 0; k < K; ++k) rows[k] = row_of[t * K + k];
     const float dg = dgl ? dgl[t] : 0.f;
     for (int c = lane * 8; c < H; c += 256) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      auto add = [&](const bf16* src) {
-        const uint4 v = *reinterpret_cast<const uint4*>(src);
+      auto add = [&](const uint4& v) {
         const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -1038,10 +1035,20 @@ __global__ void dx_reduce_kernel(const bf16* __restrict__ dxs, const int* __rest
           acc[2 * j + 1] += f.y;
         }
       };
-      if (dxs)
-        for (int k = 0; k < K; ++k) add(dxs + (long long)rows[k] * H + c);
-      if (dx_sh) add(dx_sh + t * H + c);
-      if (dx_r) add(dx_r + t * H + c);
+      if (dxs) {
+        // the rows of eight k are loaded together, then added in k order
+        for (int k0 = 0; k0 < K; k0 += 8) {
+          uint4 v[8];
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            if (k0 + kk < K) v[kk] = *reinterpret_cast<const uint4*>(dxs + (long long)row_of[t * K + k0 + kk] * H + c);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            if (k0 + kk < K) add(v[kk]);
+        }
+      }
+      if (dx_sh) add(*reinterpret_cast<const uint4*>(dx_sh + t * H + c));
+      if (dx_r) add(*reinterpret_cast<const uint4*>(dx_r + t * H + c));
       if (dgl && w_sg) {
         const uint4 v = *reinterpret_cast<const uint4*>(w_sg + c);
         const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
