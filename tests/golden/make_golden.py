@@ -57,9 +57,12 @@ def lora_tensors(H, I, S, n_sel, r, alpha, gen):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE"),
+                    help="the smel-ft source tree (default: $SMEL_REFERENCE)")
     ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf", "hf_gemma"])
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <smel-ft source tree> or set SMEL_REFERENCE")
     sys.path.insert(0, args.reference)
     if args.only == "pack":
         make_pack()
