@@ -242,8 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   // or 4 dequant-warp arrivals)
   uint64_t* full = bars;
   uint64_t* empty = full + kStages;         // MMAs reading the stage (weight and token tile) are done
-  uint64_t* q_full = empty + kStages;       // packed nibbles + (scale, zero) of 4 k-blocks landed
-  uint64_t* q_empty = q_full + kQStages;    // all 4 k-blocks of the staging stage dequantized
+  uint64_t* q_full = empty + kStages;       // packed nibbles + (scale, zero) of a stage's kQSub k-blocks landed
+  uint64_t* q_empty = q_full + kQStages;    // every dequant warp is done with the staging stage
   uint64_t* acc_full = q_empty + kQStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_drain = acc_full + 4;
@@ -563,9 +563,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
   } else if (warp < kWarpEpi0) {
     // ============================================================================ int4 dequant (three groups)
     // Group grp owns the k-blocks whose ring index is grp mod kNumDeqGroups and walks only those. Every dequant warp
-    // takes part in every int4 staging stage once, in stage order: it waits for a stage before its k-block there
-    // and releases the stage after it; a stage where the group owns no k-block is waited for and released on its
-    // own when the walk passes it.
+    // takes part in every int4 staging stage once, in stage order: it waits for a stage before its first k-block
+    // there and releases the stage after its last one (a group owns one or two of a 4-k-block stage's k-blocks); a
+    // stage where the group owns no k-block is waited for and released on its own when the walk passes it.
     const int grp = (warp - kWarpDeq0) / kNumDeqWarps;
     const int pt = ((warp - kWarpDeq0) % kNumDeqWarps) * 32 + lane;  // 0..127 within the group
     const int lq = warp & 3;                                         // TMEM lane quarter this warp may access
