@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         }
         tma_prefetch_desc(&P.tmB);
         if (P.mode == kTokN) tma_prefetch_desc(&P.tmB32);
+        if (P.b16) tma_prefetch_desc(&P.tmB16);
         if (P.has_ext) {
           tma_prefetch_desc(&P.tmAe);
           tma_prefetch_desc(&P.tmBe);
@@ -366,6 +367,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int ext_kb = (!tokk && P.has_ext) ? ti.nkb - 1 : -1;
       const CUtensorMap* mB = &P.tmB;
       const CUtensorMap* mB32 = &P.tmB32;
+      const CUtensorMap* mB16 = &P.tmB16;
+      // with the 16-row map, a token tile loads the rows the MMA reads: 64-row boxes, then 32 and / or 16 rows
+      const bool exact = !tokk && P.b16;
+      const int b_rows = (ti.n_valid + 15) & ~15;
       const CUtensorMap* mBe = &P.tmBe;
       const CUtensorMap* mAmain = &P.tmA;
       const CUtensorMap* mAext = &P.tmAe;
@@ -384,11 +389,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           const bool ext = kb == ext_kb;
           const bool a_tma = ext || !int4;  // the weight tile comes by TMA (else the dequant warps fill it)
           const bool b32 = !tokk && !ext && ti.n_valid <= 32;
-          mbar_arrive_expect_tx(f, (b32 ? 4096 : nb * 8192) + (a_tma ? kAStageBytes : 0));
+          const uint32_t b_bytes = (exact && !ext) ? (uint32_t)b_rows * 128u : (b32 ? 4096u : (uint32_t)nb * 8192u);
+          mbar_arrive_expect_tx(f, b_bytes + (a_tma ? kAStageBytes : 0));
           // token tile
           if (tokk) {  // B = tokens^T (MN-major)
             const int krow = ti.n0 + kb * kBK;
             for (int i = 0; i < nb; ++i) tma_load_2d(sB + i * 8192, mB, b_x0 + 64 * i, krow, f);
+          } else if (exact && !ext) {
+            const int n64 = b_rows >> 6, rem = b_rows & 63;
+            for (int i = 0; i < n64; ++i) tma_load_2d(sB + i * 8192, mB, kb * kBK, ti.n0 + 64 * i, f);
+            if (rem & 32) tma_load_2d(sB + n64 * 8192, mB32, kb * kBK, ti.n0 + 64 * n64, f);
+            if (rem & 16) tma_load_2d(sB + n64 * 8192 + (rem & 32) * 128, mB16, kb * kBK, ti.n0 + 64 * n64 + (rem & 32), f);
           } else if (b32) {
             tma_load_2d(sB, mB32, kb * kBK, ti.n0, f);
           } else {

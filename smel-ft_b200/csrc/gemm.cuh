@@ -102,6 +102,7 @@ struct alignas(64) Problem {
   CUtensorMap tmA;   // bf16 A (weights [rows][k] / [k][m], or tokens [rows][m] in kTokK); unused for int4
   CUtensorMap tmB;   // tokens: kTokN [rows][k] K-major (64-row box); kTokK [rows][n] (MN-major B)
   CUtensorMap tmB32; // kTokN tokens with a 32-row box (token tiles of at most 32 rows)
+  CUtensorMap tmB16; // kTokN tokens with a 16-row box (valid when b16 is set)
   CUtensorMap tmAe;  // LoRA extension, weight side [nW * e_wrows][64]
   CUtensorMap tmBe;  // LoRA extension, token side [rows][64]
   CUtensorMap tmQ;   // int4 nibbles (uint8): K-major [nW*rows][K/2], box 128 B x 64 rows;
@@ -117,6 +118,7 @@ struct alignas(64) Problem {
   int a_x0;     // kTokK: column offset into tmA
   int b_x0;     // kTokK: column offset into tmB
   int has_ext;
+  int b16;      // kTokN: tmB16 is set, so a token tile loads exactly the rows the MMA reads (a multiple of 16)
   int e_wrows;  // ext A rows per weight index
   int q_rows;   // int4: rows of the stored matrix per weight index (K-major: M-dim rows; MN-major: K rows)
   int q_groups; // int4: groups per stored row (= stored row length / 64)

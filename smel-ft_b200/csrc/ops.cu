@@ -109,6 +109,8 @@ int set_b_tokens(Problem& P, const void* X, long long rows, int cols, int BN = k
   P.mode = kTokN;
   P.BN = BN < kMaxBN ? BN : kMaxBN;
   TRY(tm_bf16(&P.tmB32, X, rows, cols, 32));
+  TRY(tm_bf16(&P.tmB16, X, rows, cols, 16));
+  P.b16 = 1;
   return tm_bf16(&P.tmB, X, rows, cols, 64);
 }
 
