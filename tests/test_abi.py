@@ -57,3 +57,45 @@ def test_cpu_tensors_are_rejected():
         smelb.quantize_int4(torch.randn(2, 64))
     with pytest.raises(smelb.SmelbError):
         smelb.route(torch.randn(4, 64, dtype=torch.bfloat16), torch.randn(8, 64, dtype=torch.bfloat16), 2)
+
+
+def test_chunked_ce_workspace_sizes():
+    """Workspace of smelb_chunked_ce: the bf16 logit tile of one (token chunk, vocabulary chunk), the fp32 state of
+    every row, the gradient's fp32 partials and accumulators only when the gradient is formed, and a bf16 copy of
+    one head chunk only for an int8 head."""
+    from smelb import _lib
+    ws = _lib.load().smelb_chunked_ce_workspace_bytes
+    N, tc, H, vc = 4092, 1024, 2048, 32768
+    full = ws(N, tc, H, vc, 0, 1)
+    assert full >= tc * vc * 2 + 2 * N * H * 4 + 4 * tc * H * 4
+    assert ws(N, tc, H, vc, 1, 1) - full == vc * H * 2           # the dequantised head chunk
+    assert ws(N, tc, H, vc, 0, 0) < full - 2 * N * H * 4          # no accumulators without the gradient
+    assert ws(N, 2 * tc, H, vc, 0, 1) > full                      # the logit tile grows with the token chunk
+    assert ws(N, 4 * N, H, vc, 0, 1) == ws(N, N, H, vc, 0, 1)     # token chunks are capped at N rows
+    assert ws(0, tc, H, vc, 0, 1) == 256                          # empty input: a minimal buffer
+    assert _lib.load().smelb_lm_logits_workspace_bytes(N, H, vc, 1) >= N * vc * 2 + vc * H * 2
+
+
+def test_ce_and_int8_argument_errors():
+    """The CE and int8-row entry points reject bad arguments before launching anything."""
+    from smelb import _lib
+    with pytest.raises(_lib.SmelbError, match="null pointer"):
+        _lib.call("smelb_chunked_ce", None, None, 4, 64, None, None, None, 100, 64, 64, 0.0, 1.0, None, None, None,
+                  None, 0, None)
+    fake = 1 << 20  # never dereferenced: the shape check fails first
+    with pytest.raises(_lib.SmelbError, match="exactly one"):
+        _lib.call("smelb_chunked_ce", fake, fake, 4, 64, fake, fake, fake, 100, 64, 64, 0.0, 1.0, fake, fake, None,
+                  fake, 1 << 30, None)
+    with pytest.raises(_lib.SmelbError, match="H=100"):
+        _lib.call("smelb_chunked_ce", fake, fake, 4, 100, fake, None, None, 100, 64, 64, 0.0, 1.0, fake, fake, None,
+                  fake, 1 << 30, None)
+    with pytest.raises(_lib.SmelbError, match="softcap"):
+        _lib.call("smelb_chunked_ce", fake, fake, 4, 64, fake, None, None, 100, 64, 64, -1.0, 1.0, fake, fake, None,
+                  fake, 1 << 30, None)
+    with pytest.raises(_lib.SmelbError, match="workspace"):
+        _lib.call("smelb_chunked_ce", fake, fake, 4, 64, fake, None, None, 100, 64, 64, 0.0, 1.0, fake, fake, None,
+                  fake, 16, None)
+    with pytest.raises(_lib.SmelbError, match="null pointer"):
+        _lib.call("smelb_int8_rows_quantize", None, 0, 4, 64, None, None, None)
+    with pytest.raises(_lib.SmelbError, match="null pointer"):
+        _lib.call("smelb_int8_rows_dequant", None, None, 4, 64, None, 0, None)
