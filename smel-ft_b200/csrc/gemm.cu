@@ -609,10 +609,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       // staged swizzled (16-byte chunk c of row r at chunk c ^ qswz(r)).
       // MN-major: k-row kr, half `half` of the 128 output features -> one 128-byte row of the swizzled smem tile.
       const int sr = P.epi == kEpiGlu ? glu_stage_row(trow) : trow;
-      const int kr = pt >> 1, half = pt & 1;
-      const int q_off = kmajor ? sr * kQRowBytes : kr * 64 + half * 32;  // + j * 64 * 64 for MN-major
+      // MN-major: the 8 threads of each quarter-warp take 8 consecutive k-rows (one half of the features), so both
+      // their 16-byte reads of the 64B-swizzled nibble rows and their 16-byte writes of the 128B-swizzled tile rows
+      // fall in 8 distinct bank groups (with two threads per k-row the writes were 2-way conflicted)
+      const int kr = (pt & 7) | ((pt >> 4) << 3), half = (pt >> 3) & 1;
+      const int q_off = kmajor ? sr * kQRowBytes : kr * 64;  // + j * 64 * 64 for MN-major
       const int sz_off = (kmajor ? (sr >> 6) : half) * (kQSub * 64) + (kmajor ? (sr & 63) : kr);  // + j * 64
-      const int swz = kmajor ? qswz(sr) : 0;
+      const int swz = kmajor ? qswz(sr) : ((kr >> 1) & 3);  // k-row j * 64 + kr of the stage: (row >> 1) & 3
       int qdone = 0;   // staging stages of this tile the warp has released
       int qheld = -1;  // the staging stage the warp has waited for and not released yet
       for (int kb = kb0; kb < nkb; kb += kNumDeqGroups) {
@@ -635,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           const uint8_t* sQ = smem + kOffQ + qs * kQStageBytes + q_off + (kmajor ? 0 : j * 64 * 64);
           const uint32_t sz = reinterpret_cast<const uint32_t*>(smem + kOffSZ + qs * kSZStageBytes)[sz_off + j * 64];
           uint32_t o[32];
-          dq64(sQ, kmajor ? 2 * j : 0, swz, sz, o);
+          dq64(sQ, kmajor ? 2 * j : 2 * half, swz, sz, o);
           // the stage is released after the group's last k-block in it (a group owns one or two of a stage's k-blocks)
           const int kb_next = kb + kNumDeqGroups;
           if (kb_next >= nkq || kb_next / kQSub != kq) {

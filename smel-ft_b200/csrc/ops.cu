@@ -30,9 +30,9 @@ int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int b
 int tm_q(CUtensorMap* m, const void* q, long long rows, long long cols, bool mn_major) {
   // packed nibbles of a stored matrix [rows][cols]: [rows][cols/2] bytes. K-major tiles stage kQSub k-blocks per
   // row (kQRowBytes, swizzled over the row so the dequant warps' row reads are free of bank conflicts); MN-major
-  // tiles stage kQSub k-blocks of 64 k-rows x 64 B.
+  // tiles stage kQSub k-blocks of 64 k-rows x 64 B, 64-byte swizzled for the same reason.
   return make_tmap_2d(m, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols / 2, cols / 2, mn_major ? 64 : kQRowBytes,
-                      mn_major ? kQSub * 64 : 64, mn_major ? 0 : kQRowBytes);
+                      mn_major ? kQSub * 64 : 64, mn_major ? 64 : kQRowBytes);
 }
 int tm_sz(CUtensorMap* m, const uint32_t* sz, long long nw_groups, long long rows, bool mn_major) {
   return make_tmap_2d(m, sz, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, nw_groups, rows, rows * 4,
