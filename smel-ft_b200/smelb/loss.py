@@ -54,23 +54,11 @@ class LMHead:
         for v0 in range(0, self.vocab, self.vocab_chunk):
             yield v0, min(self.vocab, v0 + self.vocab_chunk)
 
-    def _head_ptrs(self, device):
-        if self.w is not None:
-            w = self.w if self.w.dtype == torch.bfloat16 else self.w.to(torch.bfloat16)
-            w = w.contiguous()
-            if w.device != device:
-                raise _lib.SmelbError(f"LMHead: head on {w.device}, hidden rows on {device}")
-            return (w,), (_lib.ptr(w), None, None), False
-        q, s = self.q["q"].contiguous(), self.q["scale"].contiguous()
-        if q.device != device:
-            raise _lib.SmelbError(f"LMHead: head on {q.device}, hidden rows on {device}")
-        return (q, s), (None, _lib.ptr(q), _lib.ptr(s)), True
-
     def logits(self, h):
         """cap(h @ W^T) in fp32 [N, V] (smel/loss.py:45-47), chunk by chunk on the GEMM engine."""
         h = _check_h(h, "LMHead.logits")
         N, H = h.shape
-        keep, (wp, qp, sp), int8 = self._head_ptrs(h.device)
+        keep, (wp, qp, sp), int8 = _head_ptrs(self, h.device)
         out = torch.empty(N, self.vocab, dtype=torch.float32, device=h.device)
         if N == 0:
             return out
@@ -80,6 +68,21 @@ class LMHead:
         _lib.call("smelb_lm_logits", _lib.ptr(h), N, H, wp, qp, sp, self.vocab, self.vocab_chunk, self.softcap,
                   _lib.ptr(out), _lib.ptr(ws), nb, _lib.stream_ptr(h.device))
         return out
+
+
+def _head_ptrs(head, device):
+    """(tensors to keep alive, (w, q, scale) pointers, int8?) of a head: this module's LMHead or the reference's
+    (smel/loss.py:12-47), which has the same fields (w or q, vocab, vocab_chunk, softcap)."""
+    if head.w is not None:
+        w = head.w if head.w.dtype == torch.bfloat16 else head.w.to(torch.bfloat16)
+        w = w.contiguous()
+        if w.device != device:
+            raise _lib.SmelbError(f"LMHead: head on {w.device}, hidden rows on {device}")
+        return (w,), (_lib.ptr(w), None, None), False
+    q, s = head.q["q"].contiguous(), head.q["scale"].contiguous()
+    if q.device != device:
+        raise _lib.SmelbError(f"LMHead: head on {q.device}, hidden rows on {device}")
+    return (q, s), (None, _lib.ptr(q), _lib.ptr(s)), True
 
 
 def _check_h(h, who):
@@ -95,7 +98,7 @@ def _check_h(h, who):
 def _run(h, head: LMHead, tgt, denom, token_chunk, need_grad):
     """One smelb_chunked_ce call: (loss fp32 0-dim, per-row losses fp32 [N], gradient bf16 [N, H] or None)."""
     N, H = h.shape
-    keep, (wp, qp, sp), int8 = head._head_ptrs(h.device)
+    keep, (wp, qp, sp), int8 = _head_ptrs(head, h.device)
     tgt = tgt.to(device=h.device, dtype=torch.int64).contiguous()
     tc = max(1, min(int(token_chunk), N))
     vc = min(head.vocab_chunk, head.vocab)

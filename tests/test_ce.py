@@ -45,6 +45,17 @@ def test_oracle_int8_rows_match_reference(golden):
                                                                 d["int8"]["scale"].view(torch.int16))
 
 
+def test_head_fields_are_read_duck_typed():
+    """chunked_ce reads only the head's fields (w or q, vocab, vocab_chunk, softcap), so a head built by the
+    reference's LMHead (same fields) reaches the same device check instead of failing on a missing method."""
+    import types
+    import smelb
+    head = types.SimpleNamespace(w=torch.randn(100, 64).bfloat16(), q=None, vocab=100, vocab_chunk=64, softcap=0.0)
+    from smelb import loss as L
+    with pytest.raises(smelb.SmelbError, match="head on cpu"):
+        L._head_ptrs(head, torch.device("cuda", 0))
+
+
 def test_cpu_tensors_are_rejected():
     import smelb
     w = torch.randn(100, 64).bfloat16()
