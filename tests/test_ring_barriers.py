@@ -5,7 +5,9 @@ semantics the kernel relies on, under random interleavings of its warp roles:
   TMA-Q (1 warp): wait `q_empty`, arrive `q_full` with transaction bytes, stage by stage
   dequant (3 groups x 4 warps, k-blocks of ring index g mod 3): pass staging stages they own nothing of, wait
       `empty`, wait `q_full` on their first k-block of a stage, release `q_empty` after their last, arrive `full`
-  MMA (1 warp): wait `full` of every k-block in order, then commit `empty` (when its MMAs complete)
+  MMA (1 warp): per tile wait `acc_empty` of its accumulator (two, alternating), then wait `full` of every k-block
+      in order and commit `empty` (when its MMAs complete), then commit `acc_full`
+  epilogue (12 warps): per tile wait `acc_full`, read the accumulator, arrive `acc_empty`
 
 A barrier phase completes when all its arrivals are in and its transaction bytes have landed. TMA completions are
 asynchronous events in any order; MMA commits arrive in issue order (a tcgen05.commit arrives once every MMA issued
@@ -17,7 +19,7 @@ import random
 
 import pytest
 
-STAGES, GROUPS, DEQ_WARPS = 4, 3, 4
+STAGES, GROUPS, DEQ_WARPS, EPI_WARPS = 4, 3, 4, 12
 
 
 class Bar:
@@ -49,6 +51,8 @@ def roles(tiles, q_stages, Q_SUB):
     empty = [Bar(f"empty{s}", 1) for s in range(STAGES)]
     q_full = [Bar(f"q_full{s}", 1) for s in range(q_stages)]
     q_empty = [Bar(f"q_empty{s}", GROUPS * DEQ_WARPS) for s in range(q_stages)]
+    acc_full = [Bar(f"acc_full{a}", 1) for a in range(2)]
+    acc_empty = [Bar(f"acc_empty{a}", EPI_WARPS) for a in range(2)]
 
     def producer(prod):
         it = 0
@@ -69,12 +73,22 @@ def roles(tiles, q_stages, Q_SUB):
                 qi += 1
 
     def mma():
-        it = 0
+        it = acc_it = 0
         for nkb, nkq in tiles:
+            acc = acc_it & 1
+            yield ("wait", acc_empty[acc], (acc_it >> 1) - 1)
             for kb in range(nkb):
                 yield ("wait", full[it % STAGES], it // STAGES)
                 yield ("commit", empty[it % STAGES])
                 it += 1
+            yield ("commit", acc_full[acc])
+            acc_it += 1
+
+    def epilogue():
+        for acc_it in range(len(tiles)):
+            acc = acc_it & 1
+            yield ("wait", acc_full[acc], acc_it >> 1)
+            yield ("arrive", acc_empty[acc])
 
     def dequant(g):
         it = qi = 0
@@ -112,6 +126,7 @@ def roles(tiles, q_stages, Q_SUB):
 
     gens = [producer(0), producer(1), tma_q(), mma()]
     gens += [dequant(g) for g in range(GROUPS) for _ in range(DEQ_WARPS)]
+    gens += [epilogue() for _ in range(EPI_WARPS)]
     return gens
 
 
