@@ -127,8 +127,8 @@ def config_json(cfg, meta, world, parallel="dp"):
     return {"workload": "qwen3.6-35b-a3b moe layer (config 2): fwd + recompute + bwd", "tokens": cfg["T"],
             "hidden": cfg["H"], "experts": cfg["E"], "top_k": cfg["K"], "expert_inter": cfg["I"],
             "shared_inter": cfg["S"], "frozen": "int4 group-64", "lora_experts": cfg["n_sel"],
-            "lora_rank": cfg["r"], "routing": f"zipf s=1.1 over a seeded permutation, top-12 gate share "
-            f"{meta.get('share', 0):.3f}", "seed": meta.get("seed"),
+            "lora_rank": cfg["r"], "routing": "zipf s=1.1 over a seeded permutation, temperature bisected so the "
+            "12 LoRA experts hold 50% +- 2% of the renormalised top-8 gate mass", "seed": meta.get("seed"),
             "l2": "weights 0.53 GB > L2 126 MB: each step streams the banks from HBM",
             "parallelism": "single" if world == 1 else
             (f"ep{world}: experts split over {world} GPUs, {cfg['T']} tokens per GPU (weak scaling)" if parallel == "ep"
@@ -137,21 +137,43 @@ def config_json(cfg, meta, world, parallel="dp"):
 
 
 # ------------------------------------------------------------------------------------------ CPU baseline
-def cpu_baseline(layer, tokens, dtype=torch.float32):
-    """The reference's torch CPU path (oracle/cpu_step.py) on `tokens` tokens, one warm-up + one timed step."""
+def cpu_model():
+    """The host CPU's model name (lscpu's "Model name", read from /proc/cpuinfo)."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _time_cpu_step(p, tokens, dtype):
     from oracle import cpu_step
-    torch.set_num_threads(os.cpu_count() or 1)
-    p = cpu_step.prepare(layer, dtype=dtype, tokens=tokens)
     gy = torch.randn(p["x"].shape, generator=torch.Generator().manual_seed(9)).to(dtype)
     small = dict(p)
     small["x"] = p["x"][:64]
     cpu_step.step(small, gy[:64])  # warm-up (allocator, thread pool)
     t0 = time.perf_counter()
     cpu_step.step(p, gy)
-    dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{tokens} tokens of the same layer, 1 step (fwd no-grad + recompute + bwd), {str(dtype)[6:]}, "
-                      f"{dt:.2f} s"}
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(layer, tokens, bf16_tokens=1024):
+    """The reference's torch CPU path (oracle/cpu_step.py) on the host cores: `tokens` tokens in fp32 (the headline
+    value) and `bf16_tokens` in bf16, one warm-up + one timed step each."""
+    from oracle import cpu_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    dt = _time_cpu_step(cpu_step.prepare(layer, dtype=torch.float32, tokens=tokens), tokens, torch.float32)
+    res = {"value": tokens / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+           "cpu_model": cpu_model(),
+           "sample": f"{tokens} tokens of the same layer, 1 step (fwd no-grad + recompute + bwd), float32, {dt:.2f} s"}
+    if bf16_tokens:
+        db = _time_cpu_step(cpu_step.prepare(layer, dtype=torch.bfloat16, tokens=bf16_tokens), bf16_tokens,
+                            torch.bfloat16)
+        res["bf16"] = {"value": bf16_tokens / db, "unit": "tokens/s",
+                       "sample": f"{bf16_tokens} tokens of the same layer, 1 step, bfloat16, {db:.2f} s"}
+    return res
 
 
 # ------------------------------------------------------------------------------------------ our arm
@@ -361,7 +383,8 @@ def run_ours(args, world, rank, local):
     res = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random-init weights of the layer shape)",
-           "config": dict(config_json(cfg, layer["meta"], world, args.parallel), timing=timing), "roofline": roof,
+           "config": config_json(cfg, layer["meta"], world, args.parallel), "timing": timing,
+           "routing_share": round(layer["meta"].get("share", 0.0), 4), "roofline": roof,
            "e2e": e2e,
            "gpu_launches": int(launches), "clocks": ck}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -561,23 +584,26 @@ def run_sweep(args, local):
 
 # ------------------------------------------------------------------------------------------ reference arm
 def run_reference(args, world, rank):
-    """The reference's CPU torch path (restated in oracle/cpu_step.py) on the host cores, same metric and config."""
+    """The reference's CPU torch path (restated in oracle/cpu_step.py) on the host cores, same metric and config.
+    The synthetic inputs come from the same seeded construction as our arm (smelb.synth.qwen_layer_tensors: torch
+    operations only) with the bank quantized by the reference's algorithm (the oracle's quantizer, as torch
+    operations); libsmelb is never loaded in this process. The timed steps run on the CPU alone."""
     if rank != 0:
         return None
     from oracle import cpu_step
-    from smelb.synth import qwen_layer
+    from smelb.synth import qwen_layer_tensors
     cfg = layer_config(args)
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
-    if dev.type == "cpu":
-        return {"impl": "reference", "unavailable": "building the synthetic layer needs the GPU quantizer"}
-    layer = qwen_layer(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"], n_sel=cfg["n_sel"],
-                       r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
+    t = qwen_layer_tensors(T=cfg["T"], H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"],
+                           n_sel=cfg["n_sel"], r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
     torch.set_num_threads(os.cpu_count() or 1)
     tokens = min(cfg["T"], args.ref_tokens)
-    p = cpu_step.prepare(layer, dtype=torch.float32, tokens=tokens)
+    p = cpu_step.prepare_tensors(t, dtype=torch.float32, tokens=tokens)
+    meta = t["meta"]
     gy = torch.randn(p["x"].shape, generator=torch.Generator().manual_seed(9))
-    del layer
-    torch.cuda.empty_cache()
+    del t
+    if dev.type == "cuda":
+        torch.cuda.empty_cache()
     times = []
     budget = args.ref_budget_s
     t_start = time.perf_counter()
@@ -594,10 +620,12 @@ def run_reference(args, world, rank):
     res = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": len(times),
            "warmup": args.warmup, "ms_per_step": round(1e3 * tot / len(times), 2), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-           "config": config_json(cfg, {"seed": 0}, 1), "impl": "reference",
+           "config": config_json(cfg, meta, world, args.parallel), "impl": "reference",
+           "timing": "wall clock of the CPU steps (time.perf_counter)", "routing_share": round(meta.get("share", 0.0), 4),
            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(),
-                            "kind": "port", "sample": f"{tokens} tokens per step, fp32 (the reference's faster CPU "
-                                                      f"dtype), {len(times)} timed steps"},
+                            "kind": "port", "cpu_model": cpu_model(),
+                            "sample": f"{tokens} tokens per step, fp32 (the reference's faster CPU dtype), "
+                                      f"{len(times)} timed steps"},
            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     return res
 

@@ -57,6 +57,19 @@ int smelb_read_status_detail(int device, int* words, int reset);
 int smelb_int4_dequant(const void* q, const void* scale, const void* zero, void* out, int64_t rows, int64_t k,
                        int64_t groups, int out_fp32, void* stream);
 
+/* smel/quant.py:87-94 dequant_int4_torch: the same dequant with every operation in the output dtype, as torch runs
+ * it: with a bf16 output the product q * scale is rounded to bf16 before zero is added, and the sum is rounded again
+ * (two roundings; smelb_int4_dequant rounds once). With out_fp32 != 0 the two entry points agree. */
+int smelb_int4_dequant_stepwise(const void* q, const void* scale, const void* zero, void* out, int64_t rows,
+                                int64_t k, int64_t groups, int out_fp32, void* stream);
+
+/* smel/pack.py:28-46 merge_experts / merge_mlp with smel/lora.py:31-36,52-56 delta(): out [rows, cols] =
+ * w + (scale * B) @ A, the rank-r product in fp32 as a fused multiply-add chain over the rank (the order of the
+ * reference's fp32 matmul), added to w in fp32 and rounded once to w's dtype (bf16, or fp32 when w_fp32 != 0).
+ * B fp32 [rows, r], A fp32 [r, cols]; out may alias w. */
+int smelb_lora_merge(const void* w, int w_fp32, int64_t rows, int64_t cols, const float* B, const float* A, int64_t r,
+                     float scale, void* out, void* stream);
+
 /* smel/quant.py:14-44 quantize_int4 with group = 64: w [rows, k] (bf16, or fp32 when w_fp32 != 0) -> q uint8
  * [rows, k/2] (low nibble = even column), scale / zero bf16 [rows, k/64]. Per group the [min, max] range is shrunk
  * towards its center by each of the n_clip factors in `clip` (host array, 1..8 entries, the reference's
@@ -156,6 +169,37 @@ int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64
                              const void* dn_q, const uint32_t* dn_sz, int act, const void* h, void* h_buf,
                              void* dh_buf, void* dx, void* stream);
 
+/* smel/moe.py:18-32 BF16Experts through FrozenExpertsFn (moe.py:110-143): the same two calls over a bf16 bank,
+ * gate_up bf16 [E, 2I, H] and down bf16 [E, H, I], with the bank's tiles loaded by TMA instead of dequantized. */
+int smelb_frozen_experts_bf16_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts,
+                                  int64_t E, const void* gate_up, const void* down, int act, void* h_save, void* a_buf,
+                                  void* out, void* stream);
+int smelb_frozen_experts_bf16_bwd(const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
+                                  const int32_t* counts, int64_t E, const void* gate_up, const void* down, int act,
+                                  const void* h, void* h_buf, void* dh_buf, void* dx, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------- lora_linear
+ * smel/lora.py:61-69 lora_linear and smel/lora.py:72-83 lora_gate_up: y bf16 [T, out] = x [T, in] w^T +
+ * scale * (x A^T) B^T, computed as one GEMM whose last k-block is the LoRA term (the reference adds it in the addmm
+ * epilogue before rounding as well). x, w (bf16 [out, in]) and y are bf16; A (fp32 [r, in]) and B (fp32 [out', r])
+ * are the LoRA parameters. One pair (A0, B0; out' = out) is lora_linear; two pairs (A0, B0, A1, B1; out' = out / 2)
+ * are lora_gate_up over the stacked [gate; up] weight, pair b acting on output rows [b out/2, (b+1) out/2). No pair
+ * (A0 = B0 = NULL) is the plain x w^T. in and out are multiples of 64, r a multiple of 8 with (pairs * r) <= 64.
+ * xa (bf16 [T, 64]) receives x [A0; A1]^T, which the backward reads; workspace: 256-byte aligned,
+ * smelb_lora_linear_workspace_bytes(T, in, out) bytes. */
+int64_t smelb_lora_linear_workspace_bytes(int64_t T, int64_t in_features, int64_t out_features);
+int smelb_lora_linear_fwd(const void* x, int64_t T, int64_t in_features, const void* w, int64_t out_features,
+                          const float* A0, const float* B0, const float* A1, const float* B1, int64_t r, float scale,
+                          void* y, void* xa, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Backward of smelb_lora_linear_fwd for dy (bf16 [T, out]): dx (bf16 [T, in]) = dy w + scale (dy B) A per pair,
+ * gA_b (fp32, A_b's shape) = scale (dy_b B_b)^T x and gB_b (fp32, B_b's shape) = scale dy_b^T (x A_b^T), with dy_b
+ * the pair's output columns. Any of dx / gA_b / gB_b may be NULL (not computed). xa is the forward's. */
+int smelb_lora_linear_bwd(const void* x, const void* dy, int64_t T, int64_t in_features, const void* w,
+                          int64_t out_features, const float* A0, const float* B0, const float* A1, const float* B1,
+                          int64_t r, float scale, const void* xa, void* dx, float* gA0, float* gB0, float* gA1,
+                          float* gB1, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* No counterpart in the reference. smelb_frozen_experts_fwd without caller scratch and without any allocation:
  * the activated intermediate (bf16 [rows, I]) lives in a file-scope device array of
  * SMELB_NOALLOC_SCRATCH_BYTES (plus a 256-byte head of wait-timeout status words), so rows * I * 2 may not exceed
@@ -163,12 +207,18 @@ int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64
  * call on a device resolves the array's address (cudaGetSymbolAddress) with that device current; make that first
  * call before any stream capture. Every call on a device shares the array, so calls whose kernels overlap on the
  * GPU (different streams without ordering) race. Each call clears the status head first; a bounded wait that gives
- * up inside this call is recorded there, not in smelb_read_status. Same arguments as smelb_frozen_experts_fwd
- * minus a_buf. */
+ * up inside this call is recorded there, not in smelb_read_status: read it with
+ * smelb_frozen_experts_fwd_noalloc_status. Same arguments as smelb_frozen_experts_fwd minus a_buf. */
 #define SMELB_NOALLOC_SCRATCH_BYTES 33554432LL
 int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts,
                                      int64_t E, const void* gu_q, const uint32_t* gu_sz, const void* dn_q,
                                      const uint32_t* dn_sz, int act, void* h_save, void* out, void* stream);
+
+/* No counterpart in the reference. The status head of smelb_frozen_experts_fwd_noalloc on `device`: synchronizes the
+ * device and copies it out without allocating. words[0] is 0, or the code of a bounded device-side wait that gave up
+ * during the last call (that call's output is then incomplete); words[1..3] the block, tile and k-block where it did.
+ * reset != 0 clears the head. words has 4 entries. */
+int smelb_frozen_experts_fwd_noalloc_status(int device, int* words, int reset);
 
 /* ---------------------------------------------------------------------------------------------------- the layer
  * smel/moe.py:255-263 moe_forward (route -> routed_experts -> + shared_mlp) and its autograd backward, as two calls.
@@ -180,6 +230,7 @@ int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, int64_t H, in
 #define SMELB_F_SHARED_GATE 8  /* multiply the shared expert by sigmoid(x @ w_sgate^T) */
 #define SMELB_F_SAVE 16        /* keep activations for smelb_moe_layer_bwd */
 #define SMELB_F_TOPV_FP32 32   /* topv / topv_in are fp32 (Gemma 4 routing) */
+#define SMELB_F_RECOMPUTE 64   /* backward: h / sh_h were not kept by the forward; recompute them from x / xs first */
 
 typedef struct smelb_moe_layer {
   /* shapes */

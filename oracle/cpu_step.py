@@ -114,18 +114,36 @@ def layer_forward(x, W, bank, sel, sel_gu, sel_dn, lex, lsh, K, group=32, act_na
 def prepare(layer, dtype=torch.float32, tokens=None):
     """CPU copies of a synthetic layer (smelb.synth.qwen_layer output) for the baseline: bf16 weights cast to `dtype`,
     the int4 bank kept packed, LoRA tensors as leaf tensors requiring grad. `tokens` takes the first rows of x."""
-    ex, lora, W = layer["ex"], layer["lora"], layer["W"]
-    x = layer["x"][:tokens] if tokens else layer["x"]
-    bank = {"gu_q": ex.frozen.gu["q"].cpu(), "gu_s": ex.frozen.gu["scale"].cpu(), "gu_z": ex.frozen.gu["zero"].cpu(),
-            "dn_q": ex.frozen.dn["q"].cpu(), "dn_s": ex.frozen.dn["scale"].cpu(), "dn_z": ex.frozen.dn["zero"].cpu()}
+    ex = layer["ex"]
+    bank = {"gu_q": ex.frozen.gu["q"], "gu_s": ex.frozen.gu["scale"], "gu_z": ex.frozen.gu["zero"],
+            "dn_q": ex.frozen.dn["q"], "dn_s": ex.frozen.dn["scale"], "dn_z": ex.frozen.dn["zero"]}
+    return prepare_parts(layer["x"], layer["W"], bank, layer["meta"]["selected"], ex.sel_gate_up, ex.sel_down,
+                         layer["lora"], layer["meta"]["K"], dtype, tokens)
+
+
+def prepare_tensors(t, dtype=torch.float32, tokens=None):
+    """The same from smelb.synth.qwen_layer_tensors output (the bf16 bank before quantization): the bank is
+    quantized with the reference's algorithm (moe_oracle.quantize_int4, as torch operations on the bank's device),
+    so building the baseline's inputs runs nothing of libsmelb."""
+    gu, dn, sel = t["gate_up"], t["down"], t["sel"]
+    on_dev = gu.is_cuda
+    qg = O.quantize_int4(gu, 64, on_device=on_dev)
+    qd = O.quantize_int4(dn, 64, on_device=on_dev)
+    bank = {"gu_q": qg["q"], "gu_s": qg["scale"], "gu_z": qg["zero"],
+            "dn_q": qd["q"], "dn_s": qd["scale"], "dn_z": qd["zero"]}
+    return prepare_parts(t["x"], t["W"], bank, sel, gu[sel], dn[sel], t["lora"], t["meta"]["K"], dtype, tokens)
+
+
+def prepare_parts(x, W, bank, sel, sel_gu, sel_dn, lora, K, dtype=torch.float32, tokens=None):
     names = ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down")
+    x = x[:tokens] if tokens else x
     lex = {n: getattr(lora.experts, n).detach().cpu().to(dtype).requires_grad_(True) for n in names}
     lex["scale"] = lora.experts.scale
     lsh = {n: getattr(lora.shared, n).detach().cpu().to(dtype).requires_grad_(True) for n in names}
     lsh["scale"] = lora.shared.scale
     return {"x": x.detach().cpu().to(dtype), "W": {k: v.detach().cpu().to(dtype) for k, v in W.items()},
-            "bank": bank, "sel": layer["meta"]["selected"], "sel_gu": ex.sel_gate_up.cpu().to(dtype),
-            "sel_dn": ex.sel_down.cpu().to(dtype), "lex": lex, "lsh": lsh, "K": layer["meta"]["K"]}
+            "bank": {k: v.cpu() for k, v in bank.items()}, "sel": list(sel), "sel_gu": sel_gu.cpu().to(dtype),
+            "sel_dn": sel_dn.cpu().to(dtype), "lex": lex, "lsh": lsh, "K": K}
 
 
 def step(p, gy):

@@ -21,14 +21,16 @@ GELU_C = 0.7978845608028654  # sqrt(2 / pi)
 
 
 # ============================================================================================== int4 format
-def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=(1.0, 0.95, 0.9, 0.85, 0.8)) -> dict:
+def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=(1.0, 0.95, 0.9, 0.85, 0.8),
+                  on_device: bool = False) -> dict:
     """smel/quant.py:5-44. Per group of `group` values along the last dim: try each clip factor c (range shrunk
     towards the group midpoint), scale = bf16(max((hi - lo) / 15, 1e-8)), zero = bf16(lo),
     q = clamp(round((w - zero) / scale), 0, 15); keep the first c with the smallest squared error.
-    Packs two codes per byte, the even column in the low nibble."""
-    w = w.detach().cpu()
+    Packs two codes per byte, the even column in the low nibble. on_device: run the same torch operations on w's
+    device (used to build large synthetic banks quickly) and return CPU tensors."""
+    w = w.detach() if on_device else w.detach().cpu()
     if w.dim() == 3 and w.shape[0] > 16:
-        parts = [quantize_int4(w[i:i + 16], group, clip_search) for i in range(0, w.shape[0], 16)]
+        parts = [quantize_int4(w[i:i + 16], group, clip_search, on_device) for i in range(0, w.shape[0], 16)]
         return {k: torch.cat([p[k] for p in parts]) for k in parts[0]}
     K = w.shape[-1]
     assert K % group == 0 and group % 2 == 0
@@ -50,10 +52,13 @@ def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=(1.0, 0.95, 0.9,
             m = err < best[0]
             best = [torch.where(m, err, best[0]), torch.where(m, q, best[1]), torch.where(m, scale, best[2]),
                     torch.where(m, zero, best[3])]
-    codes = best[1].to(torch.uint8).reshape(*w.shape[:-1], K).numpy()
-    packed = pack_nibbles(codes)
-    return {"q": torch.from_numpy(packed), "scale": best[2].squeeze(-1).to(torch.bfloat16),
-            "zero": best[3].squeeze(-1).to(torch.bfloat16)}
+    codes = best[1].to(torch.uint8).reshape(*w.shape[:-1], K)
+    if on_device:  # the same packing as pack_nibbles, as torch operations
+        packed = (codes[..., 0::2] | (codes[..., 1::2] << 4)).cpu()
+    else:
+        packed = torch.from_numpy(pack_nibbles(codes.numpy()))
+    return {"q": packed, "scale": best[2].squeeze(-1).to(torch.bfloat16).cpu(),
+            "zero": best[3].squeeze(-1).to(torch.bfloat16).cpu()}
 
 
 def pack_nibbles(codes: np.ndarray) -> np.ndarray:
@@ -78,6 +83,17 @@ def dequant_int4(q, scale, zero, dtype=torch.float32) -> torch.Tensor:
     K = codes.shape[-1]
     w = codes.reshape(*codes.shape[:-1], G, K // G) * s.unsqueeze(-1) + z.unsqueeze(-1)
     return w.reshape(*codes.shape[:-1], K).to(dtype)
+
+
+def dequant_int4_stepwise(q, scale, zero, dtype=torch.bfloat16) -> torch.Tensor:
+    """smel/quant.py:87-94 dequant_int4_torch as torch runs it in `dtype`: codes cast to dtype, times scale (rounded
+    to dtype), plus zero (rounded again). In bf16 this differs from dequant_int4 on many weights."""
+    codes = torch.from_numpy(unpack_nibbles(q.cpu().numpy() if isinstance(q, torch.Tensor) else q))
+    G = scale.shape[-1]
+    K = codes.shape[-1]
+    w = codes.reshape(*codes.shape[:-1], G, K // G).to(dtype)
+    w = w * scale.cpu().unsqueeze(-1).to(dtype) + zero.cpu().unsqueeze(-1).to(dtype)
+    return w.reshape(*codes.shape[:-1], K)
 
 
 # ============================================================================================== routing
@@ -197,6 +213,12 @@ def lora_linear(x, w, A, B, scale):
     if A is None:
         return y
     return y + scale * ((x @ A.to(x.dtype).t()) @ B.to(x.dtype).t())
+
+
+def lora_gate_up(x, w_gate_up, A_gate, B_gate, A_up, B_up, scale):
+    """smel/lora.py:72-83: (gate, up) over the stacked weight, each half with its LoRA pair."""
+    I = w_gate_up.shape[0] // 2
+    return (lora_linear(x, w_gate_up[:I], A_gate, B_gate, scale), lora_linear(x, w_gate_up[I:], A_up, B_up, scale))
 
 
 def mlp(x, w_gate, w_up, w_down, lora, act_name="silu"):
@@ -321,6 +343,25 @@ def moe_block_gemma4(h, xm, W, bank_gu, bank_dn, top_k, eps, sel_ids=(), sel_gu=
 
 
 # ============================================================================================== metrics
+def routing_disagreements(topi_got, logits_ref, top_k):
+    """Rows whose expert set differs from the reference top-k of `logits_ref` (high precision logits of the same
+    inputs), with the logit gap of each swap: the largest |logit(e_ref) - logit(e_got)| over the experts that one
+    side chose and the other did not (SURVEY-style near-tie report: a bf16 logit moves by up to half an ulp, so only
+    near-ties may flip). Returns a list of (row, gap)."""
+    ref = topk_stable(torch.softmax(logits_ref.double(), -1), top_k)
+    got = topi_got.cpu()
+    out = []
+    for t in range(got.shape[0]):
+        a, b = set(got[t].tolist()), set(ref[t].tolist())
+        if a != b:
+            only_got = sorted(a - b)
+            only_ref = sorted(b - a)
+            gap = max(abs(float(logits_ref[t, i]) - float(logits_ref[t, j])) for i in only_got for j in only_ref)
+            out.append((t, gap))
+    return out
+
+
+
 def rel_err(a, b) -> float:
     """||a - b|| / ||b|| (smel/quant.py:108-110)."""
     a, b = a.detach().double(), b.detach().double()

@@ -1,6 +1,8 @@
 // Persistent grouped multi-problem GEMM for sm_100a: TMA producer warps, a warp-elected tcgen05.mma issuer with TMEM
 // accumulators (double-buffered across tiles), three groups of four int4 dequant warps and a team of epilogue warps.
 // See gemm.cuh for the operand conventions and the warp roles.
+#include <mutex>
+
 #include "gemm.cuh"
 #include "host.h"
 
@@ -843,38 +845,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------------------------------ host side
-int launch_gemm(LaunchArgs& args, cudaStream_t stream) {
-  int dev = 0;
-  SMELB_CUDA(cudaGetDevice(&dev));
+// One launch path for every caller: the kernel's shared-memory opt-in once per device, the argument checks, the
+// optional CUDA-event timing and the launch count. `err` is the 4-word status area the kernel's bounded waits report
+// to (the per-device word, or one the caller owns).
+static int launch_gemm_impl(LaunchArgs& args, cudaStream_t stream, int dev, int* err) {
+  static std::mutex mu;
   static bool configured[64] = {false};
-  if (dev < 64 && !configured[dev]) {
-    SMELB_CUDA(cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc));
-    configured[dev] = true;
-  }
-  SMELB_CHECK_ARG(args.nprob >= 1 && args.nprob <= kMaxProblems, kErrArg, "gemm: %d problems in one launch",
-                  args.nprob);
-  int total_groups = 0;
-  for (int p = 0; p < args.nprob; ++p) total_groups += args.p[p].ngroups;
-  SMELB_CHECK_ARG(total_groups <= kMaxGroups, kErrShape, "gemm: %d groups in one launch (max %d)", total_groups,
-                  kMaxGroups);
-  args.err = device_status(dev);
-  SMELB_CHECK_ARG(args.err != nullptr, kErrCuda, "gemm: no device status word");
-  const bool timed = gemm_timing_enabled();
-  if (timed) gemm_timing_begin(stream);
-  moe_gemm_kernel<<<num_sms(dev), kThreads, kSmemAlloc, stream>>>(args);
-  SMELB_CUDA(cudaGetLastError());
-  if (timed) gemm_timing_end(stream);
-  count_launch();
-  return kOk;
-}
-
-int launch_gemm_status(LaunchArgs& args, cudaStream_t stream, int* err) {
-  int dev = 0;
-  SMELB_CUDA(cudaGetDevice(&dev));
-  static bool configured[64] = {false};
-  if (dev < 64 && !configured[dev]) {
-    SMELB_CUDA(cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc));
-    configured[dev] = true;
+  SMELB_CHECK_ARG(dev >= 0 && dev < 64, kErrArg, "gemm: device %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+      SMELB_CUDA(cudaFuncSetAttribute(moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAlloc));
+      configured[dev] = true;
+    }
   }
   SMELB_CHECK_ARG(args.nprob >= 1 && args.nprob <= kMaxProblems, kErrArg, "gemm: %d problems in one launch",
                   args.nprob);
@@ -884,10 +867,27 @@ int launch_gemm_status(LaunchArgs& args, cudaStream_t stream, int* err) {
                   kMaxGroups);
   SMELB_CHECK_ARG(err != nullptr, kErrArg, "gemm: no status words");
   args.err = err;
+  const bool timed = gemm_timing_enabled();
+  if (timed) gemm_timing_begin(stream);
   moe_gemm_kernel<<<num_sms(dev), kThreads, kSmemAlloc, stream>>>(args);
   SMELB_CUDA(cudaGetLastError());
+  if (timed) gemm_timing_end(stream);
   count_launch();
   return kOk;
+}
+
+int launch_gemm(LaunchArgs& args, cudaStream_t stream) {
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  int* err = device_status(dev);
+  SMELB_CHECK_ARG(err != nullptr, kErrCuda, "gemm: no device status word");
+  return launch_gemm_impl(args, stream, dev, err);
+}
+
+int launch_gemm_status(LaunchArgs& args, cudaStream_t stream, int* err) {
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  return launch_gemm_impl(args, stream, dev, err);
 }
 
 }  // namespace smelb

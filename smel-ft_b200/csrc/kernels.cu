@@ -10,9 +10,12 @@
 namespace smelb {
 
 // ============================================================================================ int4 dequant
-// out[r][2j] = lo(q[r][j]) * s + z, out[r][2j+1] = hi(q[r][j]) * s + z with (s, z) of group (2j) / group_size,
-// computed in fp32 and rounded once to the output type.
-template <bool F32>
+// out[r][2j] = lo(q[r][j]) * s + z, out[r][2j+1] = hi(q[r][j]) * s + z with (s, z) of group (2j) / group_size.
+// Single (smel/quant.py:51-67, the Triton kernel): computed in fp32 and rounded once to the output type.
+// Stepwise (smel/quant.py:87-94, dequant_int4_torch with a bf16 output): every operation in the output dtype, so the
+// product q * s is rounded to bf16 before z is added and the sum is rounded again (q * s is exact in fp32, so this is
+// torch's bf16 mul then bf16 add bit for bit). With an fp32 output the two modes are the same.
+template <bool F32, bool kStepwise>
 __global__ void int4_dequant_kernel(const uint8_t* __restrict__ q, const bf16* __restrict__ scale,
                                     const bf16* __restrict__ zero, void* __restrict__ out, long long rows, int half_k,
                                     int groups, int group) {
@@ -24,8 +27,14 @@ __global__ void int4_dequant_kernel(const uint8_t* __restrict__ q, const bf16* _
     const float s = __bfloat162float(scale[r * groups + g]);
     const float z = __bfloat162float(zero[r * groups + g]);
     const uint8_t b = q[i];
-    const float lo = fmaf((float)(b & 0xF), s, z);
-    const float hi = fmaf((float)(b >> 4), s, z);
+    float lo, hi;
+    if (kStepwise && !F32) {
+      lo = bf16_round(bf16_round((float)(b & 0xF) * s) + z);
+      hi = bf16_round(bf16_round((float)(b >> 4) * s) + z);
+    } else {
+      lo = fmaf((float)(b & 0xF), s, z);
+      hi = fmaf((float)(b >> 4), s, z);
+    }
     if (F32) {
       float2 v = make_float2(lo, hi);
       reinterpret_cast<float2*>(out)[i] = v;
@@ -36,21 +45,60 @@ __global__ void int4_dequant_kernel(const uint8_t* __restrict__ q, const bf16* _
 }
 
 int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
-                 bool out_f32, cudaStream_t st) {
+                 bool out_f32, cudaStream_t st, bool stepwise) {
   SMELB_CHECK_ARG(k > 0 && k % 2 == 0 && groups > 0 && k % groups == 0 && (k / groups) % 2 == 0, kErrShape,
                   "int4_dequant: k=%d groups=%d (need k %% groups == 0 and an even group size)", k, groups);
   if (rows == 0) return kOk;
   const long long n = rows * (k / 2);
   const int threads = 256;
   const long long blocks = std::min<long long>((n + threads - 1) / threads, 148LL * 16);
+  const uint8_t* qb = (const uint8_t*)q;
+  const bf16 *sb = (const bf16*)scale, *zb = (const bf16*)zero;
   if (out_f32)
-    int4_dequant_kernel<true><<<(int)blocks, threads, 0, st>>>((const uint8_t*)q, (const bf16*)scale,
-                                                                (const bf16*)zero, out, rows, k / 2, groups,
-                                                                k / groups);
+    int4_dequant_kernel<true, false><<<(int)blocks, threads, 0, st>>>(qb, sb, zb, out, rows, k / 2, groups, k / groups);
+  else if (stepwise)
+    int4_dequant_kernel<false, true><<<(int)blocks, threads, 0, st>>>(qb, sb, zb, out, rows, k / 2, groups, k / groups);
   else
-    int4_dequant_kernel<false><<<(int)blocks, threads, 0, st>>>((const uint8_t*)q, (const bf16*)scale,
-                                                                 (const bf16*)zero, out, rows, k / 2, groups,
-                                                                 k / groups);
+    int4_dequant_kernel<false, false><<<(int)blocks, threads, 0, st>>>(qb, sb, zb, out, rows, k / 2, groups, k / groups);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+// ============================================================================================ LoRA merge
+// out[i][c] = round(w[i][c] + sum_k fl(scale * B[i][k]) * A[k][c]) (smel/pack.py merge_experts / merge_mlp with
+// smel/lora.py delta()): the low-rank delta in fp32 as one fused multiply-add chain over k = 0..r-1 starting from 0
+// (the order of the reference's fp32 matmul for this shape), added to the weight in fp32 and rounded once to the
+// weight's dtype. One thread per output element; A's row k is shared by the block's threads through L1.
+template <bool F32>
+__global__ void lora_merge_kernel(const void* __restrict__ w, const float* __restrict__ B, const float* __restrict__ A,
+                                  int rows, int cols, int r, float scale, void* __restrict__ out) {
+  const long long n = (long long)rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / cols), c = (int)(i - (long long)row * cols);
+    const float* b = B + (long long)row * r;
+    float acc = 0.f;
+    for (int k = 0; k < r; ++k) acc = fmaf(scale * __ldg(b + k), __ldg(A + (long long)k * cols + c), acc);
+    if (F32) {
+      reinterpret_cast<float*>(out)[i] = __fadd_rn(reinterpret_cast<const float*>(w)[i], acc);
+    } else {
+      const float wv = __bfloat162float(reinterpret_cast<const bf16*>(w)[i]);
+      reinterpret_cast<bf16*>(out)[i] = __float2bfloat16_rn(__fadd_rn(wv, acc));
+    }
+  }
+}
+
+int lora_merge(const void* w, bool f32, const float* B, const float* A, int rows, int cols, int r, float scale,
+               void* out, cudaStream_t st) {
+  SMELB_CHECK_ARG(rows >= 0 && cols >= 0 && r >= 0, kErrShape, "lora_merge: rows=%d cols=%d r=%d", rows, cols, r);
+  const long long n = (long long)rows * cols;
+  if (n == 0) return kOk;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((n + threads - 1) / threads, 148LL * 16);
+  if (f32)
+    lora_merge_kernel<true><<<(int)blocks, threads, 0, st>>>(w, B, A, rows, cols, r, scale, out);
+  else
+    lora_merge_kernel<false><<<(int)blocks, threads, 0, st>>>(w, B, A, rows, cols, r, scale, out);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;

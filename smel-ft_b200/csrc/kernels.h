@@ -32,8 +32,13 @@ struct PackBatch {
   int rstart[kMaxPacks + 1];       // prefix of the output rows (J * OA)
 };
 
+// stepwise: bf16 output rounded after the product and again after the sum (torch's bf16 ops, smel/quant.py:87-94)
 int int4_dequant(const void* q, const void* scale, const void* zero, void* out, long long rows, int k, int groups,
-                 bool out_f32, cudaStream_t st);
+                 bool out_f32, cudaStream_t st, bool stepwise = false);
+// out = w + fl(scale * B) @ A (fp32 fma chain over the rank, one rounding to w's dtype): w, out [rows, cols] bf16
+// (fp32 when f32), B fp32 [rows, r], A fp32 [r, cols]. out may equal w.
+int lora_merge(const void* w, bool f32, const float* B, const float* A, int rows, int cols, int r, float scale,
+               void* out, cudaStream_t st);
 // Group-64 int4 quantizer with the clip search of smel/quant.py:5-44 (up to kMaxClip candidate factors).
 constexpr int kMaxClip = 8;
 int int4_quantize(const void* w, bool w_f32, long long rows, int k, const float* clip, int n_clip, void* q,
@@ -126,7 +131,7 @@ int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st);
 
 int launch_gemm(struct LaunchArgs& args, cudaStream_t stream);
 // Same launch with the wait-timeout status words supplied by the caller (4 ints, device memory) instead of the
-// per-device word launch_gemm allocates on first use; records no timing events.
+// per-device word launch_gemm allocates on first use (timing and launch count as launch_gemm).
 int launch_gemm_status(struct LaunchArgs& args, cudaStream_t stream, int* err);
 
 }  // namespace smelb

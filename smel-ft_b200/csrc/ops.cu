@@ -203,7 +203,7 @@ int pack_bwd(const LoraSet& L, void* dz_w, void* da_ext, void* dxa_w, void* dx_e
 }
 
 struct Flags {
-  bool router, routed, shared, sgate, save, topv32, sel, sel_lora, sh_lora, fz_bf16;
+  bool router, routed, shared, sgate, save, topv32, sel, sel_lora, sh_lora, fz_bf16, recompute;
 };
 
 int check_layer(const smelb_moe_layer& L, Flags& f) {
@@ -217,6 +217,7 @@ int check_layer(const smelb_moe_layer& L, Flags& f) {
   f.sel_lora = f.sel && L.r_sel > 0;
   f.sh_lora = f.shared && L.r_sh > 0;
   f.fz_bf16 = L.gu_q == nullptr && L.fz_gu != nullptr;
+  f.recompute = L.flags & SMELB_F_RECOMPUTE;
   SMELB_CHECK_ARG(L.T >= 0 && L.H > 0 && L.H % 64 == 0, kErrShape, "layer: H=%lld must be a multiple of 64",
                   (long long)L.H);
   SMELB_CHECK_ARG(L.act == SMELB_ACT_SILU || L.act == SMELB_ACT_GELU_TANH, kErrArg, "layer: unknown activation %d",
@@ -238,7 +239,71 @@ int check_layer(const smelb_moe_layer& L, Flags& f) {
                                 (long long)L.S);
   if (f.sel_lora) SMELB_CHECK_ARG(2 * L.r_sel <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sel);
   if (f.sh_lora) SMELB_CHECK_ARG(2 * L.r_sh <= kW64, kErrShape, "layer: LoRA rank %lld > 32", (long long)L.r_sh);
-  if (f.sel_lora) SMELB_CHECK_ARG(L.r_sel >= 1, kErrShape, "layer: LoRA rank %lld", (long long)L.r_sel);
+  // the LoRA weight-gradient GEMMs start TMA boxes at column r of the 64-wide token-side blocks: 16-byte aligned
+  // only when r is a multiple of 8
+  if (f.sel_lora) SMELB_CHECK_ARG(L.r_sel >= 8 && L.r_sel % 8 == 0, kErrShape,
+                                  "layer: LoRA rank %lld (a multiple of 8 is required)", (long long)L.r_sel);
+  if (f.sh_lora) SMELB_CHECK_ARG(L.r_sh >= 8 && L.r_sh % 8 == 0, kErrShape,
+                                 "layer: shared LoRA rank %lld (a multiple of 8 is required)", (long long)L.r_sh);
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------------------------- gated-MLP problems
+// The gate/up GEMM + GLU epilogue of the shared expert / dense MLP (LoRA as the K-extension): sh_a = act(g) * u, and
+// the pre-activations (g | u) into hout when given.
+int add_shared_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout) {
+  const int T = (int)L.T, H = (int)L.H, S = (int)L.S;
+  Problem& P = b.add();
+  TRY(set_a_bf16(P, L.sh_gu, 1, 2 * S, H, false, true));
+  TRY(set_b_tokens(P, L.x, T, H));
+  groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
+  if (f.sh_lora) TRY(set_ext(P, L.sp_gu_ext, 1, 2 * S, L.sh_xa, T, true));
+  P.epi = kEpiGlu;
+  P.C = L.sh_a;
+  P.c_sn = S;
+  P.c_sm = 1;
+  P.Hout = (bf16*)hout;
+  P.h_ld = 2 * S;
+  P.inter = S;
+  P.act = L.act_sh;
+  return kOk;
+}
+
+// The routed gate/up GEMMs + GLU epilogue: frozen experts (int4 bank, or bf16 fz_gu) and the selected bf16 experts
+// with their LoRA K-extension, a = act(g) * u over the dispatch rows, pre-activations into hout when given.
+int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout) {
+  const int H = (int)L.H, E = (int)L.E, I = (int)L.I, nsel = (int)L.n_sel, nfz = (int)(L.E - L.n_sel);
+  const long long R = L.max_rows;
+  if (nfz > 0) {
+    Problem& P = b.add();
+    if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, false, true));
+    else TRY(set_a_int4(P, Int4Mat{L.gu_q, L.gu_sz, E, 2 * I, H}, false));
+    TRY(set_b_tokens(P, L.xs, R, H));
+    groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+    P.epi = kEpiGlu;
+    P.C = L.a;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)hout;
+    P.h_ld = 2 * I;
+    P.inter = I;
+    P.act = L.act;
+  }
+  if (f.sel) {
+    Problem& P = b.add();
+    TRY(set_a_bf16(P, L.sel_gu, nsel, 2 * I, H, false, true));
+    TRY(set_b_tokens(P, L.xs, R, H));
+    groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
+    if (f.sel_lora) TRY(set_ext(P, L.p_gu_ext, nsel, 2 * I, L.xa, R, true));
+    P.epi = kEpiGlu;
+    P.C = L.a;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)hout;
+    P.h_ld = 2 * I;
+    P.inter = I;
+    P.act = L.act;
+  }
   return kOk;
 }
 
@@ -299,7 +364,6 @@ int layer_fwd(const smelb_moe_layer& L) {
                          L.src_of, (long long*)L.order, L.total, (int*)L.xs, (long long)R * H / 2, st));
     TRY(gather_rows(L.x, H, K, L.src_of, L.total, R, L.xs, st));
   }
-  const Int4Mat gu{L.gu_q, L.gu_sz, E, 2 * I, H};
   const Int4Mat dn{L.dn_q, L.dn_sz, E, H, I};
 
   // L2: selected-expert LoRA A product, shared expert gate/up (GLU)
@@ -313,56 +377,13 @@ int layer_fwd(const smelb_moe_layer& L) {
       out_bf16(P, L.xa, kW64);
       P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
-    if (f.shared) {
-      Problem& P = b.add();
-      TRY(set_a_bf16(P, L.sh_gu, 1, 2 * S, H, false, true));
-      TRY(set_b_tokens(P, L.x, T, H));
-      groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
-      if (f.sh_lora) TRY(set_ext(P, L.sp_gu_ext, 1, 2 * S, L.sh_xa, T, true));
-      P.epi = kEpiGlu;
-      P.C = L.sh_a;
-      P.c_sn = S;
-      P.c_sm = 1;
-      P.Hout = f.save ? (bf16*)L.sh_h : nullptr;
-      P.h_ld = 2 * S;
-      P.inter = S;
-      P.act = L.act_sh;
-    }
+    if (f.shared) TRY(add_shared_glu(b, L, f, f.save ? L.sh_h : nullptr));
     TRY(b.launch(st));
   }
   // L3: routed gate/up (frozen int4 + selected bf16 with LoRA), shared LoRA A of the down projection
   {
     Builder b;
-    if (f.routed && nfz > 0) {
-      Problem& P = b.add();
-      if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, false, true));
-      else TRY(set_a_int4(P, gu, false));
-      TRY(set_b_tokens(P, L.xs, R, H));
-      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
-      P.epi = kEpiGlu;
-      P.C = L.a;
-      P.c_sn = I;
-      P.c_sm = 1;
-      P.Hout = f.save ? (bf16*)L.h : nullptr;
-      P.h_ld = 2 * I;
-      P.inter = I;
-      P.act = L.act;
-    }
-    if (f.sel) {
-      Problem& P = b.add();
-      TRY(set_a_bf16(P, L.sel_gu, nsel, 2 * I, H, false, true));
-      TRY(set_b_tokens(P, L.xs, R, H));
-      groups(P, L.gcounts, L.offsets, L.sel_ids, L.sel_slots, nsel);
-      if (f.sel_lora) TRY(set_ext(P, L.p_gu_ext, nsel, 2 * I, L.xa, R, true));
-      P.epi = kEpiGlu;
-      P.C = L.a;
-      P.c_sn = I;
-      P.c_sm = 1;
-      P.Hout = f.save ? (bf16*)L.h : nullptr;
-      P.h_ld = 2 * I;
-      P.inter = I;
-      P.act = L.act;
-    }
+    if (f.routed) TRY(add_routed_glu(b, L, f, f.save ? L.h : nullptr));
     if (f.sh_lora) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.sp_z_w, 1, rh, S, false, false));
@@ -442,6 +463,14 @@ int layer_bwd(const smelb_moe_layer& L) {
   }
   const void* topv = f.router ? L.topv : L.topv_in;
 
+  // R0: without saved gate/up pre-activations (the forward kept only its inputs), recompute them into h / sh_h
+  if (f.recompute && (f.routed || f.shared)) {
+    SMELB_CHECK_ARG((!f.routed || L.h) && (!f.shared || L.sh_h), kErrArg, "layer_bwd: recompute needs h / sh_h");
+    Builder b;
+    if (f.shared) TRY(add_shared_glu(b, L, f, L.sh_h));
+    if (f.routed) TRY(add_routed_glu(b, L, f, L.h));
+    TRY(b.launch(st));
+  }
   if (f.routed)
     TRY(combine_bwd_rows(L.g, L.y, L.src_of, L.total, R, topv, f.topv32, K, H, L.dy, L.dtopv, st));
   const void* sh_dy = L.g;
@@ -637,6 +666,270 @@ int layer_bwd(const smelb_moe_layer& L) {
   return kOk;
 }
 
+// ---------------------------------------------------------------------------------------------- frozen experts
+// A frozen bank for the stand-alone frozen-experts entry points: the int4 group-64 bank (nibbles + packed
+// (scale, zero) pairs) or, when gu_w / dn_w are set, plain bf16 weights gate_up [E, 2I, H] and down [E, H, I]
+// (smel/moe.py:18-32 BF16Experts).
+struct FrozenBank {
+  Int4Mat gu, dn;
+  const void* gu_w;
+  const void* dn_w;
+  int E;
+};
+
+// A = the bank's gate_up (gate_up = true) or down matrix, K-major (forward) or MN-major (backward, transposed).
+int set_a_frozen_w(Problem& P, const FrozenBank& b, bool gate_up, bool mn_major, int H, int I) {
+  if (!b.gu_w) return set_a_int4(P, gate_up ? b.gu : b.dn, mn_major);
+  if (gate_up) return set_a_bf16(P, b.gu_w, b.E, 2 * I, H, mn_major, !mn_major);
+  return set_a_bf16(P, b.dn_w, b.E, H, I, mn_major, false);
+}
+
+int frozen_check(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E, int act,
+                 const char* what) {
+  SMELB_CHECK_ARG(counts != nullptr && (rows == 0 || xs != nullptr), kErrArg, "%s: null pointer", what);
+  SMELB_CHECK_ARG(rows >= 0 && H > 0 && I > 0 && H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups, kErrShape,
+                  "%s: rows=%lld H=%lld I=%lld E=%lld", what, (long long)rows, (long long)H, (long long)I,
+                  (long long)E);
+  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "%s: unknown activation %d", what,
+                  act);
+  return kOk;
+}
+
+// smel/moe.py:110-126 over expert-grouped rows: a = act(xs W_gate^T) * (xs W_up^T) (GLU epilogue, gate/up
+// pre-activations kept in h_save when given), out = a W_down^T. err: status words for the launches (nullptr: the
+// per-device word).
+int frozen_fwd(const FrozenBank& bank, const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts,
+               int64_t E, int act, void* h_save, void* a_buf, void* out, cudaStream_t st, int* err) {
+  TRY(frozen_check(xs, rows, H, I, counts, E, act, "frozen_experts_fwd"));
+  SMELB_CHECK_ARG(a_buf && out, kErrArg, "frozen_experts_fwd: null output");
+  if (rows == 0) return kOk;
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_frozen_w(P, bank, true, false, (int)H, (int)I));
+    TRY(set_b_tokens(P, xs, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiGlu;
+    P.C = a_buf;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)h_save;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(err ? launch_gemm_status(b.args, st, err) : b.launch(st));
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_frozen_w(P, bank, false, false, (int)H, (int)I));
+    TRY(set_b_tokens(P, a_buf, rows, (int)I));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    out_bf16(P, out, H);
+    TRY(err ? launch_gemm_status(b.args, st, err) : b.launch(st));
+  }
+  return kOk;
+}
+
+// smel/moe.py:128-143: dx of the frozen experts (no weight gradients). Without the saved pre-activations h, the
+// gate/up GEMM is recomputed into h_buf first (the reference's save-xs-only memory contract).
+int frozen_bwd(const FrozenBank& bank, const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
+               const int32_t* counts, int64_t E, int act, const void* h, void* h_buf, void* dh_buf, void* dx,
+               cudaStream_t st) {
+  TRY(frozen_check(dy, rows, H, I, counts, E, act, "frozen_experts_bwd"));
+  SMELB_CHECK_ARG(dh_buf && dx, kErrArg, "frozen_experts_bwd: null output");
+  SMELB_CHECK_ARG(h || (xs && h_buf), kErrArg, "frozen_experts_bwd: need the saved h or xs and h_buf to recompute");
+  if (rows == 0) return kOk;
+  if (!h) {
+    // recompute gate/up pre-activations into h_buf (the GLU output goes to dh_buf, overwritten below)
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_frozen_w(P, bank, true, false, (int)H, (int)I));
+    TRY(set_b_tokens(P, xs, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiGlu;
+    P.C = dh_buf;
+    P.c_sn = I;
+    P.c_sm = 1;
+    P.Hout = (bf16*)h_buf;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(b.launch(st));
+    h = h_buf;
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_frozen_w(P, bank, false, true, (int)H, (int)I));
+    TRY(set_b_tokens(P, dy, rows, (int)H));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    P.epi = kEpiDGlu;
+    P.C = dh_buf;
+    P.c_sn = 2 * I;
+    P.Hin = (const bf16*)h;
+    P.h_ld = 2 * I;
+    P.inter = (int)I;
+    P.act = act;
+    TRY(b.launch(st));
+  }
+  {
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_frozen_w(P, bank, true, true, (int)H, (int)I));
+    TRY(set_b_tokens(P, dh_buf, rows, (int)(2 * I)));
+    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
+    out_bf16(P, dx, H);
+    TRY(b.launch(st));
+  }
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------------------------- lora_linear
+// smel/lora.py:61-83: y = x w^T + s (x A^T) B^T as one GEMM whose last k-block is the LoRA term (token side x A^T,
+// weight side s B, both zero-padded to 64 columns). With two LoRA pairs (lora_gate_up over a stacked [2I, Kd] weight)
+// pair b acts on the output rows [b N/2, (b+1) N/2): the token side is [x A_0^T | x A_1^T] and the weight side
+// block-diagonal. Backward: dz = dy (s B) (same block structure), dx = dy w + dz [A_0; A_1] (one GEMM with the LoRA
+// term as its K-extension), dA_b = dz_b^T x and dB_b = s dy_b^T (x A_b^T) as token-reduction GEMMs.
+struct LinLayout {
+  size_t xa_w, ext, tok, dz, dz_w, dx_ext, total;
+};
+
+size_t lin_align(size_t x) { return (x + 255) & ~size_t(255); }
+
+LinLayout lin_layout(int64_t T, int64_t Kd, int64_t N) {
+  LinLayout L{};
+  size_t o = 0;
+  L.tok = o;    o += 256;
+  L.xa_w = o;   o += lin_align((size_t)kW64 * Kd * 2);
+  L.ext = o;    o += lin_align((size_t)N * kW64 * 2);
+  L.dz = o;     o += lin_align((size_t)T * kW64 * 2);
+  L.dz_w = o;   o += lin_align((size_t)kW64 * N * 2);
+  L.dx_ext = o; o += lin_align((size_t)Kd * kW64 * 2);
+  L.total = o;
+  return L;
+}
+
+struct LinArgs {
+  const void* x;
+  int64_t T, Kd, N, r;
+  const void* w;
+  const float *A[2], *B[2];
+  int nblk;  // LoRA pairs: 0 (plain GEMM), 1 or 2
+  float s;
+};
+
+int lin_check(const LinArgs& a, void* ws, int64_t ws_bytes, const char* what) {
+  SMELB_CHECK_ARG(a.w && ws && (a.T == 0 || a.x), kErrArg, "%s: null pointer", what);
+  SMELB_CHECK_ARG(a.T >= 0 && a.T < (1LL << 31) && a.Kd > 0 && a.Kd % 64 == 0 && a.N > 0 && a.N % 64 == 0 &&
+                      a.Kd < (1 << 24) && a.N < (1 << 24),
+                  kErrShape, "%s: T=%lld in=%lld out=%lld (in and out must be multiples of 64)", what, (long long)a.T,
+                  (long long)a.Kd, (long long)a.N);
+  if (a.nblk) {
+    // the pairs' columns of the 64-wide token-side block start at multiples of r elements, and a TMA box must start
+    // on a 16-byte boundary: r a multiple of 8
+    SMELB_CHECK_ARG(a.r >= 8 && a.r % 8 == 0 && a.nblk * a.r <= kW64, kErrShape,
+                    "%s: LoRA rank %lld (a multiple of 8, at most %d per pair)", what, (long long)a.r, kW64 / a.nblk);
+    SMELB_CHECK_ARG(a.nblk == 1 || (a.N / 2) % 64 == 0, kErrShape, "%s: stacked output %lld (halves of 64s)", what,
+                    (long long)a.N);
+  }
+  SMELB_CHECK_ARG(ws_bytes >= (int64_t)lin_layout(a.T, a.Kd, a.N).total, kErrWorkspace,
+                  "%s: workspace %lld bytes, %lld needed", what, (long long)ws_bytes,
+                  (long long)lin_layout(a.T, a.Kd, a.N).total);
+  SMELB_CHECK_ARG(((uintptr_t)ws & 255) == 0, kErrArg, "%s: workspace must be 256-byte aligned", what);
+  return kOk;
+}
+
+int lin_fwd(const LinArgs& a, void* y, void* xa, void* ws, int64_t ws_bytes, cudaStream_t st) {
+  TRY(lin_check(a, ws, ws_bytes, "lora_linear_fwd"));
+  SMELB_CHECK_ARG(y && (a.nblk == 0 || xa), kErrArg, "lora_linear_fwd: null output");
+  if (a.T == 0) return kOk;
+  const LinLayout lay = lin_layout(a.T, a.Kd, a.N);
+  char* w8 = (char*)ws;
+  int* tok = (int*)(w8 + lay.tok);
+  TRY(set_counts(tok, 1, (int)a.T, a.T, st));
+  const int r = (int)a.r, Kd = (int)a.Kd, N = (int)a.N, Nb = a.nblk ? N / a.nblk : N;
+  if (a.nblk) {
+    PackBatch pb;
+    pb.n = 0;
+    // xa_w [nblk r, Kd] = [A_0; A_1]; ext [N, 64]: rows of pair b hold s B_b in columns [b r, (b+1) r)
+    TRY(pack(1, a.nblk * r, Kd, blk(a.A[0], 0, Kd, 1, 0, r, 0, Kd, 1.f),
+             a.nblk > 1 ? blk(a.A[1], 0, Kd, 1, r, r, 0, Kd, 1.f) : no_blk(), w8 + lay.xa_w, pb));
+    TRY(pack(1, N, kW64, blk(a.B[0], 0, r, 1, 0, Nb, 0, r, a.s),
+             a.nblk > 1 ? blk(a.B[1], 0, r, 1, Nb, Nb, r, r, a.s) : no_blk(), w8 + lay.ext, pb));
+    TRY(pack_batch(pb, st));
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_bf16(P, w8 + lay.xa_w, 1, a.nblk * r, Kd, false, false));
+    TRY(set_b_tokens(P, a.x, a.T, Kd));
+    groups(P, tok, nullptr, nullptr, nullptr, 1);
+    out_bf16(P, xa, kW64);
+    P.m_pad = kW64;  // the block's unused columns are written as zeros
+    TRY(b.launch(st));
+  }
+  Builder b;
+  Problem& P = b.add();
+  TRY(set_a_bf16(P, a.w, 1, N, Kd, false, false));
+  TRY(set_b_tokens(P, a.x, a.T, Kd));
+  groups(P, tok, nullptr, nullptr, nullptr, 1);
+  if (a.nblk) TRY(set_ext(P, w8 + lay.ext, 1, N, xa, a.T, false));
+  out_bf16(P, y, N);
+  return b.launch(st);
+}
+
+int lin_bwd(const LinArgs& a, const void* dy, const void* xa, void* dx, float* const gA[2], float* const gB[2], void* ws,
+            int64_t ws_bytes, cudaStream_t st) {
+  TRY(lin_check(a, ws, ws_bytes, "lora_linear_bwd"));
+  SMELB_CHECK_ARG((a.T == 0 || dy) && (a.nblk == 0 || xa), kErrArg, "lora_linear_bwd: null input");
+  if (a.T == 0) return kOk;
+  const LinLayout lay = lin_layout(a.T, a.Kd, a.N);
+  char* w8 = (char*)ws;
+  int* tok = (int*)(w8 + lay.tok);
+  TRY(set_counts(tok, 1, (int)a.T, a.T, st));
+  const int r = (int)a.r, Kd = (int)a.Kd, N = (int)a.N, Nb = a.nblk ? N / a.nblk : N;
+  void* dz = w8 + lay.dz;
+  if (a.nblk) {
+    PackBatch pb;
+    pb.n = 0;
+    // dz_w [nblk r, N]: pair b's rows hold s B_b^T over its output columns; dx_ext [Kd, 64] = [A_0^T | A_1^T | 0]
+    TRY(pack(1, a.nblk * r, N, blk(a.B[0], 0, 1, r, 0, r, 0, Nb, a.s),
+             a.nblk > 1 ? blk(a.B[1], 0, 1, r, r, r, Nb, Nb, a.s) : no_blk(), w8 + lay.dz_w, pb));
+    TRY(pack(1, Kd, kW64, blk(a.A[0], 0, 1, Kd, 0, Kd, 0, r, 1.f),
+             a.nblk > 1 ? blk(a.A[1], 0, 1, Kd, 0, Kd, r, r, 1.f) : no_blk(), w8 + lay.dx_ext, pb));
+    TRY(pack_batch(pb, st));
+    Builder b;
+    Problem& P = b.add();
+    TRY(set_a_bf16(P, w8 + lay.dz_w, 1, a.nblk * r, N, false, false));
+    TRY(set_b_tokens(P, dy, a.T, N));
+    groups(P, tok, nullptr, nullptr, nullptr, 1);
+    out_bf16(P, dz, kW64);
+    P.m_pad = kW64;
+    TRY(b.launch(st));
+  }
+  Builder b;
+  if (dx) {
+    Problem& P = b.add();
+    TRY(set_a_bf16(P, a.w, 1, N, Kd, true, false));
+    TRY(set_b_tokens(P, dy, a.T, N));
+    groups(P, tok, nullptr, nullptr, nullptr, 1);
+    if (a.nblk) TRY(set_ext(P, w8 + lay.dx_ext, 1, Kd, dz, a.T, false));
+    out_bf16(P, dx, Kd);
+  }
+  for (int k = 0; k < a.nblk; ++k) {
+    if (gA[k]) {
+      Problem& P = b.add();
+      TRY(set_tokk(P, a.x, a.T, Kd, 0, Kd, dz, kW64, k * r, r, gA[k], 1, Kd, 0, 1.f));
+      groups(P, tok, nullptr, nullptr, nullptr, 1);
+    }
+    if (gB[k]) {
+      Problem& P = b.add();
+      TRY(set_tokk(P, dy, a.T, N, k * Nb, Nb, xa, kW64, k * r, r, gB[k], r, 1, 0, a.s));
+      groups(P, tok, nullptr, nullptr, nullptr, 1);
+    }
+  }
+  return b.launch(st);
+}
+
 }  // namespace
 
 // ================================================================================================== C ABI
@@ -788,100 +1081,77 @@ int smelb_rmsnorm_bwd(const void* dy, const void* x, const void* w, int w_mode, 
 int smelb_frozen_experts_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts, int64_t E,
                              const void* gu_q, const uint32_t* gu_sz, const void* dn_q, const uint32_t* dn_sz,
                              int act, void* h_save, void* a_buf, void* out, void* stream) {
-  SMELB_CHECK_ARG(xs && counts && gu_q && gu_sz && dn_q && dn_sz && a_buf && out, kErrArg,
-                  "frozen_experts_fwd: null pointer");
-  SMELB_CHECK_ARG(H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups, kErrShape,
-                  "frozen_experts_fwd: H=%lld I=%lld E=%lld", (long long)H, (long long)I, (long long)E);
-  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "unknown activation %d", act);
-  if (rows == 0) return kOk;
-  cudaStream_t st = (cudaStream_t)stream;
-  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
-  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, gu, false));
-    TRY(set_b_tokens(P, xs, rows, (int)H));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    P.epi = kEpiGlu;
-    P.C = a_buf;
-    P.c_sn = I;
-    P.c_sm = 1;
-    P.Hout = (bf16*)h_save;
-    P.h_ld = 2 * I;
-    P.inter = (int)I;
-    P.act = act;
-    TRY(b.launch(st));
-  }
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, dn, false));
-    TRY(set_b_tokens(P, a_buf, rows, (int)I));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    out_bf16(P, out, H);
-    TRY(b.launch(st));
-  }
-  return kOk;
+  SMELB_CHECK_ARG(gu_q && gu_sz && dn_q && dn_sz, kErrArg, "frozen_experts_fwd: null pointer");
+  const FrozenBank bank{Int4Mat{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H}, Int4Mat{dn_q, dn_sz, (int)E, (int)H, (int)I},
+                        nullptr, nullptr, (int)E};
+  return frozen_fwd(bank, xs, rows, H, I, counts, E, act, h_save, a_buf, out, (cudaStream_t)stream, nullptr);
+}
+
+int smelb_frozen_experts_bf16_fwd(const void* xs, int64_t rows, int64_t H, int64_t I, const int32_t* counts,
+                                  int64_t E, const void* gate_up, const void* down, int act, void* h_save, void* a_buf,
+                                  void* out, void* stream) {
+  SMELB_CHECK_ARG(gate_up && down, kErrArg, "frozen_experts_bf16_fwd: null pointer");
+  const FrozenBank bank{Int4Mat{}, Int4Mat{}, gate_up, down, (int)E};
+  return frozen_fwd(bank, xs, rows, H, I, counts, E, act, h_save, a_buf, out, (cudaStream_t)stream, nullptr);
 }
 
 int smelb_frozen_experts_bwd(const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
                              const int32_t* counts, int64_t E, const void* gu_q, const uint32_t* gu_sz,
                              const void* dn_q, const uint32_t* dn_sz, int act, const void* h, void* h_buf,
                              void* dh_buf, void* dx, void* stream) {
-  SMELB_CHECK_ARG(dy && counts && gu_q && gu_sz && dn_q && dn_sz && dh_buf && dx, kErrArg,
-                  "frozen_experts_bwd: null pointer");
-  SMELB_CHECK_ARG(h || (xs && h_buf), kErrArg, "frozen_experts_bwd: need the saved h or xs and h_buf to recompute");
-  SMELB_CHECK_ARG(H % 64 == 0 && I % 64 == 0 && E >= 1 && E <= kMaxGroups, kErrShape,
-                  "frozen_experts_bwd: H=%lld I=%lld E=%lld", (long long)H, (long long)I, (long long)E);
-  SMELB_CHECK_ARG(act == SMELB_ACT_SILU || act == SMELB_ACT_GELU_TANH, kErrArg, "unknown activation %d", act);
-  if (rows == 0) return kOk;
-  cudaStream_t st = (cudaStream_t)stream;
-  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
-  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
-  if (!h) {
-    // recompute gate/up pre-activations into h_buf (the GLU output goes to dh_buf, overwritten below)
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, gu, false));
-    TRY(set_b_tokens(P, xs, rows, (int)H));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    P.epi = kEpiGlu;
-    P.C = dh_buf;
-    P.c_sn = I;
-    P.c_sm = 1;
-    P.Hout = (bf16*)h_buf;
-    P.h_ld = 2 * I;
-    P.inter = (int)I;
-    P.act = act;
-    TRY(b.launch(st));
-    h = h_buf;
-  }
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, dn, true));
-    TRY(set_b_tokens(P, dy, rows, (int)H));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    P.epi = kEpiDGlu;
-    P.C = dh_buf;
-    P.c_sn = 2 * I;
-    P.Hin = (const bf16*)h;
-    P.h_ld = 2 * I;
-    P.inter = (int)I;
-    P.act = act;
-    TRY(b.launch(st));
-  }
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, gu, true));
-    TRY(set_b_tokens(P, dh_buf, rows, (int)(2 * I)));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    out_bf16(P, dx, H);
-    TRY(b.launch(st));
-  }
-  return kOk;
+  SMELB_CHECK_ARG(gu_q && gu_sz && dn_q && dn_sz, kErrArg, "frozen_experts_bwd: null pointer");
+  const FrozenBank bank{Int4Mat{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H}, Int4Mat{dn_q, dn_sz, (int)E, (int)H, (int)I},
+                        nullptr, nullptr, (int)E};
+  return frozen_bwd(bank, xs, dy, rows, H, I, counts, E, act, h, h_buf, dh_buf, dx, (cudaStream_t)stream);
+}
+
+int smelb_frozen_experts_bf16_bwd(const void* xs, const void* dy, int64_t rows, int64_t H, int64_t I,
+                                  const int32_t* counts, int64_t E, const void* gate_up, const void* down, int act,
+                                  const void* h, void* h_buf, void* dh_buf, void* dx, void* stream) {
+  SMELB_CHECK_ARG(gate_up && down, kErrArg, "frozen_experts_bf16_bwd: null pointer");
+  const FrozenBank bank{Int4Mat{}, Int4Mat{}, gate_up, down, (int)E};
+  return frozen_bwd(bank, xs, dy, rows, H, I, counts, E, act, h, h_buf, dh_buf, dx, (cudaStream_t)stream);
+}
+
+int smelb_int4_dequant_stepwise(const void* q, const void* scale, const void* zero, void* out, int64_t rows,
+                                int64_t k, int64_t groups, int out_fp32, void* stream) {
+  SMELB_CHECK_ARG(q && scale && zero && out, kErrArg, "int4_dequant_stepwise: null pointer");
+  return int4_dequant(q, scale, zero, out, rows, (int)k, (int)groups, out_fp32 != 0, (cudaStream_t)stream, true);
+}
+
+int smelb_lora_merge(const void* w, int w_fp32, int64_t rows, int64_t cols, const float* B, const float* A, int64_t r,
+                     float scale, void* out, void* stream) {
+  SMELB_CHECK_ARG(w && B && A && out, kErrArg, "lora_merge: null pointer");
+  SMELB_CHECK_ARG(rows >= 0 && cols >= 0 && r >= 1 && rows < (1LL << 31) && cols < (1LL << 31) && r <= 4096, kErrShape,
+                  "lora_merge: rows=%lld cols=%lld r=%lld", (long long)rows, (long long)cols, (long long)r);
+  return lora_merge(w, w_fp32 != 0, B, A, (int)rows, (int)cols, (int)r, scale, out, (cudaStream_t)stream);
+}
+
+int64_t smelb_lora_linear_workspace_bytes(int64_t T, int64_t in_features, int64_t out_features) {
+  if (T < 0 || in_features <= 0 || out_features <= 0) return 0;
+  return (int64_t)lin_layout(T, in_features, out_features).total;
+}
+
+int smelb_lora_linear_fwd(const void* x, int64_t T, int64_t in_features, const void* w, int64_t out_features,
+                          const float* A0, const float* B0, const float* A1, const float* B1, int64_t r, float scale,
+                          void* y, void* xa, void* workspace, int64_t workspace_bytes, void* stream) {
+  SMELB_CHECK_ARG((A0 == nullptr) == (B0 == nullptr) && (A1 == nullptr) == (B1 == nullptr) && (A0 || !A1), kErrArg,
+                  "lora_linear_fwd: give A and B together, the second pair only with the first");
+  const LinArgs a{x, T, in_features, out_features, r, w, {A0, A1}, {B0, B1}, A0 ? (A1 ? 2 : 1) : 0, scale};
+  return lin_fwd(a, y, xa, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int smelb_lora_linear_bwd(const void* x, const void* dy, int64_t T, int64_t in_features, const void* w,
+                          int64_t out_features, const float* A0, const float* B0, const float* A1, const float* B1,
+                          int64_t r, float scale, const void* xa, void* dx, float* gA0, float* gB0, float* gA1,
+                          float* gB1, void* workspace, int64_t workspace_bytes, void* stream) {
+  SMELB_CHECK_ARG((A0 == nullptr) == (B0 == nullptr) && (A1 == nullptr) == (B1 == nullptr) && (A0 || !A1), kErrArg,
+                  "lora_linear_bwd: give A and B together, the second pair only with the first");
+  SMELB_CHECK_ARG(x || T == 0, kErrArg, "lora_linear_bwd: null x");
+  const LinArgs a{x, T, in_features, out_features, r, w, {A0, A1}, {B0, B1}, A0 ? (A1 ? 2 : 1) : 0, scale};
+  float* const gA[2] = {gA0, gA1};
+  float* const gB[2] = {gB0, gB1};
+  return lin_bwd(a, dy, xa, dx, gA, gB, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 size_t smelb_moe_layer_size(void) { return sizeof(smelb_moe_layer); }
@@ -957,36 +1227,33 @@ extern "C" int smelb_frozen_experts_fwd_noalloc(const void* xs, int64_t rows, in
   TRY(noalloc_scratch(dev, &scratch));
   cudaStream_t st = (cudaStream_t)stream;
   int* err = (int*)scratch;
-  void* a_buf = scratch + kNoAllocHead;
   SMELB_CUDA(cudaMemsetAsync(err, 0, kNoAllocHead, st));
-  const Int4Mat gu{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H};
-  const Int4Mat dn{dn_q, dn_sz, (int)E, (int)H, (int)I};
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, gu, false));
-    TRY(set_b_tokens(P, xs, rows, (int)H));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    P.epi = kEpiGlu;
-    P.C = a_buf;
-    P.c_sn = I;
-    P.c_sm = 1;
-    P.Hout = (bf16*)h_save;
-    P.h_ld = 2 * I;
-    P.inter = (int)I;
-    P.act = act;
-    TRY(launch_gemm_status(b.args, st, err));
+  const FrozenBank bank{Int4Mat{gu_q, gu_sz, (int)E, (int)(2 * I), (int)H}, Int4Mat{dn_q, dn_sz, (int)E, (int)H, (int)I},
+                        nullptr, nullptr, (int)E};
+  return frozen_fwd(bank, xs, rows, H, I, counts, E, act, h_save, scratch + kNoAllocHead, out, st, err);
+}
+
+// Status words of the last smelb_frozen_experts_fwd_noalloc call on `device`: synchronizes the device and copies the
+// head of the shared array (no allocation). words[0] is 0, or the code of a bounded device-side wait that gave up
+// inside that call (its output is then incomplete); words[1..3] block, tile and k-block.
+extern "C" int smelb_frozen_experts_fwd_noalloc_status(int device, int* words, int reset) {
+  SMELB_CHECK_ARG(words != nullptr, kErrArg, "frozen_experts_fwd_noalloc_status: null output");
+  int prev = 0;
+  SMELB_CUDA(cudaGetDevice(&prev));
+  SMELB_CUDA(cudaSetDevice(device));
+  unsigned char* scratch = nullptr;
+  int rc = noalloc_scratch(device, &scratch);
+  if (rc == kOk) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(words, scratch, kStatusWords * sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && reset) e = cudaMemset(scratch, 0, kStatusWords * sizeof(int));
+    if (e != cudaSuccess) {
+      set_last_error("frozen_experts_fwd_noalloc_status: %s", cudaGetErrorString(e));
+      rc = kErrCuda;
+    }
   }
-  {
-    Builder b;
-    Problem& P = b.add();
-    TRY(set_a_int4(P, dn, false));
-    TRY(set_b_tokens(P, a_buf, rows, (int)I));
-    groups(P, counts, nullptr, nullptr, nullptr, (int)E);
-    out_bf16(P, out, H);
-    TRY(launch_gemm_status(b.args, st, err));
-  }
-  return kOk;
+  SMELB_CUDA(cudaSetDevice(prev));
+  return rc;
 }
 
 // ---------------------------------------------------------------------------------------------------- chunked CE

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(_HERE, "libsmelb.so")
 
 ACT = {"silu": 0, "gelu_tanh": 1}
 
-F_ROUTER, F_ROUTED, F_SHARED, F_SHARED_GATE, F_SAVE, F_TOPV_FP32 = 1, 2, 4, 8, 16, 32
+F_ROUTER, F_ROUTED, F_SHARED, F_SHARED_GATE, F_SAVE, F_TOPV_FP32, F_RECOMPUTE = 1, 2, 4, 8, 16, 32, 64
 
 ERRORS = {-1: "bad shape", -2: "bad dtype", -3: "workspace too small", -4: "device wait timed out",
           -5: "CUDA error", -6: "bad argument"}
@@ -93,6 +93,18 @@ SIGNATURES = {
                                          c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "smelb_frozen_experts_fwd_noalloc": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp,
                                                  c_i32, c_vp, c_vp, c_vp]),
+    "smelb_frozen_experts_fwd_noalloc_status": (c_i32, [c_i32, ctypes.POINTER(c_i32), c_i32]),
+    "smelb_frozen_experts_bf16_fwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_i32, c_vp, c_vp,
+                                              c_vp, c_vp]),
+    "smelb_frozen_experts_bf16_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_i32, c_vp,
+                                              c_vp, c_vp, c_vp, c_vp]),
+    "smelb_int4_dequant_stepwise": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),
+    "smelb_lora_merge": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i64, c_f32, c_vp, c_vp]),
+    "smelb_lora_linear_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64]),
+    "smelb_lora_linear_fwd": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_f32, c_vp,
+                                      c_vp, c_vp, c_i64, c_vp]),
+    "smelb_lora_linear_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_f32,
+                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "smelb_int8_rows_quantize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "smelb_int8_rows_dequant": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_vp]),
     "smelb_chunked_ce_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i32, c_i32]),

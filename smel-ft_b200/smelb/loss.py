@@ -132,7 +132,7 @@ def chunked_ce(h, head: LMHead, tgt, denom: float, token_chunk: int = 1024, need
     """sum_t CE(h_t @ W.T, tgt_t) / denom (smel/loss.py:149-156). h: [N, H] bf16 (final-normed, only supervised
     rows), tgt: [N] long."""
     if h.shape[0] == 0:
-        return (h.sum() * 0.0)
+        return (h.float().sum() * 0.0)
     if need_grad and h.requires_grad:
         return _ChunkedCE.apply(h, head, tgt, float(denom), token_chunk, True)
     with torch.no_grad():

@@ -6,7 +6,11 @@ computed by the fused sm_100a kernels of libsmelb.
                    selected bf16 experts with LoRA in the GEMM K-extension -> fp32 weighted combine (moe.py:214-252)
   shared_mlp       gated MLP with LoRA and the sigmoid shared-expert gate (moe.py:183-201)
   moe_forward      all of the above as one forward call and one backward call (moe.py:255-263)
-  FrozenExpertsFn  frozen experts alone, saving the gate/up pre-activations instead of recomputing them (moe.py:110-143)
+  FrozenExpertsFn  frozen experts alone (int4 or bf16 bank), dX only in backward (moe.py:110-143)
+
+Activation memory: by default the forward under autograd keeps the gate/up pre-activations h [rows, 2I] (and the
+shared expert's), so the backward skips one gate/up GEMM. set_save_preactivations(False) restores the reference's
+contract (FrozenExpertsFn saves only xs, moe.py:1-5 and :123): the backward then recomputes h first.
 
 Activations are bf16 on CUDA. There is no CPU path: CPU tensors raise SmelbError.
 """
@@ -19,6 +23,18 @@ from .quant import dequant_int4, pack_sz, quantize_int4
 
 _LORA_NAMES = ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down")
 _W64 = 64  # width of the LoRA token-side buffers (2r <= 64)
+_SAVE_PREACT = [True]
+
+
+def set_save_preactivations(flag: bool):
+    """Keep the gate/up pre-activations from the forward for the backward (True, the default: one GEMM less per
+    backward, R x 2I bf16 more activation memory per layer call) or recompute them in the backward from the saved
+    inputs (False: the reference's activation memory)."""
+    _SAVE_PREACT[0] = bool(flag)
+
+
+def save_preactivations() -> bool:
+    return _SAVE_PREACT[0]
 
 
 # ==================================================================================================== weight banks
@@ -206,7 +222,7 @@ def _alloc_fwd(cfg, dev, save):
         b.update(counts=e(E, dtype=torch.int32), gcounts=e(E, dtype=torch.int32), offsets=e(E, dtype=torch.int32),
                  row_of=e(T * K, dtype=torch.int32), src_of=e(R, dtype=torch.int32), total=e(1, dtype=torch.int32),
                  order=e(T * K, dtype=torch.int64), xs=e(R, H), a=e(R, I), y=e(R, H))
-        if save:
+        if save and _SAVE_PREACT[0]:
             b["h"] = e(R, 2 * I)
         if n and r:
             # the 64-wide LoRA blocks: the GEMMs write every row of the selected segments, padding columns as zeros
@@ -216,7 +232,7 @@ def _alloc_fwd(cfg, dev, save):
         cfg.max_rows = 0
     if f & _lib.F_SHARED:
         b.update(sh_a=e(T, S), sh_y=e(T, H))
-        if save:
+        if save and _SAVE_PREACT[0]:
             b["sh_h"] = e(T, 2 * S)
         if rh:
             b.update(sh_xa=e(T, _W64), sh_z=e(T, _W64), sp_xa_w=e(1, 2 * rh, H), sp_gu_ext=e(1, 2 * S, _W64),
@@ -230,6 +246,11 @@ def _alloc_bwd(cfg, dev):
     e = lambda *s, dtype=torch.bfloat16: torch.empty(*s, dtype=dtype, device=dev)  # noqa: E731
     z = lambda *s, dtype=torch.bfloat16: torch.zeros(*s, dtype=dtype, device=dev)  # noqa: E731
     b = {"dx": e(T, H)}
+    if f & _lib.F_RECOMPUTE:  # the forward kept no pre-activations: the backward recomputes them here
+        if f & _lib.F_ROUTED:
+            b["h"] = e(cfg.max_rows, 2 * I)
+        if f & _lib.F_SHARED:
+            b["sh_h"] = e(T, 2 * S)
     if f & _lib.F_ROUTED:
         R = cfg.max_rows
         b.update(dy=e(R, H), dh=e(R, 2 * I), dxs=e(R, H), dtopv=e(T, K, dtype=cfg.topv_dtype))
@@ -275,8 +296,11 @@ class _MoELayerFn(torch.autograd.Function):
     def forward(ctx, x, topv_in, cfg, *params):
         dev = x.device
         save = any(ctx.needs_input_grad)
+        cfg.flags &= ~(_lib.F_SAVE | _lib.F_RECOMPUTE)
         if save:
             cfg.flags |= _lib.F_SAVE
+            if not _SAVE_PREACT[0] and cfg.flags & (_lib.F_ROUTED | _lib.F_SHARED):
+                cfg.flags |= _lib.F_RECOMPUTE
         lp = [_fp32(p) for p in params]
         t = dict(cfg.t)
         t["x"] = x
@@ -444,14 +468,17 @@ def moe_block_gemma4(h, xm, W, ex: LayerExperts, top_k: int, eps: float, act="ge
 
 
 class FrozenExpertsFn(torch.autograd.Function):
-    """Frozen experts over expert-grouped rows (moe.py:120-143): apply(xs [R, H], counts, bank, group, act_name).
-    counts may be a list (as in the reference) or an int32/int64 device tensor (no host sync). The forward keeps the
-    gate/up pre-activations when a gradient is needed; the backward re-dequantizes the bank inside the dX GEMMs."""
+    """Frozen experts over expert-grouped rows (moe.py:110-143): apply(xs [R, H], counts, bank, group, act_name).
+    bank is an Int4Experts (dequantized tile by tile inside the GEMMs) or a BF16Experts. counts may be a list (as in
+    the reference) or an int32/int64 device tensor (no host sync); `group` is the reference's memory hint and is not
+    needed. The backward gives dX only; it re-dequantizes the bank inside the dX GEMMs, and uses the gate/up
+    pre-activations kept by the forward unless set_save_preactivations(False) (then only xs is kept, as in the
+    reference, and h is recomputed)."""
 
     @staticmethod
     def forward(ctx, xs, counts, bank, group, act_name="silu"):
-        if not isinstance(bank, Int4Experts):
-            raise _lib.SmelbError("FrozenExpertsFn: the fused path takes Int4Experts banks")
+        if not isinstance(bank, (Int4Experts, BF16Experts)):
+            raise _lib.SmelbError(f"FrozenExpertsFn: unsupported bank {type(bank).__name__}")
         if act_name not in _lib.ACT:
             raise ValueError(f"unknown activation {act_name}")
         xs = _bf16(xs, "FrozenExpertsFn: xs")
@@ -464,15 +491,21 @@ class FrozenExpertsFn(torch.autograd.Function):
             counts_t = torch.tensor(list(counts), dtype=torch.int32, device=dev)
         ops = bank.kernel_operands()
         R, H = xs.shape
-        I = ops["dn_q"].shape[-1] * 2
+        int4 = "gu_q" in ops
+        I = ops["dn_q"].shape[-1] * 2 if int4 else ops["fz_dn"].shape[-1]
         E = counts_t.numel()
-        save = ctx.needs_input_grad[0]
-        h = torch.empty(R, 2 * I, dtype=torch.bfloat16, device=dev) if save else None
+        keep_h = ctx.needs_input_grad[0] and _SAVE_PREACT[0]
+        h = torch.empty(R, 2 * I, dtype=torch.bfloat16, device=dev) if keep_h else None
         a = torch.empty(R, I, dtype=torch.bfloat16, device=dev)
         out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
-        _lib.call("smelb_frozen_experts_fwd", _lib.ptr(xs), R, H, I, _lib.ptr(counts_t), E, _lib.ptr(ops["gu_q"]),
-                  _lib.ptr(ops["gu_sz"]), _lib.ptr(ops["dn_q"]), _lib.ptr(ops["dn_sz"]), _lib.ACT[act_name],
-                  _lib.ptr(h), _lib.ptr(a), _lib.ptr(out), _lib.stream_ptr(dev))
+        if int4:
+            _lib.call("smelb_frozen_experts_fwd", _lib.ptr(xs), R, H, I, _lib.ptr(counts_t), E, _lib.ptr(ops["gu_q"]),
+                      _lib.ptr(ops["gu_sz"]), _lib.ptr(ops["dn_q"]), _lib.ptr(ops["dn_sz"]), _lib.ACT[act_name],
+                      _lib.ptr(h), _lib.ptr(a), _lib.ptr(out), _lib.stream_ptr(dev))
+        else:
+            _lib.call("smelb_frozen_experts_bf16_fwd", _lib.ptr(xs), R, H, I, _lib.ptr(counts_t), E,
+                      _lib.ptr(ops["fz_gu"]), _lib.ptr(ops["fz_dn"]), _lib.ACT[act_name], _lib.ptr(h), _lib.ptr(a),
+                      _lib.ptr(out), _lib.stream_ptr(dev))
         ctx.saved = (xs, h, counts_t, ops, I, act_name)
         return out
 
@@ -481,10 +514,17 @@ class FrozenExpertsFn(torch.autograd.Function):
         xs, h, counts_t, ops, I, act_name = ctx.saved
         dy = dy.to(torch.bfloat16).contiguous()
         R, H = xs.shape
-        dh = torch.empty(R, 2 * I, dtype=torch.bfloat16, device=xs.device)
-        dx = torch.empty(R, H, dtype=torch.bfloat16, device=xs.device)
-        _lib.call("smelb_frozen_experts_bwd", _lib.ptr(xs), _lib.ptr(dy), R, H, I, _lib.ptr(counts_t),
-                  counts_t.numel(), _lib.ptr(ops["gu_q"]), _lib.ptr(ops["gu_sz"]), _lib.ptr(ops["dn_q"]),
-                  _lib.ptr(ops["dn_sz"]), _lib.ACT[act_name], _lib.ptr(h), None, _lib.ptr(dh), _lib.ptr(dx),
-                  _lib.stream_ptr(xs.device))
+        dev = xs.device
+        dh = torch.empty(R, 2 * I, dtype=torch.bfloat16, device=dev)
+        dx = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+        h_buf = torch.empty(R, 2 * I, dtype=torch.bfloat16, device=dev) if h is None else None
+        if "gu_q" in ops:
+            _lib.call("smelb_frozen_experts_bwd", _lib.ptr(xs), _lib.ptr(dy), R, H, I, _lib.ptr(counts_t),
+                      counts_t.numel(), _lib.ptr(ops["gu_q"]), _lib.ptr(ops["gu_sz"]), _lib.ptr(ops["dn_q"]),
+                      _lib.ptr(ops["dn_sz"]), _lib.ACT[act_name], _lib.ptr(h), _lib.ptr(h_buf), _lib.ptr(dh),
+                      _lib.ptr(dx), _lib.stream_ptr(dev))
+        else:
+            _lib.call("smelb_frozen_experts_bf16_bwd", _lib.ptr(xs), _lib.ptr(dy), R, H, I, _lib.ptr(counts_t),
+                      counts_t.numel(), _lib.ptr(ops["fz_gu"]), _lib.ptr(ops["fz_dn"]), _lib.ACT[act_name],
+                      _lib.ptr(h), _lib.ptr(h_buf), _lib.ptr(dh), _lib.ptr(dx), _lib.stream_ptr(dev))
         return dx, None, None, None, None

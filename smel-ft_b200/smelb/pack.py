@@ -1,45 +1,61 @@
-"""The packed on-disk block of SMEL FT (smel/pack.py:1-62): one safetensors file per layer, `layer_XX.safetensors`,
-holding the dense tensors in bf16, the frozen experts in the int4 group format and the selected experts as bf16
-copies, plus the exact merge of LoRA deltas into bf16 weights.
+"""The packed on-disk block of SMEL FT: one safetensors file per layer, `layer_XX.safetensors`, holding the layer's
+dense tensors, its frozen expert bank in the int4 group format and bf16 copies of the selected experts; plus the merge
+of trained LoRA deltas into bf16 weights. The file format and the merge arithmetic are the reference's
+(smel/pack.py:8-46); the work runs on the GPU: the bank through the CUDA int4 quantizer, the merges through one
+`smelb_lora_merge` kernel per weight block (the rank-r delta and the add fused, one rounding).
 
-Keys (names relative to the layer, as the reference writes them, so files written by either side load in the other):
-  experts.gate_up.{q,scale,zero}, experts.down.{q,scale,zero}   int4 bank (uint8 nibbles, bf16 scale / zero)
-  experts.sel.ids (int64), experts.sel.gate_up, experts.sel.down   selected experts (bf16)
-  every other tensor                                              as stored, in bf16 unless it is an integer tensor
-                                                                  or an A_log / dt_bias (kept as they are)
-The int4 banks are quantized on the GPU (smelb.quant.quantize_int4, the CUDA quantizer for group 64).
+Keys (names relative to the layer, so files written by either side load in the other):
+  experts.gate_up.{q,scale,zero}, experts.down.{q,scale,zero}      int4 bank (uint8 nibbles, bf16 scale / zero)
+  experts.sel.ids (int64), experts.sel.gate_up, experts.sel.down    selected experts (bf16 copies)
+  every tensor not under mlp.experts.                               bf16, except integer tensors and A_log / dt_bias
+                                                                    (kept as stored)
 """
 import os
 
 import torch
 
+from . import _lib
 from .quant import quantize_int4
+
+# checkpoint names of the fused expert bank, by packed part name
+BANK = {"gate_up": "mlp.experts.gate_up_proj", "down": "mlp.experts.down_proj"}
+BANK_PREFIX = "mlp.experts."
+# floating-point tensors the packed file keeps in their stored dtype (DeltaNet's A_log and dt_bias)
+KEEP_AS_STORED = ("A_log", "dt_bias")
 
 
 def layer_path(packed_dir: str, l: int) -> str:
     return os.path.join(packed_dir, f"layer_{l:02d}.safetensors")
 
 
-def pack_layer(t: dict, sel_ids=None, group: int = 64, dtype=torch.bfloat16) -> dict:
-    """smel/pack.py:8-25. t: the tensors of one layer as stored in the checkpoint (names relative to the layer),
-    with the fused bank `mlp.experts.gate_up_proj` [E, 2I, H] and `mlp.experts.down_proj` [E, H, I] on a CUDA
-    device. Returns the packed dict (tensors on the bank's device)."""
-    out = {}
-    for k, v in t.items():
-        if k.startswith("mlp.experts."):
-            continue
-        keep = k.endswith(("A_log", "dt_bias")) or not v.is_floating_point()
-        out[k] = v.contiguous() if keep else v.to(dtype).contiguous()
-    gu, dn = t["mlp.experts.gate_up_proj"], t["mlp.experts.down_proj"]
-    if sel_ids is not None and len(sel_ids):
-        ids = torch.as_tensor(list(sel_ids), dtype=torch.long)
-        out["experts.sel.ids"] = ids
-        out["experts.sel.gate_up"] = gu[ids.to(gu.device)].to(dtype).contiguous()
-        out["experts.sel.down"] = dn[ids.to(dn.device)].to(dtype).contiguous()
-    for name, w in (("gate_up", gu), ("down", dn)):
-        for kk, vv in quantize_int4(w, group).items():
-            out[f"experts.{name}.{kk}"] = vv
+def _packed_dense(name: str, t: torch.Tensor, dtype) -> torch.Tensor:
+    as_stored = not t.is_floating_point() or name.endswith(KEEP_AS_STORED)
+    return (t if as_stored else t.to(dtype)).contiguous()
+
+
+def _packed_bank(bank: dict, group: int) -> dict:
+    """experts.{part}.{q,scale,zero} straight from the quantizer's outputs (one CUDA pass per matrix)."""
+    return {f"experts.{part}.{field}": v for part, w in bank.items() for field, v in quantize_int4(w, group).items()}
+
+
+def _packed_selected(bank: dict, sel_ids, dtype) -> dict:
+    ids = torch.as_tensor(list(sel_ids), dtype=torch.long)
+    out = {"experts.sel.ids": ids}
+    for part, w in bank.items():
+        out[f"experts.sel.{part}"] = w.index_select(0, ids.to(w.device)).to(dtype).contiguous()
     return out
+
+
+def pack_layer(t: dict, sel_ids=None, group: int = 64, dtype=torch.bfloat16) -> dict:
+    """The packed tensors of one checkpoint layer `t` (names relative to the layer), whose fused bank
+    mlp.experts.gate_up_proj [E, 2I, H] / mlp.experts.down_proj [E, H, I] lies on a CUDA device (smel/pack.py:8-25).
+    Other mlp.experts.* tensors are not packed."""
+    bank = {part: t[name] for part, name in BANK.items()}
+    packed = {name: _packed_dense(name, v, dtype) for name, v in t.items() if not name.startswith(BANK_PREFIX)}
+    if sel_ids is not None and len(sel_ids):
+        packed.update(_packed_selected(bank, sel_ids, dtype))
+    packed.update(_packed_bank(bank, group))
+    return packed
 
 
 def save_layer(packed_dir: str, l: int, packed: dict):
@@ -60,23 +76,47 @@ def load_layer(packed_dir: str, l: int, pin: bool = False) -> dict:
     return out
 
 
+# ------------------------------------------------------------------------------------------ LoRA merges
+def _on_gpu(t: torch.Tensor) -> torch.Tensor:
+    if t.is_cuda:
+        return t
+    if not torch.cuda.is_available():
+        raise _lib.SmelbError("LoRA merge: smelb merges on the GPU and no CUDA device is available")
+    return t.cuda()
+
+
+def _merge_block(w: torch.Tensor, B: torch.Tensor, A: torch.Tensor, scale: float):
+    """w (a contiguous bf16 / fp32 CUDA block [rows, cols]) += (scale B) @ A in place, one rounding per element."""
+    if w.dtype not in (torch.bfloat16, torch.float32) or not w.is_contiguous():
+        raise _lib.SmelbError(f"LoRA merge: expects a contiguous bf16 or fp32 weight, got {w.dtype}")
+    B32 = B.detach().to(w.device, torch.float32).contiguous()
+    A32 = A.detach().to(w.device, torch.float32).contiguous()
+    rows, cols = w.shape
+    _lib.call("smelb_lora_merge", _lib.ptr(w), 1 if w.dtype == torch.float32 else 0, rows, cols, _lib.ptr(B32),
+              _lib.ptr(A32), A32.shape[0], float(scale), _lib.ptr(w), _lib.stream_ptr(w.device))
+
+
 @torch.no_grad()
 def merge_experts(gate_up: torch.Tensor, down: torch.Tensor, lora) -> tuple:
-    """smel/pack.py:28-39: copies of the fused expert tensors with the LoRA deltas of the selected experts added
-    (fp32 math, one rounding to the tensors' dtype)."""
-    gu, dn = gate_up.clone(), down.clone()
+    """Copies of the fused expert tensors (gate_up [E, 2I, H], down [E, H, I]) with the LoRA deltas of the selected
+    experts merged in: for slot j of expert e, gate rows += s B_gate[j] A_gate[j], up rows += s B_up[j] A_up[j],
+    down += s B_down[j] A_down[j] (smel/pack.py:28-39). Returned on the inputs' device."""
+    home = gate_up.device
+    gu, dn = _on_gpu(gate_up).clone(), _on_gpu(down).clone()
     I = dn.shape[2]
     for j, e in enumerate(lora.expert_ids.tolist()):
-        dg, du, dd = (x.to(gu.device) for x in lora.delta(j))
-        gu[e, :I] = (gu[e, :I].float() + dg).to(gu.dtype)
-        gu[e, I:] = (gu[e, I:].float() + du).to(gu.dtype)
-        dn[e] = (dn[e].float() + dd).to(dn.dtype)
-    return gu, dn
+        for block, name in ((gu[e, :I], "gate"), (gu[e, I:], "up"), (dn[e], "down")):
+            _merge_block(block, getattr(lora, "B_" + name)[j], getattr(lora, "A_" + name)[j], lora.scale)
+    return gu.to(home), dn.to(home)
 
 
 @torch.no_grad()
 def merge_mlp(gate_w, up_w, down_w, lora) -> tuple:
-    """smel/pack.py:42-46: a gated MLP's three weights with its LoRA deltas added (fp32 math, one rounding)."""
-    dg, du, dd = (x.to(gate_w.device) for x in lora.delta())
-    return ((gate_w.float() + dg).to(gate_w.dtype), (up_w.float() + du).to(up_w.dtype),
-            (down_w.float() + dd).to(down_w.dtype))
+    """A gated MLP's three weights with its LoRA deltas merged in (smel/pack.py:42-46), on the inputs' device."""
+    home = gate_w.device
+    out = []
+    for w, name in ((gate_w, "gate"), (up_w, "up"), (down_w, "down")):
+        m = _on_gpu(w).clone()
+        _merge_block(m, getattr(lora, "B_" + name), getattr(lora, "A_" + name), lora.scale)
+        out.append(m.to(home))
+    return tuple(out)

@@ -2,8 +2,9 @@
 (smel/quant.py:97-105), on CUDA.
 
 Format: w [..., K] -> q uint8 [..., K/2] (two nibbles per byte, the low nibble holds the even column),
-scale / zero bf16 [..., K/group]; w ~= q * scale + zero. Dequantization computes q * scale + zero in fp32 and rounds
-once to the output dtype (the reference's Triton kernel, smel/quant.py:51-67).
+scale / zero bf16 [..., K/group]; w ~= q * scale + zero. dequant_int4 computes q * scale + zero in fp32 and rounds
+once to the output dtype (the reference's Triton kernel, smel/quant.py:51-67); dequant_int4_torch keeps the
+reference's torch fallback rounding (smel/quant.py:87-94).
 """
 import torch
 
@@ -83,25 +84,31 @@ def quantize_int4(w: torch.Tensor, group: int = 64, clip_search=CLIP_SEARCH) -> 
     return _quantize_slab(w, group, clip_search)
 
 
-def dequant_int4(q: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
-    """q [..., K/2], scale/zero [..., G] -> [..., K] in `dtype` (bf16 or fp32), on the GPU
-    (smel/quant.py:74-84)."""
+def _dequant(q, scale, zero, dtype, entry, what):
     if dtype not in (torch.bfloat16, torch.float32):
-        raise _lib.SmelbError(f"dequant_int4: output dtype {dtype} not supported (bf16 or fp32)")
+        raise _lib.SmelbError(f"{what}: output dtype {dtype} not supported (bf16 or fp32)")
     if q.dtype != torch.uint8 or scale.dtype != torch.bfloat16 or zero.dtype != torch.bfloat16:
-        raise _lib.SmelbError("dequant_int4: expects uint8 q and bf16 scale / zero")
+        raise _lib.SmelbError(f"{what}: expects uint8 q and bf16 scale / zero")
     q, scale, zero = q.contiguous(), scale.contiguous(), zero.contiguous()
     half_k, groups = q.shape[-1], scale.shape[-1]
     out = torch.empty(*q.shape[:-1], half_k * 2, device=q.device, dtype=dtype)
     rows = q.numel() // max(half_k, 1)
-    _lib.call("smelb_int4_dequant", _lib.ptr(q), _lib.ptr(scale), _lib.ptr(zero), _lib.ptr(out), rows, half_k * 2,
-              groups, 1 if dtype == torch.float32 else 0, _lib.stream_ptr(q.device))
+    _lib.call(entry, _lib.ptr(q), _lib.ptr(scale), _lib.ptr(zero), _lib.ptr(out), rows, half_k * 2, groups,
+              1 if dtype == torch.float32 else 0, _lib.stream_ptr(q.device))
     return out
 
 
+def dequant_int4(q: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """q [..., K/2], scale/zero [..., G] -> [..., K] in `dtype` (bf16 or fp32), on the GPU: q * scale + zero in fp32,
+    rounded once to `dtype` (the reference's Triton kernel, smel/quant.py:51-67, 74-84)."""
+    return _dequant(q, scale, zero, dtype, "smelb_int4_dequant", "dequant_int4")
+
+
 def dequant_int4_torch(q, scale, zero, dtype=torch.bfloat16):
-    """Name kept from smel/quant.py:87-94. Runs the same CUDA dequant as dequant_int4 (single rounding)."""
-    return dequant_int4(q, scale, zero, dtype)
+    """smel/quant.py:87-94: the same dequant with torch's operation-by-operation rounding in `dtype`: for bf16 the
+    product q * scale is rounded to bf16 before zero is added and the sum is rounded again (it differs from
+    dequant_int4 on many weights, exactly as in the reference). fp32 output equals dequant_int4."""
+    return _dequant(q, scale, zero, dtype, "smelb_int4_dequant_stepwise", "dequant_int4_torch")
 
 
 def pack_sz(scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:

@@ -25,6 +25,10 @@ Outputs (torch.save dicts of CPU tensors):
                pins moe_forward against) at the reference's tiny config (smel/tiny.py: hidden 256, 32 experts,
                top-4, expert and shared intermediate 64): weights, inputs, the fp32 and bf16 forward and the input
                gradients of an upstream gradient (--only hf; needs transformers' qwen3_5_moe module)
+  dequant_torch.pt  smel/quant.py:87-94 dequant_int4_torch in bf16 (two roundings) of the quant.pt bank (--only
+               dequant_torch)
+  lora_fns.pt  smel/lora.py:61-83 lora_linear and lora_gate_up in fp32 on bf16-representable inputs: outputs and the
+               gradients w.r.t. x, A and B of a seeded upstream gradient (--only lora)
   hf_gemma_block.pt  the MoE part of transformers' own Gemma4TextDecoderLayer after the attention residual (dense
                MLP, router, experts, the four feed-forward norms, layer_scalar, called in the order of the module's
                forward) at the reference's tiny Gemma 4 config (smel/tiny.py: hidden 256, 16 experts, top-4), fp32
@@ -59,7 +63,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMEL_REFERENCE"),
                     help="the smel-ft source tree (default: $SMEL_REFERENCE)")
-    ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf", "hf_gemma"])
+    ap.add_argument("--only", default=None, choices=[None, "pack", "ce", "hf", "hf_gemma", "dequant_torch", "lora"])
     args = ap.parse_args()
     if not args.reference:
         ap.error("pass --reference <smel-ft source tree> or set SMEL_REFERENCE")
@@ -75,6 +79,12 @@ def main():
         return
     if args.only == "hf_gemma":
         make_hf_gemma()
+        return
+    if args.only == "dequant_torch":
+        make_dequant_torch()
+        return
+    if args.only == "lora":
+        make_lora_fns()
         return
     from smel.lora import ExpertsLoRA, LayerLoRA, MLPLoRA
     from smel.moe import FrozenExpertsFn, BF16Experts, Int4Experts, LayerExperts, moe_forward, route
@@ -216,6 +226,48 @@ def main():
                 "g_lora_sh": {n: getattr(lsh_m, n).grad for n in lsh_t}}, os.path.join(HERE, "gemma_block.pt"))
     make_pack()
     print("golden fixtures written to", HERE)
+
+
+def make_dequant_torch():
+    """The reference's torch dequant in bf16 (quant.py:87-94: product and sum each rounded to bf16) of quant.pt."""
+    from smel.quant import dequant_int4_torch
+    d = torch.load(os.path.join(HERE, "quant.pt"), weights_only=False)
+    out = {"bf16": dequant_int4_torch(d["q"], d["scale"], d["zero"], torch.bfloat16),
+           "grid_bf16": dequant_int4_torch(d["grid_q"], d["grid_scale"], d["grid_zero"], torch.bfloat16)}
+    torch.save(out, os.path.join(HERE, "dequant_torch.pt"))
+
+
+def make_lora_fns():
+    """lora_linear / lora_gate_up (smel/lora.py:61-83) in fp32 with autograd, inputs rounded to bf16 first so a bf16
+    implementation sees the same values."""
+    from smel.lora import lora_gate_up, lora_linear
+    g = torch.Generator().manual_seed(21)
+    T, Kd, N, I, r, s = 150, 256, 192, 128, 16, 2.0
+
+    def bf(t):
+        return t.bfloat16().float()
+
+    x = bf(torch.randn(T, Kd, generator=g))
+    w = bf(torch.randn(N, Kd, generator=g) * 0.05)
+    A = (torch.rand(r, Kd, generator=g) * 2 - 1) / Kd ** 0.5
+    B = torch.randn(N, r, generator=g) * 0.05
+    gy = torch.randn(T, N, generator=g)
+    xr, Ar, Br = x.clone().requires_grad_(True), A.clone().requires_grad_(True), B.clone().requires_grad_(True)
+    y = lora_linear(xr, w, Ar, Br, s)
+    y.backward(gy)
+    lin = {"x": x, "w": w, "A": A, "B": B, "scale": s, "gy": gy, "y": y.detach(), "dx": xr.grad, "dA": Ar.grad,
+           "dB": Br.grad}
+    wgu = bf(torch.randn(2 * I, Kd, generator=g) * 0.05)
+    pr = {n: ((torch.rand(r, Kd, generator=g) * 2 - 1) / Kd ** 0.5 if n.startswith("A") else
+              torch.randn(I, r, generator=g) * 0.05) for n in ("A_gate", "B_gate", "A_up", "B_up")}
+    gg, gu_ = torch.randn(T, I, generator=g), torch.randn(T, I, generator=g)
+    xr = x.clone().requires_grad_(True)
+    prr = {k: v.clone().requires_grad_(True) for k, v in pr.items()}
+    gate, up = lora_gate_up(xr, wgu, prr["A_gate"], prr["B_gate"], prr["A_up"], prr["B_up"], s)
+    (gate * gg + up * gu_).sum().backward()
+    gu = {"x": x, "w": wgu, **pr, "scale": s, "g_gate": gg, "g_up": gu_, "gate": gate.detach(), "up": up.detach(),
+          "dx": xr.grad, **{"d" + k: v.grad for k, v in prr.items()}}
+    torch.save({"linear": lin, "gate_up": gu}, os.path.join(HERE, "lora_fns.pt"))
 
 
 def make_pack():

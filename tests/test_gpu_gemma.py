@@ -135,3 +135,69 @@ def test_gemma_block_vs_oracle_and_reference(dev, golden):
     m = (topi.sort(1).values == d["topi"].sort(1).values).all(1)
     close(out.float().cpu()[m], d["out"][m], "out vs reference", rel=3e-2, cos=0.999)
     assert smelb.read_status() == 0
+
+
+class _LazyBank:
+    """One expert of an int4 bank dequantized on the CPU on first access (the oracle's view of the frozen bank)."""
+
+    def __init__(self, d, dtype):
+        self.q, self.s, self.z = d["q"].cpu(), d["scale"].cpu(), d["zero"].cpu()
+        self.shape = (self.q.shape[0], self.q.shape[1], self.q.shape[2] * 2)
+        self.dtype, self.cache = dtype, {}
+
+    def __getitem__(self, e):
+        if e not in self.cache:
+            self.cache[e] = O.dequant_int4(self.q[e], self.s[e], self.z[e]).to(self.dtype)
+        return self.cache[e]
+
+
+def test_gemma_config3_full_size(dev):
+    """Config 3 at full size (H 2816, 128 experts top-8, I 704, dense GeGLU 2112 with LoRA, 4096 tokens, 116 int4 +
+    12 LoRA experts, Zipf s=1.1): output, dh and dxm on every token and all 12 LoRA gradients against the oracle
+    (fp32, the GPU's routing forced); routing against the oracle's own top-8 of the same bf16 inputs with every
+    disagreeing row reported with its logit gap."""
+    import smelb
+    from smelb.synth import gemma_layer
+    L = gemma_layer(device=dev, seed=0)
+    meta, ex, lora, W = L["meta"], L["ex"], L["lora"], L["W"]
+    assert abs(meta["share"] - 0.5) <= 0.02
+    K, eps, sel = meta["K"], meta["eps"], meta["selected"]
+    h = L["h"].clone().requires_grad_(True)
+    xm = L["xm"].clone().requires_grad_(True)
+    gy = torch.randn(h.shape, generator=torch.Generator(device=dev).manual_seed(9), device=dev).bfloat16()
+    rec = {}
+    out = smelb.moe_block_gemma4(h, xm, W, ex, K, eps, "gelu_tanh", lora,
+                                 stats=lambda p, v, i: rec.update(p=p, v=v, i=i))
+    out.backward(gy)
+    assert smelb.read_status() == 0
+    dt = torch.float32
+    Wc = {k: v.cpu() for k, v in W.items()}
+    # routing on the oracle's prologue (bf16 steps) with fp64 logits
+    hc = h.detach().cpu()
+    x = (hc.float() * torch.pow(hc.float().pow(2).mean(-1, keepdim=True) + eps, -0.5)).bfloat16()
+    x = (x * Wc["router.scale"] * hc.shape[-1] ** -0.5).bfloat16()
+    dis = O.routing_disagreements(rec["i"], x.double() @ Wc["router.proj.weight"].double().t(), K)
+    print(f"routing: {len(dis)} of {hc.shape[0]} rows differ from the fp64 top-{K}; logit gaps "
+          f"{[round(g, 5) for _, g in dis[:20]]}")
+    assert len(dis) <= 0.01 * hc.shape[0]
+    assert all(g <= 0.05 for _, g in dis), dis
+    s = lora.experts.scale
+    lex = {n: getattr(lora.experts, n).detach().cpu().to(dt).requires_grad_(True) for n in NAMES}
+    lsh = {n: getattr(lora.shared, n).detach().cpu().to(dt).requires_grad_(True) for n in NAMES}
+    h32 = hc.to(dt).requires_grad_(True)
+    xm32 = xm.detach().cpu().to(dt).requires_grad_(True)
+    W32 = {k: v.to(dt) for k, v in Wc.items()}
+    ref, _, ref_topv, _ = O.moe_block_gemma4(h32, xm32, W32, _LazyBank(ex.frozen.gu, dt), _LazyBank(ex.frozen.dn, dt),
+                                             K, eps, sel, ex.sel_gate_up.cpu().to(dt), ex.sel_down.cpu().to(dt),
+                                             {**lex, "scale": s}, {**lsh, "scale": s}, "gelu_tanh", rec["i"].cpu())
+    ref.backward(gy.cpu().to(dt))
+    bad = []
+    items = [("out", out, ref), ("topv", rec["v"], ref_topv), ("dh", h.grad, h32.grad), ("dxm", xm.grad, xm32.grad)]
+    items += [("experts " + n, getattr(lora.experts, n).grad, lex[n].grad) for n in NAMES]
+    items += [("dense " + n, getattr(lora.shared, n).grad, lsh[n].grad) for n in NAMES]
+    for what, a, b in items:
+        e, c = O.rel_err(a.float().cpu(), b.float()), O.cosine(a.float().cpu(), b.float())
+        print(f"{what:>16s}: rel err {e:.3e} cosine {c:.7f}")
+        if not (e <= 2e-2 and c >= 0.9999):
+            bad.append(f"{what}: rel err {e:.3e}, cosine {c:.6f}")
+    assert not bad, "; ".join(bad)

@@ -153,3 +153,35 @@ def test_rmsnorm_oracle_forms():
     assert torch.allclose(O.rmsnorm(x, None, 1e-6, False), x * rstd, atol=1e-6)
     s, y = O.add_rmsnorm(h, x, w, 1e-6, False)
     assert torch.equal(s, h + x) and torch.allclose(y, O.rmsnorm(h + x, w, 1e-6, False))
+
+
+def test_oracle_dequant_stepwise_equals_reference(golden):
+    """dequant_int4_torch in bf16 (two roundings) as the reference computes it (tests/golden/dequant_torch.pt)."""
+    d, t = golden("quant.pt"), golden("dequant_torch.pt")
+    a = O.dequant_int4_stepwise(d["q"], d["scale"], d["zero"], torch.bfloat16)
+    assert torch.equal(a.view(torch.int16), t["bf16"].view(torch.int16))
+    b = O.dequant_int4_stepwise(d["grid_q"], d["grid_scale"], d["grid_zero"], torch.bfloat16)
+    assert torch.equal(b.view(torch.int16), t["grid_bf16"].view(torch.int16))
+    # and it is a different function from the single-rounding dequant on a large share of the weights
+    single = O.dequant_int4(d["q"], d["scale"], d["zero"]).to(torch.bfloat16)
+    assert (single.view(torch.int16) != a.view(torch.int16)).float().mean() > 0.2
+
+
+def test_oracle_lora_functions_equal_reference(golden):
+    """lora_linear / lora_gate_up of the oracle against the reference's own fp32 outputs and gradients."""
+    d = golden("lora_fns.pt")
+    L = d["linear"]
+    x, A, B = (L[k].clone().requires_grad_(True) for k in ("x", "A", "B"))
+    y = O.lora_linear(x, L["w"], A, B, L["scale"])
+    y.backward(L["gy"])
+    for name, a, b in (("y", y, L["y"]), ("dx", x.grad, L["dx"]), ("dA", A.grad, L["dA"]), ("dB", B.grad, L["dB"])):
+        assert O.rel_err(a, b) < 1e-5, name
+    G = d["gate_up"]
+    x = G["x"].clone().requires_grad_(True)
+    p = {k: G[k].clone().requires_grad_(True) for k in ("A_gate", "B_gate", "A_up", "B_up")}
+    g, u = O.lora_gate_up(x, G["w"], p["A_gate"], p["B_gate"], p["A_up"], p["B_up"], G["scale"])
+    (g * G["g_gate"] + u * G["g_up"]).sum().backward()
+    assert O.rel_err(g, G["gate"]) < 1e-5 and O.rel_err(u, G["up"]) < 1e-5
+    assert O.rel_err(x.grad, G["dx"]) < 1e-5
+    for k in p:
+        assert O.rel_err(p[k].grad, G["d" + k]) < 1e-5, k

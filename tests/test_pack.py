@@ -1,6 +1,6 @@
 """The packed on-disk block (smelb/pack.py, smel/pack.py:8-46) against the reference's own output
-(tests/golden/pack.pt, written by tests/golden/make_golden.py --only pack): safetensors round trip and the exact LoRA
-merges on the CPU, pack_layer with the CUDA quantizer on the GPU."""
+(tests/golden/pack.pt, written by tests/golden/make_golden.py --only pack): safetensors round trip on the CPU;
+pack_layer with the CUDA quantizer and the LoRA merges with the CUDA merge kernel on the GPU (bit-exact)."""
 import pytest
 import torch
 
@@ -24,7 +24,26 @@ def test_packed_file_round_trip(golden, tmp_path):
         assert _same(back[k], v), k
 
 
+def test_merge_without_cuda_fails_loudly(golden):
+    """There is no CPU merge: without a CUDA device the merge raises instead of computing on the host."""
+    import smelb
+    from smelb import pack
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    d = golden("pack.pt")
+    t = d["t"]
+    S, H = t["mlp.shared_expert.gate_proj.weight"].shape
+    lsh = smelb.MLPLoRA(H, S, d["r"], d["alpha"])
+    with pytest.raises(smelb.SmelbError):
+        pack.merge_mlp(t["mlp.shared_expert.gate_proj.weight"].bfloat16(),
+                       t["mlp.shared_expert.up_proj.weight"].bfloat16(),
+                       t["mlp.shared_expert.down_proj.weight"].bfloat16(), lsh)
+
+
+@pytest.mark.gpu
 def test_merges_equal_reference(golden):
+    """The CUDA merge (fp32 fma chain over the rank, one rounding) equals the reference's torch merge bit for bit,
+    for CPU inputs (moved to the GPU and back) and CUDA inputs."""
     import smelb
     from smelb import pack
     d = golden("pack.pt")
@@ -39,6 +58,10 @@ def test_merges_equal_reference(golden):
             getattr(lsh, n).copy_(d["lora_sh"][n])
     gu, dn = pack.merge_experts(t["mlp.experts.gate_up_proj"].bfloat16(), t["mlp.experts.down_proj"].bfloat16(), lex)
     assert _same(gu, d["merged_gu"]) and _same(dn, d["merged_dn"])
+    dev = torch.device("cuda", 0)
+    gu2, dn2 = pack.merge_experts(t["mlp.experts.gate_up_proj"].bfloat16().to(dev),
+                                  t["mlp.experts.down_proj"].bfloat16().to(dev), lex.to(dev))
+    assert gu2.is_cuda and _same(gu2.cpu(), d["merged_gu"]) and _same(dn2.cpu(), d["merged_dn"])
     m = pack.merge_mlp(t["mlp.shared_expert.gate_proj.weight"].bfloat16(),
                        t["mlp.shared_expert.up_proj.weight"].bfloat16(),
                        t["mlp.shared_expert.down_proj.weight"].bfloat16(), lsh)
