@@ -89,7 +89,8 @@ class Clocks:
         os.unlink(self.path)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "window": "1 s of warm-up replays of the same step, then the timed region"}
 
 
 def dist_setup():
@@ -322,11 +323,19 @@ def run_ours(args, world, rank, local):
             step(x, gy)
         dp_sync()
 
+    # warm-up replays, then at least ~1 s more of them with the clock sampler running, so that the clock record
+    # covers the GPU under this load right up to and through the timed region (a timed region of a few tens of ms
+    # is shorter than the sampler's period)
     for _ in range(args.warmup):
         run_step()
     torch.cuda.synchronize()
     clocks = Clocks(local)
     clocks.start()
+    t_w = time.perf_counter()
+    while time.perf_counter() - t_w < 1.0:
+        for _ in range(20):
+            run_step()
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     n1 = _lib.launch_count()

@@ -179,8 +179,10 @@ def test_gemma_config3_full_size(dev):
     dis = O.routing_disagreements(rec["i"], x.double() @ Wc["router.proj.weight"].double().t(), K)
     print(f"routing: {len(dis)} of {hc.shape[0]} rows differ from the fp64 top-{K}; logit gaps "
           f"{[round(g, 5) for _, g in dis[:20]]}")
-    assert len(dis) <= 0.01 * hc.shape[0]
-    assert all(g <= 0.05 for _, g in dis), dis
+    # the Gemma router's logits are small (std ~0.02 around the Zipf bias), so bf16 rounding flips more near-ties
+    # than at config 2; every flip must be a near-tie
+    assert len(dis) <= 0.03 * hc.shape[0]
+    assert all(g <= 2e-3 for _, g in dis), dis
     s = lora.experts.scale
     lex = {n: getattr(lora.experts, n).detach().cpu().to(dt).requires_grad_(True) for n in NAMES}
     lsh = {n: getattr(lora.shared, n).detach().cpu().to(dt).requires_grad_(True) for n in NAMES}
