@@ -132,7 +132,8 @@ def config_json(cfg, meta, world, parallel="dp"):
             "12 LoRA experts hold 50% +- 2% of the renormalised top-8 gate mass", "seed": meta.get("seed"),
             "l2": "weights 0.53 GB > L2 126 MB: each step streams the banks from HBM",
             "parallelism": "single" if world == 1 else
-            (f"ep{world}: experts split over {world} GPUs, {cfg['T']} tokens per GPU (weak scaling)" if parallel == "ep"
+            (f"ep{world}: experts split over {world} GPUs (load-balanced placement), rows exchanged over NVLink through "
+             f"peer memory, {cfg['T']} tokens per GPU (weak scaling)" if parallel == "ep"
              else f"dp{world}: the whole layer on each of {world} GPUs, {cfg['T']} tokens per GPU (weak scaling), "
                   f"LoRA gradients all-reduced every step")}
 
@@ -187,25 +188,38 @@ def run_ours(args, world, rank, local):
     ep_mode = world > 1 and args.parallel == "ep"
     dp_mode = world > 1 and args.parallel == "dp"
     # With several GPUs every rank brings its own cfg["T"] tokens (weak scaling) of one layer (same weights on every
-    # rank, built from one seed). dp: every GPU holds the whole layer (0.53 GB of weights, a small part of its HBM)
-    # and the LoRA gradients are summed over the ranks every step (one NCCL all-reduce of the flattened gradients);
-    # ep: the experts are split over the ranks (smelb.ep: count and row all-to-alls over NCCL).
+    # rank, built from one seed). ep (default): the experts are split over the ranks with a load-balanced placement
+    # (smelb.ep: rows exchanged over NVLink through peer memory, device-side synchronisation) and the replicated
+    # shared expert's LoRA gradients are summed every step; dp: every GPU holds the whole layer and all LoRA gradients
+    # are summed (one NCCL all-reduce of the flattened gradients).
     layer = qwen_layer(T=cfg["T"] * world, H=cfg["H"], E=cfg["E"], K=cfg["K"], I=cfg["I"], S=cfg["S"],
                        n_sel=cfg["n_sel"], r=cfg["r"], alpha=cfg["alpha"], seed=0, device=dev)
     W, ex, lora, K = layer["W"], layer["ex"], layer["lora"], cfg["K"]
     x = layer["x"][rank * cfg["T"]:(rank + 1) * cfg["T"]].contiguous()
     gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(9 + rank), device=dev).bfloat16()
+    comm = shard = None
+    placement_note = None
     if ep_mode:
         from smelb import ep
-        ex_run, lora_run = ep.shard_layer(ex, lora, rank, world)
+        rec = {}
+        with torch.no_grad():  # routing of all ranks' tokens: the per-expert loads the placement balances
+            smelb.moe_forward(layer["x"], W, ex, K, None, stats=lambda p, v, i: rec.update(i=i))
+        loads = torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist()
+        placement = ep.balanced_placement(loads, world)
+        per_rank = [sum(loads[e] for e in ids) for ids in placement]
+        placement_note = {"placement": "balanced by routed rows", "rows_per_rank": per_rank}
+        shard = ep.shard_layer(ex, lora, rank, world, placement)
+        comm = ep.EPGroup(cap=cfg["T"], H=cfg["H"], K=K)
+        params = list(shard.lora.parameters())
+        sync_params = list(shard.lora.shared.parameters())  # the replicated shared LoRA
     else:
-        ex_run, lora_run = ex, lora
-    params = list(lora_run.parameters()) if ep_mode else list(lora.parameters())
+        params = list(lora.parameters())
+        sync_params = params if dp_mode else []
 
     def layer_call(xd):
         if ep_mode:
-            return ep.moe_forward_ep(xd, W, ex_run, K, lora_run)
-        return smelb.moe_forward(xd, W, ex_run, K, lora_run)
+            return ep.moe_forward_ep(xd, W, shard, K, comm)
+        return smelb.moe_forward(xd, W, ex, K, lora)
 
     def step(xd, gd):
         for p in params:
@@ -215,17 +229,16 @@ def run_ours(args, world, rank, local):
         xr = xd.detach().requires_grad_(True)
         out = layer_call(xr)
         out.backward(gd)
-        if ep_mode:
-            ep.allreduce_shared_grads(lora_run)
         return xr.grad
 
     grad_sum = None
-    if dp_mode:
+    if sync_params:
         from smelb import dp
-        grad_sum = dp.GradAllReduce(params)
+        grad_sum = dp.GradAllReduce(sync_params)
 
     def dp_sync():
-        """Data parallel: sum the LoRA gradients over the ranks (one all-reduce of their concatenation)."""
+        """Sum the replicated LoRA gradients over the ranks (one all-reduce of their concatenation): all of them with
+        data parallelism, the shared expert's with expert parallelism."""
         if grad_sum is not None:
             grad_sum()
 
@@ -297,12 +310,7 @@ def run_ours(args, world, rank, local):
     # in a CUDA graph and replayed, so the number is the device's and not the Python host's
     graph, timing = None, "cuda-graph replay of the whole step"
     n0 = _lib.launch_count()
-    if ep_mode:
-        graph, timing = None, ("eager (expert parallel: the per-call row counts are needed on the host as the "
-                               "all-to-all split sizes, so the step is not graph-captured)")
     try:
-        if ep_mode:
-            raise RuntimeError("skip")
         torch.cuda.synchronize()
         n0 = _lib.launch_count()
         graph = torch.cuda.CUDAGraph()
@@ -310,8 +318,7 @@ def run_ours(args, world, rank, local):
             step(x, gy)
         torch.cuda.synchronize()
     except Exception as exc:  # not capturable here: time the eager step instead and say so
-        if not ep_mode:
-            graph, timing = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
+        graph, timing = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
         torch.cuda.synchronize()
         n0 = _lib.launch_count()
     per_step_launches = _lib.launch_count() - n0 if graph is not None else None
@@ -396,8 +403,248 @@ def run_ours(args, world, rank, local):
            "routing_share": round(layer["meta"].get("share", 0.0), 4), "roofline": roof,
            "e2e": e2e,
            "gpu_launches": int(launches), "clocks": ck}
+    if placement_note:
+        res["expert_parallel"] = placement_note
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(layer, min(cfg["T"], args.cpu_tokens))
+    del graph
+    if comm is not None:  # every peer has finished reading this rank's region before it is freed
+        torch.cuda.synchronize()
+        barrier(world)
+        comm.close()
+    return res
+
+
+# ------------------------------------------------------------------------------------------ graph timing helper
+def _time_graph(step, args, local, world, post=None):
+    """Capture `step` (on a side stream) in a CUDA graph and time K replays after W warm-up replays with CUDA events,
+    the clocks sampled over 1 s of replays and the timed region; eager if the capture fails. `post` (a collective,
+    kept out of the graph) runs after every step, inside the timed region. Returns (ms per step (max over ranks),
+    timing note, clocks, this library's launches in the timed region)."""
+    from smelb import _lib
+    dev = torch.device("cuda", local)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    torch.cuda.set_stream(side)
+    for _ in range(max(args.warmup, 1)):
+        step()
+        if post is not None:
+            post()
+    torch.cuda.synchronize()
+    graph, timing = None, "cuda-graph replay of the whole step"
+    try:
+        n0 = _lib.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        per = _lib.launch_count() - n0
+        torch.cuda.synchronize()
+    except Exception as exc:
+        graph, timing, per = None, f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})", None
+        torch.cuda.synchronize()
+    one = graph.replay if graph is not None else step
+
+    def run():
+        one()
+        if post is not None:
+            post()
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    t_w = time.perf_counter()
+    while time.perf_counter() - t_w < 1.0:
+        run()
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    n1 = _lib.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ck = clocks.stop()
+    launches = per * args.steps if per is not None else _lib.launch_count() - n1
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    del graph
+    return ms, timing, ck, int(launches)
+
+
+# ------------------------------------------------------------------------------------------ config 3
+def run_gemma(args, local):
+    """Config 3: the Gemma-4-26B-A4B-like MoE block (smel/layer_runner.py:249-261; H 2816, 128 experts top-8, expert
+    intermediate 704, dense GeGLU MLP 2112 with LoRA, 116 int4 + 12 bf16 LoRA experts, Zipf s=1.1) on 4096 tokens:
+    no-grad forward, then recompute + backward of h and xm, graph-timed. One JSON line with the roofline of its
+    algorithmic FLOPs (394.7 MFLOP per token over the three passes) and the CPU oracle on a token sample."""
+    import smelb
+    from smelb import _lib
+    from smelb.synth import gemma_layer
+    dev = torch.device("cuda", local)
+    T, H, E, K, I, S = 4096, 2816, 128, 8, 704, 2112
+    L = gemma_layer(T=T, seed=0, device=dev)
+    W, ex, lora, meta = L["W"], L["ex"], L["lora"], L["meta"]
+    h, xm = L["h"], L["xm"]
+    gy = torch.randn(h.shape, generator=torch.Generator(device=dev).manual_seed(9), device=dev).bfloat16()
+    params = list(lora.parameters())
+
+    def step():
+        for p in params:
+            p.grad = None
+        with torch.no_grad():
+            smelb.moe_block_gemma4(h, xm, W, ex, K, meta["eps"], "gelu_tanh", lora)
+        hr, xr = h.detach().requires_grad_(True), xm.detach().requires_grad_(True)
+        smelb.moe_block_gemma4(hr, xr, W, ex, K, meta["eps"], "gelu_tanh", lora).backward(gy)
+
+    ms, timing, ck, launches = _time_graph(step, args, local, 1)
+    assert smelb.read_status() == 0
+    _lib.gemm_timing(True)
+    _lib.gemm_timing_read()
+    step()
+    gemm_ms, gemm_n = _lib.gemm_timing_read()
+    _lib.gemm_timing(False)
+    f_tok = 2 * K * 3 * H * I + 2 * 3 * H * S + 2 * H * E
+    flops = 3 * f_tok * T
+    pk, pk_kind = peaks()
+    res = {"metric": "Gemma-4 MoE block tokens/s fwd+recompute+bwd (config 3) and % of TC roofline",
+           "value": round(T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16",
+           "data": "synthetic (seeded, random-init weights of the block shape)",
+           "config": {"workload": "gemma-4-26b-a4b-like moe block (config 3): fwd + recompute + bwd", "tokens": T,
+                      "hidden": H, "experts": E, "top_k": K, "expert_inter": I, "dense_inter": S,
+                      "frozen": "int4 group-64", "lora_experts": 12, "lora_rank": 16,
+                      "routing": "zipf s=1.1, the 12 LoRA experts hold 50% +- 2% of the gate mass"},
+           "routing_share": round(meta["share"], 4), "timing": timing,
+           "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1e3) / 1e12, 1), "peak": pk["bf16_tflops"],
+                        "unit": "TFLOP/s", "frac": round(flops / (ms / 1e3) / 1e12 / pk["bf16_tflops"], 4),
+                        "peak_kind": f"{pk_kind} bf16 burst", "algorithmic_flops_per_step": flops,
+                        "gemm_ms_per_step": round(gemm_ms, 4), "gemm_launches_per_step": gemm_n,
+                        "gemm_frac": round(flops / (gemm_ms / 1e3) / 1e12 / pk["bf16_tflops"], 4)},
+           "gpu_launches": launches, "clocks": ck}
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = _gemma_cpu_baseline(L, args.cpu_tokens)
+    return res
+
+
+def _gemma_cpu_baseline(L, tokens):
+    """The reference's torch path of the Gemma block (restated in oracle/moe_oracle.py) on the host cores, fp32,
+    forward + recompute + backward on a token sample."""
+    from oracle import moe_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = min(tokens, 512)
+    W = {k: v.float().cpu() for k, v in L["W"].items()}
+    ex, lora, meta = L["ex"], L["lora"], L["meta"]
+    q = {k: v.cpu() for k, v in ex.frozen.gu.items()}, {k: v.cpu() for k, v in ex.frozen.dn.items()}
+
+    class Lazy:  # the reference dequantizes the frozen experts per call (smel/quant.py:87-94)
+        def __init__(self, d):
+            self.d, self.shape = d, (d["q"].shape[0], d["q"].shape[1], d["q"].shape[2] * 2)
+
+        def __getitem__(self, e):
+            return O.dequant_int4(self.d["q"][e], self.d["scale"][e], self.d["zero"][e])
+
+    names = ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down")
+    s = lora.experts.scale
+    lex = {n: getattr(lora.experts, n).detach().cpu().float().requires_grad_(True) for n in names}
+    lsh = {n: getattr(lora.shared, n).detach().cpu().float().requires_grad_(True) for n in names}
+    h, xm = L["h"][:tokens].float().cpu(), L["xm"][:tokens].float().cpu()
+    sel = ex.sel_ids.tolist()
+
+    def run(hh, xx):
+        return O.moe_block_gemma4(hh, xx, W, Lazy(q[0]), Lazy(q[1]), 8, meta["eps"], sel, ex.sel_gate_up.float().cpu(),
+                                  ex.sel_down.float().cpu(), {**lex, "scale": s}, {**lsh, "scale": s}, "gelu_tanh")[0]
+    gy = torch.randn(h.shape, generator=torch.Generator().manual_seed(9))
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        run(h, xm)
+    hr, xr = h.clone().requires_grad_(True), xm.clone().requires_grad_(True)
+    run(hr, xr).backward(gy)
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": f"{tokens} tokens of the same block, 1 step (fwd no-grad + recompute + bwd), float32, {dt:.2f} s"}
+
+
+# ------------------------------------------------------------------------------------------ config 5
+def run_block(args, world, rank, local, n_layers=24, n_micro=16):
+    """Config 5: a layer-major block of 24 Qwen3.6-shape MoE layers (smel/layer_runner.py:295-371 with the MoE block
+    h + moe(h) of every layer), 16 micro-batches of 4092 tokens per rank: forward of every layer over all micro-
+    batches, then recompute + backward in reverse layer order (smelb.runner.LayerMajorRunner). With N > 1 the experts
+    of every layer are split over the GPUs (expert parallel, load-balanced placement) and each rank brings its own
+    16 micro-batches (weak scaling); the shared experts' LoRA gradients are summed every step. Every layer has its own
+    expert bank, selected experts, LoRA and shared expert; the router of layer 0 is used by all layers so that each
+    layer sees the configured Zipf skew on the residual stream. One JSON line on rank 0: whole-box tokens/s."""
+    import smelb
+    from smelb import ep
+    from smelb.runner import LayerMajorRunner, ep_layer_fn, moe_block
+    from smelb.synth import qwen_layer
+    dev = torch.device("cuda", local)
+    cfg = layer_config(args)
+    T, K = cfg["T"], cfg["K"]
+    layers, loras, comm, router, placement, x_all = {}, {}, None, None, None, None
+    if world > 1:
+        comm = ep.EPGroup(cap=T, H=cfg["H"], K=K)
+    for l in range(n_layers):
+        Ly = qwen_layer(T=(world * n_micro * T if l == 0 else 64), H=cfg["H"], E=cfg["E"], K=K, I=cfg["I"], S=cfg["S"],
+                        n_sel=cfg["n_sel"], r=cfg["r"], alpha=cfg["alpha"], seed=100 + l, device=dev)
+        W = Ly["W"]
+        if l == 0:
+            router = W["mlp.gate.weight"]
+            x_all = Ly["x"]
+            if world > 1:
+                rec = {}
+                with torch.no_grad():
+                    smelb.moe_forward(x_all[:n_micro * T], W, Ly["ex"], K, None, stats=lambda p, v, i: rec.update(i=i))
+                placement = ep.balanced_placement(torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist(),
+                                                  world)
+        else:
+            W["mlp.gate.weight"] = router
+        if world > 1:
+            shard = ep.shard_layer(Ly["ex"], Ly["lora"], rank, world, placement)
+            layers[l], loras[l] = (W, shard), shard.lora
+        else:
+            layers[l], loras[l] = (W, Ly["ex"]), Ly["lora"]
+        del Ly
+        torch.cuda.empty_cache()
+    xs = [x_all[(rank * n_micro + m) * T:(rank * n_micro + m + 1) * T].contiguous() for m in range(n_micro)]
+    del x_all
+    g = torch.Generator(device=dev).manual_seed(9 + rank)
+    gys = [torch.randn(x.shape, generator=g, device=dev).bfloat16() for x in xs]
+    block = smelb.BlockLoRA(loras)
+    params = list(block.parameters())
+    shared = [p for lo in loras.values() for p in lo.shared.parameters()]
+    runner = LayerMajorRunner(layers, range(n_layers), lora=block,
+                              layer_fn=ep_layer_fn(comm, K) if world > 1 else moe_block(K))
+    from smelb import dp
+    sync = dp.GradAllReduce(shared) if world > 1 else None
+
+    def step():
+        for p in params:
+            p.grad = None
+        runner.train_step([x.clone() for x in xs], lambda hs: ([gy.clone() for gy in gys], None))
+
+    ms_total, timing, ck, launches = _time_graph(step, args, local, world, post=sync)
+    assert smelb.read_status() == 0
+    toks = world * n_micro * T
+    res = {"metric": "layer-major block tokens/s (24 Qwen3.6-shape MoE layers, 16 micro-batches, config 5)",
+           "value": round(toks / (ms_total / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_total, 3), "higher_is_better": True, "scaling": "weak",
+           "dtype": "bf16", "data": "synthetic (seeded, random-init weights of the layer shape)",
+           "config": {"workload": "config 5: 24-layer MoE block, forward of all micro-batches then recompute + bwd",
+                      "layers": n_layers, "micro_batches": n_micro, "tokens_per_micro_batch": T,
+                      "parallelism": "single" if world == 1 else
+                      f"ep{world}: experts of every layer split over {world} GPUs (load-balanced), "
+                      f"{n_micro} micro-batches of {T} tokens per GPU (weak scaling)"},
+           "timing": timing + ("; the shared-LoRA gradient all-reduce after every replay, in the timed region"
+                               if world > 1 else ""),
+           "gpu_launches": launches, "clocks": ck}
+    torch.cuda.synchronize()
+    barrier(world)
+    if comm is not None:
+        comm.close()
     return res
 
 
@@ -655,8 +902,10 @@ def main():
                     help="layer-major forward over a stack of layers streamed from pinned host memory vs resident")
     ap.add_argument("--ce", action="store_true",
                     help="chunked cross-entropy over the Qwen3.6 LM head (one JSON line per head / chunking)")
-    ap.add_argument("--parallel", default="dp", choices=["dp", "ep"],
-                    help="with N > 1: data-parallel replicas of the layer (dp) or experts split over the GPUs (ep)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 5],
+                    help="2: the Qwen3.6 layer (default), 3: the Gemma 4 block, 5: the 24-layer layer-major block")
+    ap.add_argument("--parallel", default="ep", choices=["dp", "ep"],
+                    help="with N > 1: experts split over the GPUs (ep, the default) or data-parallel replicas (dp)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
@@ -666,6 +915,10 @@ def main():
             res = None
         elif args.impl == "reference":
             res = run_reference(args, world, rank)
+        elif args.config == 3:
+            res = run_gemma(args, local) if rank == 0 else None
+        elif args.config == 5:
+            res = run_block(args, world, rank, local)
         else:
             res = run_ours(args, world, rank, local)
         if rank == 0 and res is not None:

@@ -231,6 +231,10 @@ int smelb_frozen_experts_fwd_noalloc_status(int device, int* words, int reset);
 #define SMELB_F_SAVE 16        /* keep activations for smelb_moe_layer_bwd */
 #define SMELB_F_TOPV_FP32 32   /* topv / topv_in are fp32 (Gemma 4 routing) */
 #define SMELB_F_RECOMPUTE 64   /* backward: h / sh_h were not kept by the forward; recompute them from x / xs first */
+#define SMELB_F_EXT_DISPATCH 128 /* routed experts on a dispatch the caller built: xs, counts, gcounts, offsets, src_of,
+                                  * row_of and total are inputs (T * K dispatch entries), y (forward) and dxs
+                                  * (backward) are the outputs in dispatch order; no router, gather, combine or dX
+                                  * reduction run (the expert-parallel owner side) */
 
 typedef struct smelb_moe_layer {
   /* shapes */
@@ -298,6 +302,77 @@ typedef struct smelb_moe_layer {
   int32_t reserved;
   const void* per_expert_scale; /* bf16 [E] multiplier of the renormalised top-k weights (Gemma 4), or NULL */
 } smelb_moe_layer;
+
+/* ---------------------------------------------------------------------------------------------------- expert parallel
+ * smel/moe.py:255-263 partitioned by expert over the P ranks (GPUs) of one box; the reference itself runs on one GPU,
+ * so these entry points have no reference counterpart beyond the layer they partition. Each rank owns one region
+ * (smelb_ep_region_alloc: cudaMalloc'd here, shared by CUDA IPC; smelb_ep_region_open maps a peer's) with four
+ * exchange buffers of [P][cap][H] bf16 rows: 0 forward dispatch, 1 forward return, 2 backward dispatch, 3 backward
+ * return. A sender writes into its own region and publishes; readers pull from the sender's region and acknowledge.
+ * `regions` is a host array of the P region pointers as mapped in this process (regions[rank] its own); `cap` is
+ * the most tokens a rank brings to one call. All synchronisation is on the device (smelb_ep_sync), with bounded
+ * waits that record a status code; nothing synchronises with the host. */
+#define SMELB_EP_WAIT_DONE 0  /* sender: every reader acknowledged the buffer's previous epoch */
+#define SMELB_EP_PUBLISH 1    /* sender: publish the buffer's next epoch (its data is written) */
+#define SMELB_EP_WAIT_READY 2 /* reader: every sender published the epoch this reader expects */
+#define SMELB_EP_ACK 3        /* reader: done reading every sender's buffer of this epoch */
+int64_t smelb_ep_region_bytes(int64_t P, int64_t cap, int64_t K, int64_t H);
+int smelb_ep_region_alloc(int64_t bytes, void** region, void* ipc_handle /* 64 bytes out */);
+int smelb_ep_region_open(const void* ipc_handle, void** region);
+int smelb_ep_region_close(void* region);
+int smelb_ep_region_free(void* region);
+int smelb_ep_sync(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int op,
+                  int buffer, void* stream);
+
+/* Source side, forward: per destination rank d the tokens with at least one expert that d owns (owner[E], local id
+ * local_id[E]), in token order, de-duplicated (one row per token and destination), with their entries (local expert,
+ * k, routing weight topv[t][k], bf16 or fp32) written into buffer 0's metadata. pos [T][P]: row of token t in d's
+ * list or -1; slot_j [T][K]: slot of choice (t, k) within its row; tok_of [P][cap]: token of each row. T <= cap. */
+int smelb_ep_plan(const int64_t* topi, const void* topv, int topv_fp32, int64_t T, int64_t K, const int32_t* owner,
+                  const int32_t* local_id, const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t H,
+                  int32_t* pos, int32_t* slot_j, int32_t* tok_of, void* stream);
+
+/* Source side: rows[buffer][d][i] = src[tok_of[d][i]] (buffer 0: token rows, 2: upstream gradient rows). */
+int smelb_ep_pack_rows(const void* src, int64_t H, const int32_t* tok_of, const void* const* regions, int64_t P,
+                       int64_t rank, int64_t cap, int64_t K, int buffer, void* stream);
+
+/* Owner side: the dispatch entries every source sent (buffer 0), numbered in (source, row, slot) order: entry_e
+ * (int64 [cap_entries], the local expert, `sink` past the received entries), entry_row (source row s * cap + i),
+ * entry_w (routing weight); per source row its first entry and entry count (row_beg, row_m [P][cap]); rows received
+ * per source (recv_rows [P]); n_total [1]. More than cap_entries entries record a status code. */
+int smelb_ep_recv_plan(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H,
+                       int64_t cap_entries, int64_t sink, int64_t* entry_e, int32_t* entry_row, float* entry_w,
+                       int32_t* row_beg, int32_t* row_m, int32_t* recv_rows, int32_t* n_total, void* stream);
+
+/* Owner side: local [P][cap][H] = every source's rows of buffer 0 or 2 addressed to this rank (one NVLink pull per
+ * row). */
+int smelb_ep_pull_rows(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H,
+                       int buffer, void* local, void* stream);
+
+/* Owner side: xs[row] = local[entry_row[src_of[row]]] for the dispatch rows before offsets[sink] (zeros on padding
+ * rows), the dispatch plan being smelb_dispatch_plan_ws over entry_e with E = sink + 1. */
+int smelb_ep_gather(const void* local, const int32_t* entry_row, const int32_t* src_of, const int32_t* offsets,
+                    int64_t sink, int64_t H, int64_t max_rows, void* xs, void* stream);
+
+/* Owner side: per received row, forward (backward = 0): sum over its entries of entry_w * y[row_of[entry]] (fp32,
+ * slot order, rounded to bf16) into buffer 1; backward: the entries' dX rows y = dxs summed into buffer 3 and each
+ * entry's d weight entry_dw into buffer 3's metadata. H % 256 == 0. */
+int smelb_ep_return(const void* y, const int32_t* row_of, const float* entry_w, const float* entry_dw,
+                    const int32_t* row_beg, const int32_t* row_m, const int32_t* recv_rows, const void* const* regions,
+                    int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int backward, void* stream);
+
+/* Owner side, backward: dy[row] = bf16(g * w) of each dispatch row's entry (g: the pulled gradient rows, local) and
+ * entry_dw[entry] = sum_h g[h] * y[row][h] in fp32 (y: the forward's expert outputs in dispatch order). */
+int smelb_ep_dy(const void* g_local, const int32_t* entry_row, const float* entry_w, const int32_t* src_of,
+                const int32_t* offsets, int64_t sink, int64_t H, int64_t max_rows, const void* y, void* dy,
+                float* entry_dw, void* stream);
+
+/* Source side: out[t] = bf16(sum over destinations in rank order of the returned row (buffer 1, or 3 when backward)
+ * at pos[t][d], in fp32, + add[t] when add is given); backward also dtopv[t][k] (bf16, or fp32 if dtopv_fp32) from
+ * the owner's per-entry d weights. */
+int smelb_ep_collect(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int64_t T,
+                     const int32_t* pos, const void* add, int backward, const int64_t* topi, const int32_t* owner,
+                     const int32_t* slot_j, void* dtopv, int dtopv_fp32, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------- int8 rows
  * smel/quant.py:97-105 quantize_int8_rows / dequant_int8_rows: symmetric int8 per row of w (bf16, or fp32 when

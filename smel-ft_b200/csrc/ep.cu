@@ -1,0 +1,660 @@
+// Expert-parallel exchange of the MoE layer over peer memory (NVLink), with the C ABI of include/smelb.h.
+//
+// Every rank of an expert-parallel group owns one region of device memory (cudaMalloc'd by the library, mapped into
+// every peer by CUDA IPC). A rank is the source of its own tokens and the owner of its share of the experts. Per
+// layer call there are four exchanges, each through its own buffer b of the region:
+//   b = 0  forward dispatch: the source's token rows, de-duplicated per destination (a token goes once to each rank
+//          that owns at least one of its experts), with the (local expert, k, weight) entries of every row
+//   b = 1  forward return: per received row, the owner's partial combine sum_j weight_j * y_j over its entries
+//   b = 2  backward dispatch: the upstream gradient rows of the same token rows
+//   b = 3  backward return: per received row the summed dX of its entries, and d weight per entry
+// A sender writes into its own region and publishes; the readers pull from the sender's region and acknowledge. The
+// synchronisation is device-side (epoch counters per buffer, release / acquire at system scope), so a whole layer
+// step can be captured in a CUDA graph and no call synchronises with the host. Every wait is bounded: after
+// SMELB_WAIT_NS it records kDevErrEpWait in the status word and returns.
+#include <cstring>
+
+#include "../../include/smelb.h"
+#include "common.cuh"
+#include "host.h"
+#include "kernels.h"
+
+namespace smelb {
+
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpMaxK = 16;
+constexpr int kDevErrEpWait = 13;     // a peer's flag did not arrive in time
+constexpr int kDevErrEpCapacity = 14; // more dispatch entries than the owner's capacity
+
+// ------------------------------------------------------------------------------------------ region layout
+struct EpLayout {
+  size_t ready, done, send_epoch, recv_epoch, counts, nent, meta, wts, eoff, dwts, rows[4], total;
+};
+
+static size_t ep_al(size_t x) { return (x + 255) & ~size_t(255); }
+
+static EpLayout ep_layout(int P, int cap, int K, int H) {
+  EpLayout L{};
+  L.ready = 0;                       // u32 [4]: last published epoch of each buffer
+  L.done = 64;                       // u32 [4][kEpMaxRanks]: epoch each reader has finished reading
+  L.send_epoch = 256;                // u32 [4] (local)
+  L.recv_epoch = 320;                // u32 [4] (local)
+  L.counts = 512;                    // int [4][kEpMaxRanks]: rows per destination
+  L.nent = 768;                      // int [kEpMaxRanks]: dispatch entries per destination
+  size_t o = 1024;
+  const size_t rk = (size_t)P * cap * K;
+  L.meta = o;  o += ep_al(rk * 4);   // int [P][cap][K]: local expert | k << 16, -1 after a row's entries
+  L.wts = o;   o += ep_al(rk * 4);   // f32 [P][cap][K]: routing weight of each entry
+  L.eoff = o;  o += ep_al((size_t)P * cap * 4);  // int [P][cap]: first entry of each row among the destination's
+  L.dwts = o;  o += ep_al(rk * 4);   // f32 [P][cap][K]: backward return, d weight of each entry
+  for (int b = 0; b < 4; ++b) {
+    L.rows[b] = o;
+    o += ep_al((size_t)P * cap * H * 2);  // bf16 [P][cap][H]
+  }
+  L.total = o;
+  return L;
+}
+
+struct EpPeers {
+  char* base[kEpMaxRanks];
+};
+
+// ------------------------------------------------------------------------------------------ flags
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// bounded wait until *p >= want (monotonic epoch); false after SMELB_WAIT_NS (status recorded)
+__device__ bool ep_wait_ge(const uint32_t* p, uint32_t want, int* err, int who) {
+  if (ld_acquire_sys(p) >= want) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t ns = 32;
+  while (ld_acquire_sys(p) < want) {
+    if (globaltimer_ns() - t0 > SMELB_WAIT_NS) {
+      dev_fail_at(err, kDevErrEpWait, who, (int)want);
+      return false;
+    }
+    __nanosleep(ns);
+    ns = ns < 1024 ? 2 * ns : ns;
+  }
+  return true;
+}
+
+// sender: every reader (all ranks, itself included) has acknowledged the previous epoch of buffer b
+__global__ void ep_wait_done_kernel(char* mine, EpLayout L, int P, int b, int* err) {
+  const int d = threadIdx.x;
+  if (d >= P) return;
+  const uint32_t* done = reinterpret_cast<const uint32_t*>(mine + L.done) + b * kEpMaxRanks;
+  const uint32_t want = reinterpret_cast<const uint32_t*>(mine + L.send_epoch)[b];
+  ep_wait_ge(done + d, want, err, 100 * b + d);
+}
+
+// sender: the buffer's data (written by earlier kernels of the stream) is complete; publish the next epoch
+__global__ void ep_publish_kernel(char* mine, EpLayout L, int b) {
+  __threadfence_system();
+  uint32_t* ep = reinterpret_cast<uint32_t*>(mine + L.send_epoch) + b;
+  const uint32_t e = *ep + 1;
+  *ep = e;
+  st_release_sys(reinterpret_cast<uint32_t*>(mine + L.ready) + b, e);
+}
+
+// reader: every source has published the epoch this reader expects next
+__global__ void ep_wait_ready_kernel(EpPeers peers, char* mine, EpLayout L, int P, int b, int* err) {
+  const int s = threadIdx.x;
+  if (s >= P) return;
+  const uint32_t want = reinterpret_cast<const uint32_t*>(mine + L.recv_epoch)[b] + 1;
+  ep_wait_ge(reinterpret_cast<const uint32_t*>(peers.base[s] + L.ready) + b, want, err, 1000 + 100 * b + s);
+}
+
+// reader: done reading every source's buffer b of this epoch
+__global__ void ep_ack_kernel(EpPeers peers, char* mine, EpLayout L, int P, int rank, int b) {
+  __shared__ uint32_t e;
+  if (threadIdx.x == 0) e = reinterpret_cast<const uint32_t*>(mine + L.recv_epoch)[b] + 1;
+  __syncthreads();
+  __threadfence_system();
+  const int s = threadIdx.x;
+  if (s < P) st_release_sys(reinterpret_cast<uint32_t*>(peers.base[s] + L.done) + b * kEpMaxRanks + rank, e);
+  __syncthreads();
+  if (threadIdx.x == 0) reinterpret_cast<uint32_t*>(mine + L.recv_epoch)[b] = e;
+}
+
+// ------------------------------------------------------------------------------------------ block scan
+// exclusive scan of (a, b) over a 1024-thread block; returns the block totals in tot_a / tot_b
+__device__ __forceinline__ void scan2(int a, int b, int& ex_a, int& ex_b, int& tot_a, int& tot_b) {
+  __shared__ int wa[32], wb[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int ia = a, ib = b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ta = __shfl_up_sync(0xffffffffu, ia, o), tb = __shfl_up_sync(0xffffffffu, ib, o);
+    if (lane >= o) {
+      ia += ta;
+      ib += tb;
+    }
+  }
+  __syncthreads();  // wa / wb may still be read by the previous scan
+  if (lane == 31) {
+    wa[w] = ia;
+    wb[w] = ib;
+  }
+  __syncthreads();
+  if (w == 0) {
+    int va = lane < (int)(blockDim.x >> 5) ? wa[lane] : 0, vb = lane < (int)(blockDim.x >> 5) ? wb[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ta = __shfl_up_sync(0xffffffffu, va, o), tb = __shfl_up_sync(0xffffffffu, vb, o);
+      if (lane >= o) {
+        va += ta;
+        vb += tb;
+      }
+    }
+    wa[lane] = va;
+    wb[lane] = vb;
+  }
+  __syncthreads();
+  const int pa = w ? wa[w - 1] : 0, pb = w ? wb[w - 1] : 0;
+  ex_a = pa + ia - a;
+  ex_b = pb + ib - b;
+  tot_a = wa[(blockDim.x >> 5) - 1];
+  tot_b = wb[(blockDim.x >> 5) - 1];
+}
+
+// ------------------------------------------------------------------------------------------ source side
+// One block per destination d: the tokens with at least one expert owned by d, in token order (so the exchange is
+// deterministic), their row position pos[t][d], the row's entries (local expert id and k, in k order) with their
+// routing weights, the entry offset of every row and the slot j of every choice (t, k) within its row.
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const long long* __restrict__ topi, const void* __restrict__ topv,
+                                                       int topv_f32, int T, int K, const int* __restrict__ owner,
+                                                       const int* __restrict__ local_id, int P, int cap, char* mine,
+                                                       EpLayout L, int* __restrict__ pos, int* __restrict__ slot_j,
+                                                       int* __restrict__ tok_of) {
+  const int d = blockIdx.x;
+  int* meta = reinterpret_cast<int*>(mine + L.meta);
+  float* wts = reinterpret_cast<float*>(mine + L.wts);
+  int* eoff = reinterpret_cast<int*>(mine + L.eoff);
+  int carry_r = 0, carry_e = 0;
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    int m = 0;
+    if (t < T)
+      for (int k = 0; k < K; ++k) m += owner[topi[(long long)t * K + k]] == d;
+    int pr, pe, tr, te;
+    scan2(m > 0, m, pr, pe, tr, te);
+    if (t < T) {
+      if (m > 0) {
+        const int p = carry_r + pr;
+        const long long row = (long long)d * cap + p;
+        tok_of[row] = t;
+        pos[(long long)t * P + d] = p;
+        eoff[row] = carry_e + pe;
+        int j = 0;
+        for (int k = 0; k < K; ++k) {
+          const long long e = topi[(long long)t * K + k];
+          if (owner[e] != d) continue;
+          meta[row * K + j] = local_id[e] | (k << 16);
+          wts[row * K + j] = topv_f32 ? reinterpret_cast<const float*>(topv)[(long long)t * K + k]
+                                      : __bfloat162float(reinterpret_cast<const bf16*>(topv)[(long long)t * K + k]);
+          slot_j[(long long)t * K + k] = j;
+          ++j;
+        }
+        for (; j < K; ++j) meta[row * K + j] = -1;
+      } else {
+        pos[(long long)t * P + d] = -1;
+      }
+    }
+    carry_r += tr;
+    carry_e += te;
+  }
+  if (threadIdx.x == 0) {
+    reinterpret_cast<int*>(mine + L.counts)[d] = carry_r;
+    reinterpret_cast<int*>(mine + L.nent)[d] = carry_e;
+  }
+}
+
+// rows[b][d][i] = src[tok_of[d][i]] for the rows of every destination (16-byte copies); counts[b] = counts[0]
+__global__ void ep_pack_rows_kernel(const bf16* __restrict__ src, int H, const int* __restrict__ tok_of, int P,
+                                    int cap, char* mine, EpLayout L, int b) {
+  const int* cnt = reinterpret_cast<const int*>(mine + L.counts);
+  const int vpr = H / 8;
+  const long long n = (long long)P * cap * vpr;
+  uint4* dst = reinterpret_cast<uint4*>(mine + L.rows[b]);
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
+    const long long row = v / vpr;
+    const int d = (int)(row / cap), i = (int)(row - (long long)d * cap);
+    if (i >= cnt[d]) continue;
+    const int c = (int)(v - row * vpr);
+    dst[v] = reinterpret_cast<const uint4*>(src + (long long)tok_of[row] * H)[c];
+  }
+  if (b != 0 && blockIdx.x == 0 && threadIdx.x < P)
+    reinterpret_cast<int*>(mine + L.counts)[b * kEpMaxRanks + threadIdx.x] = cnt[threadIdx.x];
+}
+
+// ------------------------------------------------------------------------------------------ owner side
+// One block per source s: the rows s sent to this rank and their dispatch entries, numbered in (source, row, slot)
+// order: entry n of row (s, i) slot j is base_s + eoff + j. Writes per entry its local expert (int64, the dispatch
+// plan's input), source row (s * cap + i) and weight; per row its first entry and entry count; per source its row
+// count.
+__global__ void __launch_bounds__(1024) ep_recv_plan_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int K,
+                                                            long long cap_e, long long* __restrict__ entry_e,
+                                                            int* __restrict__ entry_row, float* __restrict__ entry_w,
+                                                            int* __restrict__ row_beg, int* __restrict__ row_m,
+                                                            int* __restrict__ rc, int* __restrict__ n_total, int* err) {
+  const int s = blockIdx.x;
+  const char* src = peers.base[s];
+  const int c = reinterpret_cast<const int*>(src + L.counts)[rank];
+  long long base = 0, total = 0;
+  for (int q = 0; q < P; ++q) {
+    const int ne = reinterpret_cast<const int*>(peers.base[q] + L.nent)[rank];
+    if (q < s) base += ne;
+    total += ne;
+  }
+  if (threadIdx.x == 0) {
+    rc[s] = c;
+    if (s == 0) *n_total = (int)(total < cap_e ? total : cap_e);
+    if (s == 0 && total > cap_e) dev_fail_at(err, kDevErrEpCapacity, (int)total, (int)cap_e);
+  }
+  const int* meta = reinterpret_cast<const int*>(src + L.meta) + (long long)rank * cap * K;
+  const float* wts = reinterpret_cast<const float*>(src + L.wts) + (long long)rank * cap * K;
+  const int* eoff = reinterpret_cast<const int*>(src + L.eoff) + (long long)rank * cap;
+  for (int i = threadIdx.x; i < c; i += blockDim.x) {
+    const long long beg = base + eoff[i];
+    int m = 0;
+    for (int j = 0; j < K; ++j) {
+      const int mt = meta[(long long)i * K + j];
+      if (mt < 0) break;
+      const long long nn = beg + j;
+      if (nn < cap_e) {
+        entry_e[nn] = mt & 0xFFFF;
+        entry_row[nn] = s * cap + i;
+        entry_w[nn] = wts[(long long)i * K + j];
+      }
+      ++m;
+    }
+    row_beg[(long long)s * cap + i] = (int)(beg < cap_e ? beg : cap_e);
+    row_m[(long long)s * cap + i] = (int)(beg + m <= cap_e ? m : (beg < cap_e ? cap_e - beg : 0));  // kept entries
+  }
+}
+
+// entries past the received ones go to the sink expert, whose dispatch segment no GEMM reads
+__global__ void ep_fill_sink_kernel(long long* __restrict__ entry_e, long long cap_e, const int* __restrict__ n_total,
+                                    int sink) {
+  const int n0 = *n_total;
+  for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < cap_e; n += (long long)gridDim.x * blockDim.x)
+    if (n >= n0) entry_e[n] = sink;
+}
+
+// local[s][i] = source s's rows[b][rank][i] for its rows (the one pull over NVLink per row and exchange)
+__global__ void ep_pull_rows_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int H, int b,
+                                    bf16* __restrict__ local) {
+  const int vpr = H / 8;
+  const long long n = (long long)P * cap * vpr;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
+    const long long row = v / vpr;
+    const int s = (int)(row / cap), i = (int)(row - (long long)s * cap);
+    const char* src = peers.base[s];
+    if (i >= reinterpret_cast<const int*>(src + L.counts)[b * kEpMaxRanks + rank]) continue;
+    const int c = (int)(v - row * vpr);
+    const uint4* r = reinterpret_cast<const uint4*>(src + L.rows[b]) + ((long long)rank * cap + i) * vpr;
+    reinterpret_cast<uint4*>(local)[v] = r[c];
+  }
+}
+
+// xs[row] = local[entry_row[src_of[row]]] for the dispatch rows before the sink segment (zeros on padding rows)
+__global__ void ep_gather_kernel(const bf16* __restrict__ local, const int* __restrict__ entry_row,
+                                 const int* __restrict__ src_of, const int* __restrict__ offsets, int sink, int H,
+                                 bf16* __restrict__ xs) {
+  const int rows = offsets[sink];
+  const int vpr = H / 8;
+  const long long n = (long long)rows * vpr;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
+    const long long row = v / vpr;
+    const int c = (int)(v - row * vpr);
+    const int e = src_of[row];
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (e >= 0) val = reinterpret_cast<const uint4*>(local + (long long)entry_row[e] * H)[c];
+    reinterpret_cast<uint4*>(xs)[v] = val;
+  }
+}
+
+// One warp per received row (s, i): sum over its entries of w * y[row_of[entry]] (fp32, slot order) -> bf16 into this
+// rank's rows[1][s][i]; counts[1][s] = rows received from s. Backward (bwd != 0): the entries' dX rows summed into
+// rows[3] and each entry's d weight into dwts[s][i][j].
+__global__ void ep_return_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
+                                 const float* __restrict__ entry_w, const float* __restrict__ entry_dw,
+                                 const int* __restrict__ row_beg, const int* __restrict__ row_m, const int* __restrict__ rc,
+                                 int P, int cap, int K, int H, char* mine, EpLayout L, int bwd) {
+  const int b = bwd ? 3 : 1;
+  const int lane = threadIdx.x & 31;
+  const long long nw = (long long)P * cap;
+  bf16* out = reinterpret_cast<bf16*>(mine + L.rows[b]);
+  for (long long wr = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; wr < nw;
+       wr += ((long long)gridDim.x * blockDim.x) >> 5) {
+    const int s = (int)(wr / cap), i = (int)(wr - (long long)s * cap);
+    if (i >= rc[s]) continue;
+    const int beg = row_beg[wr], m = row_m[wr];
+    if (bwd && lane < m) reinterpret_cast<float*>(mine + L.dwts)[wr * K + lane] = entry_dw[beg + lane];
+    for (int c0 = lane * 8; c0 < H; c0 += 256) {
+      float acc[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+      for (int j = 0; j < m; ++j) {
+        const float w = bwd ? 1.0f : entry_w[beg + j];
+        const uint4 v = *reinterpret_cast<const uint4*>(y + (long long)row_of[beg + j] * H + c0);
+        const bf16* pv = reinterpret_cast<const bf16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(__bfloat162float(pv[q]), w, acc[q]);
+      }
+      uint4 o;
+      bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
+      *reinterpret_cast<uint4*>(out + wr * H + c0) = o;
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < P) reinterpret_cast<int*>(mine + L.counts)[b * kEpMaxRanks + threadIdx.x] =
+                                              rc[threadIdx.x];
+}
+
+// One warp per dispatch row before the sink segment: dy[row] = bf16(g * w) of the entry's pulled gradient row and the
+// entry's d weight sum_h g[h] * y[row][h] (fp32), the backward of the owner's share of smel/moe.py:248-252.
+__global__ void ep_dy_kernel(const bf16* __restrict__ g_local, const int* __restrict__ entry_row,
+                             const float* __restrict__ entry_w, const int* __restrict__ src_of,
+                             const int* __restrict__ offsets, int sink, int H, const bf16* __restrict__ y,
+                             bf16* __restrict__ dy, float* __restrict__ entry_dw) {
+  const int rows = offsets[sink];
+  const int lane = threadIdx.x & 31;
+  for (long long row = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((long long)gridDim.x * blockDim.x) >> 5) {
+    const int e = src_of[row];
+    float dot = 0.f;
+    const float w = e >= 0 ? entry_w[e] : 0.f;
+    const bf16* gr = e >= 0 ? g_local + (long long)entry_row[e] * H : nullptr;
+    for (int c0 = lane * 8; c0 < H; c0 += 256) {
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (e >= 0) {
+        const uint4 gv = *reinterpret_cast<const uint4*>(gr + c0);
+        const uint4 yv = *reinterpret_cast<const uint4*>(y + row * H + c0);
+        const bf16 *pg = reinterpret_cast<const bf16*>(&gv), *py = reinterpret_cast<const bf16*>(&yv);
+        bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float gf = __bfloat162float(pg[q]);
+          po[q] = __float2bfloat16_rn(gf * w);
+          dot = fmaf(gf, __bfloat162float(py[q]), dot);
+        }
+      }
+      *reinterpret_cast<uint4*>(dy + row * H + c0) = o;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (lane == 0 && e >= 0) entry_dw[e] = dot;
+  }
+}
+
+// ------------------------------------------------------------------------------------------ source side, returns
+// One warp per token: out[t] = bf16(sum over destinations d in rank order of the returned row rows[1 or 3][rank]
+// [pos[t][d]] from d's region (fp32) + add[t]); backward also dtopv[t][k] = d's dwts[rank][pos][slot_j[t][k]].
+__global__ void ep_collect_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int K, int H, int T,
+                                  const int* __restrict__ pos, const bf16* __restrict__ add, int bwd,
+                                  const long long* __restrict__ topi, const int* __restrict__ owner,
+                                  const int* __restrict__ slot_j, void* __restrict__ dtopv, int dtopv_f32,
+                                  bf16* __restrict__ out) {
+  const int b = bwd ? 3 : 1;
+  const int lane = threadIdx.x & 31;
+  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T;
+       t += ((long long)gridDim.x * blockDim.x) >> 5) {
+    int pt[kEpMaxRanks];
+#pragma unroll
+    for (int d = 0; d < kEpMaxRanks; ++d) pt[d] = d < P ? pos[t * P + d] : -1;
+    for (int c0 = lane * 8; c0 < H; c0 += 256) {
+      float acc[8];
+      if (add) {
+        const uint4 av = *reinterpret_cast<const uint4*>(add + t * H + c0);
+        const bf16* pa = reinterpret_cast<const bf16*>(&av);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+      }
+#pragma unroll
+      for (int d = 0; d < kEpMaxRanks; ++d) {
+        if (pt[d] < 0) continue;
+        const bf16* r = reinterpret_cast<const bf16*>(peers.base[d] + L.rows[b]) + ((long long)rank * cap + pt[d]) * H;
+        const uint4 v = *reinterpret_cast<const uint4*>(r + c0);
+        const bf16* pv = reinterpret_cast<const bf16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
+      }
+      uint4 o;
+      bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
+      *reinterpret_cast<uint4*>(out + t * H + c0) = o;
+    }
+    if (bwd && lane < K) {
+      const int d = owner[topi[t * K + lane]];
+      const float dw = reinterpret_cast<const float*>(peers.base[d] + L.dwts)[((long long)rank * cap + pt[d]) * K +
+                                                                              slot_j[t * K + lane]];
+      if (dtopv_f32) reinterpret_cast<float*>(dtopv)[t * K + lane] = dw;
+      else reinterpret_cast<bf16*>(dtopv)[t * K + lane] = __float2bfloat16_rn(dw);
+    }
+  }
+}
+
+static int ep_grid(long long work, int threads) {
+  return (int)std::min<long long>(std::max<long long>((work + threads - 1) / threads, 1), 148LL * 16);
+}
+
+static int ep_peers(const void* const* bases, int P, EpPeers& pr) {
+  SMELB_CHECK_ARG(P >= 1 && P <= kEpMaxRanks, kErrShape, "ep: %d ranks (1..%d)", P, kEpMaxRanks);
+  memset(&pr, 0, sizeof(pr));
+  for (int s = 0; s < P; ++s) {
+    SMELB_CHECK_ARG(bases[s] != nullptr, kErrArg, "ep: null region of rank %d", s);
+    pr.base[s] = (char*)bases[s];
+  }
+  return kOk;
+}
+
+}  // namespace smelb
+
+using namespace smelb;
+
+// ================================================================================================== C ABI
+extern "C" {
+
+int64_t smelb_ep_region_bytes(int64_t P, int64_t cap, int64_t K, int64_t H) {
+  if (P < 1 || P > kEpMaxRanks || cap < 1 || K < 1 || K > kEpMaxK || H < 8) return 0;
+  return (int64_t)ep_layout((int)P, (int)cap, (int)K, (int)H).total;
+}
+
+int smelb_ep_region_alloc(int64_t bytes, void** region, void* ipc_handle) {
+  SMELB_CHECK_ARG(region && ipc_handle && bytes > 0, kErrArg, "ep_region_alloc: bad arguments");
+  void* p = nullptr;
+  SMELB_CUDA(cudaMalloc(&p, (size_t)bytes));
+  SMELB_CUDA(cudaMemset(p, 0, (size_t)bytes));
+  cudaIpcMemHandle_t h;
+  SMELB_CUDA(cudaIpcGetMemHandle(&h, p));
+  memcpy(ipc_handle, &h, sizeof(h));
+  *region = p;
+  return kOk;
+}
+
+int smelb_ep_region_open(const void* ipc_handle, void** region) {
+  SMELB_CHECK_ARG(region && ipc_handle, kErrArg, "ep_region_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  SMELB_CUDA(cudaIpcOpenMemHandle(region, h, cudaIpcMemLazyEnablePeerAccess));
+  return kOk;
+}
+
+int smelb_ep_region_close(void* region) {
+  SMELB_CUDA(cudaIpcCloseMemHandle(region));
+  return kOk;
+}
+
+int smelb_ep_region_free(void* region) {
+  SMELB_CUDA(cudaFree(region));
+  return kOk;
+}
+
+int smelb_ep_sync(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int op,
+                  int buffer, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(rank >= 0 && rank < P && buffer >= 0 && buffer < 4 && op >= 0 && op < 4, kErrArg,
+                  "ep_sync: rank %lld buffer %d op %d", (long long)rank, buffer, op);
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  int* err = device_status(dev);
+  SMELB_CHECK_ARG(err != nullptr, kErrCuda, "ep_sync: no device status word");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  char* mine = pr.base[rank];
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (op) {
+    case SMELB_EP_WAIT_DONE: ep_wait_done_kernel<<<1, 32, 0, st>>>(mine, L, (int)P, buffer, err); break;
+    case SMELB_EP_PUBLISH: ep_publish_kernel<<<1, 1, 0, st>>>(mine, L, buffer); break;
+    case SMELB_EP_WAIT_READY: ep_wait_ready_kernel<<<1, 32, 0, st>>>(pr, mine, L, (int)P, buffer, err); break;
+    default: ep_ack_kernel<<<1, 32, 0, st>>>(pr, mine, L, (int)P, (int)rank, buffer); break;
+  }
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_plan(const int64_t* topi, const void* topv, int topv_fp32, int64_t T, int64_t K, const int32_t* owner,
+                  const int32_t* local_id, const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t H,
+                  int32_t* pos, int32_t* slot_j, int32_t* tok_of, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(topi && topv && owner && local_id && pos && slot_j && tok_of, kErrArg, "ep_plan: null pointer");
+  SMELB_CHECK_ARG(T >= 0 && T <= cap && K >= 1 && K <= kEpMaxK && rank >= 0 && rank < P, kErrShape,
+                  "ep_plan: T=%lld cap=%lld K=%lld", (long long)T, (long long)cap, (long long)K);
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  ep_plan_kernel<<<(int)P, 1024, 0, (cudaStream_t)stream>>>((const long long*)topi, topv, topv_fp32, (int)T, (int)K,
+                                                             owner, local_id, (int)P, (int)cap, pr.base[rank], L, pos,
+                                                             slot_j, tok_of);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_pack_rows(const void* src, int64_t H, const int32_t* tok_of, const void* const* regions, int64_t P,
+                       int64_t rank, int64_t cap, int64_t K, int buffer, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(src && tok_of && (buffer == 0 || buffer == 2) && H % 8 == 0, kErrArg, "ep_pack_rows: bad arguments");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  ep_pack_rows_kernel<<<ep_grid(P * cap * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)src, (int)H, tok_of, (int)P, (int)cap, pr.base[rank], L, buffer);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_recv_plan(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H,
+                       int64_t cap_entries, int64_t sink, int64_t* entry_e, int32_t* entry_row, float* entry_w,
+                       int32_t* row_beg, int32_t* row_m, int32_t* recv_rows, int32_t* n_total, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(entry_e && entry_row && entry_w && row_beg && row_m && recv_rows && n_total && cap_entries > 0,
+                  kErrArg, "ep_recv_plan: bad arguments");
+  int dev = 0;
+  SMELB_CUDA(cudaGetDevice(&dev));
+  int* err = device_status(dev);
+  SMELB_CHECK_ARG(err != nullptr, kErrCuda, "ep_recv_plan: no device status word");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  cudaStream_t st = (cudaStream_t)stream;
+  ep_recv_plan_kernel<<<(int)P, 1024, 0, st>>>(pr, L, (int)P, (int)rank, (int)cap, (int)K, cap_entries, (long long*)entry_e,
+                                               entry_row, entry_w, row_beg, row_m, recv_rows, n_total, err);
+  SMELB_CUDA(cudaGetLastError());
+  ep_fill_sink_kernel<<<ep_grid(cap_entries, 256), 256, 0, st>>>((long long*)entry_e, cap_entries, n_total, (int)sink);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_pull_rows(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H,
+                       int buffer, void* local, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(local && (buffer == 0 || buffer == 2) && H % 8 == 0, kErrArg, "ep_pull_rows: bad arguments");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  ep_pull_rows_kernel<<<ep_grid(P * cap * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(pr, L, (int)P, (int)rank,
+                                                                                         (int)cap, (int)H, buffer,
+                                                                                         (bf16*)local);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_gather(const void* local, const int32_t* entry_row, const int32_t* src_of, const int32_t* offsets,
+                    int64_t sink, int64_t H, int64_t max_rows, void* xs, void* stream) {
+  SMELB_CHECK_ARG(local && entry_row && src_of && offsets && xs && H % 8 == 0, kErrArg, "ep_gather: bad arguments");
+  ep_gather_kernel<<<ep_grid(max_rows * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)local, entry_row, src_of, offsets, (int)sink, (int)H, (bf16*)xs);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_return(const void* y, const int32_t* row_of, const float* entry_w, const float* entry_dw,
+                    const int32_t* row_beg, const int32_t* row_m, const int32_t* recv_rows, const void* const* regions,
+                    int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int backward, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(y && row_of && row_beg && row_m && recv_rows && (backward ? entry_dw != nullptr : entry_w != nullptr) &&
+                      H % 256 == 0,
+                  kErrArg, "ep_return: bad arguments (H a multiple of 256)");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  ep_return_kernel<<<ep_grid(P * cap * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)y, row_of, entry_w, entry_dw, row_beg, row_m, recv_rows, (int)P, (int)cap, (int)K, (int)H,
+      pr.base[rank], L, backward != 0);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_dy(const void* g_local, const int32_t* entry_row, const float* entry_w, const int32_t* src_of,
+                const int32_t* offsets, int64_t sink, int64_t H, int64_t max_rows, const void* y, void* dy,
+                float* entry_dw, void* stream) {
+  SMELB_CHECK_ARG(g_local && entry_row && entry_w && src_of && offsets && y && dy && entry_dw && H % 256 == 0, kErrArg,
+                  "ep_dy: bad arguments (H a multiple of 256)");
+  ep_dy_kernel<<<ep_grid(max_rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)g_local, entry_row, entry_w, src_of, offsets, (int)sink, (int)H, (const bf16*)y, (bf16*)dy,
+      entry_dw);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+int smelb_ep_collect(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int64_t T,
+                     const int32_t* pos, const void* add, int backward, const int64_t* topi, const int32_t* owner,
+                     const int32_t* slot_j, void* dtopv, int dtopv_fp32, void* out, void* stream) {
+  EpPeers pr;
+  const int rc = ep_peers(regions, (int)P, pr);
+  if (rc != kOk) return rc;
+  SMELB_CHECK_ARG(pos && out && H % 256 == 0 && (!backward || (topi && owner && slot_j && dtopv)), kErrArg,
+                  "ep_collect: bad arguments (H a multiple of 256)");
+  const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
+  ep_collect_kernel<<<ep_grid(T * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      pr, L, (int)P, (int)rank, (int)cap, (int)K, (int)H, (int)T, pos, (const bf16*)add, backward != 0,
+      (const long long*)topi, owner, slot_j, dtopv, dtopv_fp32, (bf16*)out);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
+
+}  // extern "C"

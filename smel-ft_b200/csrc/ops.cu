@@ -203,7 +203,7 @@ int pack_bwd(const LoraSet& L, void* dz_w, void* da_ext, void* dxa_w, void* dx_e
 }
 
 struct Flags {
-  bool router, routed, shared, sgate, save, topv32, sel, sel_lora, sh_lora, fz_bf16, recompute;
+  bool router, routed, shared, sgate, save, topv32, sel, sel_lora, sh_lora, fz_bf16, recompute, ext;
 };
 
 int check_layer(const smelb_moe_layer& L, Flags& f) {
@@ -218,6 +218,9 @@ int check_layer(const smelb_moe_layer& L, Flags& f) {
   f.sh_lora = f.shared && L.r_sh > 0;
   f.fz_bf16 = L.gu_q == nullptr && L.fz_gu != nullptr;
   f.recompute = L.flags & SMELB_F_RECOMPUTE;
+  f.ext = L.flags & SMELB_F_EXT_DISPATCH;
+  SMELB_CHECK_ARG(!f.ext || (f.routed && !f.router && !f.shared), kErrArg,
+                  "layer: an external dispatch is for the routed experts alone");
   SMELB_CHECK_ARG(L.T >= 0 && L.H > 0 && L.H % 64 == 0, kErrShape, "layer: H=%lld must be a multiple of 64",
                   (long long)L.H);
   SMELB_CHECK_ARG(L.act == SMELB_ACT_SILU || L.act == SMELB_ACT_GELU_TANH, kErrArg, "layer: unknown activation %d",
@@ -358,7 +361,7 @@ int layer_fwd(const smelb_moe_layer& L) {
   const void* topv = f.router ? L.topv : L.topv_in;
   const long long* topi = (const long long*)(f.router ? L.topi : L.topi_in);
 
-  if (f.routed) {
+  if (f.routed && !f.ext) {
     // the dispatch buffer xs is written only by the gather that follows, so the plan may use it as scratch
     TRY(dispatch_plan_mt(topi, (long long)T * K, E, L.sel_mask, 64, L.counts, L.gcounts, L.offsets, L.row_of,
                          L.src_of, (long long*)L.order, L.total, (int*)L.xs, (long long)R * H / 2, st));
@@ -436,7 +439,7 @@ int layer_fwd(const smelb_moe_layer& L) {
     }
     TRY(b.launch(st));
   }
-  if (f.routed || f.shared)
+  if ((f.routed || f.shared) && !f.ext)
     TRY(combine_fwd(f.routed ? L.y : nullptr, L.row_of, topv, f.topv32, T, K, H, f.shared ? L.sh_y : nullptr,
                     f.sgate ? L.sgate_logit : nullptr, L.out, st));
   return kOk;
@@ -471,7 +474,7 @@ int layer_bwd(const smelb_moe_layer& L) {
     if (f.routed) TRY(add_routed_glu(b, L, f, L.h));
     TRY(b.launch(st));
   }
-  if (f.routed)
+  if (f.routed && !f.ext)
     TRY(combine_bwd_rows(L.g, L.y, L.src_of, L.total, R, topv, f.topv32, K, H, L.dy, L.dtopv, st));
   const void* sh_dy = L.g;
   if (f.sgate) {
@@ -661,6 +664,7 @@ int layer_bwd(const smelb_moe_layer& L) {
     }
     TRY(b.launch(st));
   }
+  if (f.ext) return kOk;  // the caller reduces dxs (dispatch order) itself
   TRY(dx_reduce(f.routed ? L.dxs : nullptr, L.row_of, K, T, H, f.shared ? L.sh_dx : nullptr,
                 f.router ? L.dx_router : nullptr, f.sgate ? L.dgl : nullptr, L.w_sgate, L.dx, st));
   return kOk;

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libsmelb.so")
 ACT = {"silu": 0, "gelu_tanh": 1}
 
 F_ROUTER, F_ROUTED, F_SHARED, F_SHARED_GATE, F_SAVE, F_TOPV_FP32, F_RECOMPUTE = 1, 2, 4, 8, 16, 32, 64
+F_EXT_DISPATCH = 128
 
 ERRORS = {-1: "bad shape", -2: "bad dtype", -3: "workspace too small", -4: "device wait timed out",
           -5: "CUDA error", -6: "bad argument"}
@@ -105,6 +106,24 @@ SIGNATURES = {
                                       c_vp, c_vp, c_i64, c_vp]),
     "smelb_lora_linear_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_f32,
                                       c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "smelb_ep_region_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
+    "smelb_ep_region_alloc": (c_i32, [c_i64, c_vp, c_vp]),
+    "smelb_ep_region_open": (c_i32, [c_vp, c_vp]),
+    "smelb_ep_region_close": (c_i32, [c_vp]),
+    "smelb_ep_region_free": (c_i32, [c_vp]),
+    "smelb_ep_sync": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_vp]),
+    "smelb_ep_plan": (c_i32, [c_vp, c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+                              c_vp, c_vp]),
+    "smelb_ep_pack_rows": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp]),
+    "smelb_ep_recv_plan": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                   c_vp, c_vp, c_vp]),
+    "smelb_ep_pull_rows": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp]),
+    "smelb_ep_gather": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "smelb_ep_return": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                c_i32, c_vp]),
+    "smelb_ep_dy": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
+    "smelb_ep_collect": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp,
+                                 c_vp, c_i32, c_vp, c_vp]),
     "smelb_int8_rows_quantize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "smelb_int8_rows_dequant": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_vp]),
     "smelb_chunked_ce_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i32, c_i32]),

@@ -1,35 +1,44 @@
-"""Expert parallelism for the MoE layer (smel/moe.py:255-263 partitioned by expert over the ranks of one box).
+"""Expert parallelism for the MoE layer: smel/moe.py:255-263 partitioned by expert over the P ranks (GPUs) of one box.
 
-Rank p of P owns experts [p E/P, (p+1) E/P): its slice of the frozen int4 bank, its selected (LoRA) experts and
-their LoRA factors. The router and the shared expert (with its LoRA) are replicated; every rank routes and combines
-its own tokens. One call:
+Rank p owns the experts `placement[p]` (E / P of them: its slice of the frozen int4 bank, its selected experts and
+their LoRA factors); the router and the shared expert with its LoRA are replicated and every rank routes and combines
+its own tokens. One call, on every rank at once:
 
-  1. route the rank's tokens over all E experts (the replicated router);
-  2. plan the stable dispatch by expert id; experts are contiguous per rank, so the dispatch order is also grouped
-     by destination rank (moe.py:216-223 order, unchanged);
-  3. exchange per-expert row counts (all-to-all, E/P ints per peer), then the token rows themselves
-     (all-to-all-v of bf16 H-vectors, NCCL over NVLink);
-  4. every owner runs its experts on the rows it received, as K=1 tokens with routing weight 1 (the combine of that
-     call is then the identity), through the same fused kernels as the single-GPU layer;
-  5. the expert outputs travel back by the reverse all-to-all and are combined at the source in fp32, k order
-     (moe.py:248-252), then the shared expert is added (moe.py:263).
+  source  route its T tokens; plan, per destination rank, the tokens that have at least one expert there (one row
+          per token and destination, however many of its K experts that rank owns), in token order, with the row's
+          entries (local expert, k, routing weight); copy those rows into its exchange region
+  owner   pull the rows addressed to it from every source's region over NVLink (one read per row), number their
+          entries in (source, row, slot) order, build the expert dispatch of the entries (the stable counting sort of
+          the single-GPU layer) and run its experts through the same fused GEMMs (smelb_moe_layer_fwd with an
+          external dispatch); per received row, sum its entries' outputs times their weights in fp32 and publish
+          that one partial row
+  source  out[t] = the fp32 sum over the owners of t's partial rows, in rank order, plus the shared expert
 
-Autograd mirrors it: the backward of each all-to-all is the reverse all-to-all, the owners produce dX rows for the
-rows they received and the LoRA gradients of their selected experts (which stay on the owner). The shared expert's
-LoRA gradients are per-rank partial sums; `allreduce_shared_grads` sums them (once per optimizer step).
+Backward mirrors it with the upstream gradient: the owners form dY = g * w and d w = g . y per entry, run the expert
+backward (dX and their LoRA gradients, which stay with the owner), and return one summed dX row per received row and
+the d w of every entry. The shared expert's LoRA gradients are per-rank partial sums; `allreduce_shared_grads` adds
+them (once per optimizer step).
 
-The compute steps go through an `ops` object; the default runs the smelb kernels on CUDA tensors (no CPU path).
+The exchange lives in device memory the library allocates per rank and maps into the peers by CUDA IPC (EPGroup);
+all synchronisation is device-side with bounded waits (csrc/ep.cu), so nothing synchronises with the host and a
+training step stays capturable in a CUDA graph. Rounding differs from the single-GPU combine only in that each
+owner's partial sum is rounded to bf16 before the source adds the partials.
 """
-import numpy as np
+import ctypes
+import math
+
 import torch
 import torch.distributed as dist
 
 from . import _lib
 from .lora import ExpertsLoRA, LayerLoRA
-from .moe import BF16Experts, Int4Experts, LayerExperts, _bf16, route, routed_experts, shared_mlp
+from .moe import (_SAVE_PREACT, BF16Experts, Int4Experts, LayerExperts, _alloc_bwd, _alloc_fwd, _bf16, _Cfg, _fp32,
+                  _LORA_NAMES, _set_routed, _struct, route, shared_mlp)
+
+SYNC = {"wait_done": 0, "publish": 1, "wait_ready": 2, "ack": 3}
 
 
-# ------------------------------------------------------------------------------------------ sharding
+# ------------------------------------------------------------------------------------------ placement
 def expert_range(E: int, rank: int, world: int):
     if E % world:
         raise ValueError(f"{E} experts do not split evenly over {world} ranks")
@@ -37,41 +46,94 @@ def expert_range(E: int, rank: int, world: int):
     return rank * n, (rank + 1) * n
 
 
-def shard_layer(ex: LayerExperts, lora_layer, rank: int, world: int):
-    """(local LayerExperts, local LayerLoRA) of `rank`: the frozen-bank slice of its experts, its selected experts
-    (local ids) and fresh Parameters holding its selected experts' LoRA factors; the shared LoRA is kept as is
-    (replicated)."""
-    e0, e1 = expert_range(ex.E, rank, world)
+def contiguous_placement(E: int, world: int):
+    return [list(range(*expert_range(E, r, world))) for r in range(world)]
+
+
+def balanced_placement(loads, world: int):
+    """E / world experts per rank with the routed load balanced: the experts in decreasing load (ties: smaller id)
+    each go to the least-loaded rank that still has room (ties: smaller rank). Returns the sorted expert ids of every
+    rank. `loads`: rows routed to each expert on a representative batch."""
+    loads = [float(v) for v in loads]
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    cap = E // world
+    order = sorted(range(E), key=lambda e: (-loads[e], e))
+    tot = [0.0] * world
+    out = [[] for _ in range(world)]
+    for e in order:
+        r = min((q for q in range(world) if len(out[q]) < cap), key=lambda q: (tot[q], q))
+        out[r].append(e)
+        tot[r] += loads[e]
+    return [sorted(v) for v in out]
+
+
+class EPShard:
+    """One rank's share of a layer: its experts (a LayerExperts over its local ids), its LoRA (the selected local
+    experts' factors and the replicated shared LoRA), the placement and the device maps expert -> owner rank and
+    expert -> local id."""
+
+    def __init__(self, ex, lora, placement, rank, E):
+        self.ex, self.lora, self.placement, self.rank, self.E = ex, lora, placement, rank, E
+        self._dev = {}
+
+    def maps(self, device):
+        key = str(device)
+        if key not in self._dev:
+            owner = torch.empty(self.E, dtype=torch.int32)
+            local = torch.empty(self.E, dtype=torch.int32)
+            for r, ids in enumerate(self.placement):
+                for j, e in enumerate(ids):
+                    owner[e], local[e] = r, j
+            meta = self.ex.meta(device)
+            mask = torch.zeros(self.ex.E + 1, dtype=torch.uint8)  # + the sink expert of unused dispatch entries
+            mask[:self.ex.E] = meta["sel_mask"].cpu()
+            self._dev[key] = {"owner": owner.to(device), "local": local.to(device), "sel_mask_sink": mask.to(device)}
+        return self._dev[key]
+
+
+def shard_layer(ex: LayerExperts, lora_layer, rank: int, world: int, placement=None) -> EPShard:
+    """Rank `rank`'s EPShard of a layer: the experts placement[rank] (default: contiguous ranges) as local ids 0..,
+    their frozen-bank rows copied out of the bank, their selected experts and fresh Parameters with their LoRA
+    factors; the shared LoRA is kept as it is (replicated)."""
+    E = ex.E
+    placement = placement or contiguous_placement(E, world)
+    if len(placement) != world or sorted(e for p in placement for e in p) != list(range(E)):
+        raise ValueError("placement must split all experts over the ranks")
+    ids = list(placement[rank])
+    idx = torch.tensor(ids, dtype=torch.long)
     fz = ex.frozen
     if isinstance(fz, Int4Experts):
-        bank = Int4Experts({k: v[e0:e1] for k, v in fz.gu.items()}, {k: v[e0:e1] for k, v in fz.dn.items()},
-                           fz.dtype)
+        pick = lambda d: {k: v.index_select(0, idx.to(v.device)).contiguous() for k, v in d.items()}  # noqa: E731
+        bank = Int4Experts(pick(fz.gu), pick(fz.dn), fz.dtype)
     elif isinstance(fz, BF16Experts):
-        bank = BF16Experts(fz.gate_up[e0:e1], fz.down[e0:e1])
+        bank = BF16Experts(fz.gate_up.index_select(0, idx.to(fz.gate_up.device)).contiguous(),
+                           fz.down.index_select(0, idx.to(fz.down.device)).contiguous())
     else:
         raise TypeError(f"shard_layer: unsupported bank {type(fz).__name__}")
+    where = {e: j for j, e in enumerate(ids)}
     slots, loc_ids = [], []
     if ex.sel_ids is not None:
         for j, e in enumerate(ex.sel_ids.tolist()):
-            if e0 <= e < e1:
+            if e in where:
                 slots.append(j)
-                loc_ids.append(e - e0)
+                loc_ids.append(where[e])
     if slots:
         ex_loc = LayerExperts(bank, loc_ids, ex.sel_gate_up[slots], ex.sel_down[slots], ex.group, ex.act)
     else:
         ex_loc = LayerExperts(bank, None, None, None, ex.group, ex.act)
     lora_loc = None
     if lora_layer is not None:
-        le = lora_layer.experts
-        le_loc = None
+        le, le_loc = lora_layer.experts, None
         if le is not None and slots:
             H, I = le.A_gate.shape[2], le.B_gate.shape[1]
             le_loc = ExpertsLoRA(loc_ids, H, I, le.r, le.alpha).to(le.A_gate.device)
             with torch.no_grad():
-                for n in ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down"):
+                for n in _LORA_NAMES:
                     getattr(le_loc, n).copy_(getattr(le, n)[slots])
         lora_loc = LayerLoRA(le_loc, lora_layer.shared)
-    return ex_loc, lora_loc
+    return EPShard(ex_loc, lora_loc, placement, rank, E)
 
 
 def allreduce_shared_grads(lora_layer, group=None):
@@ -83,154 +145,202 @@ def allreduce_shared_grads(lora_layer, group=None):
             dist.all_reduce(p.grad, group=group)
 
 
-# ------------------------------------------------------------------------------------------ exchange
-class _AllToAll(torch.autograd.Function):
-    """Rows exchange: `in_splits[p]` rows of x go to rank p, `out_splits[p]` rows arrive from rank p (in rank
-    order). The backward is the reverse exchange."""
+# ------------------------------------------------------------------------------------------ exchange regions
+class EPGroup:
+    """The exchange regions of one expert-parallel group: this rank's (allocated by the library) and every peer's
+    (mapped by CUDA IPC). `cap` is the most tokens a rank brings to one call, `K` the router's top-k. With one rank
+    (or no process group) the exchange runs against the rank's own region. close() (after a barrier) unmaps and
+    frees them."""
+
+    def __init__(self, cap: int, H: int, K: int, group=None, device=None):
+        self.group = group
+        init = dist.is_available() and dist.is_initialized()
+        self.P = dist.get_world_size(group) if init else 1
+        self.rank = dist.get_rank(group) if init else 0
+        self.cap, self.H, self.K = int(cap), int(H), int(K)
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nbytes = int(lib.smelb_ep_region_bytes(self.P, self.cap, self.K, self.H))
+        if nbytes <= 0:
+            raise _lib.SmelbError(f"EPGroup: unsupported shape P={self.P} cap={cap} K={K} H={H}")
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _lib.call("smelb_ep_region_alloc", nbytes, ctypes.byref(base), handle)
+        self._own = base.value
+        handles = [bytes(handle)]
+        if self.P > 1:
+            handles = [None] * self.P
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        bases, self._opened = [], []
+        for s in range(self.P):
+            if s == self.rank:
+                bases.append(self._own)
+                continue
+            h = (ctypes.c_char * 64).from_buffer_copy(handles[s])
+            p = ctypes.c_void_p()
+            _lib.call("smelb_ep_region_open", h, ctypes.byref(p))
+            bases.append(p.value)
+            self._opened.append(p.value)
+        self._arr = (ctypes.c_void_p * self.P)(*bases)
+        self.regions = ctypes.cast(self._arr, ctypes.c_void_p).value
+
+    def sync(self, op: str, buffer: int):
+        _lib.call("smelb_ep_sync", self.regions, self.P, self.rank, self.cap, self.K, self.H, SYNC[op], buffer,
+                  _lib.stream_ptr(self.device))
+
+    def close(self):
+        for p in self._opened:
+            _lib.call("smelb_ep_region_close", p)
+        self._opened = []
+        if self._own:
+            _lib.call("smelb_ep_region_free", self._own)
+            self._own = None
+
+
+# ------------------------------------------------------------------------------------------ the routed part
+def _i32(*s, dev):
+    return torch.empty(*s, dtype=torch.int32, device=dev)
+
+
+class _EPRoutedFn(torch.autograd.Function):
+    """out = routed experts (partitioned over the group) + sh. Inputs: x, topv, sh (the shared expert's output),
+    topi, shard, comm, cap_factor, then the local selected experts' six LoRA parameters (or None)."""
 
     @staticmethod
-    def forward(ctx, x, out_splits, in_splits, group):
-        ctx.splits = (out_splits, in_splits)
-        ctx.group = group
-        out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
-        dist.all_to_all_single(out, x.contiguous(), out_splits, in_splits, group=group)
-        return out
-
-    @staticmethod
-    def backward(ctx, g):
-        out_splits, in_splits = ctx.splits
-        gi = g.new_empty((sum(in_splits),) + tuple(g.shape[1:]))
-        dist.all_to_all_single(gi, g.contiguous(), in_splits, out_splits, group=ctx.group)
-        return gi, None, None, None
-
-
-# ------------------------------------------------------------------------------------------ CUDA ops
-class _Plan:
-    def __init__(self, counts, row_of, src_of, order, total, R):
-        self.counts, self.row_of, self.src_of, self.order, self.total, self.R = counts, row_of, src_of, order, total, R
-
-
-class _GatherFn(torch.autograd.Function):
-    """xs[row] = x[src_of[row] // K] (moe.py:221); backward dx[t] = sum_k dxs[row_of[t, k]] (fp32, k order)."""
-
-    @staticmethod
-    def forward(ctx, x, plan, K):
+    def forward(ctx, x, topv, sh, topi, shard, comm, cap_factor, *lora_params):
+        dev = x.device
         T, H = x.shape
-        xs = torch.empty(plan.R, H, dtype=torch.bfloat16, device=x.device)
-        _lib.call("smelb_gather_rows", _lib.ptr(x), H, K, _lib.ptr(plan.src_of), _lib.ptr(plan.total), plan.R,
-                  _lib.ptr(xs), _lib.stream_ptr(x.device))
-        ctx.plan, ctx.K, ctx.T = plan, K, T
-        return xs
-
-    @staticmethod
-    def backward(ctx, g):
-        g = g.to(torch.bfloat16).contiguous()
-        H = g.shape[1]
-        dx = torch.empty(ctx.T, H, dtype=torch.bfloat16, device=g.device)
-        _lib.call("smelb_gather_rows_bwd", _lib.ptr(g), _lib.ptr(ctx.plan.row_of), ctx.T, ctx.K, H, _lib.ptr(dx),
-                  _lib.stream_ptr(g.device))
-        return dx, None, None
-
-
-class _CombineFn(torch.autograd.Function):
-    """out[t] = bf16(sum_k fp32(y[row_of[t, k]]) * fp32(topv[t, k])) (moe.py:248-252) and its backward."""
-
-    @staticmethod
-    def forward(ctx, y, topv, plan, K):
-        y = y.contiguous()
-        T = topv.shape[0]
-        H = y.shape[1]
+        K = topi.shape[1]
+        P, r, cap = comm.P, comm.rank, comm.cap
+        if T > cap or H != comm.H or K != comm.K:
+            raise _lib.SmelbError(f"moe_forward_ep: T={T} H={H} K={K} against the group's cap={cap} H={comm.H} "
+                                  f"K={comm.K}")
+        maps = shard.maps(dev)
+        ex = shard.ex
+        E_loc = ex.E
+        cap_e = int(math.ceil(cap_factor * cap * K))
+        st = _lib.stream_ptr(dev)
+        reg = comm.regions
+        topi = topi.contiguous()
         f32 = topv.dtype == torch.float32
-        out = torch.empty(T, H, dtype=torch.bfloat16, device=y.device)
-        _lib.call("smelb_combine_fwd", _lib.ptr(y), _lib.ptr(plan.row_of), _lib.ptr(topv), 1 if f32 else 0, T, K, H,
-                  _lib.ptr(out), _lib.stream_ptr(y.device))
-        ctx.save_for_backward(y, topv)
-        ctx.plan, ctx.K = plan, K
+        topv = topv.contiguous()
+        # ---- source: plan and publish the token rows (buffer 0)
+        pos, slot_j, tok_of = _i32(T, P, dev=dev), _i32(T, K, dev=dev), _i32(P, cap, dev=dev)
+        comm.sync("wait_done", 0)
+        _lib.call("smelb_ep_plan", _lib.ptr(topi), _lib.ptr(topv), 1 if f32 else 0, T, K, _lib.ptr(maps["owner"]),
+                  _lib.ptr(maps["local"]), reg, P, r, cap, H, _lib.ptr(pos), _lib.ptr(slot_j), _lib.ptr(tok_of), st)
+        _lib.call("smelb_ep_pack_rows", _lib.ptr(x), H, _lib.ptr(tok_of), reg, P, r, cap, K, 0, st)
+        comm.sync("publish", 0)
+        # ---- owner: pull, number the entries, dispatch them to the local experts
+        comm.sync("wait_ready", 0)
+        entry_e = torch.empty(cap_e, dtype=torch.int64, device=dev)
+        entry_row, entry_w = _i32(cap_e, dev=dev), torch.empty(cap_e, dtype=torch.float32, device=dev)
+        row_beg, row_m, rc, n_tot = _i32(P * cap, dev=dev), _i32(P * cap, dev=dev), _i32(P, dev=dev), _i32(1, dev=dev)
+        _lib.call("smelb_ep_recv_plan", reg, P, r, cap, K, H, cap_e, E_loc, _lib.ptr(entry_e), _lib.ptr(entry_row),
+                  _lib.ptr(entry_w), _lib.ptr(row_beg), _lib.ptr(row_m), _lib.ptr(rc), _lib.ptr(n_tot), st)
+        x_loc = torch.empty(P * cap, H, dtype=torch.bfloat16, device=dev)
+        _lib.call("smelb_ep_pull_rows", reg, P, r, cap, K, H, 0, _lib.ptr(x_loc), st)
+        comm.sync("ack", 0)
+        lora_ex = shard.lora.experts if shard.lora is not None else None
+        cfg = _Cfg(0, torch.empty(cap_e, H, device="meta"), 1, E_loc, ex.act)
+        _set_routed(cfg, ex, lora_ex, dev)
+        cfg.flags |= _lib.F_EXT_DISPATCH
+        save = any(ctx.needs_input_grad)
+        if save:
+            cfg.flags |= _lib.F_SAVE
+            if not _SAVE_PREACT[0]:
+                cfg.flags |= _lib.F_RECOMPUTE
+        t = dict(cfg.t)
+        lp = [_fp32(p) for p in lora_params]
+        for i, name in enumerate(_LORA_NAMES):
+            t[name] = lp[i]
+        t.update(_alloc_fwd(cfg, dev, save))
+        t.pop("out")  # the owner's outputs stay in dispatch order (y)
+        R = cfg.max_rows
+        t.update(counts=_i32(E_loc + 1, dev=dev), gcounts=_i32(E_loc + 1, dev=dev), offsets=_i32(E_loc + 1, dev=dev))
+        ws = _i32(148 * (E_loc + 1), dev=dev)
+        _lib.call("smelb_dispatch_plan_ws", _lib.ptr(entry_e), cap_e, 1, E_loc + 1, _lib.ptr(maps["sel_mask_sink"]),
+                  64, _lib.ptr(t["counts"]), _lib.ptr(t["gcounts"]), _lib.ptr(t["offsets"]), _lib.ptr(t["row_of"]),
+                  _lib.ptr(t["src_of"]), _lib.ptr(t["order"]), _lib.ptr(t["total"]), _lib.ptr(ws), ws.numel(), st)
+        _lib.call("smelb_ep_gather", _lib.ptr(x_loc), _lib.ptr(entry_row), _lib.ptr(t["src_of"]),
+                  _lib.ptr(t["offsets"]), E_loc, H, R, _lib.ptr(t["xs"]), st)
+        L = _struct(cfg, t)
+        _lib.call("smelb_moe_layer_fwd", ctypes.byref(L))
+        # ---- owner: one partial row per received row (buffer 1)
+        comm.sync("wait_done", 1)
+        _lib.call("smelb_ep_return", _lib.ptr(t["y"]), _lib.ptr(t["row_of"]), _lib.ptr(entry_w), None,
+                  _lib.ptr(row_beg), _lib.ptr(row_m), _lib.ptr(rc), reg, P, r, cap, K, H, 0, st)
+        comm.sync("publish", 1)
+        # ---- source: add the partial rows of every owner and the shared expert
+        comm.sync("wait_ready", 1)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), _lib.ptr(sh.contiguous()), 0, None,
+                  None, None, None, 0, _lib.ptr(out), st)
+        comm.sync("ack", 1)
+        if save:
+            ctx.save_for_backward(topi, pos, slot_j, tok_of, entry_row, entry_w, row_beg, row_m, rc)
+            ctx.t, ctx.cfg, ctx.shard, ctx.comm = t, cfg, shard, comm
+            ctx.meta = (T, H, K, E_loc, R, f32, [None if p is None else p.dtype for p in lora_params])
         return out
 
     @staticmethod
     def backward(ctx, g):
-        y, topv = ctx.saved_tensors
+        topi, pos, slot_j, tok_of, entry_row, entry_w, row_beg, row_m, rc = ctx.saved_tensors
+        t, cfg, shard, comm = dict(ctx.t), ctx.cfg, ctx.shard, ctx.comm
+        T, H, K, E_loc, R, f32, dtypes = ctx.meta
+        P, r, cap = comm.P, comm.rank, comm.cap
+        dev = g.device
+        st = _lib.stream_ptr(dev)
+        reg = comm.regions
         g = g.to(torch.bfloat16).contiguous()
-        f32 = topv.dtype == torch.float32
-        dy = torch.empty_like(y)
-        dtopv = torch.empty_like(topv)
-        _lib.call("smelb_combine_bwd", _lib.ptr(g), _lib.ptr(y), _lib.ptr(ctx.plan.src_of), _lib.ptr(ctx.plan.total),
-                  ctx.plan.R, _lib.ptr(topv), 1 if f32 else 0, ctx.K, y.shape[1], _lib.ptr(dy), _lib.ptr(dtopv),
-                  _lib.stream_ptr(g.device))
-        return dy, dtopv, None, None
+        maps = shard.maps(dev)
+        # ---- source: the gradient rows of the same token rows (buffer 2)
+        comm.sync("wait_done", 2)
+        _lib.call("smelb_ep_pack_rows", _lib.ptr(g), H, _lib.ptr(tok_of), reg, P, r, cap, K, 2, st)
+        comm.sync("publish", 2)
+        # ---- owner: pull them, dY and d w per entry, the expert backward
+        comm.sync("wait_ready", 2)
+        g_loc = torch.empty(P * cap, H, dtype=torch.bfloat16, device=dev)
+        _lib.call("smelb_ep_pull_rows", reg, P, r, cap, K, H, 2, _lib.ptr(g_loc), st)
+        comm.sync("ack", 2)
+        b = _alloc_bwd(cfg, dev)
+        t.update(b)
+        entry_dw = torch.zeros(entry_w.shape, dtype=torch.float32, device=dev)
+        _lib.call("smelb_ep_dy", _lib.ptr(g_loc), _lib.ptr(entry_row), _lib.ptr(entry_w), _lib.ptr(t["src_of"]),
+                  _lib.ptr(t["offsets"]), E_loc, H, R, _lib.ptr(t["y"]), _lib.ptr(t["dy"]), _lib.ptr(entry_dw), st)
+        L = _struct(cfg, t)
+        _lib.call("smelb_moe_layer_bwd", ctypes.byref(L))
+        # ---- owner: summed dX per received row and d w per entry (buffer 3)
+        comm.sync("wait_done", 3)
+        _lib.call("smelb_ep_return", _lib.ptr(t["dxs"]), _lib.ptr(t["row_of"]), None, _lib.ptr(entry_dw),
+                  _lib.ptr(row_beg), _lib.ptr(row_m), _lib.ptr(rc), reg, P, r, cap, K, H, 1, st)
+        comm.sync("publish", 3)
+        # ---- source: dX of its tokens and d topv
+        comm.sync("wait_ready", 3)
+        dx = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        dtopv = torch.empty(T, K, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
+        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), None, 1, _lib.ptr(topi),
+                  _lib.ptr(maps["owner"]), _lib.ptr(slot_j), _lib.ptr(dtopv), 1 if f32 else 0, _lib.ptr(dx), st)
+        comm.sync("ack", 3)
+        grads = [b.get("g" + n) for n in _LORA_NAMES]
+        grads = [None if (gr is None or dt is None) else gr.to(dt) for gr, dt in zip(grads, dtypes)]
+        return (dx, dtopv, g, None, None, None, None, *grads)
 
 
-class CudaOps:
-    """The compute steps of an expert-parallel layer call on the smelb kernels."""
+def moe_forward_ep(x2d, W, shard: EPShard, top_k: int, comm: EPGroup, stats=None, cap_factor: float = 2.0):
+    """moe_forward (moe.py:255-263) with the routed experts partitioned over `comm`'s ranks.
 
-    def route(self, x, gate_w, top_k):
-        return route(x, gate_w, top_k)
-
-    def plan(self, topi, E):
-        T, K = topi.shape
-        dev = topi.device
-        R = T * K
-        i32 = lambda n: torch.empty(n, dtype=torch.int32, device=dev)  # noqa: E731
-        counts, gcounts, offsets, row_of, src_of, total = i32(E), i32(E), i32(E), i32(R), i32(R), i32(1)
-        order = torch.empty(R, dtype=torch.int64, device=dev)
-        ws = i32(148 * E)
-        topi = topi.contiguous()
-        _lib.call("smelb_dispatch_plan_ws", _lib.ptr(topi), T, K, E, None, 1, _lib.ptr(counts), _lib.ptr(gcounts),
-                  _lib.ptr(offsets), _lib.ptr(row_of), _lib.ptr(src_of), _lib.ptr(order), _lib.ptr(total),
-                  _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev))
-        return _Plan(counts, row_of, src_of, order, total, R)
-
-    def gather(self, x, plan, K):
-        return _GatherFn.apply(_bf16(x, "moe_forward_ep: x"), plan, K)
-
-    def combine(self, y, topv, plan, K):
-        return _CombineFn.apply(y, topv, plan, K)
-
-    def experts(self, x_recv, topi_loc, ex_loc, lora_loc):
-        lora_ex = lora_loc.experts if lora_loc is not None else None
-        topv = torch.ones(x_recv.shape[0], 1, dtype=torch.bfloat16, device=x_recv.device)
-        return routed_experts(x_recv, topv, topi_loc, ex_loc, lora_ex)
-
-    def shared(self, x, W, lora_loc):
-        return shared_mlp(x, W, lora_loc.shared if lora_loc is not None else None)
-
-    def counts_of(self, plan):
-        return plan.counts
-
-
-# ------------------------------------------------------------------------------------------ the layer
-def moe_forward_ep(x2d, W, ex_loc, top_k, lora_loc=None, group=None, ops=None, stats=None, n_experts=None):
-    """moe_forward (moe.py:255-263) with the routed experts partitioned over the ranks of `group`.
-
-    x2d: this rank's tokens [T, H]; W: the replicated router / shared-expert tensors; ex_loc, lora_loc: this rank's
-    experts and LoRA (from shard_layer). Returns this rank's [T, H] output, differentiable w.r.t. x2d, the local
-    LoRA parameters and the shared LoRA parameters."""
-    ops = ops or CudaOps()
-    P = dist.get_world_size(group)
-    E = n_experts if n_experts is not None else W["mlp.gate.weight"].shape[0]
-    E_loc = E // P
-    if E_loc * P != E:
-        raise ValueError(f"{E} experts do not split evenly over {P} ranks")
-    probs, topv, topi = ops.route(x2d, W["mlp.gate.weight"], top_k)
+    x2d: this rank's tokens [T, H] bf16 (T <= comm.cap); W: the replicated router / shared-expert tensors; shard:
+    this rank's EPShard. Every rank of the group must make the same sequence of calls. cap_factor bounds the
+    dispatch entries an owner can take (cap_factor * cap * top_k); more record a device status code. Returns this
+    rank's [T, H] output, differentiable w.r.t. x2d, the local selected experts' LoRA parameters and the shared LoRA
+    parameters."""
+    x2d = _bf16(x2d, "moe_forward_ep: x")
+    probs, topv, topi = route(x2d, W["mlp.gate.weight"], top_k)
     if stats is not None:
         stats(probs, topv, topi)
-    plan = ops.plan(topi, E)
-    counts = ops.counts_of(plan)
-    recv_counts = torch.empty_like(counts)
-    dist.all_to_all_single(recv_counts, counts.contiguous(), group=group)
-    ch = torch.stack((counts, recv_counts)).cpu().numpy().astype(np.int64)  # one small copy: the row splits
-    send_splits = ch[0].reshape(P, E_loc).sum(1).tolist()
-    recv_splits = ch[1].reshape(P, E_loc).sum(1).tolist()
-    xs = ops.gather(x2d, plan, top_k)
-    x_recv = _AllToAll.apply(xs, recv_splits, send_splits, group)
-    # local expert id of every received row: by source rank, then by expert (the sender's dispatch order)
-    ids = np.repeat(np.tile(np.arange(E_loc), P), ch[1])
-    topi_loc = torch.from_numpy(ids).to(x_recv.device).view(-1, 1)
-    if x_recv.shape[0]:
-        y_recv = ops.experts(x_recv, topi_loc, ex_loc, lora_loc)
-    else:
-        y_recv = x_recv * 0
-    y_back = _AllToAll.apply(y_recv, send_splits, recv_splits, group)
-    out = ops.combine(y_back, topv, plan, top_k)
-    return out + ops.shared(x2d, W, lora_loc)
+    lora_sh = shard.lora.shared if shard.lora is not None else None
+    sh = shared_mlp(x2d, W, lora_sh)
+    lex = shard.lora.experts if shard.lora is not None else None
+    params = [getattr(lex, n) for n in _LORA_NAMES] if lex is not None else [None] * 6
+    return _EPRoutedFn.apply(x2d, topv, sh, topi, shard, comm, float(cap_factor), *params)

@@ -1,7 +1,13 @@
-"""Expert parallelism on two GPUs (NCCL): smelb.ep.moe_forward_ep over two ranks, each holding half of the experts,
-against the single-GPU fused layer (smelb.moe_forward) on the union of the tokens: output, dX and the LoRA
-gradients (owner-side for the selected experts, all-reduced for the shared expert) within the tolerance of the
-other layer tests (max relative error 2e-2, cosine 0.9999). Skipped with fewer than two GPUs."""
+"""Expert parallelism through the peer-memory exchange (smelb/ep.py, csrc/ep.cu) against the single-GPU fused layer
+(smelb.moe_forward) on the same tokens: output, dX and the LoRA gradients (owner-side for the selected experts,
+all-reduced for the shared expert) within the tolerance of the other layer tests (max relative error 2e-2, cosine
+0.9999).
+
+One rank on one GPU runs every kernel of the exchange against its own region (plan, row packing, entry numbering,
+dispatch, partial combine, collection, and the backward's dY, d weight and dX return); two ranks on two GPUs (skipped
+with fewer) exchange over NVLink with a load-balanced expert placement. A CUDA-graph capture of the one-rank step
+must replay to the eager step's bits."""
+import copy
 import os
 import socket
 import sys
@@ -18,11 +24,86 @@ REL, COS = 2e-2, 0.9999
 NAMES = ("A_gate", "B_gate", "A_up", "B_up", "A_down", "B_down")
 
 
+def _bad(checks):
+    from oracle import moe_oracle as O
+    bad = []
+    for name, a, b in checks:
+        e, c = O.rel_err(a.float().cpu(), b.float().cpu()), O.cosine(a.float().cpu(), b.float().cpu())
+        print(f"{name:>14s}: rel err {e:.3e} cosine {c:.7f}")
+        if not (e <= REL and c >= COS):
+            bad.append(f"{name}: rel err {e:.3e} cosine {c:.6f}")
+    return bad
+
+
+def test_expert_parallel_one_rank_matches_fused_layer():
+    import smelb
+    from smelb import ep
+    from smelb.synth import qwen_layer
+    dev = torch.device("cuda:0")
+    K = 4
+    L = qwen_layer(T=700, H=512, E=32, K=K, I=256, S=256, n_sel=4, r=16, seed=3, device=dev)
+    W, ex, lora, x = L["W"], L["ex"], L["lora"], L["x"]
+    gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(5), device=dev).bfloat16()
+    xr = x.detach().clone().requires_grad_(True)
+    ref = smelb.moe_forward(xr, W, ex, K, lora)
+    ref.backward(gy)
+    ref_sel = {n: getattr(lora.experts, n).grad.clone() for n in NAMES}
+    ref_sh = {n: getattr(lora.shared, n).grad.clone() for n in NAMES}
+    for p in lora.parameters():
+        p.grad = None
+    # fresh LoRA parameters for the expert-parallel steps, all of which run on one side stream: a parameter's
+    # gradient accumulation is bound to the stream of its first backward, and a graph can only replay on its own
+    lora_ep = copy.deepcopy(lora)
+    shard = ep.shard_layer(ex, lora_ep, 0, 1)
+    comm = ep.EPGroup(cap=x.shape[0], H=x.shape[1], K=K)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    torch.cuda.set_stream(s)
+    try:
+        def step():
+            for p in shard.lora.parameters():
+                p.grad = None
+            xl = x.detach().clone().requires_grad_(True)
+            out = ep.moe_forward_ep(xl, W, shard, K, comm)
+            out.backward(gy)
+            return out.detach(), xl.grad, {n: getattr(shard.lora.experts, n).grad.clone() for n in NAMES}
+        out, dx, g_sel = step()
+        bad = _bad([("out", out, ref), ("dx", dx, xr.grad)] + [(f"sel {n}", g_sel[n], ref_sel[n]) for n in NAMES] +
+                   [(f"shared {n}", getattr(shard.lora.shared, n).grad, ref_sh[n]) for n in NAMES])
+        # one rank: every token's entries go to the one owner, whose weighted sum is the fused layer's combine
+        assert torch.equal(out, ref.detach())
+        assert not bad, "; ".join(bad)
+        assert smelb.read_status() == 0
+        # a second eager step gives the same bits, and so does a CUDA-graph replay of the step
+        out2, dx2, g2 = step()
+        assert torch.equal(out, out2) and torch.equal(dx, dx2)
+        xg = x.detach().clone().requires_grad_(True)
+        for p in shard.lora.parameters():
+            p.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            og = ep.moe_forward_ep(xg, W, shard, K, comm)
+            og.backward(gy)
+        for p in shard.lora.parameters():
+            p.grad.zero_()
+        xg.grad.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(og, out) and torch.equal(xg.grad, dx)
+        for n in NAMES:
+            assert torch.equal(getattr(shard.lora.experts, n).grad, g_sel[n]), n
+        del graph
+        assert smelb.read_status() == 0
+    finally:
+        torch.cuda.synchronize()
+        torch.cuda.set_stream(torch.cuda.default_stream(dev))
+        comm.close()
+
+
 def _worker(rank, world, port, errq, T):
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "smel-ft_b200"))
-        from oracle import moe_oracle as O
         import smelb
         from smelb import ep
         from smelb.synth import qwen_layer
@@ -30,38 +111,43 @@ def _worker(rank, world, port, errq, T):
         dev = torch.device("cuda", rank)
         os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
-        L = qwen_layer(T=world * T, H=512, E=32, K=4, I=256, S=256, n_sel=4, r=16, seed=3, device=dev)
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+        K = 4
+        L = qwen_layer(T=world * T, H=512, E=32, K=K, I=256, S=256, n_sel=4, r=16, seed=3, device=dev)
         W, ex, lora, x = L["W"], L["ex"], L["lora"], L["x"]
         gy = torch.randn(x.shape, generator=torch.Generator(device=dev).manual_seed(5), device=dev).bfloat16()
         # single-GPU reference over all tokens
         xr = x.detach().clone().requires_grad_(True)
-        ref = smelb.moe_forward(xr, W, ex, 4, lora)
+        rec = {}
+        ref = smelb.moe_forward(xr, W, ex, K, lora, stats=lambda p, v, i: rec.update(i=i))
         ref.backward(gy)
         ref_sel = {n: getattr(lora.experts, n).grad.clone() for n in NAMES}
         ref_sh = {n: getattr(lora.shared, n).grad.clone() for n in NAMES}
         for p in lora.parameters():
             p.grad = None
-        # expert parallel: this rank's tokens and half of the experts
-        ex_loc, lora_loc = ep.shard_layer(ex, lora, rank, world)
-        e0, e1 = ep.expert_range(ex.E, rank, world)
-        slots = [j for j, e in enumerate(ex.sel_ids.tolist()) if e0 <= e < e1]
+        # expert parallel: this rank's tokens, its load-balanced share of the experts
+        loads = torch.bincount(rec["i"].reshape(-1), minlength=ex.E).tolist()
+        placement = ep.balanced_placement(loads, world)
+        shard = ep.shard_layer(ex, lora, rank, world, placement)
+        comm = ep.EPGroup(cap=T, H=x.shape[1], K=K)
         sl = slice(rank * T, (rank + 1) * T)
         xl = x[sl].detach().clone().requires_grad_(True)
-        out = ep.moe_forward_ep(xl, W, ex_loc, 4, lora_loc)
+        out = ep.moe_forward_ep(xl, W, shard, K, comm)
         out.backward(gy[sl])
-        ep.allreduce_shared_grads(lora_loc)
+        ep.allreduce_shared_grads(shard.lora)
+        slots = [j for j, e in enumerate(ex.sel_ids.tolist()) if e in set(placement[rank])]
         checks = [("out", out, ref[sl]), ("dx", xl.grad, xr.grad[sl])]
         if slots:
-            checks += [(f"sel {n}", getattr(lora_loc.experts, n).grad, ref_sel[n][slots]) for n in NAMES]
-        checks += [(f"shared {n}", getattr(lora_loc.shared, n).grad, ref_sh[n]) for n in NAMES]
-        bad = []
-        for name, a, b in checks:
-            e, c = O.rel_err(a.float().cpu(), b.float().cpu()), O.cosine(a.float().cpu(), b.float().cpu())
-            if not (e <= REL and c >= COS):
-                bad.append(f"{name}: rel err {e:.3e} cosine {c:.6f}")
+            checks += [(f"sel {n}", getattr(shard.lora.experts, n).grad, ref_sel[n][slots]) for n in NAMES]
+        checks += [(f"shared {n}", getattr(shard.lora.shared, n).grad, ref_sh[n]) for n in NAMES]
+        bad = _bad(checks)
         assert not bad, f"rank {rank}: " + "; ".join(bad)
         assert smelb.read_status() == 0
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
