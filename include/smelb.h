@@ -415,6 +415,11 @@ int smelb_lm_logits(const void* h, int64_t N, int64_t H, const void* w, const vo
  * recorded since the previous read. */
 long long smelb_launch_count(void);
 int smelb_gemm_timing(int enable);
+/* Dispatch-row count at or below which the forward's frozen int4 experts (smelb_moe_layer_fwd, and
+ * smelb_frozen_experts_fwd over its rows) run as a dequant-GEMV instead of the tile engine; returns the previous
+ * value (default 4096; 0 keeps every call on the tile engine). Replaces the size switch of no reference interface:
+ * smel/moe.py:58-85 has one path at every size. */
+int64_t smelb_set_gemv_rows(int64_t rows);
 int smelb_gemm_timing_read(double* ms_total, long long* launches);
 
 /* sizeof(smelb_moe_layer), for bindings to check their mirror of the struct. */

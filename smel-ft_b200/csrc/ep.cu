@@ -321,7 +321,8 @@ __global__ void ep_gather_kernel(const bf16* __restrict__ local, const int* __re
   }
 }
 
-// One warp per received row (s, i): sum over its entries of w * y[row_of[entry]] (fp32, slot order) -> bf16 into this
+// One warp per received row (s, i): sum over its entries of w * y[row_of[entry]] (fp32, each product rounded before
+// it is added, in slot order: the reference's y.float() * topv then sum, smel/moe.py:248-252) -> bf16 into this
 // rank's rows[1][s][i]; counts[1][s] = rows received from s. Backward (bwd != 0): the entries' dX rows summed into
 // rows[3] and each entry's d weight into dwts[s][i][j].
 __global__ void ep_return_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
@@ -347,7 +348,7 @@ __global__ void ep_return_kernel(const bf16* __restrict__ y, const int* __restri
         const uint4 v = *reinterpret_cast<const uint4*>(y + (long long)row_of[beg + j] * H + c0);
         const bf16* pv = reinterpret_cast<const bf16*>(&v);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = fmaf(__bfloat162float(pv[q]), w, acc[q]);
+        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(__bfloat162float(pv[q]), w));
       }
       uint4 o;
       bf16* po = reinterpret_cast<bf16*>(&o);

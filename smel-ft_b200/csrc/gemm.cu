@@ -96,47 +96,7 @@ __device__ __forceinline__ TileInfo tile_at(const LaunchArgs& args, const Tables
 }
 
 // ------------------------------------------------------------------------------------------ int4 dequant helpers
-// A group takes the bf16x2 fast path when every value q*s + z (q in 0..15) is exactly representable in fp32: then
-// rounding the exact value once to bf16 (fma.rn.bf16x2) equals the reference's fp32 dequant followed by a bf16
-// cast. Other groups (extreme scale/zero exponent gaps, subnormals, non-finite) are expanded in fp32.
-__device__ __forceinline__ bool dq_fast_ok(uint32_t sz) {
-  const uint32_t s = sz & 0xFFFFu, z = sz >> 16;
-  if ((z & 0x7FFFu) == 0 || (s & 0x7FFFu) == 0) return true;
-  const int es = (s >> 7) & 0xFF, ez = (z >> 7) & 0xFF;
-  if (es < 32 || ez < 32 || es == 0xFF || ez == 0xFF) return false;
-  const int d = ez - es;
-  return d <= 15 && d >= -11;
-}
-
-__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ __nv_bfloat162 bits_bf162(uint32_t v) { return *reinterpret_cast<__nv_bfloat162*>(&v); }
-
-// One 32-bit word = 8 nibbles, byte j holding element 2j (low nibble) and 2j+1 (high nibble) -> 8 bf16.
-// (0x4300 | n) is the bf16 encoding of 128 + n, so subtracting 128 recovers n exactly.
-__device__ __forceinline__ uint4 dq8_fast(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 z2) {
-  const uint32_t y = w >> 4;
-  const __nv_bfloat162 c128 = bits_bf162(0x43004300u);
-  const uint32_t p0 = (__byte_perm(w, y, 0x0400) & 0x000F000Fu) | 0x43004300u;
-  const uint32_t p1 = (__byte_perm(w, y, 0x0501) & 0x000F000Fu) | 0x43004300u;
-  const uint32_t p2 = (__byte_perm(w, y, 0x0602) & 0x000F000Fu) | 0x43004300u;
-  const uint32_t p3 = (__byte_perm(w, y, 0x0703) & 0x000F000Fu) | 0x43004300u;
-  uint4 r;
-  r.x = bf162_bits(__hfma2(__hsub2(bits_bf162(p0), c128), s2, z2));
-  r.y = bf162_bits(__hfma2(__hsub2(bits_bf162(p1), c128), s2, z2));
-  r.z = bf162_bits(__hfma2(__hsub2(bits_bf162(p2), c128), s2, z2));
-  r.w = bf162_bits(__hfma2(__hsub2(bits_bf162(p3), c128), s2, z2));
-  return r;
-}
-
-__device__ __forceinline__ uint4 dq8_exact(uint32_t w, float s, float z) {
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t b = (w >> (8 * j)) & 0xFFu;
-    o[j] = bf162_bits(__floats2bfloat162_rn(fmaf((float)(b & 0xFu), s, z), fmaf((float)(b >> 4), s, z)));
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
+// dq_fast_ok, dq8_fast, dq8_exact (common.cuh): the int4 -> bf16 expansion shared with the small-token kernels.
 
 // 32 packed bytes (64 values sharing one (scale, zero) pair) -> 32 words of two bf16 in k order. The bytes are two
 // 16-byte chunks of a staged row: chunk `c0` and `c0 + 1`, each stored at chunk position c ^ swz.
@@ -184,20 +144,7 @@ __device__ __forceinline__ void dq64(const uint8_t* src, int c0, int swz, uint32
 }
 
 // ------------------------------------------------------------------------------------------ epilogue math
-// Activations in fp32 on the bf16-rounded pre-activation, as the reference's bf16 `act` (smel/moe.py:91-107), using
-// the hardware exp2 / reciprocal / tanh approximations: their relative error (~1e-6, and 2^-11 for tanh) is far below
-// the bf16 rounding that follows. Short and inline so the unrolled epilogue columns overlap.
-__device__ __forceinline__ float tanh_approx(float x) {
-  float y;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float act_fwd(float x, int act) {
-  if (act == kActSilu) return __fdividef(x, 1.0f + __expf(-x));
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanh_approx(k0 * (x + k1 * x * x * x)));
-}
+// act_fwd / tanh_approx (common.cuh): the activations of the GLU epilogue.
 
 // (act(g), d act / d g) in fp32
 __device__ __forceinline__ float2 act_and_grad(float g, int act) {

@@ -137,6 +137,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                   "tensor map swizzle span %d for a %u-byte box row", swizzle_bytes, box_cols * elem_bytes);
   const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                        : CU_TENSOR_MAP_SWIZZLE_NONE;
   if (rows == 0) rows = 1;  // an empty matrix still needs a valid (never read) map
   cuuint64_t dims[2] = {cols, rows};
@@ -150,6 +151,31 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
                   "cuTensorMapEncodeTiled failed (%d): rows=%llu cols=%llu pitch=%llu box=%ux%u", (int)r,
                   (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)row_bytes, box_cols,
                   box_rows);
+  return kOk;
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
+                 const uint64_t strides_bytes[2], const uint32_t box[3], int swizzle_bytes) {
+  auto fn = encode_fn();
+  SMELB_CHECK_ARG(fn != nullptr, kErrCuda, "cuTensorMapEncodeTiled is not available from the driver");
+  SMELB_CHECK_ARG(base != nullptr, kErrArg, "tensor map over a null pointer");
+  SMELB_CHECK_ARG((reinterpret_cast<uintptr_t>(base) & 15) == 0, kErrShape, "tensor map base not 16-byte aligned");
+  SMELB_CHECK_ARG(strides_bytes[0] % 16 == 0 && strides_bytes[1] % 16 == 0, kErrShape,
+                  "tensor map strides %llu, %llu not multiples of 16 bytes", (unsigned long long)strides_bytes[0],
+                  (unsigned long long)strides_bytes[1]);
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
+  cuuint64_t d[3] = {dims[0], dims[1] ? dims[1] : 1, dims[2] ? dims[2] : 1};
+  cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  SMELB_CHECK_ARG(r == CUDA_SUCCESS, kErrShape, "cuTensorMapEncodeTiled (3-d) failed (%d): dims=%llux%llux%llu box=%ux%ux%u",
+                  (int)r, (unsigned long long)d[0], (unsigned long long)d[1], (unsigned long long)d[2], bx[0], bx[1],
+                  bx[2]);
   return kOk;
 }
 

@@ -126,6 +126,31 @@ int int8_rows_quantize(const void* w, bool w_fp32, long long rows, int H, void* 
 int int8_rows_dequant(const void* q, const void* scale, long long rows, int H, void* out, cudaStream_t s,
                       bool out_fp32 = false);
 
+// Small-token dequant-GEMV over a frozen int4 bank (gemv.cu): the rows of expert ids[i] (i itself when ids is null)
+// are the token rows offsets[e] .. offsets[e] + counts[e] - 1 of xs (without offsets: the experts' rows follow one
+// another in id order); q [E][rows_w][K/2], sz [E][K/64][rows_w] (scale | zero << 16).
+// glu: out[., inter] = act(x W[0:inter]^T) * (x W[inter:2 inter]^T), pre-activations into hout when given;
+// otherwise out[., rows_w] = x W^T. tok_hint: the expected rows per active expert (sizes the token tile).
+struct GemvArgs {
+  const bf16* xs;
+  long long ldx;
+  const int *counts, *offsets, *ids;
+  int n_ids;
+  int n_experts;  // experts in the bank (bounds of q / sz)
+  const uint8_t* q;
+  const uint32_t* sz;
+  int rows_w, K, inter, act;
+  bool glu;
+  int tok_hint;
+  bf16* out;
+  long long ldo;
+  bf16* hout;
+  long long ldh;
+};
+int int4_gemv(const GemvArgs& a, cudaStream_t st);
+// Whether the GEMV takes a reduction length K (its shared-memory stages must hold two tasks).
+bool int4_gemv_supported(bool glu, int K);
+
 int rmsnorm_fwd(const NormArgs& a, cudaStream_t st);
 int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st);
 

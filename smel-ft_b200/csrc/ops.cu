@@ -1,5 +1,7 @@
 // C ABI of smelb (include/smelb.h): argument checks, GEMM problem construction and the sequencing of the MoE layer's
 // forward and backward launches.
+#include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -22,6 +24,39 @@ namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
 constexpr int kW64 = 64;       // column width of the LoRA token-side buffers and extension blocks
+
+// Dispatch-row count at or below which the forward's frozen int4 experts take the dequant-GEMV (gemv.cu) instead of
+// the tile engine: few rows per expert make the call a stream of the touched experts' weights.
+std::atomic<long long> g_gemv_rows{4096};
+
+// The frozen int4 gate/up (glu) or down matrix over expert-grouped rows on the GEMV (rows_est: the expected number
+// of rows over all n_ids experts, which sizes the token tile).
+int gemv_frozen(bool glu, const void* xs, long long ldx, const int* counts, const int* offsets, const int* ids,
+                int n_ids, int n_experts, const void* q, const uint32_t* sz, int rows_w, int K, int inter, int act, long long rows_est,
+                void* out, long long ldo, void* hout, long long ldh, cudaStream_t st) {
+  GemvArgs g;
+  g.xs = (const bf16*)xs;
+  g.ldx = ldx;
+  g.counts = counts;
+  g.offsets = offsets;
+  g.ids = ids;
+  g.n_ids = n_ids;
+  g.n_experts = n_experts;
+  g.q = (const uint8_t*)q;
+  g.sz = sz;
+  g.rows_w = rows_w;
+  g.K = K;
+  g.inter = inter;
+  g.act = act;
+  g.glu = glu;
+  const long long busy = std::max(1LL, std::min<long long>(n_ids, rows_est));
+  g.tok_hint = (int)std::min<long long>(1 << 20, (rows_est + busy - 1) / busy);
+  g.out = (bf16*)out;
+  g.ldo = ldo;
+  g.hout = (bf16*)hout;
+  g.ldh = ldh;
+  return int4_gemv(g, st);
+}
 
 // ---------------------------------------------------------------------------------------------- tensor maps
 int tm_bf16(CUtensorMap* m, const void* p, long long rows, long long cols, int box_rows) {
@@ -272,12 +307,13 @@ int add_shared_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* h
   return kOk;
 }
 
-// The routed gate/up GEMMs + GLU epilogue: frozen experts (int4 bank, or bf16 fz_gu) and the selected bf16 experts
-// with their LoRA K-extension, a = act(g) * u over the dispatch rows, pre-activations into hout when given.
-int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout) {
+// The routed gate/up GEMMs + GLU epilogue: frozen experts (int4 bank, or bf16 fz_gu; left out when !frozen) and the
+// selected bf16 experts with their LoRA K-extension, a = act(g) * u over the dispatch rows, pre-activations into
+// hout when given.
+int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout, bool frozen = true) {
   const int H = (int)L.H, E = (int)L.E, I = (int)L.I, nsel = (int)L.n_sel, nfz = (int)(L.E - L.n_sel);
   const long long R = L.max_rows;
-  if (nfz > 0) {
+  if (nfz > 0 && frozen) {
     Problem& P = b.add();
     if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, false, true));
     else TRY(set_a_int4(P, Int4Mat{L.gu_q, L.gu_sz, E, 2 * I, H}, false));
@@ -308,6 +344,14 @@ int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* h
     P.act = L.act;
   }
   return kOk;
+}
+
+// Few dispatch rows: the frozen int4 experts stream through the dequant-GEMV (forward, and the backward's recompute
+// of the same pre-activations, so that saving and recomputing them give the same bits).
+long long routed_rows(const smelb_moe_layer& L, const Flags& f) { return f.ext ? L.max_rows : L.T * L.K; }
+bool gemv_fits(int64_t H, int64_t I) { return int4_gemv_supported(true, (int)H) && int4_gemv_supported(false, (int)I); }
+bool frozen_on_gemv(const smelb_moe_layer& L, const Flags& f) {
+  return f.routed && L.E > L.n_sel && !f.fz_bf16 && routed_rows(L, f) <= g_gemv_rows.load() && gemv_fits(L.H, L.I);
 }
 
 // ---------------------------------------------------------------------------------------------- layer forward
@@ -383,10 +427,12 @@ int layer_fwd(const smelb_moe_layer& L) {
     if (f.shared) TRY(add_shared_glu(b, L, f, f.save ? L.sh_h : nullptr));
     TRY(b.launch(st));
   }
+  const long long rows_est = routed_rows(L, f);
+  const bool gemv = frozen_on_gemv(L, f);
   // L3: routed gate/up (frozen int4 + selected bf16 with LoRA), shared LoRA A of the down projection
   {
     Builder b;
-    if (f.routed) TRY(add_routed_glu(b, L, f, f.save ? L.h : nullptr));
+    if (f.routed) TRY(add_routed_glu(b, L, f, f.save ? L.h : nullptr, !gemv));
     if (f.sh_lora) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.sp_z_w, 1, rh, S, false, false));
@@ -397,6 +443,9 @@ int layer_fwd(const smelb_moe_layer& L) {
     }
     TRY(b.launch(st));
   }
+  if (gemv)
+    TRY(gemv_frozen(true, L.xs, H, L.gcounts, L.offsets, L.frozen_ids, nfz, E, L.gu_q, L.gu_sz, 2 * I, H, I, L.act,
+                    rows_est, L.a, I, f.save ? L.h : nullptr, 2 * I, st));
   // L4: selected LoRA A of the down projection, shared down projection
   {
     Builder b;
@@ -419,9 +468,12 @@ int layer_fwd(const smelb_moe_layer& L) {
     TRY(b.launch(st));
   }
   // L5: routed down projections
+  if (gemv)
+    TRY(gemv_frozen(false, L.a, I, L.gcounts, L.offsets, L.frozen_ids, nfz, E, L.dn_q, L.dn_sz, H, I, 0, 0, rows_est,
+                    L.y, H, nullptr, 0, st));
   if (f.routed) {
     Builder b;
-    if (nfz > 0) {
+    if (nfz > 0 && !gemv) {
       Problem& P = b.add();
       if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_dn, E, H, I, false, false));
       else TRY(set_a_int4(P, dn, false));
@@ -469,10 +521,14 @@ int layer_bwd(const smelb_moe_layer& L) {
   // R0: without saved gate/up pre-activations (the forward kept only its inputs), recompute them into h / sh_h
   if (f.recompute && (f.routed || f.shared)) {
     SMELB_CHECK_ARG((!f.routed || L.h) && (!f.shared || L.sh_h), kErrArg, "layer_bwd: recompute needs h / sh_h");
+    const bool gemv = frozen_on_gemv(L, f);
     Builder b;
     if (f.shared) TRY(add_shared_glu(b, L, f, L.sh_h));
-    if (f.routed) TRY(add_routed_glu(b, L, f, L.h));
+    if (f.routed) TRY(add_routed_glu(b, L, f, L.h, !gemv));
     TRY(b.launch(st));
+    if (gemv)
+      TRY(gemv_frozen(true, L.xs, H, L.gcounts, L.offsets, L.frozen_ids, (int)(E - L.n_sel), E, L.gu_q, L.gu_sz, 2 * I,
+                      H, I, L.act, routed_rows(L, f), L.a, I, L.h, 2 * I, st));
   }
   if (f.routed && !f.ext)
     TRY(combine_bwd_rows(L.g, L.y, L.src_of, L.total, R, topv, f.topv32, K, H, L.dy, L.dtopv, st));
@@ -707,6 +763,12 @@ int frozen_fwd(const FrozenBank& bank, const void* xs, int64_t rows, int64_t H, 
   TRY(frozen_check(xs, rows, H, I, counts, E, act, "frozen_experts_fwd"));
   SMELB_CHECK_ARG(a_buf && out, kErrArg, "frozen_experts_fwd: null output");
   if (rows == 0) return kOk;
+  if (!bank.gu_w && rows <= g_gemv_rows.load() && gemv_fits(H, I)) {
+    TRY(gemv_frozen(true, xs, H, counts, nullptr, nullptr, (int)E, (int)E, bank.gu.q, bank.gu.sz, (int)(2 * I), (int)H,
+                    (int)I, act, rows, a_buf, I, h_save, 2 * I, st));
+    return gemv_frozen(false, a_buf, I, counts, nullptr, nullptr, (int)E, (int)E, bank.dn.q, bank.dn.sz, (int)H, (int)I, 0,
+                       0, rows, out, H, nullptr, 0, st);
+  }
   {
     Builder b;
     Problem& P = b.add();
@@ -744,6 +806,12 @@ int frozen_bwd(const FrozenBank& bank, const void* xs, const void* dy, int64_t r
   SMELB_CHECK_ARG(dh_buf && dx, kErrArg, "frozen_experts_bwd: null output");
   SMELB_CHECK_ARG(h || (xs && h_buf), kErrArg, "frozen_experts_bwd: need the saved h or xs and h_buf to recompute");
   if (rows == 0) return kOk;
+  if (!h && !bank.gu_w && rows <= g_gemv_rows.load() && gemv_fits(H, I)) {
+    // recompute on the GEMV as the forward did (the GLU output goes to dh_buf, overwritten below)
+    TRY(gemv_frozen(true, xs, H, counts, nullptr, nullptr, (int)E, (int)E, bank.gu.q, bank.gu.sz, (int)(2 * I), (int)H,
+                    (int)I, act, rows, dh_buf, I, h_buf, 2 * I, st));
+    h = h_buf;
+  }
   if (!h) {
     // recompute gate/up pre-activations into h_buf (the GLU output goes to dh_buf, overwritten below)
     Builder b;
@@ -1161,6 +1229,10 @@ int smelb_lora_linear_bwd(const void* x, const void* dy, int64_t T, int64_t in_f
 size_t smelb_moe_layer_size(void) { return sizeof(smelb_moe_layer); }
 
 long long smelb_launch_count(void) { return smelb::launch_count(); }
+
+int64_t smelb_set_gemv_rows(int64_t rows) {
+  return g_gemv_rows.exchange(rows < 0 ? 0 : (long long)rows);
+}
 
 int smelb_gemm_timing(int enable) {
   smelb::set_gemm_timing(enable != 0);

@@ -12,7 +12,7 @@ Drop-in names for the reference modules:
 All compute runs in libsmelb.so (hand-written CUDA for sm_100a) through the C ABI in include/smelb.h.
 """
 from . import _lib
-from ._lib import SmelbError, read_status
+from ._lib import SmelbError, read_status, set_gemv_rows
 from .loss import LMHead, chunked_ce
 from .lora import BlockLoRA, ExpertsLoRA, LayerLoRA, MLPLoRA, lora_gate_up, lora_linear
 from .moe import (BF16Experts, FrozenExpertsFn, Int4Experts, LayerExperts, mlp_lora, moe_block_gemma4, moe_forward,
@@ -24,7 +24,7 @@ __all__ = ["BF16Experts", "BlockLoRA", "ExpertsLoRA", "FrozenExpertsFn", "Int4Ex
            "LayerLoRA", "MLPLoRA", "SmelbError", "add_rmsnorm", "chunked_ce", "dequant_int4", "dequant_int4_torch",
            "dequant_int8_rows", "lora_gate_up", "lora_linear", "mlp_lora", "moe_block_gemma4", "moe_forward",
            "quantize_int4", "quantize_int8_rows", "read_status", "rel_err", "rmsnorm", "route", "route_gemma4",
-           "routed_experts", "set_save_preactivations", "shared_mlp"]
+           "routed_experts", "set_gemv_rows", "set_save_preactivations", "shared_mlp"]
 
 
 def load_library():

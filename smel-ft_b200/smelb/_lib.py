@@ -134,6 +134,7 @@ SIGNATURES = {
     "smelb_moe_layer_size": (ctypes.c_size_t, []),
     "smelb_launch_count": (ctypes.c_longlong, []),
     "smelb_gemm_timing": (c_i32, [c_i32]),
+    "smelb_set_gemv_rows": (c_i64, [c_i64]),
     "smelb_gemm_timing_read": (c_i32, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
     "smelb_moe_layer_fwd": (c_i32, [ctypes.POINTER(MoELayerStruct)]),
     "smelb_moe_layer_bwd": (c_i32, [ctypes.POINTER(MoELayerStruct)]),
@@ -183,6 +184,12 @@ def read_status(device=None, reset=True) -> int:
 def launch_count() -> int:
     """Kernels launched by libsmelb so far."""
     return int(load().smelb_launch_count())
+
+
+def set_gemv_rows(rows: int) -> int:
+    """Dispatch rows at or below which the forward's frozen int4 experts run as the dequant-GEMV (0: never);
+    returns the previous value."""
+    return int(load().smelb_set_gemv_rows(int(rows)))
 
 
 def gemm_timing(enable: bool):

@@ -33,7 +33,7 @@ import torch.distributed as dist
 from . import _lib
 from .lora import ExpertsLoRA, LayerLoRA
 from .moe import (_SAVE_PREACT, BF16Experts, Int4Experts, LayerExperts, _alloc_bwd, _alloc_fwd, _bf16, _Cfg, _fp32,
-                  _LORA_NAMES, _set_routed, _struct, route, shared_mlp)
+                  _LORA_NAMES, _set_routed, _struct, router_and_shared)
 
 SYNC = {"wait_done": 0, "publish": 1, "wait_ready": 2, "ack": 3}
 
@@ -336,11 +336,8 @@ def moe_forward_ep(x2d, W, shard: EPShard, top_k: int, comm: EPGroup, stats=None
     rank's [T, H] output, differentiable w.r.t. x2d, the local selected experts' LoRA parameters and the shared LoRA
     parameters."""
     x2d = _bf16(x2d, "moe_forward_ep: x")
-    probs, topv, topi = route(x2d, W["mlp.gate.weight"], top_k)
-    if stats is not None:
-        stats(probs, topv, topi)
     lora_sh = shard.lora.shared if shard.lora is not None else None
-    sh = shared_mlp(x2d, W, lora_sh)
+    sh, probs, topv, topi = router_and_shared(x2d, W, top_k, lora_sh, stats)
     lex = shard.lora.experts if shard.lora is not None else None
     params = [getattr(lex, n) for n in _LORA_NAMES] if lex is not None else [None] * 6
     return _EPRoutedFn.apply(x2d, topv, sh, topi, shard, comm, float(cap_factor), *params)

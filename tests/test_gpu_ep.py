@@ -6,7 +6,8 @@ all-reduced for the shared expert) within the tolerance of the other layer tests
 One rank on one GPU runs every kernel of the exchange against its own region (plan, row packing, entry numbering,
 dispatch, partial combine, collection, and the backward's dY, d weight and dX return); two ranks on two GPUs (skipped
 with fewer) exchange over NVLink with a load-balanced expert placement. A CUDA-graph capture of the one-rank step
-must replay to the eager step's bits."""
+must replay to the eager step's bits. The one-rank comparison runs with the frozen experts on the tile engine and
+again on the small-token GEMV (smelb.set_gemv_rows), the fused layer and the owner taking the same path each time."""
 import copy
 import os
 import socket
@@ -35,7 +36,17 @@ def _bad(checks):
     return bad
 
 
-def test_expert_parallel_one_rank_matches_fused_layer():
+@pytest.mark.parametrize("gemv_rows", [0, 1 << 30])
+def test_expert_parallel_one_rank_matches_fused_layer(gemv_rows):
+    import smelb
+    prev = smelb.set_gemv_rows(gemv_rows)
+    try:
+        _one_rank()
+    finally:
+        smelb.set_gemv_rows(prev)
+
+
+def _one_rank():
     import smelb
     from smelb import ep
     from smelb.synth import qwen_layer
