@@ -28,8 +28,10 @@ constexpr int kDevErrEpCapacity = 14; // more dispatch entries than the owner's 
 
 // ------------------------------------------------------------------------------------------ region layout
 struct EpLayout {
-  size_t ready, done, send_epoch, recv_epoch, counts, nent, meta, wts, eoff, dwts, rows[4], total;
+  size_t ready, done, send_epoch, recv_epoch, counts, nent, tcnt, meta, wts, eoff, dwts, rows[4], total;
 };
+
+constexpr int kPlanTile = 256;  // tokens per block of the source-side plan
 
 static size_t ep_al(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -42,6 +44,7 @@ static EpLayout ep_layout(int P, int cap, int K, int H) {
   L.counts = 512;                    // int [4][kEpMaxRanks]: rows per destination
   L.nent = 768;                      // int [kEpMaxRanks]: dispatch entries per destination
   size_t o = 1024;
+  L.tcnt = o;  o += ep_al((size_t)((cap + kPlanTile - 1) / kPlanTile) * kEpMaxRanks * 2 * 4);  // int [tiles][P][2]
   const size_t rk = (size_t)P * cap * K;
   L.meta = o;  o += ep_al(rk * 4);   // int [P][cap][K]: local expert | k << 16, -1 after a row's entries
   L.wts = o;   o += ep_al(rk * 4);   // f32 [P][cap][K]: routing weight of each entry
@@ -124,7 +127,7 @@ __global__ void ep_ack_kernel(EpPeers peers, char* mine, EpLayout L, int P, int 
 }
 
 // ------------------------------------------------------------------------------------------ block scan
-// exclusive scan of (a, b) over a 1024-thread block; returns the block totals in tot_a / tot_b
+// exclusive scan of (a, b) over the block (up to 1024 threads); returns the block totals in tot_a / tot_b
 __device__ __forceinline__ void scan2(int a, int b, int& ex_a, int& ex_b, int& tot_a, int& tot_b) {
   __shared__ int wa[32], wb[32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -165,119 +168,190 @@ __device__ __forceinline__ void scan2(int a, int b, int& ex_a, int& ex_b, int& t
 }
 
 // ------------------------------------------------------------------------------------------ source side
-// One block per destination d: the tokens with at least one expert owned by d, in token order (so the exchange is
-// deterministic), their row position pos[t][d], the row's entries (local expert id and k, in k order) with their
-// routing weights, the entry offset of every row and the slot j of every choice (t, k) within its row.
-__global__ void __launch_bounds__(1024) ep_plan_kernel(const long long* __restrict__ topi, const void* __restrict__ topv,
-                                                       int topv_f32, int T, int K, const int* __restrict__ owner,
-                                                       const int* __restrict__ local_id, int P, int cap, char* mine,
-                                                       EpLayout L, int* __restrict__ pos, int* __restrict__ slot_j,
-                                                       int* __restrict__ tok_of) {
-  const int d = blockIdx.x;
+// The source-side plan, in token order (so the exchange is deterministic): for every destination d the tokens with
+// at least one expert owned by d, their row position pos[t][d], the row's entries (local expert id and k, in k order)
+// with their routing weights, the entry offset of every row and the slot j of every choice (t, k) within its row.
+// Two passes over tiles of kPlanTile tokens: the tiles' row and entry counts per destination, then every tile writes
+// its rows at the running offsets of the tiles before it.
+
+// 5-bit count per destination of the token's choices it owns (K <= 16, P <= 8)
+__device__ __forceinline__ unsigned long long plan_mask(const long long* __restrict__ topi,
+                                                        const int* __restrict__ owner, int t, int T, int K) {
+  unsigned long long m = 0;
+  if (t >= T) return 0;
+  long long e[kEpMaxK];
+#pragma unroll
+  for (int k = 0; k < kEpMaxK; ++k)
+    if (k < K) e[k] = topi[(long long)t * K + k];
+#pragma unroll
+  for (int k = 0; k < kEpMaxK; ++k)
+    if (k < K) m += 1ull << (5 * owner[e[k]]);
+  return m;
+}
+
+__global__ void __launch_bounds__(kPlanTile) ep_plan_count_kernel(const long long* __restrict__ topi, int T, int K,
+                                                                  const int* __restrict__ owner, int P, char* mine,
+                                                                  EpLayout L) {
+  __shared__ int part[kPlanTile / 32][kEpMaxRanks][2];
+  const int t = blockIdx.x * kPlanTile + threadIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const unsigned long long m = plan_mask(topi, owner, t, T, K);
+#pragma unroll
+  for (int d = 0; d < kEpMaxRanks; ++d) {
+    if (d >= P) break;
+    const unsigned c = (unsigned)(m >> (5 * d)) & 31u;
+    const unsigned r = __reduce_add_sync(0xffffffffu, c > 0 ? 1u : 0u), n = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) {
+      part[w][d][0] = (int)r;
+      part[w][d][1] = (int)n;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * P) {
+    const int d = threadIdx.x >> 1, q = threadIdx.x & 1;
+    int v = 0;
+    for (int i = 0; i < kPlanTile / 32; ++i) v += part[i][d][q];
+    reinterpret_cast<int*>(mine + L.tcnt)[((long long)blockIdx.x * kEpMaxRanks + d) * 2 + q] = v;
+  }
+}
+
+__global__ void __launch_bounds__(kPlanTile) ep_plan_fill_kernel(const long long* __restrict__ topi,
+                                                                 const void* __restrict__ topv, int topv_f32, int T,
+                                                                 int K, const int* __restrict__ owner,
+                                                                 const int* __restrict__ local_id, int P, int cap,
+                                                                 char* mine, EpLayout L, int* __restrict__ pos,
+                                                                 int* __restrict__ slot_j, int* __restrict__ tok_of) {
+  __shared__ int base[kEpMaxRanks][2];
+  const int t = blockIdx.x * kPlanTile + threadIdx.x;
+  const int* tcnt = reinterpret_cast<const int*>(mine + L.tcnt);
+  if (threadIdx.x < 2 * P) {
+    // running offsets of this tile per destination: the sums over the tiles before it (and, in the last tile, the
+    // destination's totals)
+    const int d = threadIdx.x >> 1, q = threadIdx.x & 1;
+    int v = 0;
+    for (int i = 0; i < (int)blockIdx.x; ++i) v += tcnt[((long long)i * kEpMaxRanks + d) * 2 + q];
+    base[d][q] = v;
+    if (blockIdx.x == gridDim.x - 1)
+      reinterpret_cast<int*>(mine + (q ? L.nent : L.counts))[d] = v + tcnt[((long long)blockIdx.x * kEpMaxRanks + d) * 2 + q];
+  }
+  __syncthreads();
+  const unsigned long long m = plan_mask(topi, owner, t, T, K);
   int* meta = reinterpret_cast<int*>(mine + L.meta);
   float* wts = reinterpret_cast<float*>(mine + L.wts);
   int* eoff = reinterpret_cast<int*>(mine + L.eoff);
-  int carry_r = 0, carry_e = 0;
-  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
-    const int t = t0 + threadIdx.x;
-    int m = 0;
-    if (t < T)
-      for (int k = 0; k < K; ++k) m += owner[topi[(long long)t * K + k]] == d;
+  for (int d = 0; d < P; ++d) {
+    const int c = (int)((m >> (5 * d)) & 31u);
     int pr, pe, tr, te;
-    scan2(m > 0, m, pr, pe, tr, te);
-    if (t < T) {
-      if (m > 0) {
-        const int p = carry_r + pr;
-        const long long row = (long long)d * cap + p;
-        tok_of[row] = t;
-        pos[(long long)t * P + d] = p;
-        eoff[row] = carry_e + pe;
-        int j = 0;
-        for (int k = 0; k < K; ++k) {
-          const long long e = topi[(long long)t * K + k];
-          if (owner[e] != d) continue;
-          meta[row * K + j] = local_id[e] | (k << 16);
-          wts[row * K + j] = topv_f32 ? reinterpret_cast<const float*>(topv)[(long long)t * K + k]
-                                      : __bfloat162float(reinterpret_cast<const bf16*>(topv)[(long long)t * K + k]);
-          slot_j[(long long)t * K + k] = j;
-          ++j;
-        }
-        for (; j < K; ++j) meta[row * K + j] = -1;
-      } else {
-        pos[(long long)t * P + d] = -1;
-      }
+    scan2(c > 0, c, pr, pe, tr, te);
+    if (t >= T) continue;
+    if (c == 0) {
+      pos[(long long)t * P + d] = -1;
+      continue;
     }
-    carry_r += tr;
-    carry_e += te;
-  }
-  if (threadIdx.x == 0) {
-    reinterpret_cast<int*>(mine + L.counts)[d] = carry_r;
-    reinterpret_cast<int*>(mine + L.nent)[d] = carry_e;
+    const int p = base[d][0] + pr;
+    const long long row = (long long)d * cap + p;
+    tok_of[row] = t;
+    pos[(long long)t * P + d] = p;
+    eoff[row] = base[d][1] + pe;
+    int j = 0;
+    for (int k = 0; k < K; ++k) {
+      const long long e = topi[(long long)t * K + k];
+      if (owner[e] != d) continue;
+      meta[row * K + j] = local_id[e] | (k << 16);
+      wts[row * K + j] = topv_f32 ? reinterpret_cast<const float*>(topv)[(long long)t * K + k]
+                                  : __bfloat162float(reinterpret_cast<const bf16*>(topv)[(long long)t * K + k]);
+      slot_j[(long long)t * K + k] = j;
+      ++j;
+    }
+    for (; j < K; ++j) meta[row * K + j] = -1;
   }
 }
 
-// rows[b][d][i] = src[tok_of[d][i]] for the rows of every destination (16-byte copies); counts[b] = counts[0]
+// rows[b][d][i] = src[tok_of[d][i]] for the rows of every destination, one warp per row (16-byte copies);
+// counts[b] = counts[0]
 __global__ void ep_pack_rows_kernel(const bf16* __restrict__ src, int H, const int* __restrict__ tok_of, int P,
-                                    int cap, char* mine, EpLayout L, int b) {
-  const int* cnt = reinterpret_cast<const int*>(mine + L.counts);
-  const int vpr = H / 8;
-  const long long n = (long long)P * cap * vpr;
-  uint4* dst = reinterpret_cast<uint4*>(mine + L.rows[b]);
-  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
-    const long long row = v / vpr;
-    const int d = (int)(row / cap), i = (int)(row - (long long)d * cap);
-    if (i >= cnt[d]) continue;
-    const int c = (int)(v - row * vpr);
-    dst[v] = reinterpret_cast<const uint4*>(src + (long long)tok_of[row] * H)[c];
+                                    int cap, char* mine, size_t counts_off, size_t rows_off, int b) {
+  __shared__ int cnt[kEpMaxRanks];
+  if (threadIdx.x < kEpMaxRanks) cnt[threadIdx.x] = threadIdx.x < P ? reinterpret_cast<const int*>(mine + counts_off)[threadIdx.x] : 0;
+  __syncthreads();
+  const int vpr = H / 8, lane = threadIdx.x & 31;
+  const int nw = P * cap;
+  uint4* dst = reinterpret_cast<uint4*>(mine + rows_off);
+  for (int row = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5); row < nw;
+       row += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
+    const int d = row / cap;
+    if (row - d * cap >= cnt[d]) continue;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + (long long)tok_of[row] * H);
+    uint4* d4 = dst + (long long)row * vpr;
+    for (int c = lane; c < vpr; c += 32) d4[c] = s4[c];
   }
   if (b != 0 && blockIdx.x == 0 && threadIdx.x < P)
-    reinterpret_cast<int*>(mine + L.counts)[b * kEpMaxRanks + threadIdx.x] = cnt[threadIdx.x];
+    reinterpret_cast<int*>(mine + counts_off)[b * kEpMaxRanks + threadIdx.x] = cnt[threadIdx.x];
 }
 
 // ------------------------------------------------------------------------------------------ owner side
-// One block per source s: the rows s sent to this rank and their dispatch entries, numbered in (source, row, slot)
-// order: entry n of row (s, i) slot j is base_s + eoff + j. Writes per entry its local expert (int64, the dispatch
-// plan's input), source row (s * cap + i) and weight; per row its first entry and entry count; per source its row
-// count.
-__global__ void __launch_bounds__(1024) ep_recv_plan_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int K,
-                                                            long long cap_e, long long* __restrict__ entry_e,
-                                                            int* __restrict__ entry_row, float* __restrict__ entry_w,
-                                                            int* __restrict__ row_beg, int* __restrict__ row_m,
-                                                            int* __restrict__ rc, int* __restrict__ n_total, int* err) {
-  const int s = blockIdx.x;
+// The rows every source s sent to this rank and their dispatch entries, numbered in (source, row, slot) order: entry n
+// of row (s, i) slot j is base_s + eoff + j. Writes per entry its local expert (int64, the dispatch plan's input),
+// source row (s * cap + i) and weight; per row its first entry and entry count; per source its row count. Blocks of
+// 256 rows of one source (grid: row tiles x sources).
+__global__ void __launch_bounds__(256) ep_recv_plan_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int K,
+                                                           long long cap_e, long long* __restrict__ entry_e,
+                                                           int* __restrict__ entry_row, float* __restrict__ entry_w,
+                                                           int* __restrict__ row_beg, int* __restrict__ row_m,
+                                                           int* __restrict__ rc, int* __restrict__ n_total, int* err) {
+  __shared__ long long s_base;
+  __shared__ int s_c;
+  const int s = blockIdx.y;
   const char* src = peers.base[s];
-  const int c = reinterpret_cast<const int*>(src + L.counts)[rank];
-  long long base = 0, total = 0;
-  for (int q = 0; q < P; ++q) {
-    const int ne = reinterpret_cast<const int*>(peers.base[q] + L.nent)[rank];
-    if (q < s) base += ne;
-    total += ne;
-  }
-  if (threadIdx.x == 0) {
-    rc[s] = c;
-    if (s == 0) *n_total = (int)(total < cap_e ? total : cap_e);
-    if (s == 0 && total > cap_e) dev_fail_at(err, kDevErrEpCapacity, (int)total, (int)cap_e);
-  }
-  const int* meta = reinterpret_cast<const int*>(src + L.meta) + (long long)rank * cap * K;
-  const float* wts = reinterpret_cast<const float*>(src + L.wts) + (long long)rank * cap * K;
-  const int* eoff = reinterpret_cast<const int*>(src + L.eoff) + (long long)rank * cap;
-  for (int i = threadIdx.x; i < c; i += blockDim.x) {
-    const long long beg = base + eoff[i];
-    int m = 0;
-    for (int j = 0; j < K; ++j) {
-      const int mt = meta[(long long)i * K + j];
-      if (mt < 0) break;
-      const long long nn = beg + j;
-      if (nn < cap_e) {
-        entry_e[nn] = mt & 0xFFFF;
-        entry_row[nn] = s * cap + i;
-        entry_w[nn] = wts[(long long)i * K + j];
-      }
-      ++m;
+  if (threadIdx.x < 32) {
+    // entries every source sends this rank (one remote read per source, in parallel over the lanes)
+    const int q = threadIdx.x;
+    const long long ne = q < P ? reinterpret_cast<const int*>(peers.base[q] + L.nent)[rank] : 0;
+    long long before = q < s ? ne : 0, total = ne;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      total += __shfl_xor_sync(0xffffffffu, total, o);
     }
-    row_beg[(long long)s * cap + i] = (int)(beg < cap_e ? beg : cap_e);
-    row_m[(long long)s * cap + i] = (int)(beg + m <= cap_e ? m : (beg < cap_e ? cap_e - beg : 0));  // kept entries
+    if (q == 0) {
+      s_base = before;
+      s_c = reinterpret_cast<const int*>(src + L.counts)[rank];
+      if (blockIdx.x == 0) {
+        rc[s] = s_c;
+        if (s == 0) {
+          *n_total = (int)(total < cap_e ? total : cap_e);
+          if (total > cap_e) dev_fail_at(err, kDevErrEpCapacity, (int)total, (int)cap_e);
+        }
+      }
+    }
   }
+  __syncthreads();
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= s_c) return;
+  const int* meta = reinterpret_cast<const int*>(src + L.meta) + ((long long)rank * cap + i) * K;
+  const float* wts = reinterpret_cast<const float*>(src + L.wts) + ((long long)rank * cap + i) * K;
+  const long long beg = s_base + reinterpret_cast<const int*>(src + L.eoff)[(long long)rank * cap + i];
+  int mt[kEpMaxK];
+  float wv[kEpMaxK];
+#pragma unroll
+  for (int j = 0; j < kEpMaxK; ++j)
+    if (j < K) {
+      mt[j] = meta[j];
+      wv[j] = wts[j];
+    }
+  int m = 0;
+#pragma unroll
+  for (int j = 0; j < kEpMaxK; ++j) {
+    if (j >= K || mt[j] < 0) break;
+    const long long nn = beg + j;
+    if (nn < cap_e) {
+      entry_e[nn] = mt[j] & 0xFFFF;
+      entry_row[nn] = s * cap + i;
+      entry_w[nn] = wv[j];
+    }
+    ++m;
+  }
+  row_beg[(long long)s * cap + i] = (int)(beg < cap_e ? beg : cap_e);
+  row_m[(long long)s * cap + i] = (int)(beg + m <= cap_e ? m : (beg < cap_e ? cap_e - beg : 0));  // kept entries
 }
 
 // entries past the received ones go to the sink expert, whose dispatch segment no GEMM reads
@@ -288,36 +362,47 @@ __global__ void ep_fill_sink_kernel(long long* __restrict__ entry_e, long long c
     if (n >= n0) entry_e[n] = sink;
 }
 
-// local[s][i] = source s's rows[b][rank][i] for its rows (the one pull over NVLink per row and exchange)
-__global__ void ep_pull_rows_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int H, int b,
-                                    bf16* __restrict__ local) {
-  const int vpr = H / 8;
-  const long long n = (long long)P * cap * vpr;
-  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
-    const long long row = v / vpr;
-    const int s = (int)(row / cap), i = (int)(row - (long long)s * cap);
-    const char* src = peers.base[s];
-    if (i >= reinterpret_cast<const int*>(src + L.counts)[b * kEpMaxRanks + rank]) continue;
-    const int c = (int)(v - row * vpr);
-    const uint4* r = reinterpret_cast<const uint4*>(src + L.rows[b]) + ((long long)rank * cap + i) * vpr;
-    reinterpret_cast<uint4*>(local)[v] = r[c];
+// local[s][i] = source s's rows[b][rank][i] for its rows (the one pull over NVLink per row and exchange), one warp per
+// row; the row counts of the sources are read once per block
+__global__ void ep_pull_rows_kernel(EpPeers peers, size_t counts_off, size_t rows_off, int P, int rank, int cap, int H,
+                                    int b, bf16* __restrict__ local) {
+  __shared__ int cnt[kEpMaxRanks];
+  __shared__ const char* base[kEpMaxRanks];
+  if (threadIdx.x < kEpMaxRanks) {
+    const int s = threadIdx.x;
+    base[s] = s < P ? peers.base[s] : nullptr;
+    cnt[s] = s < P ? reinterpret_cast<const int*>(peers.base[s] + counts_off)[b * kEpMaxRanks + rank] : 0;
+  }
+  __syncthreads();
+  const int vpr = H / 8, lane = threadIdx.x & 31;
+  const int nw = P * cap;
+  for (int row = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5); row < nw;
+       row += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
+    const int s = row / cap, i = row - s * cap;
+    if (i >= cnt[s]) continue;
+    const uint4* r = reinterpret_cast<const uint4*>(base[s] + rows_off) + ((long long)rank * cap + i) * vpr;
+    uint4* d4 = reinterpret_cast<uint4*>(local) + (long long)row * vpr;
+    for (int c = lane; c < vpr; c += 32) d4[c] = r[c];
   }
 }
 
-// xs[row] = local[entry_row[src_of[row]]] for the dispatch rows before the sink segment (zeros on padding rows)
+// xs[row] = local[entry_row[src_of[row]]] for the dispatch rows before the sink segment (zeros on padding rows), one
+// warp per row
 __global__ void ep_gather_kernel(const bf16* __restrict__ local, const int* __restrict__ entry_row,
                                  const int* __restrict__ src_of, const int* __restrict__ offsets, int sink, int H,
                                  bf16* __restrict__ xs) {
   const int rows = offsets[sink];
-  const int vpr = H / 8;
-  const long long n = (long long)rows * vpr;
-  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n; v += (long long)gridDim.x * blockDim.x) {
-    const long long row = v / vpr;
-    const int c = (int)(v - row * vpr);
+  const int vpr = H / 8, lane = threadIdx.x & 31;
+  for (int row = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5); row < rows;
+       row += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
     const int e = src_of[row];
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (e >= 0) val = reinterpret_cast<const uint4*>(local + (long long)entry_row[e] * H)[c];
-    reinterpret_cast<uint4*>(xs)[v] = val;
+    uint4* d4 = reinterpret_cast<uint4*>(xs) + (long long)row * vpr;
+    if (e < 0) {
+      for (int c = lane; c < vpr; c += 32) d4[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4* s4 = reinterpret_cast<const uint4*>(local + (long long)entry_row[e] * H);
+    for (int c = lane; c < vpr; c += 32) d4[c] = s4[c];
   }
 }
 
@@ -328,36 +413,56 @@ __global__ void ep_gather_kernel(const bf16* __restrict__ local, const int* __re
 __global__ void ep_return_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
                                  const float* __restrict__ entry_w, const float* __restrict__ entry_dw,
                                  const int* __restrict__ row_beg, const int* __restrict__ row_m, const int* __restrict__ rc,
-                                 int P, int cap, int K, int H, char* mine, EpLayout L, int bwd) {
+                                 int P, int cap, int K, int H, char* mine, size_t counts_off, size_t rows_off,
+                                 size_t dwts_off, int bwd) {
   const int b = bwd ? 3 : 1;
   const int lane = threadIdx.x & 31;
-  const long long nw = (long long)P * cap;
-  bf16* out = reinterpret_cast<bf16*>(mine + L.rows[b]);
-  for (long long wr = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; wr < nw;
-       wr += ((long long)gridDim.x * blockDim.x) >> 5) {
-    const int s = (int)(wr / cap), i = (int)(wr - (long long)s * cap);
+  const int nw = P * cap;
+  bf16* out = reinterpret_cast<bf16*>(mine + rows_off);
+  for (int wr = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5); wr < nw;
+       wr += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
+    const int s = wr / cap, i = wr - s * cap;
     if (i >= rc[s]) continue;
     const int beg = row_beg[wr], m = row_m[wr];
-    if (bwd && lane < m) reinterpret_cast<float*>(mine + L.dwts)[wr * K + lane] = entry_dw[beg + lane];
-    for (int c0 = lane * 8; c0 < H; c0 += 256) {
-      float acc[8];
+    if (bwd && lane < m) reinterpret_cast<float*>(mine + dwts_off)[(long long)wr * K + lane] = entry_dw[beg + lane];
+    // the row's entries, one per lane, broadcast below
+    const int ro = lane < m ? row_of[beg + lane] : 0;
+    const float wl = lane < m ? (bwd ? 1.0f : entry_w[beg + lane]) : 0.f;
+    // four 256-column chunks per pass, each entry's four loads issued together
+    for (int c0 = lane * 8; c0 < H; c0 += 1024) {
+      float acc[4][8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[u][q] = 0.f;
+#pragma unroll 2
       for (int j = 0; j < m; ++j) {
-        const float w = bwd ? 1.0f : entry_w[beg + j];
-        const uint4 v = *reinterpret_cast<const uint4*>(y + (long long)row_of[beg + j] * H + c0);
-        const bf16* pv = reinterpret_cast<const bf16*>(&v);
+        const float w = __shfl_sync(0xffffffffu, wl, j);
+        const bf16* yr = y + (long long)__shfl_sync(0xffffffffu, ro, j) * H;
+        uint4 v[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(__bfloat162float(pv[q]), w));
+        for (int u = 0; u < 4; ++u)
+          if (c0 + u * 256 < H) v[u] = *reinterpret_cast<const uint4*>(yr + c0 + u * 256);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (c0 + u * 256 >= H) break;
+          const bf16* pv = reinterpret_cast<const bf16*>(&v[u]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[u][q] = __fadd_rn(acc[u][q], __fmul_rn(__bfloat162float(pv[q]), w));
+        }
       }
-      uint4 o;
-      bf16* po = reinterpret_cast<bf16*>(&o);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
-      *reinterpret_cast<uint4*>(out + wr * H + c0) = o;
+      for (int u = 0; u < 4; ++u) {
+        if (c0 + u * 256 >= H) break;
+        uint4 o;
+        bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[u][q]);
+        *reinterpret_cast<uint4*>(out + (long long)wr * H + c0 + u * 256) = o;
+      }
     }
   }
-  if (blockIdx.x == 0 && threadIdx.x < P) reinterpret_cast<int*>(mine + L.counts)[b * kEpMaxRanks + threadIdx.x] =
+  if (blockIdx.x == 0 && threadIdx.x < P) reinterpret_cast<int*>(mine + counts_off)[b * kEpMaxRanks + threadIdx.x] =
                                               rc[threadIdx.x];
 }
 
@@ -470,7 +575,8 @@ using namespace smelb;
 extern "C" {
 
 int64_t smelb_ep_region_bytes(int64_t P, int64_t cap, int64_t K, int64_t H) {
-  if (P < 1 || P > kEpMaxRanks || cap < 1 || K < 1 || K > kEpMaxK || H < 8) return 0;
+  // rows of all sources are indexed in 32 bits (P * cap), entries as P * cap * K
+  if (P < 1 || P > kEpMaxRanks || cap < 1 || K < 1 || K > kEpMaxK || H < 8 || P * cap * K >= (1LL << 31)) return 0;
   return (int64_t)ep_layout((int)P, (int)cap, (int)K, (int)H).total;
 }
 
@@ -539,10 +645,21 @@ int smelb_ep_plan(const int64_t* topi, const void* topv, int topv_fp32, int64_t 
   SMELB_CHECK_ARG(T >= 0 && T <= cap && K >= 1 && K <= kEpMaxK && rank >= 0 && rank < P, kErrShape,
                   "ep_plan: T=%lld cap=%lld K=%lld", (long long)T, (long long)cap, (long long)K);
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
-  ep_plan_kernel<<<(int)P, 1024, 0, (cudaStream_t)stream>>>((const long long*)topi, topv, topv_fp32, (int)T, (int)K,
-                                                             owner, local_id, (int)P, (int)cap, pr.base[rank], L, pos,
-                                                             slot_j, tok_of);
+  const int tiles = (int)((T + kPlanTile - 1) / kPlanTile);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (tiles == 0) {
+    // no tokens: every destination gets zero rows and entries
+    SMELB_CUDA(cudaMemsetAsync(pr.base[rank] + L.counts, 0, kEpMaxRanks * sizeof(int), st));
+    SMELB_CUDA(cudaMemsetAsync(pr.base[rank] + L.nent, 0, kEpMaxRanks * sizeof(int), st));
+    return kOk;
+  }
+  ep_plan_count_kernel<<<tiles, kPlanTile, 0, st>>>((const long long*)topi, (int)T, (int)K, owner, (int)P,
+                                                    pr.base[rank], L);
   SMELB_CUDA(cudaGetLastError());
+  ep_plan_fill_kernel<<<tiles, kPlanTile, 0, st>>>((const long long*)topi, topv, topv_fp32, (int)T, (int)K, owner,
+                                                   local_id, (int)P, (int)cap, pr.base[rank], L, pos, slot_j, tok_of);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
   count_launch();
   return kOk;
 }
@@ -554,8 +671,8 @@ int smelb_ep_pack_rows(const void* src, int64_t H, const int32_t* tok_of, const 
   if (rc != kOk) return rc;
   SMELB_CHECK_ARG(src && tok_of && (buffer == 0 || buffer == 2) && H % 8 == 0, kErrArg, "ep_pack_rows: bad arguments");
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
-  ep_pack_rows_kernel<<<ep_grid(P * cap * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)src, (int)H, tok_of, (int)P, (int)cap, pr.base[rank], L, buffer);
+  ep_pack_rows_kernel<<<ep_grid(P * cap * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const bf16*)src, (int)H, tok_of, (int)P, (int)cap, pr.base[rank], L.counts, L.rows[buffer], buffer);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -575,8 +692,9 @@ int smelb_ep_recv_plan(const void* const* regions, int64_t P, int64_t rank, int6
   SMELB_CHECK_ARG(err != nullptr, kErrCuda, "ep_recv_plan: no device status word");
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
   cudaStream_t st = (cudaStream_t)stream;
-  ep_recv_plan_kernel<<<(int)P, 1024, 0, st>>>(pr, L, (int)P, (int)rank, (int)cap, (int)K, cap_entries, (long long*)entry_e,
-                                               entry_row, entry_w, row_beg, row_m, recv_rows, n_total, err);
+  ep_recv_plan_kernel<<<dim3((unsigned)((cap + 255) / 256), (unsigned)P), 256, 0, st>>>(
+      pr, L, (int)P, (int)rank, (int)cap, (int)K, cap_entries, (long long*)entry_e, entry_row, entry_w, row_beg, row_m,
+      recv_rows, n_total, err);
   SMELB_CUDA(cudaGetLastError());
   ep_fill_sink_kernel<<<ep_grid(cap_entries, 256), 256, 0, st>>>((long long*)entry_e, cap_entries, n_total, (int)sink);
   SMELB_CUDA(cudaGetLastError());
@@ -592,9 +710,8 @@ int smelb_ep_pull_rows(const void* const* regions, int64_t P, int64_t rank, int6
   if (rc != kOk) return rc;
   SMELB_CHECK_ARG(local && (buffer == 0 || buffer == 2) && H % 8 == 0, kErrArg, "ep_pull_rows: bad arguments");
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
-  ep_pull_rows_kernel<<<ep_grid(P * cap * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(pr, L, (int)P, (int)rank,
-                                                                                         (int)cap, (int)H, buffer,
-                                                                                         (bf16*)local);
+  ep_pull_rows_kernel<<<ep_grid(P * cap * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      pr, L.counts, L.rows[buffer], (int)P, (int)rank, (int)cap, (int)H, buffer, (bf16*)local);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -603,7 +720,7 @@ int smelb_ep_pull_rows(const void* const* regions, int64_t P, int64_t rank, int6
 int smelb_ep_gather(const void* local, const int32_t* entry_row, const int32_t* src_of, const int32_t* offsets,
                     int64_t sink, int64_t H, int64_t max_rows, void* xs, void* stream) {
   SMELB_CHECK_ARG(local && entry_row && src_of && offsets && xs && H % 8 == 0, kErrArg, "ep_gather: bad arguments");
-  ep_gather_kernel<<<ep_grid(max_rows * H / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+  ep_gather_kernel<<<ep_grid(max_rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
       (const bf16*)local, entry_row, src_of, offsets, (int)sink, (int)H, (bf16*)xs);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
@@ -622,7 +739,7 @@ int smelb_ep_return(const void* y, const int32_t* row_of, const float* entry_w, 
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
   ep_return_kernel<<<ep_grid(P * cap * 32, 256), 256, 0, (cudaStream_t)stream>>>(
       (const bf16*)y, row_of, entry_w, entry_dw, row_beg, row_m, recv_rows, (int)P, (int)cap, (int)K, (int)H,
-      pr.base[rank], L, backward != 0);
+      pr.base[rank], L.counts, L.rows[backward ? 3 : 1], L.dwts, backward != 0);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
