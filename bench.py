@@ -13,6 +13,7 @@ ranks: by default (`--parallel dp`) every GPU holds the whole layer and the LoRA
 """
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -120,6 +121,14 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def steps_for(seconds, t0, done, world):
+    """The number of further steps that fill `seconds`, from `done` steps timed since perf_counter() t0 (after a
+    synchronize) and agreed by every rank (the slowest one's step time): each step holds collectives, so every rank
+    must take the same number of them."""
+    per = max_over_ranks((time.perf_counter() - t0) / max(done, 1), world)
+    return max(1, int(math.ceil(seconds / max(per, 1e-6))))
+
+
 def layer_config(args):
     return dict(T=args.tokens, H=2048, E=256, K=8, I=512, S=512, n_sel=12, r=16, alpha=32.0)
 
@@ -205,9 +214,13 @@ def run_ours(args, world, rank, local):
         with torch.no_grad():  # routing of all ranks' tokens: the per-expert loads the placement balances
             smelb.moe_forward(layer["x"], W, ex, K, None, stats=lambda p, v, i: rec.update(i=i))
         loads = torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist()
-        placement = ep.balanced_placement(loads, world)
+        costs = ep.expert_row_costs(ex)
+        placement = ep.balanced_placement(loads, world, costs)
         per_rank = [sum(loads[e] for e in ids) for ids in placement]
-        placement_note = {"placement": "balanced by routed rows", "rows_per_rank": per_rank}
+        placement_note = {"placement": f"balanced by routed cost (a frozen int4 row {ep.FROZEN_ROW_COST:g}x a "
+                                       f"selected expert's)",
+                          "rows_per_rank": per_rank,
+                          "cost_per_rank": [round(sum(loads[e] * costs[e] for e in ids)) for ids in placement]}
         shard = ep.shard_layer(ex, lora, rank, world, placement)
         comm = ep.EPGroup(cap=cfg["T"], H=cfg["H"], K=K)
         params = list(shard.lora.parameters())
@@ -333,16 +346,16 @@ def run_ours(args, world, rank, local):
     # warm-up replays, then at least ~1 s more of them with the clock sampler running, so that the clock record
     # covers the GPU under this load right up to and through the timed region (a timed region of a few tens of ms
     # is shorter than the sampler's period)
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
         run_step()
     torch.cuda.synchronize()
+    n_more = steps_for(1.0, t_w, args.warmup, world)
     clocks = Clocks(local)
     clocks.start()
-    t_w = time.perf_counter()
-    while time.perf_counter() - t_w < 1.0:
-        for _ in range(20):
-            run_step()
-        torch.cuda.synchronize()
+    for _ in range(n_more):
+        run_step()
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     n1 = _lib.launch_count()
@@ -448,15 +461,16 @@ def _time_graph(step, args, local, world, post=None):
         one()
         if post is not None:
             post()
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
         run()
     torch.cuda.synchronize()
+    n_more = steps_for(1.0, t_w, args.warmup, world)
     clocks = Clocks(local)
     clocks.start()
-    t_w = time.perf_counter()
-    while time.perf_counter() - t_w < 1.0:
+    for _ in range(n_more):
         run()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     n1 = _lib.launch_count()
@@ -599,7 +613,7 @@ def run_block(args, world, rank, local, n_layers=24, n_micro=16):
                 with torch.no_grad():
                     smelb.moe_forward(x_all[:n_micro * T], W, Ly["ex"], K, None, stats=lambda p, v, i: rec.update(i=i))
                 placement = ep.balanced_placement(torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist(),
-                                                  world)
+                                                  world, ep.expert_row_costs(Ly["ex"]))
         else:
             W["mlp.gate.weight"] = router
         if world > 1:

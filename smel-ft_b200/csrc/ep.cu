@@ -266,6 +266,20 @@ __global__ void __launch_bounds__(kPlanTile) ep_plan_fill_kernel(const long long
   }
 }
 
+// One warp copies a row of vpr 16-byte vectors, each lane with up to 8 loads in flight before its stores (the source
+// may be a peer's memory, where a load's latency is a few microseconds).
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int vpr, int lane) {
+  for (int c0 = lane; c0 < vpr; c0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (c0 + 32 * u < vpr) v[u] = src[c0 + 32 * u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (c0 + 32 * u < vpr) dst[c0 + 32 * u] = v[u];
+  }
+}
+
 // rows[b][d][i] = src[tok_of[d][i]] for the rows of every destination, one warp per row (16-byte copies);
 // counts[b] = counts[0]
 __global__ void ep_pack_rows_kernel(const bf16* __restrict__ src, int H, const int* __restrict__ tok_of, int P,
@@ -280,9 +294,7 @@ __global__ void ep_pack_rows_kernel(const bf16* __restrict__ src, int H, const i
        row += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
     const int d = row / cap;
     if (row - d * cap >= cnt[d]) continue;
-    const uint4* s4 = reinterpret_cast<const uint4*>(src + (long long)tok_of[row] * H);
-    uint4* d4 = dst + (long long)row * vpr;
-    for (int c = lane; c < vpr; c += 32) d4[c] = s4[c];
+    copy_row(dst + (long long)row * vpr, reinterpret_cast<const uint4*>(src + (long long)tok_of[row] * H), vpr, lane);
   }
   if (b != 0 && blockIdx.x == 0 && threadIdx.x < P)
     reinterpret_cast<int*>(mine + counts_off)[b * kEpMaxRanks + threadIdx.x] = cnt[threadIdx.x];
@@ -380,9 +392,8 @@ __global__ void ep_pull_rows_kernel(EpPeers peers, size_t counts_off, size_t row
        row += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
     const int s = row / cap, i = row - s * cap;
     if (i >= cnt[s]) continue;
-    const uint4* r = reinterpret_cast<const uint4*>(base[s] + rows_off) + ((long long)rank * cap + i) * vpr;
-    uint4* d4 = reinterpret_cast<uint4*>(local) + (long long)row * vpr;
-    for (int c = lane; c < vpr; c += 32) d4[c] = r[c];
+    copy_row(reinterpret_cast<uint4*>(local) + (long long)row * vpr,
+             reinterpret_cast<const uint4*>(base[s] + rows_off) + ((long long)rank * cap + i) * vpr, vpr, lane);
   }
 }
 
@@ -401,8 +412,7 @@ __global__ void ep_gather_kernel(const bf16* __restrict__ local, const int* __re
       for (int c = lane; c < vpr; c += 32) d4[c] = make_uint4(0, 0, 0, 0);
       continue;
     }
-    const uint4* s4 = reinterpret_cast<const uint4*>(local + (long long)entry_row[e] * H);
-    for (int c = lane; c < vpr; c += 32) d4[c] = s4[c];
+    copy_row(d4, reinterpret_cast<const uint4*>(local + (long long)entry_row[e] * H), vpr, lane);
   }
 }
 
@@ -505,50 +515,73 @@ __global__ void ep_dy_kernel(const bf16* __restrict__ g_local, const int* __rest
 // ------------------------------------------------------------------------------------------ source side, returns
 // One warp per token: out[t] = bf16(sum over destinations d in rank order of the returned row rows[1 or 3][rank]
 // [pos[t][d]] from d's region (fp32) + add[t]); backward also dtopv[t][k] = d's dwts[rank][pos][slot_j[t][k]].
-__global__ void ep_collect_kernel(EpPeers peers, EpLayout L, int P, int rank, int cap, int K, int H, int T,
-                                  const int* __restrict__ pos, const bf16* __restrict__ add, int bwd,
+__global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_off, int P, int rank, int cap, int K,
+                                  int H, int T, const int* __restrict__ pos, const bf16* __restrict__ add, int bwd,
                                   const long long* __restrict__ topi, const int* __restrict__ owner,
                                   const int* __restrict__ slot_j, void* __restrict__ dtopv, int dtopv_f32,
                                   bf16* __restrict__ out) {
-  const int b = bwd ? 3 : 1;
   const int lane = threadIdx.x & 31;
-  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T;
-       t += ((long long)gridDim.x * blockDim.x) >> 5) {
+  for (int t = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5); t < T;
+       t += (int)(((long long)gridDim.x * blockDim.x) >> 5)) {
+    // the token's partial row at every owner it was sent to (null where it was not)
     int pt[kEpMaxRanks];
+    const bf16* rp[kEpMaxRanks];
 #pragma unroll
-    for (int d = 0; d < kEpMaxRanks; ++d) pt[d] = d < P ? pos[t * P + d] : -1;
-    for (int c0 = lane * 8; c0 < H; c0 += 256) {
-      float acc[8];
-      if (add) {
-        const uint4 av = *reinterpret_cast<const uint4*>(add + t * H + c0);
-        const bf16* pa = reinterpret_cast<const bf16*>(&av);
+    for (int d = 0; d < kEpMaxRanks; ++d) {
+      pt[d] = d < P ? pos[(long long)t * P + d] : -1;
+      rp[d] = pt[d] >= 0 ? reinterpret_cast<const bf16*>(peers.base[d] + rows_off) + ((long long)rank * cap + pt[d]) * H
+                         : nullptr;
+    }
+    // two 256-column chunks per pass, every owner's loads issued before the sums (owner order, as before)
+    for (int c0 = lane * 8; c0 < H; c0 += 512) {
+      uint4 v[2][kEpMaxRanks];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
-      } else {
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+        for (int d = 0; d < kEpMaxRanks; ++d)
+          if (rp[d] != nullptr && c0 + 256 * u < H) v[u][d] = *reinterpret_cast<const uint4*>(rp[d] + c0 + 256 * u);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + 256 * u;
+        if (c >= H) break;
+        float acc[8];
+        if (add) {
+          const uint4 av = *reinterpret_cast<const uint4*>(add + (long long)t * H + c);
+          const bf16* pa = reinterpret_cast<const bf16*>(&av);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+        }
+#pragma unroll
+        for (int d = 0; d < kEpMaxRanks; ++d) {
+          if (rp[d] == nullptr) continue;
+          const bf16* pv = reinterpret_cast<const bf16*>(&v[u][d]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
+        }
+        uint4 o;
+        bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
+        *reinterpret_cast<uint4*>(out + (long long)t * H + c) = o;
       }
-#pragma unroll
-      for (int d = 0; d < kEpMaxRanks; ++d) {
-        if (pt[d] < 0) continue;
-        const bf16* r = reinterpret_cast<const bf16*>(peers.base[d] + L.rows[b]) + ((long long)rank * cap + pt[d]) * H;
-        const uint4 v = *reinterpret_cast<const uint4*>(r + c0);
-        const bf16* pv = reinterpret_cast<const bf16*>(&v);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
-      }
-      uint4 o;
-      bf16* po = reinterpret_cast<bf16*>(&o);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
-      *reinterpret_cast<uint4*>(out + t * H + c0) = o;
     }
     if (bwd && lane < K) {
-      const int d = owner[topi[t * K + lane]];
-      const float dw = reinterpret_cast<const float*>(peers.base[d] + L.dwts)[((long long)rank * cap + pt[d]) * K +
-                                                                              slot_j[t * K + lane]];
-      if (dtopv_f32) reinterpret_cast<float*>(dtopv)[t * K + lane] = dw;
-      else reinterpret_cast<bf16*>(dtopv)[t * K + lane] = __float2bfloat16_rn(dw);
+      const int d = owner[topi[(long long)t * K + lane]];
+      int p = 0;
+      const char* base = nullptr;
+#pragma unroll
+      for (int dd = 0; dd < kEpMaxRanks; ++dd)
+        if (dd == d) {
+          p = pt[dd];
+          base = peers.base[dd];
+        }
+      const float dw = reinterpret_cast<const float*>(base + dwts_off)[((long long)rank * cap + p) * K +
+                                                                       slot_j[(long long)t * K + lane]];
+      if (dtopv_f32) reinterpret_cast<float*>(dtopv)[(long long)t * K + lane] = dw;
+      else reinterpret_cast<bf16*>(dtopv)[(long long)t * K + lane] = __float2bfloat16_rn(dw);
     }
   }
 }
@@ -768,7 +801,8 @@ int smelb_ep_collect(const void* const* regions, int64_t P, int64_t rank, int64_
                   "ep_collect: bad arguments (H a multiple of 256)");
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
   ep_collect_kernel<<<ep_grid(T * 32, 256), 256, 0, (cudaStream_t)stream>>>(
-      pr, L, (int)P, (int)rank, (int)cap, (int)K, (int)H, (int)T, pos, (const bf16*)add, backward != 0,
+      pr, L.rows[backward ? 3 : 1], L.dwts, (int)P, (int)rank, (int)cap, (int)K, (int)H, (int)T, pos,
+      (const bf16*)add, backward != 0,
       (const long long*)topi, owner, slot_j, dtopv, dtopv_fp32, (bf16*)out);
   SMELB_CUDA(cudaGetLastError());
   count_launch();

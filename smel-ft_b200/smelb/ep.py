@@ -50,22 +50,40 @@ def contiguous_placement(E: int, world: int):
     return [list(range(*expert_range(E, r, world))) for r in range(world)]
 
 
-def balanced_placement(loads, world: int):
-    """E / world experts per rank with the routed load balanced: the experts in decreasing load (ties: smaller id)
+# Cost of one routed row on the owner's GEMMs, by expert kind, relative to a selected (bf16 + LoRA) expert's row: a
+# frozen int4 row costs about three (the engine's int4 tiles run at about a third of the bf16 tiles' rate, the
+# dequantisation into TMEM bounding them at ~67 rows per expert: measured 191.6 vs 59.4 us for the gate/up of the
+# two halves of config 2's rows, 119.7 vs 34.3 us for the down projection).
+FROZEN_ROW_COST = 3.0
+
+
+def expert_row_costs(ex, frozen: float = FROZEN_ROW_COST, selected: float = 1.0):
+    """Per-expert cost of one routed row for balanced_placement: `selected` for the layer's selected experts,
+    `frozen` for the rest (ex: LayerExperts)."""
+    costs = [float(frozen)] * ex.E
+    for e in (ex.sel_ids.tolist() if ex.sel_ids is not None else []):
+        costs[e] = float(selected)
+    return costs
+
+
+def balanced_placement(loads, world: int, row_cost=None):
+    """E / world experts per rank with the routed cost balanced: the experts in decreasing cost (ties: smaller id)
     each go to the least-loaded rank that still has room (ties: smaller rank). Returns the sorted expert ids of every
-    rank. `loads`: rows routed to each expert on a representative batch."""
+    rank. `loads`: rows routed to each expert on a representative batch; `row_cost`: the cost of one row of each
+    expert (expert_row_costs; default 1: rows balanced as they are)."""
     loads = [float(v) for v in loads]
     E = len(loads)
     if E % world:
         raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+    w = [loads[e] * (float(row_cost[e]) if row_cost is not None else 1.0) for e in range(E)]
     cap = E // world
-    order = sorted(range(E), key=lambda e: (-loads[e], e))
+    order = sorted(range(E), key=lambda e: (-w[e], e))
     tot = [0.0] * world
     out = [[] for _ in range(world)]
     for e in order:
         r = min((q for q in range(world) if len(out[q]) < cap), key=lambda q: (tot[q], q))
         out[r].append(e)
-        tot[r] += loads[e]
+        tot[r] += w[e]
     return [sorted(v) for v in out]
 
 
