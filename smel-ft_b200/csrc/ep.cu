@@ -532,41 +532,31 @@ __global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_of
       rp[d] = pt[d] >= 0 ? reinterpret_cast<const bf16*>(peers.base[d] + rows_off) + ((long long)rank * cap + pt[d]) * H
                          : nullptr;
     }
-    // two 256-column chunks per pass, every owner's loads issued before the sums (owner order, as before)
-    for (int c0 = lane * 8; c0 < H; c0 += 512) {
-      uint4 v[2][kEpMaxRanks];
+    // per 256-column chunk every owner's load is issued before the sums (unrolled over the owners; owner order)
+    for (int c0 = lane * 8; c0 < H; c0 += 256) {
+      float acc[8];
+      if (add) {
+        const uint4 av = *reinterpret_cast<const uint4*>(add + (long long)t * H + c0);
+        const bf16* pa = reinterpret_cast<const bf16*>(&av);
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+        for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
+      } else {
 #pragma unroll
-        for (int d = 0; d < kEpMaxRanks; ++d)
-          if (rp[d] != nullptr && c0 + 256 * u < H) v[u][d] = *reinterpret_cast<const uint4*>(rp[d] + c0 + 256 * u);
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = c0 + 256 * u;
-        if (c >= H) break;
-        float acc[8];
-        if (add) {
-          const uint4 av = *reinterpret_cast<const uint4*>(add + (long long)t * H + c);
-          const bf16* pa = reinterpret_cast<const bf16*>(&av);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-        }
-#pragma unroll
-        for (int d = 0; d < kEpMaxRanks; ++d) {
-          if (rp[d] == nullptr) continue;
-          const bf16* pv = reinterpret_cast<const bf16*>(&v[u][d]);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
-        }
-        uint4 o;
-        bf16* po = reinterpret_cast<bf16*>(&o);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
-        *reinterpret_cast<uint4*>(out + (long long)t * H + c) = o;
+        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
       }
+#pragma unroll
+      for (int d = 0; d < kEpMaxRanks; ++d) {
+        if (rp[d] == nullptr) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(rp[d] + c0);
+        const bf16* pv = reinterpret_cast<const bf16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
+      }
+      uint4 o;
+      bf16* po = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) po[q] = __float2bfloat16_rn(acc[q]);
+      *reinterpret_cast<uint4*>(out + (long long)t * H + c0) = o;
     }
     if (bwd && lane < K) {
       const int d = owner[topi[(long long)t * K + lane]];
