@@ -301,6 +301,9 @@ typedef struct smelb_moe_layer {
   int32_t act_sh;           /* activation of the shared expert / dense MLP (SMELB_ACT_*) */
   int32_t reserved;
   const void* per_expert_scale; /* bf16 [E] multiplier of the renormalised top-k weights (Gemma 4), or NULL */
+  int32_t* split_counts;    /* int32 [2 E] scratch of the small-token path: with at least 1024 dispatch rows on the
+                               GEMV (smelb_set_gemv_rows), experts with more than 16 rows stay on the tile engine
+                               and the rest take the GEMV; NULL: every frozen expert takes the GEMV */
 } smelb_moe_layer;
 
 /* ---------------------------------------------------------------------------------------------------- expert parallel
@@ -417,7 +420,7 @@ long long smelb_launch_count(void);
 int smelb_gemm_timing(int enable);
 /* Dispatch-row count at or below which the forward's frozen int4 experts (smelb_moe_layer_fwd, and
  * smelb_frozen_experts_fwd over its rows) run as a dequant-GEMV instead of the tile engine; returns the previous
- * value (default 4096; 0 keeps every call on the tile engine). Replaces the size switch of no reference interface:
+ * value (default 512; 0 keeps every call on the tile engine). Replaces the size switch of no reference interface:
  * smel/moe.py:58-85 has one path at every size. */
 int64_t smelb_set_gemv_rows(int64_t rows);
 int smelb_gemm_timing_read(double* ms_total, long long* launches);

@@ -171,6 +171,22 @@ __device__ __forceinline__ bool is_int4(const Problem& P) {
   return P.mode == kTokN && (P.a_kind == kAInt4K || P.a_kind == kAInt4MN);
 }
 
+// Group tables of a launch, step 1 (out of line: the prologue's registers stay out of the role loops' allocation):
+// thread i reads the i-th group's weight slot, row count and first row (0 where the problem has no offsets).
+static __device__ __noinline__ void load_group_tables(const LaunchArgs& args, int* gcnt, int* gw, int* goff) {
+  int total_groups = 0;
+  for (int p = 0; p < args.nprob; ++p) total_groups += args.p[p].ngroups;
+  for (int i = threadIdx.x; i < total_groups; i += blockDim.x) {
+    int p = 0, g = i;
+    while (g >= args.p[p].ngroups) g -= args.p[p++].ngroups;
+    const Problem& P = args.p[p];
+    const int e = P.gid_of ? P.gid_of[g] : g;
+    gw[i] = P.widx_of ? P.widx_of[g] : e;
+    gcnt[i] = P.counts[e];
+    goff[i] = P.offsets ? P.offsets[e] : 0;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_constant__ LaunchArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -233,6 +249,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
         }
       }
     }
+  } else if (warp == kWarpMma) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  // group tables, step 1: every thread reads one group of the launch (its expert id, weight slot, row count and first
+  // row) into shared memory, so the scan below reads no global memory (a warp walking the groups 32 at a time paid
+  // a dependent global round trip per 32 groups, ~10 us for a routed launch's 256 groups)
+  load_group_tables(args, T.gcnt, T.gw, T.goff);
+  __syncthreads();
+  // step 2: one warp scans the counts per problem: rows (first rows where no offsets are given) and token tiles
+  if (warp == kWarpTmaB) {
     int gbase = 0, total = 0;
     for (int p = 0; p < args.nprob; ++p) {
       const Problem& P = args.p[p];
@@ -244,12 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       const int gp = gbase + p;
       for (int g0 = 0; g0 < P.ngroups; g0 += 32) {
         const int g = g0 + lane;
-        int cnt = 0, e = 0, w = 0;
-        if (g < P.ngroups) {
-          e = P.gid_of ? P.gid_of[g] : g;
-          w = P.widx_of ? P.widx_of[g] : e;
-          cnt = P.counts[e];
-        }
+        const int cnt = g < P.ngroups ? T.gcnt[gbase + g] : 0;
         const int nt = (P.mode == kTokN) ? (cnt + P.BN - 1) / P.BN : 0;
         int rows_inc = cnt, tiles_inc = nt;
 #pragma unroll
@@ -262,9 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
           }
         }
         if (g < P.ngroups) {
-          T.gcnt[gbase + g] = cnt;
-          T.goff[gbase + g] = P.offsets ? P.offsets[e] : carry_rows + rows_inc - cnt;
-          T.gw[gbase + g] = w;
+          if (!P.offsets) T.goff[gbase + g] = carry_rows + rows_inc - cnt;
           T.gpre[gp + g] = carry_tiles + tiles_inc - nt;
         }
         carry_rows += __shfl_sync(0xffffffffu, rows_inc, 31);
@@ -276,9 +296,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gemm_kernel(const __grid_cons
       gbase += P.ngroups;
     }
     if (lane == 0) T.tstart[args.nprob] = total;
-  } else if (warp == kWarpMma) {
-    tmem_alloc(s_tmem, 512);
-    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();

@@ -305,22 +305,35 @@ __global__ void __launch_bounds__(kThreads, 1) int4_gemv_kernel(const __grid_con
   // experts' rows follow one another in id order: the running sum of the counts before them) and the running cost
   // of their tasks (tiles x 16-token passes)
   if (warp == 0) {
+    // every lane's ids, counts and offsets are requested before the scan (one round trip each, not one per 32)
+    constexpr int kPer = kMaxIds / 32;
+    int ev[kPer], cv[kPer], ov[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int i = q * 32 + lane;
+      ev[q] = i < a.n_ids ? (a.ids ? a.ids[i] : i) : -1;
+    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      cv[q] = ev[q] >= 0 ? a.counts[ev[q]] : 0;
+      ov[q] = ev[q] >= 0 && a.offsets ? a.offsets[ev[q]] : 0;
+    }
     int n = 0, run = 0;
     long long crun = 0;
-    for (int b = 0; b < a.n_ids; b += 32) {
-      const int i = b + lane;
-      const int e = i < a.n_ids ? (a.ids ? a.ids[i] : i) : -1;
-      const int cnt = e >= 0 ? a.counts[e] : 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      if (q * 32 >= a.n_ids) break;
+      const int e = ev[q], cnt = cv[q];
       const int pass = (cnt + 15) / 16;
       int incl = cnt;
       long long cincl = (long long)pass * tiles;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        const long long cv = __shfl_up_sync(0xffffffffu, cincl, o);
+        const long long cv2 = __shfl_up_sync(0xffffffffu, cincl, o);
         if (lane >= o) {
           incl += v;
-          cincl += cv;
+          cincl += cv2;
         }
       }
       const bool on = cnt > 0;
@@ -329,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) int4_gemv_kernel(const __grid_con
         const int slot = n + __popc(m & ((1u << lane) - 1));
         s_act[slot] = e;
         s_cnt[slot] = cnt;
-        s_off[slot] = a.offsets ? a.offsets[e] : run + incl - cnt;
+        s_off[slot] = a.offsets ? ov[q] : run + incl - cnt;
         s_pass[slot] = pass;
         s_cost[slot] = crun + cincl - (long long)pass * tiles;
       }
@@ -543,7 +556,24 @@ bool shape_of(bool glu, int K, Shape& sh) {
   return sh.nstage >= 2;
 }
 
+__global__ void split_counts_kernel(const int* __restrict__ counts, int E, int thr, int* __restrict__ hot,
+                                    int* __restrict__ cold) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) {
+    const int c = counts[e];
+    hot[e] = c > thr ? c : 0;
+    cold[e] = c > thr ? 0 : c;
+  }
+}
+
 }  // namespace
+
+int split_counts(const int* counts, int E, int thr, int* hot, int* cold, cudaStream_t st) {
+  if (E <= 0) return kOk;
+  split_counts_kernel<<<(E + 255) / 256, 256, 0, st>>>(counts, E, thr, hot, cold);
+  SMELB_CUDA(cudaGetLastError());
+  count_launch();
+  return kOk;
+}
 
 bool int4_gemv_supported(bool glu, int K) {
   Shape sh;

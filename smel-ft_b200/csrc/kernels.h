@@ -148,6 +148,9 @@ struct GemvArgs {
   long long ldh;
 };
 int int4_gemv(const GemvArgs& a, cudaStream_t st);
+// hot[e] = counts[e] if counts[e] > thr else 0, cold[e] = the rest (e < E): the experts the tile engine and the GEMV
+// take in a split small-token call.
+int split_counts(const int* counts, int E, int thr, int* hot, int* cold, cudaStream_t st);
 // Whether the GEMV takes a reduction length K (its shared-memory stages must hold two tasks).
 bool int4_gemv_supported(bool glu, int K);
 

@@ -27,7 +27,7 @@ constexpr int kW64 = 64;       // column width of the LoRA token-side buffers an
 
 // Dispatch-row count at or below which the forward's frozen int4 experts take the dequant-GEMV (gemv.cu) instead of
 // the tile engine: few rows per expert make the call a stream of the touched experts' weights.
-std::atomic<long long> g_gemv_rows{4096};
+std::atomic<long long> g_gemv_rows{512};
 
 // The frozen int4 gate/up (glu) or down matrix over expert-grouped rows on the GEMV (rows_est: the expected number
 // of rows over all n_ids experts, which sizes the token tile).
@@ -307,18 +307,18 @@ int add_shared_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* h
   return kOk;
 }
 
-// The routed gate/up GEMMs + GLU epilogue: frozen experts (int4 bank, or bf16 fz_gu; left out when !frozen) and the
-// selected bf16 experts with their LoRA K-extension, a = act(g) * u over the dispatch rows, pre-activations into
-// hout when given.
-int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout, bool frozen = true) {
+// The routed gate/up GEMMs + GLU epilogue: frozen experts (int4 bank, or bf16 fz_gu) with row counts fz_counts (left
+// out when null) and the selected bf16 experts with their LoRA K-extension, a = act(g) * u over the dispatch rows,
+// pre-activations into hout when given.
+int add_routed_glu(Builder& b, const smelb_moe_layer& L, const Flags& f, void* hout, const int* fz_counts) {
   const int H = (int)L.H, E = (int)L.E, I = (int)L.I, nsel = (int)L.n_sel, nfz = (int)(L.E - L.n_sel);
   const long long R = L.max_rows;
-  if (nfz > 0 && frozen) {
+  if (nfz > 0 && fz_counts) {
     Problem& P = b.add();
     if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_gu, E, 2 * I, H, false, true));
     else TRY(set_a_int4(P, Int4Mat{L.gu_q, L.gu_sz, E, 2 * I, H}, false));
     TRY(set_b_tokens(P, L.xs, R, H));
-    groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+    groups(P, fz_counts, L.offsets, L.frozen_ids, nullptr, nfz);
     P.epi = kEpiGlu;
     P.C = L.a;
     P.c_sn = I;
@@ -352,6 +352,27 @@ long long routed_rows(const smelb_moe_layer& L, const Flags& f) { return f.ext ?
 bool gemv_fits(int64_t H, int64_t I) { return int4_gemv_supported(true, (int)H) && int4_gemv_supported(false, (int)I); }
 bool frozen_on_gemv(const smelb_moe_layer& L, const Flags& f) {
   return f.routed && L.E > L.n_sel && !f.fz_bf16 && routed_rows(L, f) <= g_gemv_rows.load() && gemv_fits(L.H, L.I);
+}
+
+// Which frozen experts go where. On the GEMV path with at least kSplitRows dispatch rows (and scratch for the split),
+// experts with more than kHotRows rows stay on the tile engine (the GEMV repeats its dequantisation for every 16
+// rows, the engine's tensor-core tiles take up to 192 at once) and the rest take the GEMV; a skewed routing at 128
+// tokens then costs what it costs on the engine alone, while a call without such experts pays one empty engine
+// launch (5-10 us, which is why small calls do not split).
+constexpr long long kSplitRows = 1024;
+constexpr int kHotRows = 16;
+struct FrozenPlan {
+  bool gemv, split;
+  const int* engine;  // row counts of the frozen experts on the tile engine (null: none there)
+  const int* small;   // row counts of the frozen experts on the GEMV
+};
+FrozenPlan frozen_plan(const smelb_moe_layer& L, const Flags& f) {
+  FrozenPlan p;
+  p.gemv = frozen_on_gemv(L, f);
+  p.split = p.gemv && L.split_counts != nullptr && routed_rows(L, f) >= kSplitRows;
+  p.engine = p.gemv ? (p.split ? L.split_counts : nullptr) : L.gcounts;
+  p.small = p.split ? L.split_counts + L.E : L.gcounts;
+  return p;
 }
 
 // ---------------------------------------------------------------------------------------------- layer forward
@@ -428,11 +449,12 @@ int layer_fwd(const smelb_moe_layer& L) {
     TRY(b.launch(st));
   }
   const long long rows_est = routed_rows(L, f);
-  const bool gemv = frozen_on_gemv(L, f);
+  const FrozenPlan fp = frozen_plan(L, f);
+  if (fp.split) TRY(split_counts(L.gcounts, E, kHotRows, L.split_counts, L.split_counts + E, st));
   // L3: routed gate/up (frozen int4 + selected bf16 with LoRA), shared LoRA A of the down projection
   {
     Builder b;
-    if (f.routed) TRY(add_routed_glu(b, L, f, f.save ? L.h : nullptr, !gemv));
+    if (f.routed) TRY(add_routed_glu(b, L, f, f.save ? L.h : nullptr, fp.engine));
     if (f.sh_lora) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.sp_z_w, 1, rh, S, false, false));
@@ -443,8 +465,8 @@ int layer_fwd(const smelb_moe_layer& L) {
     }
     TRY(b.launch(st));
   }
-  if (gemv)
-    TRY(gemv_frozen(true, L.xs, H, L.gcounts, L.offsets, L.frozen_ids, nfz, E, L.gu_q, L.gu_sz, 2 * I, H, I, L.act,
+  if (fp.gemv)
+    TRY(gemv_frozen(true, L.xs, H, fp.small, L.offsets, L.frozen_ids, nfz, E, L.gu_q, L.gu_sz, 2 * I, H, I, L.act,
                     rows_est, L.a, I, f.save ? L.h : nullptr, 2 * I, st));
   // L4: selected LoRA A of the down projection, shared down projection
   {
@@ -468,17 +490,17 @@ int layer_fwd(const smelb_moe_layer& L) {
     TRY(b.launch(st));
   }
   // L5: routed down projections
-  if (gemv)
-    TRY(gemv_frozen(false, L.a, I, L.gcounts, L.offsets, L.frozen_ids, nfz, E, L.dn_q, L.dn_sz, H, I, 0, 0, rows_est,
+  if (fp.gemv)
+    TRY(gemv_frozen(false, L.a, I, fp.small, L.offsets, L.frozen_ids, nfz, E, L.dn_q, L.dn_sz, H, I, 0, 0, rows_est,
                     L.y, H, nullptr, 0, st));
   if (f.routed) {
     Builder b;
-    if (nfz > 0 && !gemv) {
+    if (nfz > 0 && fp.engine) {
       Problem& P = b.add();
       if (f.fz_bf16) TRY(set_a_bf16(P, L.fz_dn, E, H, I, false, false));
       else TRY(set_a_int4(P, dn, false));
       TRY(set_b_tokens(P, L.a, R, I));
-      groups(P, L.gcounts, L.offsets, L.frozen_ids, nullptr, nfz);
+      groups(P, fp.engine, L.offsets, L.frozen_ids, nullptr, nfz);
       out_bf16(P, L.y, H);
     }
     if (f.sel) {
@@ -521,13 +543,14 @@ int layer_bwd(const smelb_moe_layer& L) {
   // R0: without saved gate/up pre-activations (the forward kept only its inputs), recompute them into h / sh_h
   if (f.recompute && (f.routed || f.shared)) {
     SMELB_CHECK_ARG((!f.routed || L.h) && (!f.shared || L.sh_h), kErrArg, "layer_bwd: recompute needs h / sh_h");
-    const bool gemv = frozen_on_gemv(L, f);
+    // the forward's split of the frozen experts (its counts are still in split_counts) and the same kernels
+    const FrozenPlan fp = frozen_plan(L, f);
     Builder b;
     if (f.shared) TRY(add_shared_glu(b, L, f, L.sh_h));
-    if (f.routed) TRY(add_routed_glu(b, L, f, L.h, !gemv));
+    if (f.routed) TRY(add_routed_glu(b, L, f, L.h, fp.engine));
     TRY(b.launch(st));
-    if (gemv)
-      TRY(gemv_frozen(true, L.xs, H, L.gcounts, L.offsets, L.frozen_ids, (int)(E - L.n_sel), E, L.gu_q, L.gu_sz, 2 * I,
+    if (fp.gemv)
+      TRY(gemv_frozen(true, L.xs, H, fp.small, L.offsets, L.frozen_ids, (int)(E - L.n_sel), E, L.gu_q, L.gu_sz, 2 * I,
                       H, I, L.act, routed_rows(L, f), L.a, I, L.h, 2 * I, st));
   }
   if (f.routed && !f.ext)

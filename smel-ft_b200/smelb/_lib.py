@@ -57,7 +57,7 @@ _LAYER_FIELDS = [
     ("gshA_gate", c_vp), ("gshB_gate", c_vp), ("gshA_up", c_vp), ("gshB_up", c_vp), ("gshA_down", c_vp),
     ("gshB_down", c_vp),
     ("dprobs", c_vp), ("fz_gu", c_vp), ("fz_dn", c_vp), ("act_sh", c_i32), ("reserved", c_i32),
-    ("per_expert_scale", c_vp),
+    ("per_expert_scale", c_vp), ("split_counts", c_vp),
 ]
 
 

@@ -221,7 +221,8 @@ def _alloc_fwd(cfg, dev, save):
         cfg.max_rows = R
         b.update(counts=e(E, dtype=torch.int32), gcounts=e(E, dtype=torch.int32), offsets=e(E, dtype=torch.int32),
                  row_of=e(T * K, dtype=torch.int32), src_of=e(R, dtype=torch.int32), total=e(1, dtype=torch.int32),
-                 order=e(T * K, dtype=torch.int64), xs=e(R, H), a=e(R, I), y=e(R, H))
+                 order=e(T * K, dtype=torch.int64), xs=e(R, H), a=e(R, I), y=e(R, H),
+                 split_counts=e(2 * (E + 1), dtype=torch.int32))
         if save and _SAVE_PREACT[0]:
             b["h"] = e(R, 2 * I)
         if n and r:

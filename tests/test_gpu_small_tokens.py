@@ -1,5 +1,5 @@
 """Small-token path: the frozen int4 experts as a dequant-GEMV (csrc/gemv.cu) when a call has few dispatch rows
-(smelb.set_gemv_rows; by default T*K <= 4096 rows take it). Parity against the oracle at 1 to 128 tokens, uniform
+(smelb.set_gemv_rows; by default T*K <= 512 rows take it). Parity against the oracle at 1 to 128 tokens, uniform
 and Zipf routing (a hot expert then holds more rows than one token tile and takes several passes), with the
 reference layer's expert choices forced as in the other layer tests; the training forward's saved pre-activations
 through the backward; and the GEMV against the tile engine at the config-4 shape (Qwen layer, all 256 experts
@@ -77,13 +77,16 @@ def test_small_token_forward_vs_oracle(T, routing, gemv_rows):
     assert smelb.read_status() == 0
 
 
-def test_small_token_training_step_vs_oracle(gemv_rows):
+@pytest.mark.parametrize("T", [24, 200])
+def test_small_token_training_step_vs_oracle(T, gemv_rows):
     """Forward with the pre-activations saved by the GEMV epilogue (and with them recomputed instead), backward on
-    the engine: out, dX and every LoRA gradient (12 selected experts and the shared expert) against the oracle."""
+    the engine: out, dX and every LoRA gradient (the selected experts and the shared expert) against the oracle. At
+    200 tokens (1600 dispatch rows, Zipf routing) the experts with more than 16 rows stay on the tile engine and the
+    rest take the GEMV, in the forward and in the backward's recompute alike."""
     import smelb
     from smelb.synth import qwen_layer
     gemv_rows(1 << 30)
-    L = qwen_layer(T=24, H=1024, E=48, K=8, I=256, S=256, n_sel=6, r=16, seed=21, device="cuda:0")
+    L = qwen_layer(T=T, H=1024, E=48, K=8, I=256, S=256, n_sel=6, r=16, seed=21, device="cuda:0")
     meta, ex, lora = L["meta"], L["ex"], L["lora"]
     gy = torch.randn(L["x"].shape, generator=torch.Generator(device="cuda:0").manual_seed(3),
                      device="cuda:0").bfloat16()
@@ -102,6 +105,8 @@ def test_small_token_training_step_vs_oracle(gemv_rows):
         results.append((out.detach(), x.grad, {n: getattr(lora.experts, n).grad.clone() for n in NAMES},
                         {n: getattr(lora.shared, n).grad.clone() for n in NAMES}, rec["i"].cpu()))
     out, dx, g_ex, g_sh, topi = results[0]
+    counts = torch.bincount(topi.reshape(-1), minlength=48)
+    print(f"T={T}: hottest expert {int(counts.max())} rows, {int((counts > 16).sum())} above 16")
     assert torch.equal(out, results[1][0]) and torch.equal(dx, results[1][1])
     dt = torch.float64
     x64 = L["x"].cpu().to(dt).requires_grad_(True)
