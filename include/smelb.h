@@ -232,9 +232,11 @@ int smelb_frozen_experts_fwd_noalloc_status(int device, int* words, int reset);
 #define SMELB_F_TOPV_FP32 32   /* topv / topv_in are fp32 (Gemma 4 routing) */
 #define SMELB_F_RECOMPUTE 64   /* backward: h / sh_h were not kept by the forward; recompute them from x / xs first */
 #define SMELB_F_EXT_DISPATCH 128 /* routed experts on a dispatch the caller built: xs, counts, gcounts, offsets, src_of,
-                                  * row_of and total are inputs (T * K dispatch entries), y (forward) and dxs
+                                  * row_of and total are inputs (max_rows dispatch rows), y (forward) and dxs
                                   * (backward) are the outputs in dispatch order; no router, gather, combine or dX
-                                  * reduction run (the expert-parallel owner side) */
+                                  * reduction run (the expert-parallel owner side). With SMELB_F_SHARED the shared
+                                  * expert runs on the T rows of x in the same launches and leaves sh_y (and
+                                  * sgate_logit; backward: sh_dx and dgl from g) to the caller. */
 
 typedef struct smelb_moe_layer {
   /* shapes */
@@ -370,11 +372,14 @@ int smelb_ep_dy(const void* g_local, const int32_t* entry_row, const float* entr
                 const int32_t* offsets, int64_t sink, int64_t H, int64_t max_rows, const void* y, void* dy,
                 float* entry_dw, void* stream);
 
-/* Source side: out[t] = bf16(sum over destinations in rank order of the returned row (buffer 1, or 3 when backward)
- * at pos[t][d], in fp32, + add[t] when add is given); backward also dtopv[t][k] (bf16, or fp32 if dtopv_fp32) from
- * the owner's per-entry d weights. */
+/* Source side: out[t] = bf16(a[t] + the returned rows (buffer 1, or 3 when backward) at pos[t][d] over the
+ * destinations in rank order, in fp32), where a = add (bf16 [T, H]; zero when add is NULL), gated in the forward by
+ * the shared expert's gate when gate_logit (bf16 [T]) is given: a = bf16(add * bf16(sigmoid(gate_logit))), the fused
+ * layer's combine (smel/moe.py:197-201,248-252). Backward: + dgl[t] * w_sgate (fp32 [T], bf16 [H]; the shared gate's
+ * share of dX, when given), and dtopv[t][k] (bf16, or fp32 if dtopv_fp32) from the owners' per-entry d weights. */
 int smelb_ep_collect(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int64_t T,
-                     const int32_t* pos, const void* add, int backward, const int64_t* topi, const int32_t* owner,
+                     const int32_t* pos, const void* add, const void* gate_logit, const float* dgl,
+                     const void* w_sgate, int backward, const int64_t* topi, const int32_t* owner,
                      const int32_t* slot_j, void* dtopv, int dtopv_fp32, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------- int8 rows

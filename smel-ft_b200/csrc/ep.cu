@@ -516,7 +516,9 @@ __global__ void ep_dy_kernel(const bf16* __restrict__ g_local, const int* __rest
 // One warp per token: out[t] = bf16(sum over destinations d in rank order of the returned row rows[1 or 3][rank]
 // [pos[t][d]] from d's region (fp32) + add[t]); backward also dtopv[t][k] = d's dwts[rank][pos][slot_j[t][k]].
 __global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_off, int P, int rank, int cap, int K,
-                                  int H, int T, const int* __restrict__ pos, const bf16* __restrict__ add, int bwd,
+                                  int H, int T, const int* __restrict__ pos, const bf16* __restrict__ add,
+                                  const bf16* __restrict__ gl, const float* __restrict__ dgl,
+                                  const bf16* __restrict__ w_sg, int bwd,
                                   const long long* __restrict__ topi, const int* __restrict__ owner,
                                   const int* __restrict__ slot_j, void* __restrict__ dtopv, int dtopv_f32,
                                   bf16* __restrict__ out) {
@@ -532,6 +534,9 @@ __global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_of
       rp[d] = pt[d] >= 0 ? reinterpret_cast<const bf16*>(peers.base[d] + rows_off) + ((long long)rank * cap + pt[d]) * H
                          : nullptr;
     }
+    // the shared expert's gate of this token, rounded as the fused combine does
+    const float sg = gl ? bf16_round(1.0f / (1.0f + expf(-__bfloat162float(gl[t])))) : 1.f;
+    const float dg = dgl ? dgl[t] : 0.f;
     // per 256-column chunk every owner's load is issued before the sums (unrolled over the owners; owner order)
     for (int c0 = lane * 8; c0 < H; c0 += 256) {
       float acc[8];
@@ -539,7 +544,7 @@ __global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_of
         const uint4 av = *reinterpret_cast<const uint4*>(add + (long long)t * H + c0);
         const bf16* pa = reinterpret_cast<const bf16*>(&av);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = __bfloat162float(pa[q]);
+        for (int q = 0; q < 8; ++q) acc[q] = gl ? bf16_round(__bfloat162float(pa[q]) * sg) : __bfloat162float(pa[q]);
       } else {
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] = 0.f;
@@ -551,6 +556,12 @@ __global__ void ep_collect_kernel(EpPeers peers, size_t rows_off, size_t dwts_of
         const bf16* pv = reinterpret_cast<const bf16*>(&v);
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] += __bfloat162float(pv[q]);
+      }
+      if (dgl) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(w_sg + c0);
+        const bf16* pw = reinterpret_cast<const bf16*>(&wv);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(dg, __bfloat162float(pw[q]), acc[q]);
       }
       uint4 o;
       bf16* po = reinterpret_cast<bf16*>(&o);
@@ -782,17 +793,20 @@ int smelb_ep_dy(const void* g_local, const int32_t* entry_row, const float* entr
 }
 
 int smelb_ep_collect(const void* const* regions, int64_t P, int64_t rank, int64_t cap, int64_t K, int64_t H, int64_t T,
-                     const int32_t* pos, const void* add, int backward, const int64_t* topi, const int32_t* owner,
+                     const int32_t* pos, const void* add, const void* gate_logit, const float* dgl,
+                     const void* w_sgate, int backward, const int64_t* topi, const int32_t* owner,
                      const int32_t* slot_j, void* dtopv, int dtopv_fp32, void* out, void* stream) {
   EpPeers pr;
   const int rc = ep_peers(regions, (int)P, pr);
   if (rc != kOk) return rc;
   SMELB_CHECK_ARG(pos && out && H % 256 == 0 && (!backward || (topi && owner && slot_j && dtopv)), kErrArg,
                   "ep_collect: bad arguments (H a multiple of 256)");
+  SMELB_CHECK_ARG(!gate_logit || (add && !backward), kErrArg, "ep_collect: the gate applies to the forward's add");
+  SMELB_CHECK_ARG(!dgl == !w_sgate && (!dgl || backward), kErrArg, "ep_collect: dgl and w_sgate go together");
   const EpLayout L = ep_layout((int)P, (int)cap, (int)K, (int)H);
   ep_collect_kernel<<<ep_grid(T * 32, 256), 256, 0, (cudaStream_t)stream>>>(
       pr, L.rows[backward ? 3 : 1], L.dwts, (int)P, (int)rank, (int)cap, (int)K, (int)H, (int)T, pos,
-      (const bf16*)add, backward != 0,
+      (const bf16*)add, (const bf16*)gate_logit, dgl, (const bf16*)w_sgate, backward != 0,
       (const long long*)topi, owner, slot_j, dtopv, dtopv_fp32, (bf16*)out);
   SMELB_CUDA(cudaGetLastError());
   count_launch();

@@ -254,8 +254,8 @@ int check_layer(const smelb_moe_layer& L, Flags& f) {
   f.fz_bf16 = L.gu_q == nullptr && L.fz_gu != nullptr;
   f.recompute = L.flags & SMELB_F_RECOMPUTE;
   f.ext = L.flags & SMELB_F_EXT_DISPATCH;
-  SMELB_CHECK_ARG(!f.ext || (f.routed && !f.router && !f.shared), kErrArg,
-                  "layer: an external dispatch is for the routed experts alone");
+  SMELB_CHECK_ARG(!f.ext || (f.routed && !f.router), kErrArg,
+                  "layer: an external dispatch takes the routed experts (and the shared expert), not the router");
   SMELB_CHECK_ARG(L.T >= 0 && L.H > 0 && L.H % 64 == 0, kErrShape, "layer: H=%lld must be a multiple of 64",
                   (long long)L.H);
   SMELB_CHECK_ARG(L.act == SMELB_ACT_SILU || L.act == SMELB_ACT_GELU_TANH, kErrArg, "layer: unknown activation %d",

@@ -122,8 +122,8 @@ SIGNATURES = {
     "smelb_ep_return": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
                                 c_i32, c_vp]),
     "smelb_ep_dy": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]),
-    "smelb_ep_collect": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp,
-                                 c_vp, c_i32, c_vp, c_vp]),
+    "smelb_ep_collect": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32,
+                                 c_vp, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),
     "smelb_int8_rows_quantize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "smelb_int8_rows_dequant": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_vp]),
     "smelb_chunked_ce_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i64, c_i32, c_i32]),

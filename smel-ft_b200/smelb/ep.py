@@ -12,7 +12,8 @@ its own tokens. One call, on every rank at once:
           the single-GPU layer) and run its experts through the same fused GEMMs (smelb_moe_layer_fwd with an
           external dispatch); per received row, sum its entries' outputs times their weights in fp32 and publish
           that one partial row
-  source  out[t] = the fp32 sum over the owners of t's partial rows, in rank order, plus the shared expert
+  source  out[t] = the fp32 sum over the owners of t's partial rows, in rank order, plus the gated shared expert,
+          which runs on the source's own tokens in the same GEMM launches as its share of the routed experts
 
 Backward mirrors it with the upstream gradient: the owners form dY = g * w and d w = g . y per entry, run the expert
 backward (dX and their LoRA gradients, which stay with the owner), and return one summed dX row per received row and
@@ -33,7 +34,7 @@ import torch.distributed as dist
 from . import _lib
 from .lora import ExpertsLoRA, LayerLoRA
 from .moe import (_SAVE_PREACT, BF16Experts, Int4Experts, LayerExperts, _alloc_bwd, _alloc_fwd, _bf16, _Cfg, _fp32,
-                  _LORA_NAMES, _set_routed, _struct, router_and_shared)
+                  _LORA_NAMES, _set_routed, _set_shared, _struct, route)
 
 SYNC = {"wait_done": 0, "publish": 1, "wait_ready": 2, "ack": 3}
 
@@ -221,11 +222,12 @@ def _i32(*s, dev):
 
 
 class _EPRoutedFn(torch.autograd.Function):
-    """out = routed experts (partitioned over the group) + sh. Inputs: x, topv, sh (the shared expert's output),
-    topi, shard, comm, cap_factor, then the local selected experts' six LoRA parameters (or None)."""
+    """out = routed experts (partitioned over the group) + the gated shared expert. Inputs: x, topv, topi, shard, comm,
+    cap_factor, shw (the shared expert's (gate_up, down, gate) weights), then the local selected experts' six LoRA
+    parameters and the shared expert's six (or None)."""
 
     @staticmethod
-    def forward(ctx, x, topv, sh, topi, shard, comm, cap_factor, *lora_params):
+    def forward(ctx, x, topv, topi, shard, comm, cap_factor, shw, *lora_params):
         dev = x.device
         T, H = x.shape
         K = topi.shape[1]
@@ -260,21 +262,30 @@ class _EPRoutedFn(torch.autograd.Function):
         _lib.call("smelb_ep_pull_rows", reg, P, r, cap, K, H, 0, _lib.ptr(x_loc), st)
         comm.sync("ack", 0)
         lora_ex = shard.lora.experts if shard.lora is not None else None
+        lora_sh = shard.lora.shared if shard.lora is not None else None
+        # the owner's experts on its received entries (cap_e dispatch "tokens" of weight 1) and the shared expert on
+        # this rank's T tokens, one layer call: the buffers of each from its own description, then one struct
         cfg = _Cfg(0, torch.empty(cap_e, H, device="meta"), 1, E_loc, ex.act)
         _set_routed(cfg, ex, lora_ex, dev)
-        cfg.flags |= _lib.F_EXT_DISPATCH
+        cfg_sh = _Cfg(0, x, 0, 0)
+        _set_shared(cfg_sh, shw[0], shw[1], lora_sh, shw[2])
         save = any(ctx.needs_input_grad)
+        t = dict(cfg.t)
+        t.update(_alloc_fwd(cfg, dev, save))
+        t.pop("out")  # the owner's outputs stay in dispatch order (y)
+        t.update(cfg_sh.t)
+        t.update({k: v for k, v in _alloc_fwd(cfg_sh, dev, save).items() if k != "out"})
+        R = cfg.max_rows
+        cfg.flags |= cfg_sh.flags | _lib.F_EXT_DISPATCH
+        cfg.T, cfg.S, cfg.r_sh, cfg.s_sh, cfg.act_sh = T, cfg_sh.S, cfg_sh.r_sh, cfg_sh.s_sh, cfg_sh.act_sh
         if save:
             cfg.flags |= _lib.F_SAVE
             if not _SAVE_PREACT[0]:
                 cfg.flags |= _lib.F_RECOMPUTE
-        t = dict(cfg.t)
+        t["x"] = x
         lp = [_fp32(p) for p in lora_params]
         for i, name in enumerate(_LORA_NAMES):
-            t[name] = lp[i]
-        t.update(_alloc_fwd(cfg, dev, save))
-        t.pop("out")  # the owner's outputs stay in dispatch order (y)
-        R = cfg.max_rows
+            t[name], t["sh" + name] = lp[i], lp[6 + i]
         t.update(counts=_i32(E_loc + 1, dev=dev), gcounts=_i32(E_loc + 1, dev=dev), offsets=_i32(E_loc + 1, dev=dev))
         ws = _i32(148 * (E_loc + 1), dev=dev)
         _lib.call("smelb_dispatch_plan_ws", _lib.ptr(entry_e), cap_e, 1, E_loc + 1, _lib.ptr(maps["sel_mask_sink"]),
@@ -292,8 +303,8 @@ class _EPRoutedFn(torch.autograd.Function):
         # ---- source: add the partial rows of every owner and the shared expert
         comm.sync("wait_ready", 1)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), _lib.ptr(sh.contiguous()), 0, None,
-                  None, None, None, 0, _lib.ptr(out), st)
+        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), _lib.ptr(t["sh_y"]),
+                  _lib.ptr(t.get("sgate_logit")), None, None, 0, None, None, None, None, 0, _lib.ptr(out), st)
         comm.sync("ack", 1)
         if save:
             ctx.save_for_backward(topi, pos, slot_j, tok_of, entry_row, entry_w, row_beg, row_m, rc)
@@ -323,6 +334,7 @@ class _EPRoutedFn(torch.autograd.Function):
         comm.sync("ack", 2)
         b = _alloc_bwd(cfg, dev)
         t.update(b)
+        t["g"] = g  # the shared expert's upstream gradient (this rank's tokens)
         entry_dw = torch.zeros(entry_w.shape, dtype=torch.float32, device=dev)
         _lib.call("smelb_ep_dy", _lib.ptr(g_loc), _lib.ptr(entry_row), _lib.ptr(entry_w), _lib.ptr(t["src_of"]),
                   _lib.ptr(t["offsets"]), E_loc, H, R, _lib.ptr(t["y"]), _lib.ptr(t["dy"]), _lib.ptr(entry_dw), st)
@@ -337,12 +349,13 @@ class _EPRoutedFn(torch.autograd.Function):
         comm.sync("wait_ready", 3)
         dx = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         dtopv = torch.empty(T, K, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
-        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), None, 1, _lib.ptr(topi),
+        _lib.call("smelb_ep_collect", reg, P, r, cap, K, H, T, _lib.ptr(pos), _lib.ptr(t["sh_dx"]), None,
+                  _lib.ptr(t.get("dgl")), _lib.ptr(t.get("w_sgate")) if "dgl" in t else None, 1, _lib.ptr(topi),
                   _lib.ptr(maps["owner"]), _lib.ptr(slot_j), _lib.ptr(dtopv), 1 if f32 else 0, _lib.ptr(dx), st)
         comm.sync("ack", 3)
-        grads = [b.get("g" + n) for n in _LORA_NAMES]
+        grads = [b.get("g" + n) for n in _LORA_NAMES] + [b.get("gsh" + n) for n in _LORA_NAMES]
         grads = [None if (gr is None or dt is None) else gr.to(dt) for gr, dt in zip(grads, dtypes)]
-        return (dx, dtopv, g, None, None, None, None, *grads)
+        return (dx, dtopv, None, None, None, None, None, *grads)
 
 
 def moe_forward_ep(x2d, W, shard: EPShard, top_k: int, comm: EPGroup, stats=None, cap_factor: float = 2.0):
@@ -354,8 +367,16 @@ def moe_forward_ep(x2d, W, shard: EPShard, top_k: int, comm: EPGroup, stats=None
     rank's [T, H] output, differentiable w.r.t. x2d, the local selected experts' LoRA parameters and the shared LoRA
     parameters."""
     x2d = _bf16(x2d, "moe_forward_ep: x")
-    lora_sh = shard.lora.shared if shard.lora is not None else None
-    sh, probs, topv, topi = router_and_shared(x2d, W, top_k, lora_sh, stats)
+    probs, topv, topi = route(x2d, W["mlp.gate.weight"], top_k)
+    if stats is not None:
+        stats(probs, topv, topi)
+    pre = "mlp.shared_expert."
+    gu = W.get(pre + "gate_up_proj.weight")
+    if gu is None:
+        gu = torch.cat((W[pre + "gate_proj.weight"], W[pre + "up_proj.weight"]))
+    shw = (gu, W[pre + "down_proj.weight"], W["mlp.shared_expert_gate.weight"])
     lex = shard.lora.experts if shard.lora is not None else None
-    params = [getattr(lex, n) for n in _LORA_NAMES] if lex is not None else [None] * 6
-    return _EPRoutedFn.apply(x2d, topv, sh, topi, shard, comm, float(cap_factor), *params)
+    lsh = shard.lora.shared if shard.lora is not None else None
+    params = ([getattr(lex, n) for n in _LORA_NAMES] if lex is not None else [None] * 6) + \
+             ([getattr(lsh, n) for n in _LORA_NAMES] if lsh is not None else [None] * 6)
+    return _EPRoutedFn.apply(x2d, topv, topi, shard, comm, float(cap_factor), shw, *params)
