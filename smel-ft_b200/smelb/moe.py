@@ -448,26 +448,6 @@ def moe_forward(x2d, W, ex: LayerExperts, top_k: int, lora_layer=None, stats=Non
     return out
 
 
-def router_and_shared(x2d, W, top_k, lora_sh=None, stats=None):
-    """route (moe.py:162-167) and shared_mlp (moe.py:197-201) of one layer call as one fused call (the router, the
-    shared gate and the shared expert share launches): returns (shared output [N, H] bf16, probs, topv, topi), each
-    differentiable as in the reference (topv w.r.t. x through the router). The expert-parallel layer adds its routed
-    experts to the shared output."""
-    x2d = _bf16(x2d, "router_and_shared: x")
-    cfg = _Cfg(_lib.F_ROUTER, x2d, top_k, W["mlp.gate.weight"].shape[0])
-    cfg.t["w_router"] = _bf16(W["mlp.gate.weight"], "router weight")
-    cfg.act_sh = "silu"
-    pre = "mlp.shared_expert."
-    gu = W.get(pre + "gate_up_proj.weight")
-    if gu is None:
-        gu = torch.cat((W[pre + "gate_proj.weight"], W[pre + "up_proj.weight"]))
-    _set_shared(cfg, gu, W[pre + "down_proj.weight"], lora_sh, W["mlp.shared_expert_gate.weight"])
-    out, probs, topv, topi = _apply(cfg, x2d, lora_sh=lora_sh)
-    if stats is not None:
-        stats(probs, topv, topi)
-    return out, probs, topv, topi
-
-
 def moe_block_gemma4(h, xm, W, ex: LayerExperts, top_k: int, eps: float, act="gelu_tanh", lora_layer=None,
                      stats=None):
     """The Gemma 4 MoE block of smel/layer_runner.py:249-261 after the attention residual: the dense MLP (with the
