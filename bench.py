@@ -290,29 +290,38 @@ def run_ours(args, world, rank, local):
             gd[b].copy_(gh, non_blocking=True)
             up_done[b].record(copy_s)
 
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def e2e_loop(n):
+        """n steps of the pipeline; returns the CUDA events around them (on the copy stream and the step stream)."""
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(copy_s)
+        side.wait_event(e0)
+        upload(0)
+        dxs = [None, None]
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                upload(i + 1)
+            side.wait_event(up_done[b])
+            if i >= 2:
+                side.wait_event(down_done[b])  # the host copy of dX two steps back has left this buffer's slot
+            dxs[b] = step(xd[b], gd[b])
+            dp_sync()
+            used[b].record(side)
+            with torch.cuda.stream(copy_s):
+                copy_s.wait_event(used[b])
+                dxh[b].copy_(dxs[b], non_blocking=True)
+                down_done[b].record(copy_s)
+        side.wait_stream(copy_s)
+        e1.record(side)
+        return e0, e1
+
+    # untimed warm-up of the same pipeline first: the copy stream, the device buffers and the first pinned
+    # transfers cost ~0.2 s once, which spread over the timed steps would halve the number
+    e2e_loop(max(args.warmup, 2))
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
-    e0.record(copy_s)
-    side.wait_event(e0)
-    upload(0)
-    dxs = [None, None]
-    for i in range(args.steps):
-        b = i % 2
-        if i + 1 < args.steps:
-            upload(i + 1)
-        side.wait_event(up_done[b])
-        if i >= 2:
-            side.wait_event(down_done[b])  # the host copy of dX two steps back has left this buffer's slot
-        dxs[b] = step(xd[b], gd[b])
-        dp_sync()
-        used[b].record(side)
-        with torch.cuda.stream(copy_s):
-            copy_s.wait_event(used[b])
-            dxh[b].copy_(dxs[b], non_blocking=True)
-            down_done[b].record(copy_s)
-    side.wait_stream(copy_s)
-    e1.record(side)
+    e0, e1 = e2e_loop(args.steps)
     torch.cuda.synchronize()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
     e2e = {"value": world * cfg["T"] * args.steps / (ms_e2e / 1e3), "unit": "tokens/s",
