@@ -214,13 +214,13 @@ def run_ours(args, world, rank, local):
         with torch.no_grad():  # routing of all ranks' tokens: the per-expert loads the placement balances
             smelb.moe_forward(layer["x"], W, ex, K, None, stats=lambda p, v, i: rec.update(i=i))
         loads = torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist()
-        costs = ep.expert_row_costs(ex)
+        costs = ep.expert_costs(ex, loads)
         placement = ep.balanced_placement(loads, world, costs)
         per_rank = [sum(loads[e] for e in ids) for ids in placement]
-        placement_note = {"placement": f"balanced by routed cost (a frozen int4 row {ep.FROZEN_ROW_COST:g}x a "
-                                       f"selected expert's)",
+        placement_note = {"placement": f"balanced by routed cost (rows, + {ep.FROZEN_TILE_COST:g} per frozen expert "
+                                       f"token tile)",
                           "rows_per_rank": per_rank,
-                          "cost_per_rank": [round(sum(loads[e] * costs[e] for e in ids)) for ids in placement]}
+                          "cost_per_rank": [round(sum(costs[e] for e in ids)) for ids in placement]}
         shard = ep.shard_layer(ex, lora, rank, world, placement)
         comm = ep.EPGroup(cap=cfg["T"], H=cfg["H"], K=K)
         params = list(shard.lora.parameters())
@@ -621,8 +621,8 @@ def run_block(args, world, rank, local, n_layers=24, n_micro=16):
                 rec = {}
                 with torch.no_grad():
                     smelb.moe_forward(x_all[:n_micro * T], W, Ly["ex"], K, None, stats=lambda p, v, i: rec.update(i=i))
-                placement = ep.balanced_placement(torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist(),
-                                                  world, ep.expert_row_costs(Ly["ex"]))
+                loads = torch.bincount(rec["i"].reshape(-1), minlength=cfg["E"]).tolist()
+                placement = ep.balanced_placement(loads, world, ep.expert_costs(Ly["ex"], loads))
         else:
             W["mlp.gate.weight"] = router
         if world > 1:

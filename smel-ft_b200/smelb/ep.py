@@ -51,32 +51,36 @@ def contiguous_placement(E: int, world: int):
     return [list(range(*expert_range(E, r, world))) for r in range(world)]
 
 
-# Cost of one routed row on the owner's GEMMs, by expert kind, relative to a selected (bf16 + LoRA) expert's row: a
-# frozen int4 row costs about three (the engine's int4 tiles run at about a third of the bf16 tiles' rate, the
-# dequantisation into TMEM bounding them at ~67 rows per expert: measured 191.6 vs 59.4 us for the gate/up of the
-# two halves of config 2's rows, 119.7 vs 34.3 us for the down projection).
-FROZEN_ROW_COST = 3.0
+# The cost of an expert's routed rows on the owner's GEMMs, in row-equivalents: every row costs one, and a frozen
+# int4 expert adds a fixed cost per 192-row token tile, the expansion of its whole weight tile into TMEM for that
+# token tile. Fitted to the kernel times of a config-2 step (forward, recompute and backward: 959 us for the frozen
+# experts' 16.4k rows over 244 experts, 300 us for the selected experts' 16.4k rows over 12): 18.3 ns per row for
+# both kinds, 2.7 us (about 150 rows) per frozen expert token tile.
+FROZEN_TILE_COST = 150.0
+TOKEN_TILE_ROWS = 192
 
 
-def expert_row_costs(ex, frozen: float = FROZEN_ROW_COST, selected: float = 1.0):
-    """Per-expert cost of one routed row for balanced_placement: `selected` for the layer's selected experts,
-    `frozen` for the rest (ex: LayerExperts)."""
-    costs = [float(frozen)] * ex.E
-    for e in (ex.sel_ids.tolist() if ex.sel_ids is not None else []):
-        costs[e] = float(selected)
-    return costs
+def expert_costs(ex, loads, frozen_tile: float = FROZEN_TILE_COST):
+    """Per-expert cost of `loads` routed rows (row-equivalents) for balanced_placement; ex: LayerExperts."""
+    sel = set(ex.sel_ids.tolist()) if ex.sel_ids is not None else set()
+    out = []
+    for e, c in enumerate(loads):
+        c = float(c)
+        tiles = math.ceil(c / TOKEN_TILE_ROWS) if c > 0 else 0
+        out.append(c + (0.0 if e in sel else frozen_tile * tiles))
+    return out
 
 
-def balanced_placement(loads, world: int, row_cost=None):
+def balanced_placement(loads, world: int, cost=None):
     """E / world experts per rank with the routed cost balanced: the experts in decreasing cost (ties: smaller id)
     each go to the least-loaded rank that still has room (ties: smaller rank). Returns the sorted expert ids of every
-    rank. `loads`: rows routed to each expert on a representative batch; `row_cost`: the cost of one row of each
-    expert (expert_row_costs; default 1: rows balanced as they are)."""
+    rank. `loads`: rows routed to each expert on a representative batch; `cost`: each expert's cost of those rows
+    (expert_costs; default: the rows themselves)."""
     loads = [float(v) for v in loads]
     E = len(loads)
     if E % world:
         raise ValueError(f"{E} experts do not split evenly over {world} ranks")
-    w = [loads[e] * (float(row_cost[e]) if row_cost is not None else 1.0) for e in range(E)]
+    w = [float(cost[e]) for e in range(E)] if cost is not None else loads
     cap = E // world
     order = sorted(range(E), key=lambda e: (-w[e], e))
     tot = [0.0] * world

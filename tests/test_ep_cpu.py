@@ -49,29 +49,35 @@ def test_balanced_placement_is_even_and_balanced():
 
 
 
-def test_balanced_placement_weighs_row_cost():
-    """Config-2-like loads over 8 ranks: 12 hot selected experts (half the rows) and 244 frozen ones whose rows cost
-    three times as much. Balancing rows alone leaves the ranks with one selected expert a third more work than those
-    with two; balancing the cost evens it out, every rank keeping E / world experts."""
+def test_balanced_placement_weighs_expert_cost():
+    """Config-2-like loads over 8 ranks: 12 hot selected experts (half the rows) and 244 frozen ones, each frozen
+    expert adding a fixed cost per token tile (expert_costs). Balancing that cost keeps every rank within 2% of the
+    mean (rows alone leave more than 3%), every rank keeping E / world experts."""
     from smelb import ep
     import random
+
+    class _Ex:  # the one field expert_costs reads
+        pass
     rnd = random.Random(3)
     E, world = 256, 8
     sel = list(range(0, 24, 2))
     loads = [rnd.randint(20, 220) for _ in range(E)]
     for e in sel:
         loads[e] = 1400 + rnd.randint(0, 200)
-    costs = [1.0 if e in sel else ep.FROZEN_ROW_COST for e in range(E)]
+    ex = _Ex()
+    ex.sel_ids = torch.tensor(sel)
+    costs = ep.expert_costs(ex, loads)
+    assert all(costs[e] == loads[e] for e in sel)
+    assert all(costs[e] > loads[e] for e in range(E) if e not in sel)
 
     def spread(pl):
-        c = [sum(loads[e] * costs[e] for e in ids) for ids in pl]
+        c = [sum(costs[e] for e in ids) for ids in pl]
         return max(c) / (sum(c) / len(c))
     rows_only = ep.balanced_placement(loads, world)
     weighted = ep.balanced_placement(loads, world, costs)
     assert all(len(ids) == E // world for ids in weighted)
     assert sorted(e for ids in weighted for e in ids) == list(range(E))
     assert spread(weighted) < 1.02 < spread(rows_only)
-
 
 def test_shard_layer_takes_the_placed_experts():
     import smelb
