@@ -266,9 +266,10 @@ __global__ void router_topk_kernel(const bf16* __restrict__ logits, long long ld
       v[i] = -INFINITY;
     }
   }
-  // top-k: repeated warp arg-max; ties resolved towards the smaller expert id
-  float tv[32];
-  int te[32];
+  // top-k: repeated warp arg-max; ties resolved towards the smaller expert id. Lane k keeps the k-th choice
+  // (K <= 32), so the choices stay in registers.
+  float myv = 0.f;
+  int mye = 0;
   for (int k = 0; k < K; ++k) {
     float bv = -INFINITY;
     int be = 0x7fffffff;
@@ -292,20 +293,21 @@ __global__ void router_topk_kernel(const bf16* __restrict__ logits, long long ld
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i)
       if (lane + 32 * i == be) v[i] = -INFINITY;
-    tv[k] = bv;
-    te[k] = be;
-  }
-  if (lane == 0) {
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) s += tv[k];
-    for (int k = 0; k < K; ++k) {
-      float val = tv[k] / s;
-      if (per_expert_scale) val = val * __bfloat162float(per_expert_scale[te[k]]);
-      const long long o = (long long)warp * K + k;
-      if (topv_f32) reinterpret_cast<float*>(topv)[o] = val;
-      else reinterpret_cast<bf16*>(topv)[o] = __float2bfloat16_rn(val);
-      topi[o] = te[k];
+    if (lane == k) {
+      myv = bv;
+      mye = be;
     }
+  }
+  // the renormalising sum in k order (every lane forms the same sum), then lane k writes choice k
+  float s = 0.f;
+  for (int k = 0; k < K; ++k) s += __shfl_sync(0xffffffffu, myv, k);
+  if (lane < K) {
+    float val = myv / s;
+    if (per_expert_scale) val = val * __bfloat162float(per_expert_scale[mye]);
+    const long long o = (long long)warp * K + lane;
+    if (topv_f32) reinterpret_cast<float*>(topv)[o] = val;
+    else reinterpret_cast<bf16*>(topv)[o] = __float2bfloat16_rn(val);
+    topi[o] = mye;
   }
 }
 
