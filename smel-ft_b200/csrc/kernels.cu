@@ -228,13 +228,15 @@ int int4_pack_sz(const void* scale, const void* zero, uint32_t* szT, long long n
 // ============================================================================================ router
 // One warp per token: probs = softmax_fp32(logits), top-k by (value desc, expert id asc), renormalised in fp32 over
 // the chosen k (summed in k order), optionally multiplied by per_expert_scale (Gemma 4), stored as bf16 or fp32.
+// Lane l holds experts l, l + 32, ..., kMaxPer of them (E <= 32 * kMaxPer): the top-k rounds scan only the slots an
+// expert count can fill (the rounds are the kernel's time; a fixed 16 slots doubled it at 256 experts).
+template <int kMaxPer>
 __global__ void router_topk_kernel(const bf16* __restrict__ logits, long long ld, int T, int E, int K,
                                    float* __restrict__ probs, void* __restrict__ topv, int topv_f32,
                                    long long* __restrict__ topi, const bf16* __restrict__ per_expert_scale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const bf16* lg = logits + (long long)warp * ld;
-  constexpr int kMaxPer = 16;  // E <= 512
   float v[kMaxPer];
   float mx = -INFINITY;
 #pragma unroll
@@ -317,8 +319,9 @@ int router_topk(const void* logits, long long ld, int T, int E, int K, float* pr
   if (T == 0) return kOk;
   const int threads = 256;
   const int blocks = (T * 32 + threads - 1) / threads;
-  router_topk_kernel<<<blocks, threads, 0, st>>>((const bf16*)logits, ld, T, E, K, probs, topv, topv_f32 ? 1 : 0,
-                                                 topi, (const bf16*)per_expert_scale);
+  auto kern = E <= 128 ? router_topk_kernel<4> : E <= 256 ? router_topk_kernel<8> : router_topk_kernel<16>;
+  kern<<<blocks, threads, 0, st>>>((const bf16*)logits, ld, T, E, K, probs, topv, topv_f32 ? 1 : 0, topi,
+                                   (const bf16*)per_expert_scale);
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
@@ -545,6 +548,7 @@ int dispatch_plan(const long long* topi, long long R, int E, const uint8_t* sel_
 // contiguous chunk of choices, pass 2 derives every CTA's base per expert from the earlier chunks' counts, the
 // (padded) segment offsets, and then ranks its chunk warp by warp in order, so the result equals the single-CTA plan.
 constexpr int kPlanMtWarps = 8;
+constexpr long long kPlanMtChunk = 1024;
 
 __global__ void __launch_bounds__(256) plan_count_kernel(const long long* __restrict__ topi, long long R, int E,
                                                          long long chunk, int* __restrict__ cnt, int* __restrict__ err) {
@@ -574,11 +578,17 @@ __global__ void __launch_bounds__(kPlanMtWarps * 32) plan_rank_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = gridDim.x, b = blockIdx.x;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    // the column of e over the nb CTAs' counts, 8 loads in flight at a time
     int bs = 0, t = 0;
-    for (int bb = 0; bb < nb; ++bb) {
-      const int c = cnt[(long long)bb * E + e];
-      bs += bb < b ? c : 0;
-      t += c;
+    for (int bb0 = 0; bb0 < nb; bb0 += 8) {
+      int c[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c[j] = bb0 + j < nb ? cnt[(long long)(bb0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        bs += bb0 + j < b ? c[j] : 0;
+        t += c[j];
+      }
     }
     base[e] = bs;
     tot[e] = t;
@@ -636,9 +646,11 @@ __global__ void __launch_bounds__(kPlanMtWarps * 32) plan_rank_kernel(
   }
   __syncthreads();
   const unsigned lt_mask = (1u << lane) - 1u;
+  long long e_next = w0 + lane < w1 ? topi[w0 + lane] : -1;  // the next round's choice, loaded a round ahead
   for (long long r0 = w0; r0 < w1; r0 += 32) {
     const long long i = r0 + lane;
-    long long e64 = i < w1 ? topi[i] : -1;
+    const long long e64 = e_next;
+    e_next = r0 + 32 + lane < w1 ? topi[r0 + 32 + lane] : -1;
     const int e = (e64 >= 0 && e64 < E) ? (int)e64 : -1;
     const unsigned active = __ballot_sync(0xffffffffu, e >= 0);
     const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -663,7 +675,9 @@ int dispatch_plan_mt(const long long* topi, long long R, int E, const uint8_t* s
                      long long scratch_ints, cudaStream_t st) {
   SMELB_CHECK_ARG(E >= 1 && E <= kPlanMaxE, kErrShape, "dispatch_plan: E=%d (max %d)", E, kPlanMaxE);
   SMELB_CHECK_ARG(pad >= 1 && R >= 0 && R < (1LL << 30), kErrShape, "dispatch_plan: R=%lld pad=%d", R, pad);
-  long long nb = std::min<long long>(148, std::max<long long>(1, R / 256));
+  // CTAs: every CTA sums the counts of the CTAs before it, one dependent L2 round trip per 8 of them, so fewer CTAs
+  // with more choices each (about 1024) finish sooner than one CTA per SM (32768 choices: 11 us at 127 CTAs)
+  long long nb = R / 256 < 2 ? 1 : std::min<long long>(148, std::max<long long>(2, R / kPlanMtChunk));
   nb = std::min<long long>(nb, scratch_ints / E);
   if (nb < 2) return dispatch_plan(topi, R, E, sel_mask, pad, counts, gcounts, offsets, row_of, src_of, order, total, st);
   const long long chunk = (R + nb - 1) / nb;
@@ -809,6 +823,16 @@ int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st) {
   SMELB_CUDA(cudaGetLastError());
   count_launch();
   return kOk;
+}
+
+// CTAs of one full wave of a grid-stride kernel (every SM at its occupancy limit): launched with this many, the CTAs
+// loop over the units with no partly filled tail wave (a grid of 1184 CTAs at 6 resident per SM is 1.33 waves).
+template <class Kern>
+long long one_wave(Kern kernel, int threads) {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n < 1) n = 1;
+  return (long long)num_sms(dev) * n;
 }
 
 // ============================================================================================ gather
@@ -1012,7 +1036,8 @@ int combine_bwd_rows(const void* g, const void* y, const int* src_of, const int*
   SMELB_CHECK_ARG(H % 8 == 0, kErrShape, "combine_bwd: H=%d", H);
   if (max_rows == 0) return kOk;
   const int threads = 256;
-  const long long blocks = std::min<long long>((max_rows * 32 + threads - 1) / threads, 148LL * 8);
+  static const long long wave = one_wave(combine_bwd_rows_kernel, threads);
+  const long long blocks = std::min<long long>((max_rows * 32 + threads - 1) / threads, wave);
   combine_bwd_rows_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)g, (const bf16*)y, src_of, total, max_rows,
                                                            topv, topv_f32 ? 1 : 0, K, H, (bf16*)dy, dtopv);
   SMELB_CUDA(cudaGetLastError());
@@ -1065,56 +1090,65 @@ int shared_gate_bwd(const void* g, const void* y_sh, const void* gl, int T, int 
   return kOk;
 }
 
-// Final dX of the layer, one warp per token, fp32 accumulation then one rounding:
+// Final dX of the layer, fp32 accumulation then one rounding:
 //   dx[t] = sum_k dxs[row_of[t,k]] + dx_sh[t] + dx_r[t] + dgl[t] * w_sg
-__global__ void dx_reduce_kernel(const bf16* __restrict__ dxs, const int* __restrict__ row_of, int K, int T, int H,
-                                 const bf16* __restrict__ dx_sh, const bf16* __restrict__ dx_r,
-                                 const float* __restrict__ dgl, const bf16* __restrict__ w_sg, bf16* __restrict__ dx) {
+// One warp per (token, 256-column chunk), 8 columns per lane: a warp loads the token's row ids (one broadcast load
+// each), then eight rows' 16-byte pieces together, and adds them in k order. Small units keep many warps resident
+// (a warp per whole token, walking its 2048 columns in eight dependent steps, moved the bytes at about half of HBM).
+__global__ void __launch_bounds__(256) dx_reduce_kernel(const bf16* __restrict__ dxs, const int* __restrict__ row_of,
+                                                        int K, int T, int H, const bf16* __restrict__ dx_sh,
+                                                        const bf16* __restrict__ dx_r, const float* __restrict__ dgl,
+                                                        const bf16* __restrict__ w_sg, bf16* __restrict__ dx) {
   const int lane = threadIdx.x & 31;
+  const int chunks = (H + 255) / 256;
+  const long long units = (long long)T * chunks;
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
-    const float dg = dgl ? dgl[t] : 0.f;
-    for (int c = lane * 8; c < H; c += 256) {
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      auto add = [&](const uint4& v) {
-        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+  for (long long u = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; u < units; u += nw) {
+    const long long t = u / chunks;
+    const int c = (int)(u - t * chunks) * 256 + lane * 8;
+    if (c >= H) continue;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    auto add = [&](const uint4& v) {
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(p[j]);
-          acc[2 * j] += f.x;
-          acc[2 * j + 1] += f.y;
-        }
-      };
-      if (dxs) {
-        // the rows of eight k are loaded together, then added in k order
-        for (int k0 = 0; k0 < K; k0 += 8) {
-          uint4 v[8];
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            if (k0 + kk < K) v[kk] = *reinterpret_cast<const uint4*>(dxs + (long long)row_of[t * K + k0 + kk] * H + c);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            if (k0 + kk < K) add(v[kk]);
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
       }
-      if (dx_sh) add(*reinterpret_cast<const uint4*>(dx_sh + t * H + c));
-      if (dx_r) add(*reinterpret_cast<const uint4*>(dx_r + t * H + c));
-      if (dgl && w_sg) {
-        const uint4 v = *reinterpret_cast<const uint4*>(w_sg + c);
-        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+    };
+    if (dxs) {
+      for (int k0 = 0; k0 < K; k0 += 8) {
+        int rows[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(p[j]);
-          acc[2 * j] = fmaf(dg, f.x, acc[2 * j]);
-          acc[2 * j + 1] = fmaf(dg, f.y, acc[2 * j + 1]);
-        }
+        for (int kk = 0; kk < 8; ++kk) rows[kk] = k0 + kk < K ? row_of[t * K + k0 + kk] : 0;
+        uint4 v[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          if (k0 + kk < K) v[kk] = *reinterpret_cast<const uint4*>(dxs + (long long)rows[kk] * H + c);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          if (k0 + kk < K) add(v[kk]);
       }
-      uint4 o;
-      __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-      *reinterpret_cast<uint4*>(dx + t * H + c) = o;
     }
+    if (dx_sh) add(*reinterpret_cast<const uint4*>(dx_sh + t * H + c));
+    if (dx_r) add(*reinterpret_cast<const uint4*>(dx_r + t * H + c));
+    if (dgl && w_sg) {
+      const float dg = dgl[t];
+      const uint4 v = *reinterpret_cast<const uint4*>(w_sg + c);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p[j]);
+        acc[2 * j] = fmaf(dg, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(dg, f.y, acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) po[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(dx + t * H + c) = o;
   }
 }
 
@@ -1123,7 +1157,9 @@ int dx_reduce(const void* dxs, const int* row_of, int K, int T, int H, const voi
   SMELB_CHECK_ARG(H % 8 == 0 && K <= 32, kErrShape, "dx_reduce: H=%d K=%d", H, K);
   if (T == 0) return kOk;
   const int threads = 256;
-  const long long blocks = std::min<long long>(((long long)T * 32 + threads - 1) / threads, 148LL * 8);
+  const long long units = (long long)T * ((H + 255) / 256);
+  static const long long wave = one_wave(dx_reduce_kernel, threads);
+  const long long blocks = std::min<long long>((units * 32 + threads - 1) / threads, wave);
   dx_reduce_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)dxs, row_of, K, T, H, (const bf16*)dx_sh,
                                                     (const bf16*)dx_r, dgl, (const bf16*)w_sg, (bf16*)dx);
   SMELB_CUDA(cudaGetLastError());
