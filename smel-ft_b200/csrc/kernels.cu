@@ -876,7 +876,10 @@ int gather_rows(const void* x, int H, int K, const int* src_of, const int* total
 // One warp per unit = (token, slice of nch 256-column chunks): the unit's K row indices and weights are loaded once
 // (eight at a time), then each chunk's eight rows are loaded together and summed in k order. The slice is the whole
 // row when there are enough tokens to fill the GPU and shrinks to one chunk for a handful of tokens (decode).
-constexpr int kCombineMaxChunks = 2;
+#ifndef SMELB_COMBINE_CHUNKS
+#define SMELB_COMBINE_CHUNKS 2
+#endif
+constexpr int kCombineMaxChunks = SMELB_COMBINE_CHUNKS;
 
 __global__ void combine_fwd_kernel(const bf16* __restrict__ y, const int* __restrict__ row_of,
                                    const void* __restrict__ topv, int topv_f32, int T, int K, int H, int nch,
@@ -969,13 +972,14 @@ int combine_fwd(const void* y, const int* row_of, const void* topv, bool topv_f3
   if (T == 0) return kOk;
   const int threads = 256;
   const int chunks = (H + 255) / 256;
-  // chunks per unit: as many as keep at least ~8 warps per SM busy, at most kCombineMaxChunks (2: with 4 the
-  // kernel needs 128 registers and half the warps per SM, and runs 5% slower at 4092 tokens)
+  // chunks per unit: as many as keep at least ~8 warps per SM busy, at most kCombineMaxChunks (2: at 4092 tokens 1
+  // chunk per unit ran 15% slower, 4 chunks need 128 registers and half the warps per SM and ran 5% slower)
   int nch = kCombineMaxChunks;
   while (nch > 1 && (long long)T * ((chunks + nch - 1) / nch) < 148LL * 8) nch >>= 1;
   nch = std::min(nch, chunks);
   const long long units = (long long)T * ((chunks + nch - 1) / nch);
-  const long long blocks = std::min<long long>((units * 32 + threads - 1) / threads, 148LL * 8);
+  static const long long wave = one_wave(combine_fwd_kernel, threads);
+  const long long blocks = std::min<long long>((units * 32 + threads - 1) / threads, wave);
   combine_fwd_kernel<<<(int)blocks, threads, 0, st>>>((const bf16*)y, row_of, topv, topv_f32 ? 1 : 0, T, K, H, nch,
                                                       (const bf16*)y_sh, (const bf16*)gl, y != nullptr ? 1 : 0,
                                                       (bf16*)out);
