@@ -1009,22 +1009,32 @@ __global__ void combine_bwd_rows_kernel(const bf16* __restrict__ g, const bf16* 
     const float w = topv_f32 ? reinterpret_cast<const float*>(topv)[src]
                              : __bfloat162float(reinterpret_cast<const bf16*>(topv)[src]);
     float dot = 0.f;
-    for (int c = lane; c < H / 8; c += 32) {
-      const uint4 gv = reinterpret_cast<const uint4*>(g + t * H)[c];
-      const uint4 yv = reinterpret_cast<const uint4*>(y + r * H)[c];
-      const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
-      const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv);
-      uint4 o;
-      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+    // four 16-byte pieces of g and y per lane are loaded before any is used (the dot product keeps its order)
+    for (int c0 = lane; c0 < H / 8; c0 += 128) {
+      uint4 gv[4], yv[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 gf = __bfloat1622float2(gp[j]);
-        const float2 yf = __bfloat1622float2(yp[j]);
-        op[j] = __floats2bfloat162_rn(gf.x * w, gf.y * w);
-        dot = fmaf(gf.x, yf.x, dot);
-        dot = fmaf(gf.y, yf.y, dot);
+      for (int q = 0; q < 4; ++q)
+        if (c0 + 32 * q < H / 8) {
+          gv[q] = reinterpret_cast<const uint4*>(g + t * H)[c0 + 32 * q];
+          yv[q] = reinterpret_cast<const uint4*>(y + r * H)[c0 + 32 * q];
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (c0 + 32 * q >= H / 8) break;
+        const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv[q]);
+        const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv[q]);
+        uint4 o;
+        __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 gf = __bfloat1622float2(gp[j]);
+          const float2 yf = __bfloat1622float2(yp[j]);
+          op[j] = __floats2bfloat162_rn(gf.x * w, gf.y * w);
+          dot = fmaf(gf.x, yf.x, dot);
+          dot = fmaf(gf.y, yf.y, dot);
+        }
+        d[c0 + 32 * q] = o;
       }
-      d[c] = o;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
@@ -1059,22 +1069,31 @@ __global__ void shared_gate_bwd_kernel(const bf16* __restrict__ g, const bf16* _
   for (long long t = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; t < T; t += nw) {
     const float sb = bf16_round(1.0f / (1.0f + expf(-__bfloat162float(gl[t]))));
     float dot = 0.f;
-    for (int c = lane; c < H / 8; c += 32) {
-      const uint4 gv = reinterpret_cast<const uint4*>(g + t * H)[c];
-      const uint4 yv = reinterpret_cast<const uint4*>(y_sh + t * H)[c];
-      const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
-      const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv);
-      uint4 o;
-      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+    for (int c0 = lane; c0 < H / 8; c0 += 128) {
+      uint4 gv[4], yv[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 gf = __bfloat1622float2(gp[j]);
-        const float2 yf = __bfloat1622float2(yp[j]);
-        op[j] = __floats2bfloat162_rn(gf.x * sb, gf.y * sb);
-        dot = fmaf(gf.x, yf.x, dot);
-        dot = fmaf(gf.y, yf.y, dot);
+      for (int q = 0; q < 4; ++q)
+        if (c0 + 32 * q < H / 8) {
+          gv[q] = reinterpret_cast<const uint4*>(g + t * H)[c0 + 32 * q];
+          yv[q] = reinterpret_cast<const uint4*>(y_sh + t * H)[c0 + 32 * q];
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (c0 + 32 * q >= H / 8) break;
+        const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv[q]);
+        const __nv_bfloat162* yp = reinterpret_cast<const __nv_bfloat162*>(&yv[q]);
+        uint4 o;
+        __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 gf = __bfloat1622float2(gp[j]);
+          const float2 yf = __bfloat1622float2(yp[j]);
+          op[j] = __floats2bfloat162_rn(gf.x * sb, gf.y * sb);
+          dot = fmaf(gf.x, yf.x, dot);
+          dot = fmaf(gf.y, yf.y, dot);
+        }
+        reinterpret_cast<uint4*>(dy_sh + t * H)[c0 + 32 * q] = o;
       }
-      reinterpret_cast<uint4*>(dy_sh + t * H)[c] = o;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
