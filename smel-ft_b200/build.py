@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 OUT = os.path.join(HERE, "smelb", "libsmelb.so")
-SOURCES = ["host.cu", "kernels.cu", "gemm.cu", "ops.cu", "ep.cu", "gemv.cu"]
+SOURCES = ["host.cu", "kernels.cu", "gemm.cu", "ops.cu", "ep.cu", "gemv.cu", "dense.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
          "-Xcompiler", "-fPIC,-O2", "-I" + os.path.join(HERE, "..", "include")]

@@ -154,6 +154,31 @@ int split_counts(const int* counts, int E, int thr, int* hot, int* cold, cudaStr
 // Whether the GEMV takes a reduction length K (its shared-memory stages must hold two tasks).
 bool int4_gemv_supported(bool glu, int K);
 
+// Small-token dense projection with bf16 weights (the shared expert at a handful of tokens):
+// out[t][m] = bf16(sum_k W[m][k] x[t][k]) for m < M, or with glu, over the gate row f and the up row inter + f,
+// g = bf16(.), u = bf16(.), out[t][f] = bf16(bf16(act(g)) * u) for f < inter, (g | u) into hout when given.
+struct DenseGemvArgs {
+  const bf16* w;  // [M][ldw], M = 2 * inter with glu
+  long long ldw;
+  int M;
+  const bf16* x;  // [T][ldx]
+  long long ldx;
+  int T, K;
+  bool glu;
+  int inter, act;
+  bf16* out;
+  long long ldo;
+  bf16* hout;
+  long long ldh;
+};
+// Its FMA work grows with the tokens (~3 us per token for the Qwen3.6 shared expert against ~0.5 us for the engine's
+// tiles; 7.3 against 23.7 us at one token, 52 against 32 at sixteen), so it takes up to 6 tokens.
+constexpr int kDenseGemvMaxT = 6;
+// Whether dense_gemv takes these sizes and pointers (T <= kDenseGemvMaxT, K a multiple of 8 up to 4096, 16-byte
+// aligned rows); callers take the GEMM engine otherwise.
+bool dense_gemv_supported(const DenseGemvArgs& a);
+int dense_gemv(const DenseGemvArgs& a, cudaStream_t st);
+
 int rmsnorm_fwd(const NormArgs& a, cudaStream_t st);
 int rmsnorm_bwd(const NormBwdArgs& a, cudaStream_t st);
 

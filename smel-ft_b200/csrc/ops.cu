@@ -375,6 +375,28 @@ FrozenPlan frozen_plan(const smelb_moe_layer& L, const Flags& f) {
   return p;
 }
 
+// The shared expert at a handful of tokens and without LoRA: its gate/up + GLU and its down projection as dense
+// GEMVs instead of engine tiles (forward, and the backward's recompute of its pre-activations, so that saving and
+// recomputing them agree). Off with the small-token GEMV (smelb_set_gemv_rows(0)).
+struct SharedGemv {
+  bool on;
+  DenseGemvArgs glu, down;
+};
+SharedGemv shared_gemv(const smelb_moe_layer& L, const Flags& f, void* hout) {
+  SharedGemv g;
+  memset(&g, 0, sizeof(g));
+  const long long rows = g_gemv_rows.load();
+  if (!f.shared || f.sh_lora || rows <= 0 || L.T > kDenseGemvMaxT || L.T * std::max<long long>(L.K, 1) > rows)
+    return g;
+  const int T = (int)L.T, H = (int)L.H, S = (int)L.S;
+  g.glu = DenseGemvArgs{(const bf16*)L.sh_gu, H, 2 * S, (const bf16*)L.x, H, T, H, true, S, (int)L.act_sh,
+                        (bf16*)L.sh_a, S, (bf16*)hout, 2 * S};
+  g.down = DenseGemvArgs{(const bf16*)L.sh_dn, S, H, (const bf16*)L.sh_a, S, T, S, false, 0, 0, (bf16*)L.sh_y, H,
+                         nullptr, 0};
+  g.on = dense_gemv_supported(g.glu) && dense_gemv_supported(g.down);
+  return g;
+}
+
 // ---------------------------------------------------------------------------------------------- layer forward
 int layer_fwd(const smelb_moe_layer& L) {
   Flags f;
@@ -435,6 +457,7 @@ int layer_fwd(const smelb_moe_layer& L) {
   const Int4Mat dn{L.dn_q, L.dn_sz, E, H, I};
 
   // L2: selected-expert LoRA A product, shared expert gate/up (GLU)
+  const SharedGemv sg = shared_gemv(L, f, f.save ? L.sh_h : nullptr);
   {
     Builder b;
     if (f.sel_lora) {
@@ -445,8 +468,9 @@ int layer_fwd(const smelb_moe_layer& L) {
       out_bf16(P, L.xa, kW64);
       P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
-    if (f.shared) TRY(add_shared_glu(b, L, f, f.save ? L.sh_h : nullptr));
+    if (f.shared && !sg.on) TRY(add_shared_glu(b, L, f, f.save ? L.sh_h : nullptr));
     TRY(b.launch(st));
+    if (sg.on) TRY(dense_gemv(sg.glu, st));
   }
   const long long rows_est = routed_rows(L, f);
   const FrozenPlan fp = frozen_plan(L, f);
@@ -479,7 +503,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       out_bf16(P, L.z, kW64);
       P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
-    if (f.shared) {
+    if (f.shared && !sg.on) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.sh_dn, 1, H, S, false, false));
       TRY(set_b_tokens(P, L.sh_a, T, S));
@@ -488,6 +512,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       out_bf16(P, L.sh_y, H);
     }
     TRY(b.launch(st));
+    if (sg.on) TRY(dense_gemv(sg.down, st));
   }
   // L5: routed down projections
   if (fp.gemv)
@@ -545,10 +570,12 @@ int layer_bwd(const smelb_moe_layer& L) {
     SMELB_CHECK_ARG((!f.routed || L.h) && (!f.shared || L.sh_h), kErrArg, "layer_bwd: recompute needs h / sh_h");
     // the forward's split of the frozen experts (its counts are still in split_counts) and the same kernels
     const FrozenPlan fp = frozen_plan(L, f);
+    const SharedGemv sg = shared_gemv(L, f, L.sh_h);
     Builder b;
-    if (f.shared) TRY(add_shared_glu(b, L, f, L.sh_h));
+    if (f.shared && !sg.on) TRY(add_shared_glu(b, L, f, L.sh_h));
     if (f.routed) TRY(add_routed_glu(b, L, f, L.h, fp.engine));
     TRY(b.launch(st));
+    if (sg.on) TRY(dense_gemv(sg.glu, st));
     if (fp.gemv)
       TRY(gemv_frozen(true, L.xs, H, fp.small, L.offsets, L.frozen_ids, (int)(E - L.n_sel), E, L.gu_q, L.gu_sz, 2 * I,
                       H, I, L.act, routed_rows(L, f), L.a, I, L.h, 2 * I, st));

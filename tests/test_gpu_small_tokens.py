@@ -125,6 +125,42 @@ def test_small_token_training_step_vs_oracle(T, gemv_rows):
     assert smelb.read_status() == 0
 
 
+@pytest.mark.parametrize("T", [1, 4, 6])
+def test_small_token_shared_gemv_training_vs_oracle(T, gemv_rows):
+    """At up to 6 tokens without LoRA the shared expert's projections run as dense GEMVs (csrc/dense.cu) in the
+    forward and in the backward's recompute of its pre-activations: out and dX with the pre-activations saved and
+    recomputed are identical, and both match the oracle (the tile engine run of the same step within 1e-2)."""
+    import smelb
+    gemv_rows(1 << 30)
+    L = _layer(T, 64, "zipf", seed=30 + T)
+    gy = torch.randn(L["x"].shape, generator=torch.Generator(device="cuda:0").manual_seed(5),
+                     device="cuda:0").bfloat16()
+    runs = []
+    for rows, save in ((1 << 30, True), (1 << 30, False), (0, True)):
+        gemv_rows(rows)
+        prev = smelb.set_save_preactivations(save)
+        try:
+            x = L["x"].clone().requires_grad_(True)
+            rec = {}
+            out = smelb.moe_forward(x, L["W"], L["ex"], 8, None, stats=lambda p, v, i: rec.update(i=i))
+            out.backward(gy)
+        finally:
+            smelb.set_save_preactivations(prev)
+        runs.append((out.detach(), x.grad, rec["i"].cpu()))
+    (out, dx, topi), (out_r, dx_r, _), (out_e, dx_e, topi_e) = runs
+    assert torch.equal(out, out_r) and torch.equal(dx, dx_r)
+    if torch.equal(topi, topi_e):
+        _close([("out gemv vs engine", out, out_e), ("dx gemv vs engine", dx, dx_e)], rel=1e-2, cos=0.99995)
+    dt = torch.float64
+    x64 = L["x"].cpu().to(dt).requires_grad_(True)
+    ex = L["ex"]
+    ref, _, _, _ = O.moe_layer(x64, {k: v.cpu().to(dt) for k, v in L["W"].items()}, _Bank(ex.frozen.gu, dt),
+                               _Bank(ex.frozen.dn, dt), 8, act_name=ex.act, topi=topi)
+    ref.backward(gy.cpu().to(dt))
+    _close([("out", out, ref), ("dx", dx, x64.grad)])
+    assert smelb.read_status() == 0
+
+
 @pytest.mark.parametrize("T", [1, 16, 128, 1024])
 def test_gemv_matches_tile_engine_config4(T, gemv_rows):
     import smelb
