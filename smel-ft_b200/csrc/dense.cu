@@ -1,12 +1,13 @@
-// Small-token dense projections with bf16 weights: the shared expert's gate/up + GLU and down projection
-// (smel/moe.py:183-201, shared_mlp without LoRA) when a call has a handful of tokens. The GEMM engine walks each
-// 128-row weight tile's K one 64-wide k-block after the other on one SM (~0.5 us per k-block, 32 of them at
-// K = 2048), so at one token its two shared-expert launches took ~24 us for 6 MB of weights. Here every warp takes
-// whole output rows: a lane loads 8 consecutive k of every 256 of the row (16-byte pieces, a batch of them in flight
+// Small-token dense projections with bf16 weights: the router and shared-gate logits (smel/moe.py:162-167) and the
+// shared expert's gate/up + GLU and down projection (smel/moe.py:183-201, shared_mlp without LoRA) when a call has a
+// handful of tokens. The GEMM engine walks each 128-row weight tile's K one 64-wide k-block after the other on one
+// SM (~0.5 us per k-block, 32 of them at K = 2048), so at one token its two shared-expert launches took ~24 us for
+// 6 MB of weights and its router launch ~17 us for 1 MB. Here every warp takes whole output rows: a lane loads 8 consecutive k of every 256 of the row (16-byte pieces, a batch of them in flight
 // at once), multiplies them with the T token rows staged once per CTA in shared memory (fp32 FMA, which bounds it
 // from about 8 tokens on: it takes up to kDenseGemvMaxT), and the warp sums its lanes. Lane t then writes token t's
 // output: bf16(sum), or for the GLU the engine's epilogue g = bf16(sum_g), u = bf16(sum_u), bf16(bf16(act(g)) * u).
-// The sums are fp32 in a different order than the engine's, so results can differ from it in the last bf16 bit.
+// The sums are fp32 in a different order than the engine's, so results can differ from it in the last bf16 bit (and
+// a near-tie of the router's bf16 logits can then pick another expert).
 #include <mutex>
 
 #include "common.cuh"
@@ -41,9 +42,13 @@ __global__ void __launch_bounds__(kDenseThreads) dense_gemv_kernel(const DenseGe
   __syncthreads();
   constexpr int NR = kGlu ? 2 : 1;
   const int lane = threadIdx.x & 31;
-  const int units = kGlu ? a.inter : a.M;
+  const int units = kGlu ? a.inter : a.M + a.M2;
   const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long u = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < units; u += nw) {
+    // the unit's weight row (the second projection's rows follow the first's) and its output column
+    const bool second = !kGlu && u >= a.M;
+    const long long col = second ? u - a.M : u;
+    const bf16* wbase = second ? a.w2 + col * a.ldw2 : a.w + col * a.ldw;
     float acc[NR][kDenseGemvMaxT];
 #pragma unroll
     for (int r = 0; r < NR; ++r)
@@ -51,7 +56,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_gemv_kernel(const DenseGe
       for (int t = 0; t < kDenseGemvMaxT; ++t) acc[r][t] = 0.f;
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
-      const uint4* wr = reinterpret_cast<const uint4*>(a.w + (u + (long long)r * a.inter) * a.ldw);
+      const uint4* wr = reinterpret_cast<const uint4*>(wbase + (long long)r * a.inter * a.ldw);
       for (int v0 = lane; v0 < kv; v0 += 32 * kDenseBatch) {
         uint4 wv[kDenseBatch];
 #pragma unroll
@@ -97,8 +102,10 @@ __global__ void __launch_bounds__(kDenseThreads) dense_gemv_kernel(const DenseGe
           a.hout[(long long)lane * a.ldh + u] = __float2bfloat16_rn(gb);
           a.hout[(long long)lane * a.ldh + a.inter + u] = __float2bfloat16_rn(ub);
         }
+      } else if (second) {
+        a.out2[(long long)lane * a.ldo2 + col] = __float2bfloat16_rn(mine[0]);
       } else {
-        a.out[(long long)lane * a.ldo + u] = __float2bfloat16_rn(mine[0]);
+        a.out[(long long)lane * a.ldo + col] = __float2bfloat16_rn(mine[0]);
       }
     }
   }
@@ -121,12 +128,13 @@ void raise_smem(Kern k, int bytes) {
 bool dense_gemv_supported(const DenseGemvArgs& a) {
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   return a.T >= 1 && a.T <= kDenseGemvMaxT && a.K >= 8 && a.K % 8 == 0 && a.K <= 4096 && a.ldw % 8 == 0 &&
-         a.ldx % 8 == 0 && al16(a.w) && al16(a.x) && (!a.glu || (a.inter >= 1 && 2 * a.inter <= a.M));
+         a.ldx % 8 == 0 && al16(a.w) && al16(a.x) && (!a.glu || (a.inter >= 1 && 2 * a.inter <= a.M)) &&
+         (a.M2 == 0 || (!a.glu && a.M2 > 0 && a.w2 && a.out2 && a.ldw2 % 8 == 0 && al16(a.w2)));
 }
 
 int dense_gemv(const DenseGemvArgs& a, cudaStream_t st) {
   SMELB_CHECK_ARG(dense_gemv_supported(a), kErrShape, "dense_gemv: T=%d K=%d", a.T, a.K);
-  const int units = a.glu ? a.inter : a.M;
+  const int units = a.glu ? a.inter : a.M + a.M2;
   if (units == 0) return kOk;
   const int smem = a.T * a.K * 2;
   const int warps = kDenseThreads / 32;

@@ -170,6 +170,13 @@ struct DenseGemvArgs {
   long long ldo;
   bf16* hout;
   long long ldh;
+  // optional second plain projection of the same tokens in the same launch (units M .. M + M2 - 1): out2[t][m] =
+  // bf16(sum_k W2[m][k] x[t][k]); not with glu
+  const bf16* w2;
+  long long ldw2;
+  int M2;
+  bf16* out2;
+  long long ldo2;
 };
 // Its FMA work grows with the tokens (~3 us per token for the Qwen3.6 shared expert against ~0.5 us for the engine's
 // tiles; 7.3 against 23.7 us at one token, 52 against 32 at sixteen), so it takes up to 6 tokens.

@@ -382,12 +382,15 @@ struct SharedGemv {
   bool on;
   DenseGemvArgs glu, down;
 };
+// A call with a handful of tokens, with the small-token GEMV switched on (smelb_set_gemv_rows).
+bool dense_small(const smelb_moe_layer& L) {
+  const long long rows = g_gemv_rows.load();
+  return rows > 0 && L.T <= kDenseGemvMaxT && L.T * std::max<long long>(L.K, 1) <= rows;
+}
 SharedGemv shared_gemv(const smelb_moe_layer& L, const Flags& f, void* hout) {
   SharedGemv g;
   memset(&g, 0, sizeof(g));
-  const long long rows = g_gemv_rows.load();
-  if (!f.shared || f.sh_lora || rows <= 0 || L.T > kDenseGemvMaxT || L.T * std::max<long long>(L.K, 1) > rows)
-    return g;
+  if (!f.shared || f.sh_lora || !dense_small(L)) return g;
   const int T = (int)L.T, H = (int)L.H, S = (int)L.S;
   g.glu = DenseGemvArgs{(const bf16*)L.sh_gu, H, 2 * S, (const bf16*)L.x, H, T, H, true, S, (int)L.act_sh,
                         (bf16*)L.sh_a, S, (bf16*)hout, 2 * S};
@@ -416,17 +419,34 @@ int layer_fwd(const smelb_moe_layer& L) {
     TRY(pack_batch(pb, st));
   }
 
-  // L1: everything that reads only x: router logits, shared gate logit, shared LoRA A product
+  // L1: everything that reads only x: router logits, shared gate logit, shared LoRA A product. At a handful of
+  // tokens without the shared LoRA the two logit projections are one dense GEMV launch instead.
+  DenseGemvArgs lg;
+  memset(&lg, 0, sizeof(lg));
+  bool logits_dense = false;
+  if ((f.router || f.sgate) && !f.sh_lora && dense_small(L)) {
+    const bf16* w1 = (const bf16*)(f.router ? L.w_router : L.w_sgate);
+    lg = DenseGemvArgs{w1, H, f.router ? E : 1, (const bf16*)L.x, H, T, H, false, 0, 0,
+                       (bf16*)(f.router ? L.logits : L.sgate_logit), f.router ? E : 1, nullptr, 0};
+    if (f.router && f.sgate) {
+      lg.w2 = (const bf16*)L.w_sgate;
+      lg.ldw2 = H;
+      lg.M2 = 1;
+      lg.out2 = (bf16*)L.sgate_logit;
+      lg.ldo2 = 1;
+    }
+    logits_dense = dense_gemv_supported(lg);
+  }
   {
     Builder b;
-    if (f.router) {
+    if (f.router && !logits_dense) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.w_router, 1, E, H, false, false));
       TRY(set_b_tokens(P, L.x, T, H));
       groups(P, L.tok_count, nullptr, nullptr, nullptr, 1);
       out_bf16(P, L.logits, E);
     }
-    if (f.sgate) {
+    if (f.sgate && !logits_dense) {
       Problem& P = b.add();
       TRY(set_a_bf16(P, L.w_sgate, 1, 1, H, false, false));
       TRY(set_b_tokens(P, L.x, T, H));
@@ -442,6 +462,7 @@ int layer_fwd(const smelb_moe_layer& L) {
       P.m_pad = kW64;  // the block's unused columns are written as zeros
     }
     TRY(b.launch(st));
+    if (logits_dense) TRY(dense_gemv(lg, st));
   }
   if (f.router)
     TRY(router_topk(L.logits, E, T, E, K, L.probs, L.topv, f.topv32, (long long*)L.topi, L.per_expert_scale, st));
