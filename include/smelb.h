@@ -425,8 +425,9 @@ long long smelb_launch_count(void);
 int smelb_gemm_timing(int enable);
 /* Dispatch-row count at or below which the forward's frozen int4 experts (smelb_moe_layer_fwd, and
  * smelb_frozen_experts_fwd over its rows) run as a dequant-GEMV instead of the tile engine; returns the previous
- * value (default 512; 0 keeps every call on the tile engine). Replaces the size switch of no reference interface:
- * smel/moe.py:58-85 has one path at every size. */
+ * value (default 512; 0 keeps every call on the tile engine). Within it, layer calls of at most 6 tokens also take
+ * the router / shared-gate logits and the shared expert (without its LoRA) as dense GEMVs. Replaces the size switch
+ * of no reference interface: smel/moe.py:58-85 has one path at every size. */
 int64_t smelb_set_gemv_rows(int64_t rows);
 int smelb_gemm_timing_read(double* ms_total, long long* launches);
 

@@ -187,8 +187,9 @@ def launch_count() -> int:
 
 
 def set_gemv_rows(rows: int) -> int:
-    """Dispatch rows at or below which the forward's frozen int4 experts run as the dequant-GEMV (0: never);
-    returns the previous value."""
+    """Dispatch rows at or below which the forward's frozen int4 experts run as the dequant-GEMV (0: never); within
+    it, calls of at most 6 tokens also take the router / shared-gate logits and the shared expert (without LoRA) as
+    dense GEMVs. Returns the previous value."""
     return int(load().smelb_set_gemv_rows(int(rows)))
 
 
