@@ -346,8 +346,8 @@ def moe_block_gemma4(h, xm, W, bank_gu, bank_dn, top_k, eps, sel_ids=(), sel_gu=
 def routing_disagreements(topi_got, logits_ref, top_k):
     """Rows whose expert set differs from the reference top-k of `logits_ref` (high precision logits of the same
     inputs), with the logit gap of each swap: the largest |logit(e_ref) - logit(e_got)| over the experts that one
-    side chose and the other did not (SURVEY-style near-tie report: a bf16 logit moves by up to half an ulp, so only
-    near-ties may flip). Returns a list of (row, gap)."""
+    side chose and the other did not (a near-tie report: a bf16 logit moves by up to half an ulp, so only near-ties
+    may flip). Returns a list of (row, gap)."""
     ref = topk_stable(torch.softmax(logits_ref.double(), -1), top_k)
     got = topi_got.cpu()
     out = []
